@@ -1,0 +1,540 @@
+// Single translation unit of libcast_b200.so: the extern "C" entry points
+// declared in include/cast_b200.h and the host-side launch logic.
+#include <cstdarg>
+#include <cmath>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "select_quant.cuh"
+#include "attention.cuh"
+#include "par.cuh"
+
+namespace cast {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string &msg) { g_last_error = msg; }
+
+int fail(int status, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int current_device_sm100(int *num_sms) {
+  int dev = 0;
+  CAST_CUDA_TRY(cudaGetDevice(&dev));
+  int major = 0, minor = 0;
+  CAST_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  CAST_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+  if (major != 10 || minor != 0)
+    return fail(CAST_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                major, minor);
+  if (num_sms) CAST_CUDA_TRY(cudaDeviceGetAttribute(num_sms, cudaDevAttrMultiProcessorCount, dev));
+  return CAST_OK;
+}
+
+int get_encode_tiled(EncodeTiledFn *fn) {
+  static EncodeTiledFn cached = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      cached = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  if (!cached)
+    return fail(CAST_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s", cudaGetErrorString(err));
+  *fn = cached;
+  return CAST_OK;
+}
+
+int make_map_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes,
+                uint64_t d0, uint64_t d1, uint64_t d2, uint32_t box0, uint32_t box1,
+                CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc;
+  int st = get_encode_tiled(&enc);
+  if (st) return st;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * elem_bytes, d0 * d1 * elem_bytes};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CAST_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return CAST_OK;
+}
+
+}  // namespace cast
+
+using namespace cast;
+
+// ===========================================================================
+// status / version
+// ===========================================================================
+extern "C" const char *cast_status_string(int status) {
+  switch (status) {
+    case CAST_OK: return "CAST_OK";
+    case CAST_ERR_INVALID_ARGUMENT: return "CAST_ERR_INVALID_ARGUMENT";
+    case CAST_ERR_UNSUPPORTED: return "CAST_ERR_UNSUPPORTED";
+    case CAST_ERR_ALIGNMENT: return "CAST_ERR_ALIGNMENT";
+    case CAST_ERR_WORKSPACE: return "CAST_ERR_WORKSPACE";
+    case CAST_ERR_CUDA: return "CAST_ERR_CUDA";
+    case CAST_ERR_DEVICE_TIMEOUT: return "CAST_ERR_DEVICE_TIMEOUT";
+    case CAST_ERR_NO_DEVICE: return "CAST_ERR_NO_DEVICE";
+    default: return "CAST_ERR_UNKNOWN";
+  }
+}
+
+extern "C" const char *cast_last_error_message(void) { return g_last_error.c_str(); }
+
+extern "C" int cast_version(void) { return 100; }
+
+extern "C" int cast_device_error(cast_stream_t stream) {
+  CAST_CUDA_TRY(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+  int v = 0, zero = 0;
+  CAST_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_cast_device_error, sizeof(int)));
+  CAST_CUDA_TRY(cudaMemcpyToSymbol(g_cast_device_error, &zero, sizeof(int)));
+  if (v) return fail(v, "a bounded device wait gave up (%s)", cast_status_string(v));
+  return CAST_OK;
+}
+
+// ===========================================================================
+// RCSA selection + quantisation
+// ===========================================================================
+static size_t sq_pooled_bytes(int B, int H, int nqb, int nkb, int D) {
+  return align_up((size_t)B * H * (nqb + nkb) * D * sizeof(double), 256);
+}
+static size_t sq_rms_bytes(int B, int H, int nqb, int nkb) {
+  return align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256);
+}
+
+extern "C" size_t cast_rcsa_select_quant_workspace_bytes(int B, int H, int Lq, int Lk, int D,
+                                                         int block_size) {
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || D <= 0 || block_size <= 0) return 0;
+  const int nqb = ceil_div(Lq, block_size), nkb = ceil_div(Lk, block_size);
+  // pooled vectors, block RMS, and the q/k scales when the caller passes none
+  return sq_pooled_bytes(B, H, nqb, nkb, D) + sq_rms_bytes(B, H, nqb, nkb) +
+         2 * align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256);
+}
+
+extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *v, int B, int H,
+                                      int Lq, int Lk, int D, int block_size, int budget, int rule,
+                                      int32_t *sel_idx, int32_t *sel_cnt, int8_t *q_codes,
+                                      float *q_scales, int8_t *k_codes, float *k_scales,
+                                      int8_t *v_codes, float *v_scales, uint8_t *qk_mode,
+                                      int policy, float int8_tolerance, double *pooled,
+                                      void *workspace, size_t workspace_bytes,
+                                      cast_stream_t stream) {
+  if (!q || !k || !sel_idx || !sel_cnt)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "q, k, sel_idx and sel_cnt are required");
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || block_size <= 0 || budget < 0)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size (B=%d H=%d Lq=%d Lk=%d block=%d budget=%d)",
+                B, H, Lq, Lk, block_size, budget);
+  if (rule != CAST_RULE_BUDGET_CAUSAL) return fail(CAST_ERR_INVALID_ARGUMENT, "unknown rule %d", rule);
+  if (policy < CAST_POLICY_BF16 || policy > CAST_POLICY_AUTO)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "unknown precision policy %d", policy);
+  if (D != 64 && D != 128) return fail(CAST_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", D);
+  const int nqb = ceil_div(Lq, block_size), nkb = ceil_div(Lk, block_size);
+  if (nkb < nqb) return fail(CAST_ERR_INVALID_ARGUMENT, "fewer key blocks (%d) than query blocks (%d)", nkb, nqb);
+  if (budget > 256) return fail(CAST_ERR_UNSUPPORTED, "budget %d > 256", budget);
+  if (!aligned16(q) || !aligned16(k) || (v && !aligned16(v)))
+    return fail(CAST_ERR_ALIGNMENT, "q/k/v must be 16-byte aligned");
+  if ((q_codes && !aligned16(q_codes)) || (k_codes && !aligned16(k_codes)) ||
+      (v_codes && !aligned16(v_codes)))
+    return fail(CAST_ERR_ALIGNMENT, "code buffers must be 16-byte aligned");
+  if (qk_mode && policy == CAST_POLICY_AUTO && (!q_codes || !k_codes))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "the auto policy needs q_codes and k_codes");
+  const size_t need = cast_rcsa_select_quant_workspace_bytes(B, H, Lq, Lk, D, block_size);
+  if (!workspace || workspace_bytes < need)
+    return fail(CAST_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  double *pooled_ws = reinterpret_cast<double *>(ws);
+  ws += sq_pooled_bytes(B, H, nqb, nkb, D);
+  float *rms = reinterpret_cast<float *>(ws);
+  ws += sq_rms_bytes(B, H, nqb, nkb);
+  float *qs = q_scales ? q_scales : reinterpret_cast<float *>(ws);
+  ws += align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256);
+  float *ks = k_scales ? k_scales : reinterpret_cast<float *>(ws);
+  double *pooled_out = pooled ? pooled : pooled_ws;
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int nb_total = nqb + nkb + ((v && v_codes) ? nkb : 0);
+  dim3 grid(nb_total, B * H);
+  const __nv_bfloat16 *qb = static_cast<const __nv_bfloat16 *>(q);
+  const __nv_bfloat16 *kb = static_cast<const __nv_bfloat16 *>(k);
+  const __nv_bfloat16 *vb = static_cast<const __nv_bfloat16 *>(v);
+  if (D == 128)
+    castk::pool_quant_kernel<128><<<grid, 256, 0, s>>>(qb, kb, vb, Lq, Lk, block_size, nqb, nkb,
+                                                       q_codes, qs, k_codes, ks, v_codes, v_scales,
+                                                       pooled_out, rms);
+  else
+    castk::pool_quant_kernel<64><<<grid, 128, 0, s>>>(qb, kb, vb, Lq, Lk, block_size, nqb, nkb,
+                                                      q_codes, qs, k_codes, ks, v_codes, v_scales,
+                                                      pooled_out, rms);
+  CAST_CUDA_TRY(cudaGetLastError());
+  const int keep = std::min(budget, nkb - nqb);
+  const int maxdeg = keep + nqb;
+  const size_t dsm = sizeof(double) * nkb + nkb + 16;
+  if (dsm > 48 * 1024) return fail(CAST_ERR_UNSUPPORTED, "too many key blocks (%d)", nkb);
+  dim3 g2(nqb, B * H);
+  if (D == 128)
+    castk::budget_select_kernel<128><<<g2, 128, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
+                                                          budget, maxdeg, sel_idx, sel_cnt,
+                                                          qk_mode, policy, int8_tolerance);
+  else
+    castk::budget_select_kernel<64><<<g2, 128, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
+                                                         budget, maxdeg, sel_idx, sel_cnt, qk_mode,
+                                                         policy, int8_tolerance);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+// ===========================================================================
+// TABA selection
+// ===========================================================================
+extern "C" size_t cast_taba_select_workspace_bytes(int B, int H, int T, int Hl, int Wl, int D,
+                                                   int tt, int th, int tw) {
+  if (B <= 0 || H <= 0 || T <= 0 || Hl <= 0 || Wl <= 0 || D <= 0 || tt <= 0 || th <= 0 || tw <= 0)
+    return 0;
+  const size_t nblocks = (size_t)ceil_div(T, tt) * ceil_div(Hl, th) * ceil_div(Wl, tw);
+  return align_up((size_t)B * H * 2 * nblocks * D * sizeof(double), 256);
+}
+
+extern "C" int cast_taba_select(const void *q, const void *k, int B, int H, int T, int Hl, int Wl,
+                                int D, int tt, int th, int tw, const int32_t *row_degrees,
+                                int max_degree, int32_t *sel_idx, int32_t *sel_cnt,
+                                double *scores, void *workspace, size_t workspace_bytes,
+                                cast_stream_t stream) {
+  if (!q || !k || !row_degrees || !sel_idx || !sel_cnt)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "q, k, row_degrees, sel_idx, sel_cnt are required");
+  if (B <= 0 || H <= 0 || T <= 0 || Hl <= 0 || Wl <= 0 || tt <= 0 || th <= 0 || tw <= 0)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
+  if (D != 64 && D != 128) return fail(CAST_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", D);
+  const int nh = ceil_div(Hl, th), nw = ceil_div(Wl, tw), nt = ceil_div(T, tt);
+  const int nblocks = nt * nh * nw;
+  if (max_degree <= 0 || max_degree > nblocks)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "max_degree %d outside [1, %d]", max_degree, nblocks);
+  if (!aligned16(q) || !aligned16(k)) return fail(CAST_ERR_ALIGNMENT, "q/k must be 16-byte aligned");
+  const size_t need = cast_taba_select_workspace_bytes(B, H, T, Hl, Wl, D, tt, th, tw);
+  if (!workspace || workspace_bytes < need)
+    return fail(CAST_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+  const size_t dsm = 2 * sizeof(double) * nblocks + nblocks + 16;
+  if (dsm > 48 * 1024) return fail(CAST_ERR_UNSUPPORTED, "too many blocks (%d)", nblocks);
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  double *pooled = static_cast<double *>(workspace);
+  dim3 grid(2 * nblocks, B * H);
+  const __nv_bfloat16 *qb = static_cast<const __nv_bfloat16 *>(q);
+  const __nv_bfloat16 *kb = static_cast<const __nv_bfloat16 *>(k);
+  if (D == 128)
+    castk::pool_grid_kernel<128><<<grid, 256, 0, s>>>(qb, kb, T, Hl, Wl, tt, th, tw, nh, nw, nblocks, pooled);
+  else
+    castk::pool_grid_kernel<64><<<grid, 128, 0, s>>>(qb, kb, T, Hl, Wl, tt, th, tw, nh, nw, nblocks, pooled);
+  CAST_CUDA_TRY(cudaGetLastError());
+  dim3 g2(nblocks, B * H);
+  if (D == 128)
+    castk::taba_select_kernel<128><<<g2, 128, dsm, s>>>(pooled, nblocks, nh, nw, row_degrees,
+                                                        max_degree, sel_idx, sel_cnt, scores);
+  else
+    castk::taba_select_kernel<64><<<g2, 128, dsm, s>>>(pooled, nblocks, nh, nw, row_degrees,
+                                                       max_degree, sel_idx, sel_cnt, scores);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+// ===========================================================================
+// block-sparse attention
+// ===========================================================================
+extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
+                                   const int8_t *q_codes, const float *q_scales,
+                                   const int8_t *k_codes, const float *k_scales,
+                                   const uint8_t *qk_mode, const int32_t *indices,
+                                   const int32_t *counts, int max_degree,
+                                   const uint8_t *key_valid, int B, int H, int Lq, int Lk, int D,
+                                   int q_block, int k_block, float sm_scale, void *out,
+                                   float *lse, cast_stream_t stream) {
+  if (!q || !k || !v || !indices || !counts || !out)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "q, k, v, indices, counts and out are required");
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || q_block <= 0 || k_block <= 0 || max_degree <= 0)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
+  if (D != 128) return fail(CAST_ERR_UNSUPPORTED, "attention head_dim %d (supported: 128)", D);
+  if (q_block % 16 || k_block % 16)
+    return fail(CAST_ERR_UNSUPPORTED, "block sizes must be multiples of 16 (q %d, k %d)", q_block, k_block);
+  if (max_degree > castk::kMaxBlockList)
+    return fail(CAST_ERR_UNSUPPORTED, "max_degree %d > %d", max_degree, castk::kMaxBlockList);
+  const bool have_codes = q_codes && k_codes && q_scales && k_scales;
+  if ((q_codes || k_codes) && !have_codes)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "int8 QK^T needs q_codes, q_scales, k_codes and k_scales");
+  if (qk_mode && !have_codes)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "qk_mode given without int8 codes");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
+      (q_codes && !aligned16(q_codes)) || (k_codes && !aligned16(k_codes)) ||
+      (key_valid && !aligned16(key_valid)))
+    return fail(CAST_ERR_ALIGNMENT, "tensor base pointers must be 16-byte aligned");
+  if (!(sm_scale > 0.0f) || !std::isfinite(sm_scale))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "sm_scale must be positive and finite");
+  if ((long long)B * H * std::max(Lq, Lk) >= (1ll << 31))
+    return fail(CAST_ERR_UNSUPPORTED, "B*H*L exceeds the 32-bit TMA coordinate range");
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+
+  const int BH = B * H;
+  CUtensorMap tm_q8, tm_k8, tm_q16, tm_k16, tm_v;
+  memset(&tm_q8, 0, sizeof(tm_q8));
+  memset(&tm_k8, 0, sizeof(tm_k8));
+  if ((st = make_map_3d(&tm_q16, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, Lq, BH, 64, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_map_3d(&tm_k16, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, Lk, BH, 64, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_map_3d(&tm_v, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, Lk, BH, 64, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if (have_codes) {
+    if ((st = make_map_3d(&tm_q8, q_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, Lq, BH, 128, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    if ((st = make_map_3d(&tm_k8, k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, Lk, BH, 128, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  } else {
+    tm_q8 = tm_q16;  // never read: every work item runs bf16
+    tm_k8 = tm_k16;
+  }
+
+  castk::AttnParams p;
+  p.indices = indices;
+  p.counts = counts;
+  p.q_scales = q_scales;
+  p.k_scales = k_scales;
+  p.qk_mode = qk_mode;
+  p.key_valid = key_valid;
+  p.out = static_cast<__nv_bfloat16 *>(out);
+  p.lse = lse;
+  p.max_degree = max_degree;
+  p.BH = BH;
+  p.Lq = Lq;
+  p.Lk = Lk;
+  p.q_block = q_block;
+  p.k_block = k_block;
+  p.nqb = ceil_div(Lq, q_block);
+  p.nkb = ceil_div(Lk, k_block);
+  p.q_tiles = ceil_div(q_block, 128);
+  p.k_tiles = ceil_div(k_block, 128);
+  p.full_pairs = p.q_tiles / 2;
+  p.n_full_items = BH * p.nqb * p.full_pairs;
+  p.default_mode = have_codes ? 1 : 0;
+  p.sm_scale_log2 = sm_scale * 1.4426950408889634f;
+  const int n_items = p.n_full_items + (p.q_tiles % 2 ? BH * p.nqb : 0);
+
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(castk::rcsa_attention_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    castk::AttnSmem::alloc);
+  });
+  CAST_CUDA_TRY(attr_err);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  castk::rcsa_attention_kernel<<<n_items, castk::kAttnThreads, castk::AttnSmem::alloc, s>>>(
+      tm_q8, tm_k8, tm_q16, tm_k16, tm_v, p);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+// ===========================================================================
+// PAR / FC-PASM
+// ===========================================================================
+static int par_chunks(int C) { return ceil_div(C, castk::kParChunk); }
+
+extern "C" size_t cast_par_fcpasm_workspace_bytes(int T, int H, int W, int C) {
+  if (T <= 0 || H != castk::kParH || W != castk::kParW || C <= 0) return 0;
+  const int nt = std::min(T, castk::kParMaxTargets);
+  const size_t partials = (size_t)castk::kParMaxPairs * castk::kParTiles * par_chunks(C) * castk::kParPartial;
+  const size_t weights = (size_t)nt * castk::kParTiles * castk::kParFreq * 4;
+  const size_t pred = (size_t)nt * castk::kParTiles * castk::kParPix * C;
+  return align_up(partials * 4, 256) + align_up(weights * 4, 256) + align_up(pred * 4, 256);
+}
+
+static void fill_par_tables(castk::ParTables &t, float tau_low, float tau_high, float power) {
+  const double pi = 3.14159265358979323846;
+  double hh[castk::kParTH], hw[castk::kParTW];
+  for (int i = 0; i < castk::kParTH; ++i) hh[i] = 0.5 - 0.5 * std::cos(2.0 * pi * i / (castk::kParTH - 1));
+  for (int j = 0; j < castk::kParTW; ++j) hw[j] = 0.5 - 0.5 * std::cos(2.0 * pi * j / (castk::kParTW - 1));
+  for (int i = 0; i < castk::kParTH; ++i)
+    for (int j = 0; j < castk::kParTW; ++j) {
+      // torch computes the window in float32: outer product then sqrt.
+      const float prod = (float)hh[i] * (float)hw[j];
+      t.win[i * castk::kParTW + j] = std::sqrt(std::max(prod, 0.0f));
+    }
+  for (int k = 0; k < castk::kParTW; ++k) {
+    t.cw[k] = (float)std::cos(2.0 * pi * k / castk::kParTW);
+    t.sw[k] = (float)std::sin(2.0 * pi * k / castk::kParTW);
+  }
+  for (int k = 0; k < castk::kParTH; ++k) {
+    t.ch[k] = (float)std::cos(2.0 * pi * k / castk::kParTH);
+    t.shh[k] = (float)std::sin(2.0 * pi * k / castk::kParTH);
+  }
+  double fy[castk::kParTH], fx[castk::kParWF], rmax = 0.0;
+  for (int k = 0; k < castk::kParTH; ++k) {
+    const int kk = k <= (castk::kParTH - 1) / 2 ? k : k - castk::kParTH;
+    fy[k] = (double)kk / castk::kParTH;
+    t.fy[k] = (float)(2.0 * pi * fy[k]);
+  }
+  for (int k = 0; k < castk::kParWF; ++k) {
+    fx[k] = (double)k / castk::kParTW;
+    t.fx[k] = (float)(2.0 * pi * fx[k]);
+  }
+  double r[castk::kParFreq];
+  for (int a = 0; a < castk::kParTH; ++a)
+    for (int b = 0; b < castk::kParWF; ++b) {
+      r[a * castk::kParWF + b] = std::sqrt(fy[a] * fy[a] + fx[b] * fx[b]);
+      rmax = std::max(rmax, r[a * castk::kParWF + b]);
+    }
+  for (int f = 0; f < castk::kParFreq; ++f)
+    t.thr[f] = (float)(tau_low + (tau_high - tau_low) * std::pow(r[f] / std::max(rmax, 1e-8), power));
+}
+
+extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
+                               const int32_t *active_frames, int n_active, int T,
+                               int memory_length, int H, int W, int C, float tau_low,
+                               float tau_high, float freq_power, float temperature,
+                               int ramp_confidence, int current_anchor_boundary,
+                               const float *tile_confidence, float *stats_out, void *workspace,
+                               size_t workspace_bytes, cast_stream_t stream) {
+  if (!full_residual || !active_residual || !active_frames)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "full_residual, active_residual, active_frames required");
+  if (H != castk::kParH || W != castk::kParW)
+    return fail(CAST_ERR_UNSUPPORTED, "PAR grid %dx%d (supported: 22x40, 3x6 tiles of 11x10)", H, W);
+  if (C <= 0 || C % 4 || n_active <= 0 || T <= 0 || memory_length < 0 || memory_length > T)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "bad sizes (C=%d, n_active=%d, T=%d, memory=%d)", C,
+                n_active, T, memory_length);
+  if (!(temperature > 0.0f) || !(0.0f <= tau_low && tau_low <= tau_high && tau_high <= 1.0f) ||
+      !(freq_power > 0.0f))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "invalid FC knobs");
+  if (!aligned16(full_residual) || !aligned16(active_residual))
+    return fail(CAST_ERR_ALIGNMENT, "residual tensors must be 16-byte aligned");
+  for (int i = 0; i < n_active; ++i) {
+    if (active_frames[i] < 0 || active_frames[i] >= T)
+      return fail(CAST_ERR_INVALID_ARGUMENT, "active frame %d out of range", active_frames[i]);
+    if (i && active_frames[i] <= active_frames[i - 1])
+      return fail(CAST_ERR_INVALID_ARGUMENT, "active frames must be sorted and unique");
+  }
+  // Anchors: current-chunk active frames (local ids), as
+  // _correct_frequency_confidence_pasm_reference builds exact_local.
+  std::vector<int> anchor_row, anchor_local;
+  for (int i = 0; i < n_active; ++i)
+    if (active_frames[i] >= memory_length) {
+      anchor_row.push_back(i);
+      anchor_local.push_back(active_frames[i] - memory_length);
+    }
+  if (anchor_local.empty()) return fail(CAST_ERR_INVALID_ARGUMENT, "FC-PASM requires current anchors");
+  const int cur_len = T - memory_length;
+  castk::ParParams p;
+  memset(&p, 0, sizeof(p));
+  // Segment-local bracket rule; pairs in chronological order of first use.
+  std::vector<std::pair<int, int>> pairs;
+  int nt = 0;
+  for (int t = 0; t < cur_len; ++t) {
+    bool is_anchor = false;
+    for (int a : anchor_local) is_anchor |= (a == t);
+    if (is_anchor) continue;
+    const bool same = t < current_anchor_boundary;
+    int li = -1, ri = -1;
+    for (size_t i = 0; i < anchor_local.size(); ++i) {
+      const int f = anchor_local[i];
+      if ((f < current_anchor_boundary) != same) continue;
+      if (f < t) li = (int)i;
+      if (f > t && ri < 0) ri = (int)i;
+    }
+    if (li < 0 || ri < 0) continue;
+    int pi = -1;
+    for (size_t k2 = 0; k2 < pairs.size(); ++k2)
+      if (pairs[k2].first == li && pairs[k2].second == ri) pi = (int)k2;
+    if (pi < 0) {
+      if ((int)pairs.size() == castk::kParMaxPairs) return fail(CAST_ERR_UNSUPPORTED, "too many anchor pairs");
+      pairs.push_back({li, ri});
+      pi = (int)pairs.size() - 1;
+    }
+    if (nt == castk::kParMaxTargets) return fail(CAST_ERR_UNSUPPORTED, "too many targets");
+    p.target_pair[nt] = pi;
+    p.target_frame[nt] = memory_length + t;
+    p.target_alpha[nt] = (float)((double)(t - anchor_local[li]) / (double)(anchor_local[ri] - anchor_local[li]));
+    ++nt;
+  }
+  const size_t need = cast_par_fcpasm_workspace_bytes(T, H, W, C);
+  if (!workspace || workspace_bytes < need)
+    return fail(CAST_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t frame_bytes = (size_t)H * W * C * 2;
+  __nv_bfloat16 *full = static_cast<__nv_bfloat16 *>(full_residual);
+  const __nv_bfloat16 *act = static_cast<const __nv_bfloat16 *>(active_residual);
+
+  if (nt > 0) {
+    p.active = act;
+    p.full = full;
+    p.C = C;
+    p.HW = H * W;
+    p.n_chunks = par_chunks(C);
+    p.n_pairs = (int)pairs.size();
+    p.n_targets = nt;
+    for (size_t i = 0; i < pairs.size(); ++i) {
+      p.pair_left[i] = anchor_row[pairs[i].first];
+      p.pair_right[i] = anchor_row[pairs[i].second];
+    }
+    p.temperature = temperature;
+    p.ramp_confidence = ramp_confidence;
+    p.tile_confidence = tile_confidence;
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    p.partials = reinterpret_cast<float *>(ws);
+    ws += align_up((size_t)castk::kParMaxPairs * castk::kParTiles * p.n_chunks * castk::kParPartial * 4, 256);
+    p.weights = reinterpret_cast<float *>(ws);
+    ws += align_up((size_t)std::min(T, castk::kParMaxTargets) * castk::kParTiles * castk::kParFreq * 16, 256);
+    p.pred = reinterpret_cast<float *>(ws);
+    p.stats = stats_out;
+    fill_par_tables(p.tab, tau_low, tau_high, freq_power);
+
+    static std::once_flag once;
+    static cudaError_t aerr = cudaSuccess;
+    const int smem_stats = 4 * castk::kParFreq * (castk::kParChunk + 1) * 4;
+    const int smem_pred = 6 * castk::kParFreq * (castk::kParChunk + 1) * 4;
+    std::call_once(once, [&] {
+      aerr = cudaFuncSetAttribute(castk::par_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_stats);
+      if (aerr == cudaSuccess)
+        aerr = cudaFuncSetAttribute(castk::par_predict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_pred);
+    });
+    CAST_CUDA_TRY(aerr);
+    dim3 g1(p.n_chunks, castk::kParTiles, p.n_pairs);
+    castk::par_stats_kernel<<<g1, castk::kParChunk, smem_stats, s>>>(p);
+    CAST_CUDA_TRY(cudaGetLastError());
+    castk::par_finalize_kernel<<<dim3(castk::kParTiles, p.n_pairs), 128, 0, s>>>(p);
+    CAST_CUDA_TRY(cudaGetLastError());
+    castk::par_predict_kernel<<<g1, castk::kParChunk, smem_pred, s>>>(p);
+    CAST_CUDA_TRY(cudaGetLastError());
+    castk::par_ola_kernel<<<dim3(H * W, nt), 256, 0, s>>>(p);
+    CAST_CUDA_TRY(cudaGetLastError());
+  }
+  // corrected[:, active_frames] = active_residual
+  for (int i = 0; i < n_active; ++i) {
+    void *dst = full + (size_t)active_frames[i] * H * W * C;
+    const void *src = act + (size_t)i * H * W * C;
+    if (dst != src) CAST_CUDA_TRY(cudaMemcpyAsync(dst, src, frame_bytes, cudaMemcpyDeviceToDevice, s));
+  }
+  return CAST_OK;
+}

@@ -1,0 +1,420 @@
+// Pooled-QK block scoring, top-k block selection and the per-block symmetric
+// int8 quantiser (HBM-bound; one read of Q/K from HBM, the second pass of a
+// block hits L2).
+//
+// Fixed arithmetic order (mirrored by the CPU oracle so that indices and
+// codes compare bit-exactly):
+//   * block sums in float64, row r of a block accumulated into partial
+//     r % kSumLanes in increasing r, partials added in order 0..15;
+//   * ||mean||^2 and every pooled dot product: lane l (of 32) sums the
+//     products of dims d = l, l+32, ... in increasing d (multiply and add
+//     rounded separately), then an xor-butterfly over 16, 8, 4, 2, 1;
+//   * int8 code = clamp(rint_half_even(fl32(x / s)), -127, 127).
+#pragma once
+
+#include "common.cuh"
+
+namespace castk {
+
+constexpr int kSumLanes = 16;
+constexpr double kNormEps = 1e-12;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 &raw, float (&f)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// rint_half_even(fl32(x/s)) clamped to [-127,127], bit-exact with IEEE
+// division.  Fast path: x * (1/s); when that quotient lies within 1e-4 of a
+// half-integer (where the rounded product could round differently from the
+// correctly rounded quotient) the exact IEEE division is used instead.
+__device__ __forceinline__ int quant_code(float x, float s, float inv_s) {
+  const float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float qv = __fmul_rn(x, inv_s);
+  float t = __fadd_rn(qv, kMagic);
+  float r = __fsub_rn(t, kMagic);
+  if (fabsf(__fsub_rn(qv, r)) > 0.4999f) {
+    qv = __fdiv_rn(x, s);
+    t = __fadd_rn(qv, kMagic);
+  }
+  int c = __float_as_int(t) - 0x4B400000;
+  return max(-127, min(127, c));
+}
+
+__device__ __forceinline__ float quant_scale_of(float amax) {
+  return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+}
+
+// Lane-partial + butterfly sum of a[d]*b[d] over D dims (warp-collective).
+template <int D>
+__device__ __forceinline__ double warp_dot(const double *a, const double *b, int lane) {
+  double part = __dmul_rn(a[lane], b[lane]);
+#pragma unroll
+  for (int d = lane + 32; d < D; d += 32) part = __dadd_rn(part, __dmul_rn(a[d], b[d]));
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) part = __dadd_rn(part, __shfl_xor_sync(0xffffffffu, part, s));
+  return part;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 1: per-(bh, block) pooled statistics and int8 codes.
+// grid.x spans [Q blocks | K blocks | V blocks], grid.y = B*H.
+// Threads: 16 row slots x D/8 column groups (8 bf16 = 16 bytes each).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(kSumLanes *(D / 8))
+    pool_quant_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
+                      const __nv_bfloat16 *__restrict__ v, int Lq, int Lk, int block, int nqb,
+                      int nkb, int8_t *q_codes, float *q_scales, int8_t *k_codes,
+                      float *k_scales, int8_t *v_codes, float *v_scales, double *pooled,
+                      float *block_rms) {
+  constexpr int kGroups = D / 8;
+  constexpr int kThreads = kSumLanes * kGroups;
+  __shared__ double red[kSumLanes][D];
+  __shared__ double mean_s[D];
+  __shared__ float wmax[kThreads / 32];
+  __shared__ float wsq[kThreads / 32];
+  __shared__ float s_scale;
+  __shared__ double s_denom;
+
+  const int tid = threadIdx.x;
+  const int grp = tid % kGroups;
+  const int slot = tid / kGroups;
+  const int bh = blockIdx.y;
+  int blk = blockIdx.x;
+  int which;  // 0 = Q, 1 = K, 2 = V
+  if (blk < nqb) {
+    which = 0;
+  } else if (blk < nqb + nkb) {
+    which = 1;
+    blk -= nqb;
+  } else {
+    which = 2;
+    blk -= nqb + nkb;
+  }
+  const __nv_bfloat16 *X = which == 0 ? q : (which == 1 ? k : v);
+  const int L = which == 0 ? Lq : Lk;
+  int8_t *codes = which == 0 ? q_codes : (which == 1 ? k_codes : v_codes);
+  float *scales = which == 0 ? q_scales : (which == 1 ? k_scales : v_scales);
+  const int nb = which == 0 ? nqb : nkb;
+
+  const int b0 = blk * block;
+  const int rows = min(block, L - b0);
+  const __nv_bfloat16 *base = X + ((size_t)bh * L + b0) * D + grp * 8;
+
+  double acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0;
+  float amax = 0.0f, sq = 0.0f;
+  const bool pool = which != 2;
+
+  int r = slot;
+  for (; r + 3 * kSumLanes < rows; r += 4 * kSumLanes) {
+    uint4 raw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) raw[u] = ldg_nc_v4(base + (size_t)(r + u * kSumLanes) * D);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float f[8];
+      bf16x8_to_f32(raw[u], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (pool) acc[i] = __dadd_rn(acc[i], (double)f[i]);
+        amax = fmaxf(amax, fabsf(f[i]));
+        sq = fmaf(f[i], f[i], sq);
+      }
+    }
+  }
+  for (; r < rows; r += kSumLanes) {
+    float f[8];
+    bf16x8_to_f32(ldg_nc_v4(base + (size_t)r * D), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (pool) acc[i] = __dadd_rn(acc[i], (double)f[i]);
+      amax = fmaxf(amax, fabsf(f[i]));
+      sq = fmaf(f[i], f[i], sq);
+    }
+  }
+
+  // amax / sum of squares across the CTA (order-independent for amax).
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
+    sq += __shfl_xor_sync(0xffffffffu, sq, s);
+  }
+  if ((tid & 31) == 0) {
+    wmax[tid >> 5] = amax;
+    wsq[tid >> 5] = sq;
+  }
+  if (pool) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[slot][grp * 8 + i] = acc[i];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float m = 0.0f, s2 = 0.0f;
+    for (int w = 0; w < kThreads / 32; ++w) {
+      m = fmaxf(m, wmax[w]);
+      s2 += wsq[w];
+    }
+    const float sc = quant_scale_of(m);
+    s_scale = sc;
+    if (scales) scales[(size_t)bh * nb + blk] = sc;
+    if (block_rms && pool) {
+      const int row0 = which == 0 ? 0 : nqb;
+      block_rms[(size_t)bh * (nqb + nkb) + row0 + blk] =
+          sqrtf(s2 / (float)max(1, rows * D));
+    }
+  }
+  if (pool) {
+    if (tid < D) {
+      double t = red[0][tid];
+#pragma unroll
+      for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, red[p][tid]);
+      mean_s[tid] = __ddiv_rn(t, (double)max(rows, 1));
+    }
+    __syncthreads();
+    if (tid < 32) {
+      double part = __dmul_rn(mean_s[tid], mean_s[tid]);
+#pragma unroll
+      for (int d = tid + 32; d < D; d += 32) part = __dadd_rn(part, __dmul_rn(mean_s[d], mean_s[d]));
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) part = __dadd_rn(part, __shfl_xor_sync(0xffffffffu, part, s));
+      if (tid == 0) s_denom = fmax(__dsqrt_rn(part), kNormEps);
+    }
+    __syncthreads();
+    if (tid < D) {
+      const int row0 = which == 0 ? 0 : nqb;
+      pooled[((size_t)bh * (nqb + nkb) + row0 + blk) * D + tid] = __ddiv_rn(mean_s[tid], s_denom);
+    }
+  } else {
+    __syncthreads();
+  }
+
+  // Second pass: int8 codes (the block was just read; these loads hit L2).
+  if (codes) {
+    const float sc = s_scale;
+    const float inv = __frcp_rn(sc);
+    int8_t *cbase = codes + ((size_t)bh * L + b0) * D + grp * 8;
+    for (int rr = slot; rr < rows; rr += kSumLanes) {
+      float f[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4 *>(base + (size_t)rr * D), f);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) lo |= (uint32_t)(quant_code(f[i], sc, inv) & 0xFF) << (8 * i);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hi |= (uint32_t)(quant_code(f[4 + i], sc, inv) & 0xFF) << (8 * i);
+      *reinterpret_cast<uint2 *>(cbase + (size_t)rr * D) = make_uint2(lo, hi);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Warp top-k helpers: (score desc, index asc) ordering.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool better(double a, int ia, double b, int ib) {
+  return a > b || (a == b && ia < ib);
+}
+
+// Selects up to `k` best candidates among cand[0..n) (indices 0..n-1 into
+// `score`), writing them in order to out[0..k).  `taken` is scratch smem of n
+// bytes.  Warp-collective; lane 0 writes.
+__device__ void warp_topk(const double *score, int n, int k, unsigned char *taken, int32_t *out,
+                          int lane) {
+  for (int j = lane; j < n; j += 32) taken[j] = 0;
+  __syncwarp();
+  for (int t = 0; t < k; ++t) {
+    double best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = lane; j < n; j += 32) {
+      if (!taken[j] && better(score[j], j, best, bi)) {
+        best = score[j];
+        bi = j;
+      }
+    }
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+      double ob = __shfl_xor_sync(0xffffffffu, best, s);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, s);
+      if (better(ob, oi, best, bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out[t] = bi;
+      taken[bi] = 1;
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 2: budget + block-causal selection and the int8/bf16 QK^T policy.
+// grid = (nqb, B*H), 128 threads.  Dynamic smem: nkb doubles + nkb bytes.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(128)
+    budget_select_kernel(const double *__restrict__ pooled, const float *__restrict__ block_rms,
+                         const float *__restrict__ q_scales, const float *__restrict__ k_scales,
+                         int nqb, int nkb, int budget, int maxdeg, int32_t *sel_idx,
+                         int32_t *sel_cnt, uint8_t *qk_mode, int policy, float tol) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  double *score = reinterpret_cast<double *>(dsm);
+  unsigned char *taken = dsm + sizeof(double) * nkb;
+  __shared__ double qn[D];
+  __shared__ int32_t picks[256];
+  const int qb = blockIdx.x, bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const double *prow = pooled + (size_t)bh * (nqb + nkb) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = prow[(size_t)qb * D + d];
+  __syncthreads();
+  const int nhist = nkb - nqb;
+  for (int kb = warp; kb < nhist; kb += 4) {
+    double s = warp_dot<D>(qn, prow + (size_t)(nqb + kb) * D, lane);
+    if (lane == 0) score[kb] = s;
+  }
+  __syncthreads();
+  const int keep = min(budget, nhist);
+  if (warp == 0) warp_topk(score, nhist, keep, taken, picks, lane);
+  __syncthreads();
+  int32_t *out = sel_idx + ((size_t)bh * nqb + qb) * maxdeg;
+  for (int j = threadIdx.x; j < maxdeg; j += blockDim.x) {
+    int val = -1;
+    if (j < keep) val = picks[j];
+    else if (j < keep + qb + 1) val = nhist + (j - keep);
+    out[j] = val;
+  }
+  if (threadIdx.x == 0) {
+    sel_cnt[(size_t)bh * nqb + qb] = keep + qb + 1;
+    if (qk_mode) {
+      uint8_t mode = policy == CAST_POLICY_INT8 ? 1 : 0;
+      if (policy == CAST_POLICY_AUTO) {
+        // Predicted logit error of the int8 product (uniform quantisation
+        // noise, variance s^2/12 per element) times the logit spread; int8
+        // only where every selected block stays below the tolerance.
+        const float *rms = block_rms + (size_t)bh * (nqb + nkb);
+        const float rq = rms[qb], sq = q_scales[(size_t)bh * nqb + qb];
+        float worst = 0.0f;
+        for (int j = 0; j < keep + qb + 1; ++j) {
+          const int kb = j < keep ? picks[j] : nhist + (j - keep);
+          const float rk = rms[nqb + kb], sk = k_scales[(size_t)bh * nkb + kb];
+          const float err = sqrtf((sq * sq * rk * rk + sk * sk * rq * rq) * (1.0f / 12.0f));
+          worst = fmaxf(worst, err * rq * rk);
+        }
+        mode = worst <= tol ? 1 : 0;
+      }
+      qk_mode[(size_t)bh * nqb + qb] = mode;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TABA: pooled means over (tt,th,tw) tiles of the visual grid (zero padding
+// counts in the mean, as _tile_visual_tensor does), then ranking.
+// grid = (nblocks, B*H).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(kSumLanes *(D / 8))
+    pool_grid_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
+                     int T, int Hl, int Wl, int tt, int th, int tw, int nh, int nw, int nblocks,
+                     double *pooled /*[BH, 2, nblocks, D]*/) {
+  constexpr int kGroups = D / 8;
+  __shared__ double red[kSumLanes][D];
+  __shared__ double mean_s[D];
+  __shared__ double s_denom;
+  const int tid = threadIdx.x, grp = tid % kGroups, slot = tid / kGroups;
+  const int bh = blockIdx.y;
+  const int which = blockIdx.x / nblocks;
+  const int blk = blockIdx.x % nblocks;
+  const __nv_bfloat16 *X = which == 0 ? q : k;
+  const int L = T * Hl * Wl;
+  const int bt = blk / (nh * nw), bhh = (blk / nw) % nh, bw = blk % nw;
+  const int S = tt * th * tw;
+  double acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0;
+  for (int r = slot; r < S; r += kSumLanes) {
+    const int it = r / (th * tw), ih = (r / tw) % th, iw = r % tw;
+    const int t = bt * tt + it, h = bhh * th + ih, w = bw * tw + iw;
+    if (t < T && h < Hl && w < Wl) {
+      float f[8];
+      bf16x8_to_f32(ldg_nc_v4(X + ((size_t)bh * L + ((size_t)t * Hl + h) * Wl + w) * D + grp * 8), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __dadd_rn(acc[i], (double)f[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[slot][grp * 8 + i] = acc[i];
+  __syncthreads();
+  if (tid < D) {
+    double t = red[0][tid];
+#pragma unroll
+    for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, red[p][tid]);
+    mean_s[tid] = __ddiv_rn(t, (double)S);
+  }
+  __syncthreads();
+  if (tid < 32) {
+    double part = __dmul_rn(mean_s[tid], mean_s[tid]);
+#pragma unroll
+    for (int d = tid + 32; d < D; d += 32) part = __dadd_rn(part, __dmul_rn(mean_s[d], mean_s[d]));
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) part = __dadd_rn(part, __shfl_xor_sync(0xffffffffu, part, s));
+    if (tid == 0) s_denom = fmax(__dsqrt_rn(part), kNormEps);
+  }
+  __syncthreads();
+  if (tid < D)
+    pooled[(((size_t)bh * 2 + which) * nblocks + blk) * D + tid] = __ddiv_rn(mean_s[tid], s_denom);
+}
+
+// grid = (nblocks, B*H), 128 threads; dynamic smem: 2*nblocks doubles + nblocks bytes.
+template <int D>
+__global__ void __launch_bounds__(128)
+    taba_select_kernel(const double *__restrict__ pooled, int nblocks, int nh, int nw,
+                       const int32_t *__restrict__ row_degrees, int maxdeg, int32_t *sel_idx,
+                       int32_t *sel_cnt, double *scores_out) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  double *score = reinterpret_cast<double *>(dsm);
+  double *rank = score + nblocks;
+  unsigned char *taken = reinterpret_cast<unsigned char *>(rank + nblocks);
+  __shared__ double qn[D];
+  const int i = blockIdx.x, bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const double *qrow = pooled + ((size_t)bh * 2 + 0) * nblocks * D;
+  const double *krow = pooled + ((size_t)bh * 2 + 1) * nblocks * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = qrow[(size_t)i * D + d];
+  __syncthreads();
+  const int spatial = nh * nw;
+  const int ti = i / spatial, hi = (i / nw) % nh, wi = i % nw;
+  for (int j = warp; j < nblocks; j += 4) {
+    double s = warp_dot<D>(qn, krow + (size_t)j * D, lane);
+    if (lane == 0) {
+      score[j] = s;
+      const int tj = j / spatial, hj = (j / nw) % nh, wj = j % nw;
+      const bool local = abs(ti - tj) + abs(hi - hj) + abs(wi - wj) <= 1;
+      // The reference adds the stencil bonus to a float32 score.
+      const float s32 = (float)s;
+      rank[j] = (double)(local ? __fadd_rn(s32, 1.0e6f) : s32);
+    }
+  }
+  __syncthreads();
+  if (scores_out)
+    for (int j = threadIdx.x; j < nblocks; j += blockDim.x)
+      scores_out[((size_t)bh * nblocks + i) * nblocks + j] = score[j];
+  if (warp == 0) warp_topk(rank, nblocks, maxdeg, taken, sel_idx + ((size_t)bh * nblocks + i) * maxdeg, lane);
+  if (threadIdx.x == 0) sel_cnt[(size_t)bh * nblocks + i] = row_degrees[i];
+}
+
+}  // namespace castk

@@ -1,0 +1,151 @@
+"""Host side of Phase-Aware Reconstruction (FC-PASM) on B200.
+
+``FCPASMCorrector.correct`` has the keyword signature of
+``WorldAlignedSpectralResidualCorrector.correct``
+(``proposed/matrix_world_spectral_residual.py:5283-5296``) and the behaviour of
+its production FC-PASM path with the factory knobs
+(``_correct_frequency_confidence_pasm_reference``, ``:2771-3662``): the same
+``first_chunk`` / ``no_memory`` fallbacks, and an in-place write of the
+reconstructed skipped frames plus ``corrected[:, active_frames] =
+active_residual`` (lean runtime, ``:3638-3645``).  The spectral work runs in
+the CUDA kernels of ``libcast_b200.so``; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+TILES = 18
+FREQS = 66
+
+
+class FCPASMCorrector:
+    """FC-PASM corrector with the frozen factory knobs (``cast_matrix.py:74-96``)."""
+
+    mode = "frequency_confidence_phase_aligned_spectral_mixing"
+
+    def __init__(
+        self,
+        *,
+        fc_tau_low: float = 0.50,
+        fc_tau_high: float = 0.75,
+        fc_freq_power: float = 2.0,
+        fc_temperature: float = 0.03,
+        fc_ramp_confidence: bool = True,
+        current_anchor_boundary: int = 4,
+        record_stats: bool = False,
+    ):
+        if not 0.0 <= fc_tau_low <= fc_tau_high <= 1.0:
+            raise ValueError("FC-PASM thresholds must satisfy 0 <= low <= high <= 1")
+        if fc_freq_power <= 0.0 or fc_temperature <= 0.0:
+            raise ValueError("FC-PASM frequency power and temperature must be positive")
+        if not 1 <= int(current_anchor_boundary) <= 13:
+            raise ValueError("current_anchor_boundary must be in [1,13]")
+        self.fc_tau_low = float(fc_tau_low)
+        self.fc_tau_high = float(fc_tau_high)
+        self.fc_freq_power = float(fc_freq_power)
+        self.fc_temperature = float(fc_temperature)
+        self.fc_ramp_confidence = bool(fc_ramp_confidence)
+        self.current_anchor_boundary = int(current_anchor_boundary)
+        self.record_stats = bool(record_stats)
+        self._chunk = 0
+        self._step = 0
+        self._records: list[dict] = []
+        self._workspace: dict = {}
+        self.last_stats: torch.Tensor | None = None
+
+    def begin_model_call(self, *, geometry=None, chunk_index: int, step_index: int, device=None) -> None:
+        """``WorldAlignedSpectralResidualCorrector.begin_model_call`` (``:544-556``)."""
+        del geometry, device
+        self._chunk = int(chunk_index)
+        self._step = int(step_index)
+
+    def _ws(self, device, nbytes: int) -> torch.Tensor:
+        buf = self._workspace.get(device)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            self._workspace[device] = buf
+        return buf
+
+    def correct(
+        self,
+        *,
+        layer_index: int,
+        full_input: torch.Tensor | None,
+        full_residual: torch.Tensor,
+        active_residual: torch.Tensor,
+        active_frames: torch.Tensor,
+        memory_length: int,
+        spatial_height: int,
+        spatial_width: int,
+        coarse_probe_residual: torch.Tensor | None = None,
+        active_frame_values: tuple[int, ...] | None = None,
+        tile_confidence: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        del full_input, coarse_probe_residual
+        fallback = None
+        if self._chunk == 0:
+            fallback = "first_chunk"
+        elif memory_length <= 0:
+            fallback = "no_memory"
+        if fallback is not None:
+            self._records.append({"layer_index": int(layer_index), "status": "temporal_fallback",
+                                  "fallback_reason": fallback})
+            return full_residual
+        if full_residual.dim() != 4 or full_residual.shape[0] != 1 or active_residual.shape[0] != 1:
+            raise RuntimeError("FC-PASM requires Matrix batch size one")
+        for name, t in (("full_residual", full_residual), ("active_residual", active_residual)):
+            if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+        if active_frame_values is None:
+            active_frame_values = tuple(int(x) for x in active_frames.tolist())
+        frames = list(active_frame_values)
+        if tuple(sorted(set(frames))) != tuple(frames):
+            raise RuntimeError("FC-R active-frame values must be sorted and unique")
+        if len(frames) != active_residual.shape[1]:
+            raise RuntimeError("active frame count differs from active_residual")
+        t_total, hw, c = full_residual.shape[1:]
+        if hw != spatial_height * spatial_width:
+            raise RuntimeError("residual token count differs from the latent grid")
+        lib = _lib.load()
+        nbytes = lib.cast_par_fcpasm_workspace_bytes(t_total, spatial_height, spatial_width, c)
+        ws = self._ws(full_residual.device, nbytes)
+        frames_arr = (_lib.ctypes.c_int32 * len(frames))(*frames)
+        stats = None
+        if self.record_stats:
+            stats = torch.empty(16 * TILES * (2 * FREQS + 5), dtype=torch.float32,
+                                device=full_residual.device)
+        if tile_confidence is not None:
+            tile_confidence = tile_confidence.to(device=full_residual.device,
+                                                 dtype=torch.float32).contiguous()
+        _lib.call(
+            "cast_par_fcpasm", full_residual.data_ptr(), active_residual.data_ptr(),
+            _lib.ctypes.cast(frames_arr, _lib.c_void_p), len(frames), t_total, int(memory_length),
+            spatial_height, spatial_width, c, self.fc_tau_low, self.fc_tau_high,
+            self.fc_freq_power, self.fc_temperature, int(self.fc_ramp_confidence),
+            self.current_anchor_boundary, _lib.ptr(tile_confidence), _lib.ptr(stats), ws.data_ptr(),
+            ws.numel(), torch.cuda.current_stream(full_residual.device).cuda_stream,
+        )
+        self.last_stats = stats
+        self._records.append({"layer_index": int(layer_index), "status": "corrected"})
+        return full_residual
+
+
+def unpack_stats(stats: torch.Tensor, n_pairs: int) -> list[dict]:
+    """Splits the per-pair statistics block written when ``record_stats`` is on."""
+    per = TILES * (2 * FREQS + 5)
+    out = []
+    for i in range(n_pairs):
+        s = stats[i * per:(i + 1) * per]
+        o = 0
+        theta = s[o:o + TILES * FREQS].view(TILES, 11, 6); o += TILES * FREQS
+        conf = s[o:o + TILES]; o += TILES
+        g = s[o:o + TILES * FREQS].view(TILES, 11, 6); o += TILES * FREQS
+        disp = s[o:o + 2 * TILES].view(TILES, 2); o += 2 * TILES
+        base = s[o:o + TILES]; o += TILES
+        ramp = s[o:o + TILES]
+        out.append({"theta": theta, "confidence": conf, "affinity": g, "displacement": disp,
+                    "base_confidence": base, "ramp_confidence": ramp})
+    return out

@@ -1,0 +1,253 @@
+"""Host side of Reconstruction-Coupled Sparse Attention (RCSA) on B200.
+
+Mirrors the reference's operator seams:
+
+* ``longcat_active`` / ``longcat_asymmetric`` -- drop-ins for
+  ``MatrixJiTSpatialAcceleration._longcat_active``
+  (``proposed/matrix_jit_spatial_acceleration.py:663-729``) and
+  ``MatrixCausalFrameLayerRelay._longcat_asymmetric``
+  (``proposed/matrix_curvature_phase_frame_weave.py:8847-8917``): same
+  arguments, same bf16 ``[B,H,L,D]`` result.
+* ``select_quant`` -- pooled-QK block scoring with the historical-budget +
+  block-causal rule, fused with per-block symmetric int8 quantisation.
+* ``rcsa_attention`` -- selection, quantisation and the int8/bf16 tcgen05
+  block-sparse attention in one call.
+
+Every function runs the CUDA kernels of ``libcast_b200.so`` on the current
+CUDA stream; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+POLICIES = {"bf16": 0, "int8": 1, "auto": 2}
+DEFAULT_INT8_TOLERANCE = 0.025
+RULE_BUDGET_CAUSAL = 0
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _need_cuda(name: str, t: torch.Tensor, dtype: torch.dtype | None = None, ndim: int | None = None):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the RCSA hot path has no CPU implementation)")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if ndim is not None and t.ndim != ndim:
+        raise ValueError(f"{name} must have {ndim} dims, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+@dataclass
+class Selection:
+    """Outputs of :func:`select_quant` (device tensors)."""
+
+    indices: torch.Tensor          # int32 [B,H,nQb,maxdeg], -1 padded
+    counts: torch.Tensor           # int32 [B,H,nQb]
+    q_codes: torch.Tensor | None   # int8 [B,H,Lq,D]
+    q_scales: torch.Tensor | None  # float32 [B,H,nQb]
+    k_codes: torch.Tensor | None   # int8 [B,H,Lk,D]
+    k_scales: torch.Tensor | None  # float32 [B,H,nKb]
+    v_codes: torch.Tensor | None
+    v_scales: torch.Tensor | None
+    qk_mode: torch.Tensor | None   # uint8 [B,H,nQb]: 1 int8, 0 bf16
+    pooled: torch.Tensor | None    # float64 [B,H,nQb+nKb,D]
+
+    @property
+    def max_degree(self) -> int:
+        return int(self.indices.shape[-1])
+
+
+class Workspace:
+    """Caller-owned scratch buffer reused across calls (grown on demand)."""
+
+    def __init__(self):
+        self._buf: dict[torch.device, torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        buf = self._buf.get(device)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            self._buf[device] = buf
+        return buf
+
+
+_default_ws = Workspace()
+
+
+def select_quant(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor | None = None,
+    *,
+    block_size: int,
+    budget: int,
+    policy: str = "auto",
+    int8_tolerance: float = DEFAULT_INT8_TOLERANCE,
+    quantize: bool = True,
+    quantize_v: bool = False,
+    return_pooled: bool = False,
+    workspace: Workspace | None = None,
+) -> Selection:
+    """Pooled-QK block selection fused with per-block int8 quantisation.
+
+    ``q``: bf16 ``[B,H,Lq,D]`` (current chunk); ``k``/``v``: bf16
+    ``[B,H,Lk,D]`` with history blocks first and the chunk's own blocks last.
+    Selection: per (b, h, query block i) the ``budget`` historical blocks of
+    highest pooled cosine (``F.normalize(mean)`` dot product, as
+    ``proposed/qk_uncertainty_tangent_attention.py:1021-1042``; ties to the
+    lower index), then current blocks ``0..i``.
+    """
+    if policy not in POLICIES:
+        raise ValueError(f"policy must be one of {sorted(POLICIES)}")
+    _need_cuda("q", q, torch.bfloat16, 4)
+    _need_cuda("k", k, torch.bfloat16, 4)
+    if v is not None:
+        _need_cuda("v", v, torch.bfloat16, 4)
+    b, h, lq, d = q.shape
+    lk = k.shape[2]
+    if k.shape[:2] != (b, h) or k.shape[3] != d:
+        raise ValueError(f"k shape {tuple(k.shape)} incompatible with q {tuple(q.shape)}")
+    nqb, nkb = -(-lq // block_size), -(-lk // block_size)
+    keep = min(budget, nkb - nqb)
+    dev = q.device
+    idx = torch.empty(b, h, nqb, keep + nqb, dtype=torch.int32, device=dev)
+    cnt = torch.empty(b, h, nqb, dtype=torch.int32, device=dev)
+    qc = torch.empty_like(q, dtype=torch.int8) if quantize else None
+    kc = torch.empty_like(k, dtype=torch.int8) if quantize else None
+    qs = torch.empty(b, h, nqb, dtype=torch.float32, device=dev) if quantize else None
+    ks = torch.empty(b, h, nkb, dtype=torch.float32, device=dev) if quantize else None
+    vc = torch.empty_like(v, dtype=torch.int8) if (quantize_v and v is not None) else None
+    vs = torch.empty(b, h, nkb, dtype=torch.float32, device=dev) if vc is not None else None
+    mode = torch.empty(b, h, nqb, dtype=torch.uint8, device=dev) if quantize else None
+    pooled = torch.empty(b, h, nqb + nkb, d, dtype=torch.float64, device=dev) if return_pooled else None
+    lib = _lib.load()
+    nbytes = lib.cast_rcsa_select_quant_workspace_bytes(b, h, lq, lk, d, block_size)
+    ws = (workspace or _default_ws).get(dev, nbytes)
+    P = _lib.ptr
+    _lib.call(
+        "cast_rcsa_select_quant", P(q), P(k), P(v) if vc is not None else None, b, h, lq, lk, d,
+        block_size, budget, RULE_BUDGET_CAUSAL, P(idx), P(cnt), P(qc), P(qs), P(kc), P(ks), P(vc),
+        P(vs), P(mode), POLICIES[policy], float(int8_tolerance), P(pooled), P(ws), ws.numel(),
+        _stream(dev),
+    )
+    return Selection(idx, cnt, qc, qs, kc, ks, vc, vs, mode, pooled)
+
+
+def block_sparse_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    indices: torch.Tensor,
+    counts: torch.Tensor,
+    *,
+    q_block: int,
+    k_block: int,
+    key_valid: torch.Tensor | None = None,
+    sm_scale: float | None = None,
+    q_codes: torch.Tensor | None = None,
+    q_scales: torch.Tensor | None = None,
+    k_codes: torch.Tensor | None = None,
+    k_scales: torch.Tensor | None = None,
+    qk_mode: torch.Tensor | None = None,
+    return_lse: bool = False,
+    out: torch.Tensor | None = None,
+):
+    """Block-sparse attention over listed key blocks (tcgen05, sm_100a).
+
+    ``O = softmax(Q K^T * sm_scale) V`` per query row over the keys of blocks
+    ``indices[b,h,i,:counts[b,h,i]]`` with ``key_valid`` (uint8 ``[Lk]``)
+    set.  ``sm_scale`` defaults to ``1/sqrt(D)`` as the reference launch does.
+    With int8 codes/scales the QK^T product runs in int8 where ``qk_mode`` is 1.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _need_cuda(name, t, torch.bfloat16, 4)
+    _need_cuda("indices", indices, torch.int32, 4)
+    _need_cuda("counts", counts, torch.int32, 3)
+    if key_valid is not None:
+        _need_cuda("key_valid", key_valid, torch.uint8, 1)
+    b, h, lq, d = q.shape
+    lk = k.shape[2]
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty_like(q)
+    lse = torch.empty(b, h, lq, dtype=torch.float32, device=q.device) if return_lse else None
+    P = _lib.ptr
+    _lib.call(
+        "cast_rcsa_attention", P(q), P(k), P(v), P(q_codes), P(q_scales), P(k_codes), P(k_scales),
+        P(qk_mode), P(indices), P(counts), int(indices.shape[-1]), P(key_valid), b, h, lq, lk, d,
+        q_block, k_block, float(sm_scale), P(out), P(lse), _stream(q.device),
+    )
+    return (out, lse) if return_lse else out
+
+
+def longcat_active(q, k, v, indices, counts, valid, block_size):
+    """Drop-in for ``MatrixJiTSpatialAcceleration._longcat_active``.
+
+    Same arguments and result as the reference launch of the block-sparse
+    kernel (``proposed/matrix_jit_spatial_acceleration.py:663-729``): bf16
+    ``[B,H,L,D]`` q/k/v, int32 block indices/counts, a ``[nBlocks,S]`` key
+    validity mask, square blocks of ``block_size``, ``sm_scale = 1/sqrt(D)``.
+    """
+    q = q.to(torch.bfloat16).contiguous()
+    k = k.to(torch.bfloat16).contiguous()
+    v = v.to(torch.bfloat16).contiguous()
+    indices = indices.to(torch.int32).contiguous()
+    counts = counts.to(torch.int32).contiguous()
+    key_valid = valid.reshape(-1).to(torch.uint8).contiguous()
+    return block_sparse_attention(q, k, v, indices, counts, q_block=block_size,
+                                  k_block=block_size, key_valid=key_valid)
+
+
+def longcat_asymmetric(q, k, v, indices, counts, key_valid, *, query_block_size, key_block_size):
+    """Drop-in for ``MatrixCausalFrameLayerRelay._longcat_asymmetric``
+    (``proposed/matrix_curvature_phase_frame_weave.py:8847-8917``)."""
+    q = q.to(torch.bfloat16).contiguous()
+    k = k.to(torch.bfloat16).contiguous()
+    v = v.to(torch.bfloat16).contiguous()
+    if q.shape[2] % query_block_size or k.shape[2] % key_block_size:
+        raise RuntimeError("asymmetric sparse storage is not block aligned")
+    return block_sparse_attention(
+        q, k, v, indices.to(torch.int32).contiguous(), counts.to(torch.int32).contiguous(),
+        q_block=query_block_size, k_block=key_block_size,
+        key_valid=key_valid.reshape(-1).to(torch.uint8).contiguous(),
+    )
+
+
+def rcsa_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    block_size: int,
+    budget: int,
+    policy: str = "auto",
+    int8_tolerance: float = DEFAULT_INT8_TOLERANCE,
+    sm_scale: float | None = None,
+    workspace: Workspace | None = None,
+):
+    """Full RCSA step: select + quantise, then block-sparse attention.
+
+    Returns ``(out bf16 [B,H,Lq,D], Selection)``.  ``policy`` picks the QK^T
+    precision per (b, h, query block): ``"int8"`` everywhere, ``"bf16"``
+    everywhere, or ``"auto"`` (int8 where the predicted logit error of the
+    int8 product, times the logit spread, stays below ``int8_tolerance``).
+    """
+    sel = select_quant(q, k, None, block_size=block_size, budget=budget, policy=policy,
+                       int8_tolerance=int8_tolerance, quantize=policy != "bf16",
+                       workspace=workspace)
+    out = block_sparse_attention(
+        q, k, v, sel.indices, sel.counts, q_block=block_size, k_block=block_size,
+        sm_scale=sm_scale, q_codes=sel.q_codes, q_scales=sel.q_scales, k_codes=sel.k_codes,
+        k_scales=sel.k_scales, qk_mode=sel.qk_mode,
+    )
+    return out, sel

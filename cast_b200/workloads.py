@@ -1,0 +1,139 @@
+"""Seeded synthetic inputs for the five RCSA/PAR workloads.
+
+There is no public dataset on this path; every input is drawn from a CPU
+``torch.Generator`` so the same tensors are produced on any host, then moved
+to the requested device.  Shapes and distributions follow the benchmark
+configurations of the hot path:
+
+* ``config1`` -- CPU plumbing: B=1, H=4, D=64, 64-token frames (8x8 grid),
+  8 history + 2 current frames, budget 4, fp32 N(0,1), seed 0 (Q, K, V drawn
+  in that order over all 10 frames).
+* ``config2`` -- one Matrix-shaped DiT layer: H=24, D=128, 880-token frames
+  (22x40), 32 history + 4 current frames, budget 8, bf16 N(0,1)*s_h with
+  s_h ~ U(0.5, 2) per head, seed 1.
+* ``config3`` -- long history: 128 history frames, budget 16, queries on
+  anchor frames 0 and 3 only, historical K drift ``+0.1*f*u_h`` with a fixed
+  unit vector ``u_h`` per head, seed 2.
+* ``config4`` -- PAR: residual bf16 ``[1, 1+4, 880, 3072]`` ~ N(0, 0.02)
+  (one memory frame then four current frames), anchors 0 and 3, seed 3.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass
+class RCSAWorkload:
+    name: str
+    q: torch.Tensor  # [B,H,Lq,D] packed queries (current chunk)
+    k: torch.Tensor  # [B,H,Lk,D] packed keys: history blocks then current blocks
+    v: torch.Tensor  # [B,H,Lk,D]
+    block_size: int
+    budget: int
+    latent_hw: tuple[int, int]
+    head_scale: torch.Tensor | None = None
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def n_query_blocks(self) -> int:
+        return self.q.shape[2] // self.block_size
+
+    @property
+    def n_key_blocks(self) -> int:
+        return self.k.shape[2] // self.block_size
+
+
+def config1(device: str | torch.device = "cpu") -> RCSAWorkload:
+    g = torch.Generator().manual_seed(0)
+    b, h, d, f, hist, cur = 1, 4, 64, 64, 8, 2
+    total = (hist + cur) * f
+    q_all = torch.randn(b, h, total, d, generator=g)
+    k = torch.randn(b, h, total, d, generator=g)
+    v = torch.randn(b, h, total, d, generator=g)
+    q = q_all[:, :, hist * f:].contiguous()
+    return RCSAWorkload(
+        "config1", q.to(device), k.to(device), v.to(device), f, 4, (8, 8),
+        meta={"q_full": q_all.to(device), "history_frames": hist, "current_frames": cur},
+    )
+
+
+def _scaled(shape, scale, g, dtype):
+    x = torch.randn(*shape, generator=g)
+    return (x * scale.view(1, -1, 1, 1)).to(dtype)
+
+
+def config2(device: str | torch.device = "cpu", heads: int = 24,
+            history: int = 32, current: int = 4, seed: int = 1) -> RCSAWorkload:
+    g = torch.Generator().manual_seed(seed)
+    b, d, f = 1, 128, 880
+    s = 0.5 + 1.5 * torch.rand(heads, generator=g)
+    q = _scaled((b, heads, current * f, d), s, g, torch.bfloat16)
+    k = _scaled((b, heads, (history + current) * f, d), s, g, torch.bfloat16)
+    v = _scaled((b, heads, (history + current) * f, d), s, g, torch.bfloat16)
+    return RCSAWorkload("config2", q.to(device), k.to(device), v.to(device), f, 8,
+                        (22, 40), head_scale=s,
+                        meta={"history_frames": history, "current_frames": current})
+
+
+def config3(device: str | torch.device = "cpu", heads: int = 24,
+            history: int = 128) -> RCSAWorkload:
+    """Anchor-only queries (chunk frames 0 and 3) over a 128-frame history.
+
+    Historical key frame ``f`` (0-based) is ``s_h*(N(0,1) + 0.1*f*u_h)``; only
+    history drifts, the two anchor (current) key frames are ``s_h*N(0,1)``.
+    """
+    g = torch.Generator().manual_seed(2)
+    b, d, f = 1, 128, 880
+    anchors = (0, 3)
+    s = 0.5 + 1.5 * torch.rand(heads, generator=g)
+    u = torch.randn(heads, d, generator=g)
+    u = u / u.norm(dim=1, keepdim=True)
+    q = _scaled((b, heads, len(anchors) * f, d), s, g, torch.bfloat16)
+    frames = list(range(history)) + [history + a for a in anchors]
+    k = torch.randn(b, heads, len(frames) * f, d, generator=g)
+    drift = torch.tensor(frames, dtype=torch.float32).repeat_interleave(f)
+    drift[history * f:] = 0.0  # anchors: no drift term beyond noise
+    k = k + 0.1 * drift.view(1, 1, -1, 1) * u.view(1, heads, 1, d)
+    k = (k * s.view(1, -1, 1, 1)).to(torch.bfloat16)
+    v = _scaled((b, heads, len(frames) * f, d), s, g, torch.bfloat16)
+    return RCSAWorkload("config3", q.to(device), k.to(device), v.to(device), f, 16,
+                        (22, 40), head_scale=s,
+                        meta={"history_frames": history, "anchors": anchors})
+
+
+@dataclass
+class PARWorkload:
+    name: str
+    full_residual: torch.Tensor  # [1, M+T, HW, C]
+    active_frames: list[int]     # global frame ids (memory frames first)
+    memory_length: int
+    height: int
+    width: int
+
+    @property
+    def active_residual(self) -> torch.Tensor:
+        return self.full_residual[:, self.active_frames].contiguous()
+
+
+def config4(device: str | torch.device = "cpu", channels: int = 3072,
+            seed: int = 3) -> PARWorkload:
+    g = torch.Generator().manual_seed(seed)
+    m, t, hw = 1, 4, 880
+    full = (torch.randn(1, m + t, hw, channels, generator=g) * 0.02).to(torch.bfloat16)
+    return PARWorkload("config4", full.to(device), [0, m + 0, m + 3], m, 22, 40)
+
+
+def par_motion(device: str | torch.device = "cpu", channels: int = 64,
+               seed: int = 7) -> PARWorkload:
+    """Frames that are shifted crops of one pattern (exercises the phase path)."""
+    g = torch.Generator().manual_seed(seed)
+    base = torch.randn(1, channels, 22 + 16, 40 + 16, generator=g) * 0.02
+    frames = []
+    for t in range(5):
+        crop = base[:, :, 8 + t // 2:8 + t // 2 + 22, 8 + t:8 + t + 40]
+        frames.append(crop.permute(0, 2, 3, 1).reshape(1, 880, channels))
+    full = torch.stack(frames, 1).to(torch.bfloat16)
+    return PARWorkload("par_motion", full.to(device), [0, 1, 4], 1, 22, 40)

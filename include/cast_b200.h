@@ -1,0 +1,183 @@
+/*
+ * cast_b200.h -- C ABI of the B200-native CAST RCSA/PAR hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream,
+ * enqueues its kernels on that stream (no implicit synchronisation, no
+ * allocation), and returns an int status (0 = CAST_OK).  The caller owns every
+ * buffer, including the workspace whose size the *_workspace_bytes() queries
+ * report.  Tensors are dense, contiguous, row-major in the shapes given.
+ *
+ * The reference interfaces each entry point replaces are cited beside it; all
+ * paths are inside the CAST source tree (src/interaction_accel/methods/).
+ */
+#ifndef CAST_B200_H
+#define CAST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define CAST_API __attribute__((visibility("default")))
+#else
+#define CAST_API
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st *cast_stream_t;
+
+enum cast_status {
+  CAST_OK = 0,
+  CAST_ERR_INVALID_ARGUMENT = 1,  /* null pointer, negative size, bad enum */
+  CAST_ERR_UNSUPPORTED = 2,       /* shape outside what the kernels implement */
+  CAST_ERR_ALIGNMENT = 3,         /* pointer not 16-byte aligned */
+  CAST_ERR_WORKSPACE = 4,         /* workspace too small */
+  CAST_ERR_CUDA = 5,              /* a CUDA runtime/driver call failed */
+  CAST_ERR_DEVICE_TIMEOUT = 6,    /* a bounded device-side wait gave up */
+  CAST_ERR_NO_DEVICE = 7          /* no sm_100 device current */
+};
+
+/* Human-readable name of a status code. */
+CAST_API const char *cast_status_string(int status);
+/* Detail message of the last failing call on this host thread. */
+CAST_API const char *cast_last_error_message(void);
+/* Library version (major*10000 + minor*100 + patch). */
+CAST_API int cast_version(void);
+/* Test/debug helper: synchronises `stream`, then reads and clears the device
+ * error word that bounded device-side waits set when they give up. */
+CAST_API int cast_device_error(cast_stream_t stream);
+
+/* Selection rule for cast_rcsa_select_quant. */
+enum cast_select_rule {
+  /* Historical top-`budget` by pooled cosine (ties to the lower block index),
+   * then current blocks 0..i for query block i (block-causal).  The last
+   * n_query_blocks key blocks are the current chunk. */
+  CAST_RULE_BUDGET_CAUSAL = 0
+};
+
+/* qk_mode values written by cast_rcsa_select_quant / read by the attention. */
+enum cast_qk_mode { CAST_QK_BF16 = 0, CAST_QK_INT8 = 1 };
+/* Precision policy for cast_rcsa_select_quant. */
+enum cast_qk_policy {
+  CAST_POLICY_BF16 = 0,   /* every (b,h,query block) uses bf16 QK^T */
+  CAST_POLICY_INT8 = 1,   /* every (b,h,query block) uses int8 QK^T */
+  CAST_POLICY_AUTO = 2    /* int8 where the predicted logit error is below
+                             int8_tolerance, bf16 elsewhere */
+};
+
+/*
+ * Pooled-QK block scoring + top-k historical block selection + per-block
+ * symmetric int8 quantisation (fused), on packed [B,H,L,D] bf16 tensors whose
+ * blocks of `block_size` tokens are contiguous.
+ *
+ * Replaces the pooled-Q/K top-k of
+ *   proposed/qk_uncertainty_tangent_attention.py:1011-1042 (TABA select) and
+ *   proposed/matrix_curvature_phase_frame_weave.py:5677-5831 (compact CWCA),
+ * under the historical-budget + block-causal rule.  The int8 quantiser has no
+ * reference counterpart (the reference attention is bf16,
+ * proposed/matrix_jit_spatial_acceleration.py:676-678).
+ *
+ *   q        bf16 [B,H,Lq,D]   queries of the current chunk
+ *   k        bf16 [B,H,Lk,D]   history blocks then the current chunk's blocks
+ *   v        bf16 [B,H,Lk,D]   may be NULL (then v_codes/v_scales ignored)
+ *   sel_idx  int32 [B,H,nQb,maxdeg], maxdeg = min(budget,nKb-nQb)+nQb, -1 pad
+ *   sel_cnt  int32 [B,H,nQb]
+ *   q_codes  int8 [B,H,Lq,D], q_scales float [B,H,nQb]    (may be NULL)
+ *   k_codes  int8 [B,H,Lk,D], k_scales float [B,H,nKb]    (may be NULL)
+ *   v_codes  int8 [B,H,Lk,D], v_scales float [B,H,nKb]    (may be NULL)
+ *   qk_mode  uint8 [B,H,nQb] (may be NULL), filled from `policy`
+ *   pooled   double [B,H,nQb+nKb,D] normalised pooled means (may be NULL:
+ *            then they live only in the workspace)
+ * Quantiser: s = amax/127 (s = 1 if amax == 0),
+ *            code = clamp(rint_half_even(x / s), -127, 127), IEEE division.
+ */
+CAST_API int cast_rcsa_select_quant(const void *q, const void *k, const void *v, int B, int H, int Lq,
+                           int Lk, int D, int block_size, int budget, int rule,
+                           int32_t *sel_idx, int32_t *sel_cnt, int8_t *q_codes, float *q_scales,
+                           int8_t *k_codes, float *k_scales, int8_t *v_codes, float *v_scales,
+                           uint8_t *qk_mode, int policy, float int8_tolerance, double *pooled,
+                           void *workspace, size_t workspace_bytes, cast_stream_t stream);
+CAST_API size_t cast_rcsa_select_quant_workspace_bytes(int B, int H, int Lq, int Lk, int D,
+                                              int block_size);
+
+/*
+ * TABA full-layer selection: pooled-QK cosine on the (tt,th,tw) block grid of
+ * a [T,Hl,Wl] latent, +1e6 Manhattan-<=1 stencil (added in float32 as the
+ * reference does), stable descending order truncated to max(row_degrees).
+ * Replaces MatrixTrajectoryAdaptiveBudgetAttentionCompiler.select
+ * (proposed/qk_uncertainty_tangent_attention.py:988-1082) given its compiled
+ * row degrees.  q, k: bf16 [B,H,T*Hl*Wl,D] in visual (t,h,w) order.
+ *   row_degrees int32 [N] on the device, N = blocks of the grid;
+ *   max_degree = max(row_degrees) (host int)
+ *   sel_idx int32 [B,H,N,max_degree], sel_cnt int32 [B,H,N]
+ *   scores  double [B,H,N,N] or NULL
+ */
+CAST_API int cast_taba_select(const void *q, const void *k, int B, int H, int T, int Hl, int Wl, int D,
+                     int tt, int th, int tw, const int32_t *row_degrees, int max_degree,
+                     int32_t *sel_idx, int32_t *sel_cnt, double *scores, void *workspace,
+                     size_t workspace_bytes, cast_stream_t stream);
+CAST_API size_t cast_taba_select_workspace_bytes(int B, int H, int T, int Hl, int Wl, int D, int tt,
+                                        int th, int tw);
+
+/*
+ * Block-sparse flash attention (tcgen05 tensor cores, TMEM accumulators, TMA
+ * tiles).  For every (b,h,query block i) the keys are the blocks
+ * indices[b,h,i,0:counts[b,h,i]] of K, masked by key_valid.
+ *   O = softmax(Q K^T * sm_scale) V, per row, over the allowed valid keys.
+ * QK^T runs in int8 (codes x scales, int32 accumulate) where qk_mode==1 and
+ * in bf16 where qk_mode==0; qk_mode NULL means int8 if q_codes/k_codes are
+ * given, else bf16.  PV is bf16 with fp32 accumulation.  Rows with no valid
+ * key produce zeros.
+ *
+ * Replaces MatrixJiTSpatialAcceleration._longcat_active
+ * (proposed/matrix_jit_spatial_acceleration.py:663-729) and
+ * MatrixCausalFrameLayerRelay._longcat_asymmetric
+ * (proposed/matrix_curvature_phase_frame_weave.py:8847-8917), whose launch
+ * of the external _attn_fwd_bsa_align takes the same operands.
+ *
+ *   q bf16 [B,H,Lq,D]; k, v bf16 [B,H,Lk,D]; out bf16 [B,H,Lq,D]
+ *   indices int32 [B,H,nQb,max_degree]; counts int32 [B,H,nQb]
+ *   key_valid uint8 [Lk] or NULL; lse float [B,H,Lq] (log2-domain row
+ *   log-sum-exp of the scaled logits) or NULL.
+ * Supported: D == 128, q_block and k_block multiples of 16.
+ */
+CAST_API int cast_rcsa_attention(const void *q, const void *k, const void *v, const int8_t *q_codes,
+                        const float *q_scales, const int8_t *k_codes, const float *k_scales,
+                        const uint8_t *qk_mode, const int32_t *indices, const int32_t *counts,
+                        int max_degree, const uint8_t *key_valid, int B, int H, int Lq, int Lk,
+                        int D, int q_block, int k_block, float sm_scale, void *out, float *lse,
+                        cast_stream_t stream);
+
+/*
+ * Phase-Aware Reconstruction (FC-PASM reference numerics) on one model call.
+ * Replaces WorldAlignedSpectralResidualCorrector.correct with the factory's
+ * FC knobs (proposed/matrix_world_spectral_residual.py:5283-5394 ->
+ * _correct_frequency_confidence_pasm_reference :2771-3662).
+ *
+ *   full_residual   bf16 [1,T,H*W,C], corrected IN PLACE: bracketed skipped
+ *                   current frames replaced, active frames overwritten by
+ *                   active_residual, memory frames untouched.
+ *   active_residual bf16 [1,A,H*W,C] for active_frames (sorted, unique,
+ *                   host int32 array of A global frame ids)
+ *   tile_confidence float [n_pairs,P] or NULL: per-tile confidence replacing
+ *                   base*ramp (the reference's precomputed_tile_confidence),
+ *                   pairs in chronological order of the used anchor pairs.
+ *   stats_out       float or NULL: per used pair [P,11,6] theta, [P] conf,
+ *                   [P,11,6] affinity, [P,2] displacement (see par.cu).
+ * Supported: H=22, W=40 (3x6 tiles of 11x10), C multiple of 32.
+ */
+CAST_API int cast_par_fcpasm(void *full_residual, const void *active_residual, const int32_t *active_frames,
+                    int n_active, int T, int memory_length, int H, int W, int C, float tau_low,
+                    float tau_high, float freq_power, float temperature, int ramp_confidence,
+                    int current_anchor_boundary, const float *tile_confidence, float *stats_out,
+                    void *workspace, size_t workspace_bytes, cast_stream_t stream);
+CAST_API size_t cast_par_fcpasm_workspace_bytes(int T, int H, int W, int C);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAST_B200_H */
