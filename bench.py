@@ -183,6 +183,8 @@ def main():
     ap.add_argument("--shard", default="rollout", choices=["rollout", "head"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heads", type=int, default=HEADS,
+                    help="heads of the config-2 layer (smaller values only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -203,14 +205,13 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     peaks, peak_src = load_peaks()
 
-    heads = HEADS
-    head_lo, head_hi = 0, HEADS
+    head_lo, head_hi = 0, args.heads
     if args.shard == "head" and world > 1:
-        if HEADS % world:
+        if args.heads % world:
             raise SystemExit("heads must divide evenly across GPUs")
-        per = HEADS // world
+        per = args.heads // world
         head_lo, head_hi = rank * per, (rank + 1) * per
-    w = workloads.config2(seed=1 + (rank if args.shard == "rollout" else 0))
+    w = workloads.config2(heads=args.heads, seed=1 + (rank if args.shard == "rollout" else 0))
     q_h = w.q[:, head_lo:head_hi].contiguous()
     k_h = w.k[:, head_lo:head_hi].contiguous()
     v_h = w.v[:, head_lo:head_hi].contiguous()
@@ -223,13 +224,19 @@ def main():
     stream = torch.cuda.current_stream(dev)
     att_ev = []
 
+    sel_ev = []
+
     def step(record=False):
+        if record:
+            s0 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
         sel = rcsa.select_quant(q, k, None, block_size=BLOCK, budget=BUDGET, policy=args.policy,
                                 quantize=args.policy != "bf16", workspace=ws)
         if record:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
+            sel_ev.append((s0, e0))
         out = rcsa.block_sparse_attention(
             q, k, v, sel.indices, sel.counts, q_block=BLOCK, k_block=BLOCK,
             q_codes=sel.q_codes, q_scales=sel.q_scales, k_codes=sel.k_codes,
@@ -262,6 +269,7 @@ def main():
         dist.barrier()
     total_ms = t0.elapsed_time(t1)
     att_ms = statistics.mean(a.elapsed_time(b) for a, b in att_ev)
+    sel_ms = statistics.mean(a.elapsed_time(b) for a, b in sel_ev)
 
     # ---- end to end through the public API with host buffers
     e2e = None
@@ -291,10 +299,10 @@ def main():
     clocks = sampler.stop()
 
     # ---- max over ranks
-    vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0], dtype=torch.float64, device=dev)
+    vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, att_ms, e2e_ms = (float(x) for x in vals.tolist())
+    total_ms, att_ms, e2e_ms, sel_ms = (float(x) for x in vals.tolist())
     ms_per_step = total_ms / args.steps
     calls_per_step = world if (args.shard == "rollout" and world > 1) else 1
     value_us = ms_per_step * 1000.0 / calls_per_step
@@ -327,6 +335,7 @@ def main():
             "l2": "inputs larger than L2 (Q+K 216 MB read per step by the selection pass)",
         },
         "attention_us": att_ms * 1000.0,
+        "select_quant_us": sel_ms * 1000.0,
         "roofline": {
             "bound": "tensor", "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
             "frac": achieved / peak_eff, "traffic": None,
