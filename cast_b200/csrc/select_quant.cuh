@@ -120,13 +120,14 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8))
   float amax = 0.0f, sq = 0.0f;
   const bool pool = which != 2;
 
+  constexpr int kUnroll = 8;
   int r = slot;
-  for (; r + 3 * kSumLanes < rows; r += 4 * kSumLanes) {
-    uint4 raw[4];
+  for (; r + (kUnroll - 1) * kSumLanes < rows; r += kUnroll * kSumLanes) {
+    uint4 raw[kUnroll];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) raw[u] = ldg_nc_v4(base + (size_t)(r + u * kSumLanes) * D);
+    for (int u = 0; u < kUnroll; ++u) raw[u] = ldg_nc_v4(base + (size_t)(r + u * kSumLanes) * D);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kUnroll; ++u) {
       float f[8];
       bf16x8_to_f32(raw[u], f);
 #pragma unroll
@@ -208,16 +209,29 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8))
     const float sc = s_scale;
     const float inv = __frcp_rn(sc);
     int8_t *cbase = codes + ((size_t)bh * L + b0) * D + grp * 8;
-    for (int rr = slot; rr < rows; rr += kSumLanes) {
+    auto quant8 = [&](const uint4 &raw) {
       float f[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4 *>(base + (size_t)rr * D), f);
+      bf16x8_to_f32(raw, f);
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) lo |= (uint32_t)(quant_code(f[i], sc, inv) & 0xFF) << (8 * i);
 #pragma unroll
       for (int i = 0; i < 4; ++i) hi |= (uint32_t)(quant_code(f[4 + i], sc, inv) & 0xFF) << (8 * i);
-      *reinterpret_cast<uint2 *>(cbase + (size_t)rr * D) = make_uint2(lo, hi);
+      return make_uint2(lo, hi);
+    };
+    int rr = slot;
+    for (; rr + (kUnroll - 1) * kSumLanes < rows; rr += kUnroll * kSumLanes) {
+      uint4 raw[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        raw[u] = *reinterpret_cast<const uint4 *>(base + (size_t)(rr + u * kSumLanes) * D);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        *reinterpret_cast<uint2 *>(cbase + (size_t)(rr + u * kSumLanes) * D) = quant8(raw[u]);
     }
+    for (; rr < rows; rr += kSumLanes)
+      *reinterpret_cast<uint2 *>(cbase + (size_t)rr * D) =
+          quant8(*reinterpret_cast<const uint4 *>(base + (size_t)rr * D));
   }
 }
 

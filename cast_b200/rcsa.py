@@ -251,3 +251,94 @@ def rcsa_attention(
         k_scales=sel.k_scales, qk_mode=sel.qk_mode,
     )
     return out, sel
+
+
+class RCSAPlan:
+    """Preallocated RCSA layer call for a fixed problem shape.
+
+    Holds every output and scratch buffer (indices, counts, int8 codes, scales,
+    precision modes, workspace, attention output), so repeated calls allocate
+    nothing and can be captured in a CUDA graph (:meth:`capture`).  This is the
+    B200 counterpart of the reference's cached per-shape workspaces.
+    """
+
+    def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int,
+                 budget: int, policy: str = "auto",
+                 int8_tolerance: float = DEFAULT_INT8_TOLERANCE, device=None):
+        if policy not in POLICIES:
+            raise ValueError(f"policy must be one of {sorted(POLICIES)}")
+        dev = torch.device(device if device is not None else "cuda")
+        self.shape = (B, H, Lq, Lk, D)
+        self.block_size, self.budget, self.policy = block_size, budget, policy
+        self.int8_tolerance = float(int8_tolerance)
+        nqb, nkb = -(-Lq // block_size), -(-Lk // block_size)
+        keep = min(budget, nkb - nqb)
+        quant = policy != "bf16"
+        self.indices = torch.empty(B, H, nqb, keep + nqb, dtype=torch.int32, device=dev)
+        self.counts = torch.empty(B, H, nqb, dtype=torch.int32, device=dev)
+        self.q_codes = torch.empty(B, H, Lq, D, dtype=torch.int8, device=dev) if quant else None
+        self.k_codes = torch.empty(B, H, Lk, D, dtype=torch.int8, device=dev) if quant else None
+        self.q_scales = torch.empty(B, H, nqb, dtype=torch.float32, device=dev) if quant else None
+        self.k_scales = torch.empty(B, H, nkb, dtype=torch.float32, device=dev) if quant else None
+        self.qk_mode = torch.empty(B, H, nqb, dtype=torch.uint8, device=dev) if quant else None
+        self.out = torch.empty(B, H, Lq, D, dtype=torch.bfloat16, device=dev)
+        nbytes = _lib.load().cast_rcsa_select_quant_workspace_bytes(B, H, Lq, Lk, D, block_size)
+        self.workspace = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+        self.sm_scale = 1.0 / math.sqrt(D)
+        self.device = dev
+
+    def select(self, q: torch.Tensor, k: torch.Tensor) -> None:
+        B, H, Lq, Lk, D = self.shape
+        if tuple(q.shape) != (B, H, Lq, D) or tuple(k.shape) != (B, H, Lk, D):
+            raise ValueError("q/k shapes differ from the plan")
+        _need_cuda("q", q, torch.bfloat16, 4)
+        _need_cuda("k", k, torch.bfloat16, 4)
+        P = _lib.ptr
+        _lib.call(
+            "cast_rcsa_select_quant", P(q), P(k), None, B, H, Lq, Lk, D, self.block_size,
+            self.budget, RULE_BUDGET_CAUSAL, P(self.indices), P(self.counts), P(self.q_codes),
+            P(self.q_scales), P(self.k_codes), P(self.k_scales), None, None, P(self.qk_mode),
+            POLICIES[self.policy], self.int8_tolerance, None, P(self.workspace),
+            self.workspace.numel(), _stream(self.device),
+        )
+
+    def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        B, H, Lq, Lk, D = self.shape
+        _need_cuda("v", v, torch.bfloat16, 4)
+        P = _lib.ptr
+        _lib.call(
+            "cast_rcsa_attention", P(q), P(k), P(v), P(self.q_codes), P(self.q_scales),
+            P(self.k_codes), P(self.k_scales), P(self.qk_mode), P(self.indices), P(self.counts),
+            int(self.indices.shape[-1]), None, B, H, Lq, Lk, D, self.block_size, self.block_size,
+            float(self.sm_scale), P(self.out), None, _stream(self.device),
+        )
+        return self.out
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        self.select(q, k)
+        return self.attend(q, k, v)
+
+    def selection(self) -> Selection:
+        return Selection(self.indices, self.counts, self.q_codes, self.q_scales, self.k_codes,
+                         self.k_scales, None, None, self.qk_mode, None)
+
+    def capture(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, parts: str = "all"):
+        """CUDA graph of one call on these input buffers (``parts``: all,
+        select or attend).  Replaying it recomputes from the buffers' current
+        contents."""
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self._run_parts(q, k, v, parts)  # warm the launch paths on this stream
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.graph(g, stream=s):
+            self._run_parts(q, k, v, parts)
+        return g
+
+    def _run_parts(self, q, k, v, parts):
+        if parts in ("all", "select"):
+            self.select(q, k)
+        if parts in ("all", "attend"):
+            self.attend(q, k, v)
