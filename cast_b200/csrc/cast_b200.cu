@@ -549,3 +549,60 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
   }
   return CAST_OK;
 }
+
+// ===========================================================================
+// allocation-free RCSA selection + quantisation
+// ===========================================================================
+// One static scratch array per device (each device's copy of this module has
+// its own); every call on that device shares it, so calls must not overlap on
+// the GPU.  Nothing in it needs to start at zero.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CAST_NOALLOC_SCRATCH_BYTES];
+
+static constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_noalloc_mutex;
+static void *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Address of the current device's scratch, looked up once per device with
+// that device current.
+static int noalloc_scratch(void **out) {
+  int dev = 0;
+  CAST_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(CAST_ERR_UNSUPPORTED, "device ordinal %d >= %d", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void *ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(CAST_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return CAST_OK;
+}
+
+extern "C" int cast_rcsa_select_quant_noalloc(const void *q, const void *k, const void *v, int B,
+                                              int H, int Lq, int Lk, int D, int block_size,
+                                              int budget, int rule, int32_t *sel_idx,
+                                              int32_t *sel_cnt, int8_t *q_codes, float *q_scales,
+                                              int8_t *k_codes, float *k_scales, int8_t *v_codes,
+                                              float *v_scales, uint8_t *qk_mode, int policy,
+                                              float int8_tolerance, double *pooled,
+                                              cast_stream_t stream) {
+  const size_t need = cast_rcsa_select_quant_workspace_bytes(B, H, Lq, Lk, D, block_size);
+  if (need > CAST_NOALLOC_SCRATCH_BYTES)
+    return fail(CAST_ERR_WORKSPACE,
+                "needs %zu bytes of scratch; the static scratch holds %zu "
+                "(use cast_rcsa_select_quant with a caller workspace)",
+                need, (size_t)CAST_NOALLOC_SCRATCH_BYTES);
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  void *scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st) return st;
+  return cast_rcsa_select_quant(q, k, v, B, H, Lq, Lk, D, block_size, budget, rule, sel_idx,
+                                sel_cnt, q_codes, q_scales, k_codes, k_scales, v_codes, v_scales,
+                                qk_mode, policy, int8_tolerance, pooled, scratch,
+                                CAST_NOALLOC_SCRATCH_BYTES, stream);
+}

@@ -104,6 +104,38 @@ CAST_API size_t cast_rcsa_select_quant_workspace_bytes(int B, int H, int Lq, int
                                               int block_size);
 
 /*
+ * Allocation-free variant of cast_rcsa_select_quant (no counterpart in the
+ * reference).  Same arguments, outputs and results, minus the workspace: the
+ * scratch lives in one static device array of CAST_NOALLOC_SCRATCH_BYTES per
+ * device, inside this library.  The call makes no cudaMalloc / cudaFree or
+ * other allocating call; its first call on a device looks up that array's
+ * address (cudaGetSymbolAddress) with the device current.
+ *
+ * For callers that must not allocate device memory on the call path: hosts
+ * with no caching allocator (a C, Go or Java process calling the C ABI), where
+ * a cudaMalloc/cudaFree pair per call would synchronise the device and stall
+ * every other stream, and serving processes that have reserved all free HBM up
+ * front and have none left to hand out.
+ *
+ * Limit: cast_rcsa_select_quant_workspace_bytes(B,H,Lq,Lk,D,block_size) must
+ * be <= CAST_NOALLOC_SCRATCH_BYTES, else CAST_ERR_WORKSPACE is returned before
+ * anything is launched (for D=128 that is about 8,000 (b, h, block) triples,
+ * counting query and key blocks).
+ * Nothing in the scratch needs to start at zero: every element the selection
+ * reads is written earlier in the same call.
+ * Every call on a device shares the one array: calls whose kernels overlap on
+ * the GPU (different streams without ordering between them) race and corrupt
+ * each other's results.  Issue them on one stream, or order them with events.
+ */
+#define CAST_NOALLOC_SCRATCH_BYTES (8u << 20)
+CAST_API int cast_rcsa_select_quant_noalloc(const void *q, const void *k, const void *v, int B, int H,
+                                   int Lq, int Lk, int D, int block_size, int budget, int rule,
+                                   int32_t *sel_idx, int32_t *sel_cnt, int8_t *q_codes,
+                                   float *q_scales, int8_t *k_codes, float *k_scales,
+                                   int8_t *v_codes, float *v_scales, uint8_t *qk_mode, int policy,
+                                   float int8_tolerance, double *pooled, cast_stream_t stream);
+
+/*
  * TABA full-layer selection: pooled-QK cosine on the (tt,th,tw) block grid of
  * a [T,Hl,Wl] latent, +1e6 Manhattan-<=1 stencil (added in float32 as the
  * reference does), stable descending order truncated to max(row_degrees).
