@@ -36,6 +36,10 @@ sys.path.insert(0, ROOT)
 METRIC = "RCSA int8 sparse-attn µs/call & % tensor-core peak; scaling at 1/2/4/8 B200"
 BLOCK, BUDGET, HEADS, D = 880, 8, 24, 128
 HIST, CUR = 32, 4
+# DRAM bytes (read + write) of one attention launch on the full config-2
+# workload, from the ncu launch list in profiles/launches_rcsa_config2_auto.md
+# (auto policy); other policies have no capture.
+ATTN_TRAFFIC_BYTES = {"auto": 701.3e6}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -195,6 +199,7 @@ def main():
     import torch
     import torch.distributed as dist
 
+    from cast_b200 import distributed as cdist
     from cast_b200 import rcsa, workloads
 
     torch.cuda.set_device(local)
@@ -207,10 +212,7 @@ def main():
 
     head_lo, head_hi = 0, args.heads
     if args.shard == "head" and world > 1:
-        if args.heads % world:
-            raise SystemExit("heads must divide evenly across GPUs")
-        per = args.heads // world
-        head_lo, head_hi = rank * per, (rank + 1) * per
+        head_lo, head_hi = cdist.head_range(args.heads, world, rank)
     w = workloads.config2(heads=args.heads, seed=1 + (rank if args.shard == "rollout" else 0))
     q_h = w.q[:, head_lo:head_hi].contiguous()
     k_h = w.k[:, head_lo:head_hi].contiguous()
@@ -218,7 +220,7 @@ def main():
     q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
     gathered = None
     if args.shard == "head" and world > 1:
-        gathered = torch.empty(world, *q.shape, dtype=q.dtype, device=dev)
+        gathered = torch.empty(world * q.shape[0], *q.shape[1:], dtype=q.dtype, device=dev)
 
     stream = torch.cuda.current_stream(dev)
     b_, h_, lq_, d_ = q.shape
@@ -264,7 +266,7 @@ def main():
     def full_step():
         g_all.replay()
         if gathered is not None:
-            dist.all_gather_into_tensor(gathered, plan.out)
+            cdist.gather_heads(plan.out, world, gathered=gathered)
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -338,9 +340,11 @@ def main():
         "timing": "CUDA graph replay of the 3-kernel layer call; events on the replay stream",
         "roofline": {
             "bound": "tensor", "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
-            "frac": achieved / peak_eff, "traffic": None,
+            "frac": achieved / peak_eff,
+            "traffic": ATTN_TRAFFIC_BYTES.get(args.policy) if args.heads == HEADS else None,
             "note": (f"attention kernel; peak = work-weighted harmonic of bf16 {peaks['bf16_tflops']} "
                      f"TFLOP/s ({peak_src} cuBLAS burst) and int8 = 2x bf16 (no measured int8 peak); "
+                     "traffic = ncu DRAM bytes per launch; "
                      f"ops/launch int8 {i8_ops:.4g} bf16 {bf_ops:.4g}"),
         },
         "gpu_launches": 3 * args.steps,

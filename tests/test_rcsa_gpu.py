@@ -212,3 +212,51 @@ def test_rcsa_config2_full_properties(cuda):
     assert bool(torch.isfinite(out_a.float()).all())
     diff = (out_a.float() - out_b.float()).abs()
     assert float(diff.mean()) < MEAN_ABS and float(diff.max()) < MAX_ABS
+
+
+def test_taba_select_config1_golden(cuda):
+    """TABA full-layer selection (cast_taba_select) on config 1 against the
+    reference's own ``select`` output and the oracle."""
+    from cast_b200.select import TABASelector
+
+    g = np.load(os.path.join(GOLDEN, "cfg1_select.npz"))
+    w = workloads.config1()
+    q = w.meta["q_full"].bfloat16()
+    k = w.k.bfloat16()
+    sel = TABASelector((1, 8, 8))
+    sel.set_row_degrees(torch.from_numpy(g["taba_row_degrees"]))
+    idx, cnt, report, scores = sel.select(q.cuda(), k.cuda(), geometry_indices=None,
+                                          geometry_counts=None, latent_hw=(8, 8),
+                                          block_shape=(1, 8, 8), return_scores=True)
+    torch.cuda.synchronize()
+    o_sel, o_cnt, o_sc = orc.taba_select(_np(q), _np(k), (8, 8), (1, 8, 8), g["taba_row_degrees"])
+    assert np.array_equal(scores.cpu().numpy(), o_sc)
+    assert np.array_equal(idx.cpu().numpy(), o_sel)
+    assert np.array_equal(cnt.cpu().numpy(), o_cnt)
+    assert np.array_equal(idx.cpu().numpy(), g["taba_selected"])
+    assert report.budget_max == int(g["taba_row_degrees"].max())
+
+
+@pytest.mark.parametrize("block_shape", [(1, 4, 8), (2, 11, 10), (1, 22, 40)])
+def test_taba_select_ragged_grid_bitexact(cuda, block_shape):
+    """22x40 latent (config-2 frame grid) tiled by block shapes that leave
+    ragged edge tiles; per-row degrees vary."""
+    from cast_b200.select import TABASelector
+
+    gen = torch.Generator().manual_seed(11)
+    t, hl, wl, d, heads = 4, 22, 40, 128, 3
+    q = torch.randn(1, heads, t * hl * wl, d, generator=gen).bfloat16()
+    k = (torch.randn(1, heads, t * hl * wl, d, generator=gen) + 0.3 * q.float()).bfloat16()
+    tt, th, tw = block_shape
+    nblocks = -(-t // tt) * -(-hl // th) * -(-wl // tw)
+    degrees = torch.randint(1, min(nblocks, 20) + 1, (nblocks,), generator=gen)
+    sel = TABASelector(block_shape)
+    sel.set_row_degrees(degrees)
+    idx, cnt, _, scores = sel.select(q.cuda(), k.cuda(), geometry_indices=None,
+                                     geometry_counts=None, latent_hw=(hl, wl),
+                                     block_shape=block_shape, return_scores=True)
+    torch.cuda.synchronize()
+    o_sel, o_cnt, o_sc = orc.taba_select(_np(q), _np(k), (hl, wl), block_shape, degrees.numpy())
+    assert np.array_equal(scores.cpu().numpy(), o_sc)
+    assert np.array_equal(idx.cpu().numpy(), o_sel)
+    assert np.array_equal(cnt.cpu().numpy(), o_cnt)
