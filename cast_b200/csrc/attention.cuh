@@ -2,36 +2,37 @@
 // accumulators, TMA-staged tiles (no multicast), online softmax.
 //
 // One CTA computes up to two 128-row query tiles of one (b*h, query block)
-// against the concatenated KV blocks listed for that query block.  Work per
-// KV tile j (128 keys):
-//   S_i = Q_i K_j^T      int8 x int8 -> s32 (kind::i8) or bf16 -> f32 (kind::f16)
-//   P_i = exp2(S_i * c - m_i)  (softmax warpgroup i, written back to TMEM as
-//                               bf16 over the S_i columns it was read from)
-//   O_i += P_i V_j       bf16 (kind::f16, A = P from TMEM, B = V from SMEM)
+// against the concatenated KV blocks listed for that query block.  TMA moves
+// K and V in tiles of 128 keys; the MMAs and the softmax step through them in
+// halves of 64 keys (step h = tile h/2, half h%2):
+//   S_i(h) = Q_i K_h^T    int8 x int8 -> s32 (kind::i8) or bf16 -> f32 (kind::f16)
+//   P_i(h) = exp2(S_i(h) * c - m_i)   (softmax warpgroup i; bf16 pairs written
+//                                      back over the first 32 columns of S_i(h))
+//   O_i   += P_i(h) V_h   bf16 (kind::f16, A = P from TMEM, B = V from SMEM)
 //
 // Warp roles (384 threads = 3 warpgroups):
 //   warps 0-3   softmax + epilogue of query tile 0 (TMEM lanes 0..127)
 //   warps 4-7   softmax + epilogue of query tile 1
 //   warp 8      TMA producer of Q (once) and the K ring
-//   warp 9      MMA issuer (one elected thread) + TMEM allocation
-//   warp 10     TMA producer of the V ring (independent of K, so a full V
-//               ring never delays the next K tile)
-//   warp 11     idle
-// The producer/MMA warpgroup gives registers to the two softmax warpgroups
-// (setmaxnreg), so a softmax thread holds a whole 128-column S row.
+//   warp 9      MMA issuer of query tile 0 (one thread) + TMEM allocation
+//   warp 10     TMA producer of the V ring
+//   warp 11     MMA issuer of query tile 1 (one thread)
+// Each query tile has its own issuing thread, so neither tile's MMAs wait
+// behind the other tile's barrier polls.
 //
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
-// P_i is stored in the lower 64 columns of S_i (128 bf16 keys packed in
-// pairs) after the whole S_i row has been read.  MMAs issued by one thread
-// execute in issue order, so S_i(j+1) may overwrite P_i(j) once O_i +=
-// P_i(j) V_j has been issued before it; and the commit that signals S_i(j+1)
-// also covers O_i += P_i(j) V_j, so the softmax can rescale O_i right after
-// it sees S_i(j+1).
+// TMEM (512 columns): O0 [0,128) O1 [128,256), then two S buffers of 64
+// columns per query tile: S_i buffer b at 256 + 128 i + 64 b.  S_i(h) lives in
+// buffer h%2, so the MMA thread issues S_i(h+2) right after O_i += P_i(h) V_h:
+// while the softmax works on step h, the tensor core has already produced
+// S_i(h+1), and the softmax never waits for its own PV.  MMAs issued by one
+// thread execute in issue order, so S_i(h+2) may overwrite P_i(h) once the PV
+// that reads it has been issued.
 //
-// Lazy rescale: the running max only moves when a tile's max exceeds it by
+// Lazy rescale: the running max only moves when a step's max exceeds it by
 // more than kRescaleLog2 (in log2 units); probabilities are then bounded by
 // 2^kRescaleLog2 and the final normalisation uses the same stale max in
-// numerator and denominator, so the result is exact.
+// numerator and denominator, so the result is exact.  A rescale of O_i first
+// waits for the PV of the previous step (pv_done), which is still in flight.
 #pragma once
 
 #include <climits>
@@ -44,10 +45,7 @@ constexpr int kAttnThreads = 384;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kVProducerWarp = 10;
-constexpr int kSoftmaxRegs = 216;  // setmaxnreg.inc for warpgroups 0-1
-constexpr int kServiceRegs = 56;   // setmaxnreg.dec for warpgroup 2
-// The CTA's register pool must cover the split: 256*216 + 128*56 = 62464.
-constexpr int kRegPoolNeeded = 256 * kSoftmaxRegs + 128 * kServiceRegs;
+constexpr int kMmaWarp1 = 11;  // MMA issuer of query tile 1
 constexpr int kMaxKStages = 4;
 constexpr int kVStages = 3;
 constexpr int kMaxBlockList = 256;
@@ -61,8 +59,8 @@ constexpr float kRescaleLog2 = 8.0f;
 struct AttnSmem {
   static constexpr int bars = 229376;  // 224 KB: past the largest layout
   // barriers: q_full, k_full[4], k_empty[4], v_full[3], v_empty[3],
-  //           s_full[2], p_full[2], o_final
-  static constexpr int n_bars = 1 + 2 * kMaxKStages + 2 * kVStages + 2 + 2 + 1;
+  //           s_full[2][2], p_full[2][2], pv_done[2][2], mma_drain[2]
+  static constexpr int n_bars = 1 + 2 * kMaxKStages + 2 * kVStages + 4 + 4 + 4 + 2;
   static constexpr int tmem_slot = bars + 8 * n_bars;
   static constexpr int blist = (tmem_slot + 16 + 15) / 16 * 16;
   static constexpr int total = blist + 4 * kMaxBlockList;
@@ -93,33 +91,23 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// bf16 pair with round-to-nearest (ties up) on the integer pipe: add half an
-// ulp of bf16 to the bits of the (non-negative) floats and keep the upper
-// halves; `lo` lands in the low 16 bits.
-__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
-  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h2);
 }
 
-__device__ __forceinline__ void setmaxnreg_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
-}
-__device__ __forceinline__ void setmaxnreg_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kServiceRegs));
-}
-
-// Row max of a full 128-column S row held in registers, times c2 (log2
-// units); -inf if every key is masked.  Raw scores are s32 (int8 QK^T) or
-// f32 bits (bf16 QK^T).  Eight independent accumulators keep the dependency
-// chains short.
+// Row max of a 64-column S step held in registers, times c2 (log2 units);
+// -inf if every key is masked.  Raw scores are s32 (int8 QK^T) or f32 bits
+// (bf16 QK^T).  Eight independent accumulators keep the chains short.
 template <bool kInt8, bool kMasked>
-__device__ __forceinline__ float row_max(const uint32_t (&v)[128], const uint32_t (&kmask)[4],
+__device__ __forceinline__ float row_max(const uint32_t (&v)[64], const uint32_t (&kmask)[2],
                                          float c2) {
   if (kInt8) {
     int acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = INT_MIN;
 #pragma unroll
-    for (int c = 0; c < 128; ++c) {
+    for (int c = 0; c < 64; ++c) {
       int x = (int)v[c];
       if (kMasked) x = ((kmask[c / 32] >> (c % 32)) & 1u) ? x : INT_MIN;
       acc[c & 7] = max(acc[c & 7], x);
@@ -135,7 +123,7 @@ __device__ __forceinline__ float row_max(const uint32_t (&v)[128], const uint32_
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < 128; ++c) {
+    for (int c = 0; c < 64; ++c) {
       float x = __uint_as_float(v[c]);
       if (kMasked) x = ((kmask[c / 32] >> (c % 32)) & 1u) ? x : -INFINITY;
       acc[c & 7] = fmaxf(acc[c & 7], x);
@@ -148,17 +136,17 @@ __device__ __forceinline__ float row_max(const uint32_t (&v)[128], const uint32_
   }
 }
 
-// Probabilities exp2(S*c2 - base) of the row (masked keys 0), packed bf16
-// pairs written in place into v[0..63].  Returns the row sum.  For s32 scores
+// Probabilities exp2(S*c2 - base) of the step (masked keys 0), packed bf16
+// pairs written in place into v[0..31].  Returns their sum.  For s32 scores
 // the int->float conversion is folded into the FFMA:
 // float(S) = as_float(S + 0x4B400000) - 1.5*2^23, exact for |S| < 2^22.
 template <bool kInt8, bool kMasked>
-__device__ __forceinline__ float row_probs(uint32_t (&v)[128], const uint32_t (&kmask)[4],
+__device__ __forceinline__ float row_probs(uint32_t (&v)[64], const uint32_t (&kmask)[2],
                                            float c2, float base) {
   const float bias = kInt8 ? fmaf(12582912.0f, c2, base) : base;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int c = 0; c < 64; ++c) {
+  for (int c = 0; c < 32; ++c) {
     const uint32_t a = kInt8 ? v[2 * c] + 0x4B400000u : v[2 * c];
     const uint32_t b = kInt8 ? v[2 * c + 1] + 0x4B400000u : v[2 * c + 1];
     float e0 = fast_exp2(fmaf(__uint_as_float(a), c2, -bias));
@@ -169,9 +157,106 @@ __device__ __forceinline__ float row_probs(uint32_t (&v)[128], const uint32_t (&
       e1 = ((w >> ((2 * c + 1) % 32)) & 1u) ? e1 : 0.0f;
     }
     acc[c & 3] += e0 + e1;
-    v[c] = pack_bf16x2_alu(e0, e1);
+    v[c] = pack_bf16x2(e0, e1);
   }
   return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+// Shared-memory descriptor as (lo, hi) words: hi is fixed by the LBO/SBO
+// strides, and lo = start>>4 | LBO>>4 << 16, so an operand `off` bytes further
+// on is lo + off/16 (smem addresses stay below 2^18, so nothing carries).
+struct DescW {
+  uint32_t lo, hi;
+  __device__ __forceinline__ uint64_t at(uint32_t off) const {
+    return ((uint64_t)hi << 32) | (uint64_t)(lo + (off >> 4));
+  }
+};
+__device__ __forceinline__ DescW desc_words(uint32_t addr, uint32_t lbo) {
+  const uint64_t d = castdev::smem_desc_sw128(addr, lbo, 1024);
+  return DescW{(uint32_t)d, (uint32_t)(d >> 32)};
+}
+
+// The MMA issuer of query tile i (one thread per tile).  Per 64-key step h:
+//   wait P_i(h); O_i += P_i(h) V_h; commit pv_done; then S_i(h+2) into the S
+//   buffer P_i(h) came from (issued after the PV that reads it); commit
+//   s_full.  K and V stages are released by commits after their last use;
+//   their "empty" barriers count one arrival per active tile.
+// Returns false if a wait gave up.
+template <int kInt8>
+__device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase, int n_steps,
+                                           int q_bytes, int k_off, int v_off, uint64_t *q_full,
+                                           uint64_t *k_full, uint64_t *k_empty, uint64_t *v_full,
+                                           uint64_t *v_empty, uint64_t *s_full, uint64_t *p_full,
+                                           uint64_t *pv_done, int *err) {
+  constexpr int KS = kInt8 ? 4 : 2;              // K ring depth
+  constexpr int kKBytes = kInt8 ? 16384 : 32768;  // one K stage
+  constexpr uint32_t idesc_s = kInt8 ? castdev::make_idesc(2, 1, 1, 0, 0, 128, 64)
+                                     : castdev::make_idesc(1, 1, 1, 0, 0, 128, 64);
+  constexpr uint32_t idesc_pv = castdev::make_idesc(1, 1, 1, 0, 1, 128, 128);
+  const DescW qd = desc_words(sbase + i * q_bytes, 16);
+  const DescW kd = desc_words(sbase + k_off, 16);     // + stage * kKBytes + half * 8192
+  const DescW vd = desc_words(sbase + v_off, 16384);  // + stage * 32768 + half * 8192
+  const uint32_t o_col = tmem + i * 128;
+  const uint32_t s_col = tmem + 256 + i * 128;
+  uint64_t *my_s_full = s_full + 2 * i;
+  uint64_t *my_p_full = p_full + 2 * i;
+  uint64_t *my_pv_done = pv_done + 2 * i;
+
+  auto issue_s = [&](int h) {
+    const uint32_t d = s_col + (h & 1) * 64;
+    const uint32_t ko = ((h >> 1) & (KS - 1)) * kKBytes + (h & 1) * 8192;
+    if (kInt8) {
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        castdev::mma_i8_ss(d, qd.at(32 * s), kd.at(ko + 32 * s), idesc_s, s > 0);
+    } else {
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t off = (s >> 2) * 16384 + (s & 3) * 32;
+        castdev::mma_f16_ss(d, qd.at(off), kd.at(ko + off), idesc_s, s > 0);
+      }
+    }
+  };
+
+  if (!castdev::mbar_wait(q_full, 0, err) || !castdev::mbar_wait(&k_full[0], 0, err))
+    return false;
+  castdev::tc_fence_after();
+  issue_s(0);
+  castdev::tc_commit(&my_s_full[0]);
+  issue_s(1);
+  castdev::tc_commit(&my_s_full[1]);
+  castdev::tc_commit(&k_empty[0]);
+
+  int vs = 0;
+  uint32_t vphase = 0;
+  for (int h = 0; h < n_steps; ++h) {
+    const int half = h & 1;
+    const int hn = h + 2;
+    if (!half && !castdev::mbar_wait(&v_full[vs], vphase, err)) return false;
+    if (!castdev::mbar_wait(&my_p_full[half], (h >> 1) & 1, err)) return false;
+    castdev::tc_fence_after();
+    const uint32_t vo = vs * 32768 + half * 8192;
+    const uint32_t pa = s_col + half * 64;
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      castdev::mma_f16_ts(o_col, pa + 8 * s, vd.at(vo + 2048 * s), idesc_pv, (h | s) != 0);
+    castdev::tc_commit(&my_pv_done[half]);
+    if (hn < n_steps) {
+      if (!half) {
+        const int t = hn >> 1;
+        if (!castdev::mbar_wait(&k_full[t & (KS - 1)], (t / KS) & 1, err)) return false;
+        castdev::tc_fence_after();
+      }
+      issue_s(hn);
+      castdev::tc_commit(&my_s_full[half]);
+    }
+    if (half) {
+      castdev::tc_commit(&v_empty[vs]);
+      if (++vs == kVStages) vs = 0, vphase ^= 1u;
+      if (hn < n_steps) castdev::tc_commit(&k_empty[(hn >> 1) & (KS - 1)]);
+    }
+  }
+  return true;
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -189,9 +274,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t *k_empty = k_full + kMaxKStages;
   uint64_t *v_full = k_empty + kMaxKStages;
   uint64_t *v_empty = v_full + kVStages;
-  uint64_t *s_full = v_empty + kVStages;
-  uint64_t *p_full = s_full + 2;
-  uint64_t *o_final = p_full + 2;
+  uint64_t *s_full = v_empty + kVStages;  // [tile * 2 + buffer]
+  uint64_t *p_full = s_full + 4;          // [tile * 2 + buffer]
+  uint64_t *pv_done = p_full + 4;         // [tile * 2 + buffer]
+  uint64_t *mma_drain = pv_done + 4;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + AttnSmem::tmem_slot);
   int32_t *blist = reinterpret_cast<int32_t *>(smem + AttnSmem::blist);
   int *err = &g_cast_device_error;
@@ -218,7 +304,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int nq = min(2, p.q_tiles - t0);
   const int row_item = bh * p.nqb + qb;
   const int n_blocks = min(max(p.counts[row_item], 0), min(p.max_degree, kMaxBlockList));
-  const int n_kv = n_blocks * p.k_tiles;
+  const int n_kv = n_blocks * p.k_tiles;  // 128-key tiles
+  const int n_steps = 2 * n_kv;           // 64-key steps
   const int mode = p.qk_mode ? (int)p.qk_mode[row_item] : p.default_mode;  // 1 = int8
 
   // mode-dependent layout
@@ -231,8 +318,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < AttnSmem::n_bars; ++i) castdev::mbar_init(&bar[i], 1);
-    castdev::mbar_init(&p_full[0], 4);
-    castdev::mbar_init(&p_full[1], 4);
+    for (int i = 0; i < 4; ++i) castdev::mbar_init(&p_full[i], 4);
+    // a K or V stage is free once every active tile's MMAs have read it
+    for (int i = 0; i < kMaxKStages; ++i) castdev::mbar_init(&k_empty[i], nq);
+    for (int i = 0; i < kVStages; ++i) castdev::mbar_init(&v_empty[i], nq);
     castdev::fence_barrier_init();
   }
   if (warp == kMmaWarp) {
@@ -251,11 +340,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp >= 8) {
-    setmaxnreg_dec();
     if (warp == kProducerWarp) {
       // ---------------------------------------------------- Q + K producer
       if (lane == 0 && n_kv > 0) {
-        bool ok = true;
         const int qrow0 = qb * p.q_block + t0 * 128;
         castdev::mbar_arrive_expect_tx(q_full, nq * q_bytes);
         for (int i = 0; i < nq; ++i) {
@@ -267,13 +354,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             castdev::tma_load_3d(qd + 16384, &tm_q16, q_full, 64, qrow0 + i * 128, bh);
           }
         }
-        for (int j = 0; j < n_kv && ok; ++j) {
+        int issued = 0;
+        for (int j = 0; j < n_kv; ++j) {
           const int blk = blist[j / p.k_tiles];
           const int tin = j % p.k_tiles;
           const int krow = (blk >= 0 && blk < p.nkb) ? blk * p.k_block + tin * 128 : 0;
           const int ks = j % KS;
-          if (j >= KS) ok = castdev::mbar_wait(&k_empty[ks], ((j / KS) - 1) & 1, err);
-          if (!ok) break;
+          if (j >= KS && !castdev::mbar_wait(&k_empty[ks], ((j / KS) - 1) & 1, err)) break;
           uint8_t *kd = smem + k_off + ks * k_bytes;
           castdev::mbar_arrive_expect_tx(&k_full[ks], k_bytes);
           if (mode) {
@@ -282,108 +369,56 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             castdev::tma_load_3d(kd, &tm_k16, &k_full[ks], 0, krow, bh);
             castdev::tma_load_3d(kd + 16384, &tm_k16, &k_full[ks], 64, krow, bh);
           }
+          issued = j + 1;
         }
         // Drain: every issued load completes before the CTA may exit.
-        castdev::mbar_wait(q_full, 0, err);
-        for (int j = max(0, n_kv - KS); j < n_kv; ++j)
-          castdev::mbar_wait(&k_full[j % KS], (j / KS) & 1, err);
+        castdev::mbar_wait_drain(q_full, 0, err);
+        for (int j = max(0, issued - KS); j < issued; ++j)
+          castdev::mbar_wait_drain(&k_full[j % KS], (j / KS) & 1, err);
       }
     } else if (warp == kVProducerWarp) {
       // ---------------------------------------------------- V producer
       if (lane == 0 && n_kv > 0) {
-        bool ok = true;
-        for (int j = 0; j < n_kv && ok; ++j) {
+        int issued = 0;
+        for (int j = 0; j < n_kv; ++j) {
           const int blk = blist[j / p.k_tiles];
           const int tin = j % p.k_tiles;
           const int krow = (blk >= 0 && blk < p.nkb) ? blk * p.k_block + tin * 128 : 0;
           const int vs = j % kVStages;
-          if (j >= kVStages) ok = castdev::mbar_wait(&v_empty[vs], ((j / kVStages) - 1) & 1, err);
-          if (!ok) break;
+          if (j >= kVStages && !castdev::mbar_wait(&v_empty[vs], ((j / kVStages) - 1) & 1, err))
+            break;
           uint8_t *vd = smem + v_off + vs * 32768;
           castdev::mbar_arrive_expect_tx(&v_full[vs], 32768);
           castdev::tma_load_3d(vd, &tm_v, &v_full[vs], 0, krow, bh);
           castdev::tma_load_3d(vd + 16384, &tm_v, &v_full[vs], 64, krow, bh);
+          issued = j + 1;
         }
-        for (int j = max(0, n_kv - kVStages); j < n_kv; ++j)
-          castdev::mbar_wait(&v_full[j % kVStages], (j / kVStages) & 1, err);
+        for (int j = max(0, issued - kVStages); j < issued; ++j)
+          castdev::mbar_wait_drain(&v_full[j % kVStages], (j / kVStages) & 1, err);
       }
-    } else if (warp == kMmaWarp) {
-      // ---------------------------------------------------- MMA issuer
-      if (lane == 0 && n_kv > 0) {
-        const uint32_t idesc_s = mode ? castdev::make_idesc(2, 1, 1, 0, 0, 128, 128)
-                                      : castdev::make_idesc(1, 1, 1, 0, 0, 128, 128);
-        const uint32_t idesc_pv = castdev::make_idesc(1, 1, 1, 0, 1, 128, 128);
+    } else {
+      // ---------------------------------------------------- MMA issuers
+      const int i = warp == kMmaWarp ? 0 : 1;
+      if (lane == 0 && n_kv > 0 && i < nq) {
         const uint32_t sbase = castdev::smem_u32(smem);
-        bool ok = castdev::mbar_wait(q_full, 0, err);
-        auto issue_s = [&](int i, int ks) {
-          const uint32_t d = tmem + i * 128;
-          const uint32_t qa = sbase + q_off + i * q_bytes;
-          const uint32_t ka = sbase + k_off + ks * k_bytes;
-          if (mode) {
-#pragma unroll
-            for (int s = 0; s < 4; ++s)
-              castdev::mma_i8_ss(d, castdev::smem_desc_sw128(qa + 32 * s, 16, 1024),
-                                 castdev::smem_desc_sw128(ka + 32 * s, 16, 1024), idesc_s, s > 0);
-          } else {
-#pragma unroll
-            for (int s = 0; s < 8; ++s) {
-              const uint32_t off = (s >> 2) * 16384 + (s & 3) * 32;
-              castdev::mma_f16_ss(d, castdev::smem_desc_sw128(qa + off, 16, 1024),
-                                  castdev::smem_desc_sw128(ka + off, 16, 1024), idesc_s, s > 0);
-            }
-          }
-        };
-        auto issue_pv = [&](int i, int vs, bool first) {
-          const uint32_t d = tmem + 256 + i * 128;
-          const uint32_t pa = tmem + i * 128;
-          const uint32_t va = sbase + v_off + vs * 32768;
-#pragma unroll
-          for (int s = 0; s < 8; ++s)
-            castdev::mma_f16_ts(d, pa + 8 * s, castdev::smem_desc_sw128(va + 2048 * s, 16384, 1024),
-                                idesc_pv, (!first || s > 0) ? 1u : 0u);
-        };
-        if (ok) ok = castdev::mbar_wait(&k_full[0], 0, err);
-        if (ok) {
-          castdev::tc_fence_after();
-          for (int i = 0; i < nq; ++i) {
-            issue_s(i, 0);
-            castdev::tc_commit(&s_full[i]);
-          }
-          castdev::tc_commit(&k_empty[0]);
-        }
-        for (int j = 0; j < n_kv && ok; ++j) {
-          const int vs = j % kVStages;
-          ok = castdev::mbar_wait(&v_full[vs], (j / kVStages) & 1, err);
-          for (int i = 0; i < nq && ok; ++i) {
-            ok = castdev::mbar_wait(&p_full[i], j & 1, err);
-            if (!ok) break;
-            castdev::tc_fence_after();
-            issue_pv(i, vs, j == 0);
-            if (j + 1 < n_kv) {
-              const int ks = (j + 1) % KS;
-              if (i == 0) {
-                ok = castdev::mbar_wait(&k_full[ks], ((j + 1) / KS) & 1, err);
-                if (!ok) break;
-                castdev::tc_fence_after();
-              }
-              issue_s(i, ks);
-              castdev::tc_commit(&s_full[i]);
-            }
-          }
-          castdev::tc_commit(&v_empty[vs]);
-          if (j + 1 < n_kv) castdev::tc_commit(&k_empty[(j + 1) % KS]);
-        }
-        castdev::tc_commit(o_final);
+        if (mode)
+          mma_issuer<1>(i, tmem, sbase, n_steps, q_bytes, k_off, v_off, q_full, k_full, k_empty,
+                        v_full, v_empty, s_full, p_full, pv_done, err);
+        else
+          mma_issuer<0>(i, tmem, sbase, n_steps, q_bytes, k_off, v_off, q_full, k_full, k_empty,
+                        v_full, v_empty, s_full, p_full, pv_done, err);
+        // Every MMA this thread issued completes before TMEM is released.
+        castdev::tc_commit(&mma_drain[i]);
+        castdev::mbar_wait_drain(&mma_drain[i], 0, err);
       }
     }
   } else {
-    setmaxnreg_inc();
     // ------------------------------------------------------------ softmax
     const int ti = warp >> 2;  // query tile handled by this warpgroup
     const int row = (warp & 3) * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + ti * 128;
-    const uint32_t o_addr = tmem + lane_off + 256 + ti * 128;
+    const uint32_t o_addr = tmem + lane_off + ti * 128;
+    const uint32_t s_addr = tmem + lane_off + 256 + ti * 128;
     const bool active = ti < nq;
     const int qrow_in_block = (t0 + ti) * 128 + row;
     const int qrow = qb * p.q_block + qrow_in_block;
@@ -391,61 +426,90 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float qscale = mode ? p.q_scales[row_item] : 1.0f;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
+    // QK^T scale of list entry jb in log2 units (int8: q_scale * k_scale)
+    auto block_c2 = [&](int jb) {
+      float c = p.sm_scale_log2;
+      if (mode && jb < n_blocks) {
+        const int b = blist[jb];
+        if (b >= 0 && b < p.nkb) c *= qscale * p.k_scales[(size_t)bh * p.nkb + b];
+      }
+      return c;
+    };
     if (active) {
-      for (int j = 0; j < n_kv; ++j) {
-        const int blk = blist[j / p.k_tiles];
-        const int tin = j % p.k_tiles;
+      // loop-carried position: list entry jb, 128-key tile tin inside it; the
+      // next entry's scale is loaded one entry ahead
+      int jb = 0, tin = 0;
+      float c2 = block_c2(0), c2_next = block_c2(1);
+      for (int h = 0; h < n_steps; ++h) {
+        const int j = h >> 1, half = h & 1;
+        const int blk = blist[jb];
         const bool blk_ok = blk >= 0 && blk < p.nkb;
-        const int krow = blk_ok ? blk * p.k_block + tin * 128 : 0;
-        const int valid_cols = blk_ok ? min(128, min(p.k_block - tin * 128, p.Lk - krow)) : 0;
-        const float c2 = (mode && blk_ok ? qscale * p.k_scales[(size_t)bh * p.nkb + blk] : 1.0f) *
-                         p.sm_scale_log2;
-        // Key mask of this tile: columns >= valid_cols, and key_valid == 0.
-        uint32_t kmask[4];
+        const int koff = tin * 128 + 64 * half;
+        const int krow = blk_ok ? blk * p.k_block + koff : 0;
+        const int valid_cols = blk_ok ? max(0, min(64, min(p.k_block - koff, p.Lk - krow))) : 0;
+        // Key mask of this step: columns >= valid_cols, and key_valid == 0.
+        uint32_t kmask[2];
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
+        for (int w = 0; w < 2; ++w) {
           const int lo = valid_cols - 32 * w;
           kmask[w] = lo >= 32 ? 0xffffffffu : (lo <= 0 ? 0u : ((1u << lo) - 1u));
         }
         if (p.key_valid && valid_cols > 0) {
-          const uint4 *kv4 = reinterpret_cast<const uint4 *>(p.key_valid + krow);
+          // 16-byte loads for whole chunks inside the step's valid keys, byte
+          // loads for a ragged last chunk; nothing past key valid_cols - 1.
+          const uint8_t *kv = p.key_valid + krow;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
+          for (int w = 0; w < 2; ++w) {
             uint32_t bits = 0;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint4 b = kv4[2 * w + h];
-              const uint32_t words[4] = {b.x, b.y, b.z, b.w};
+            for (int q2 = 0; q2 < 2; ++q2) {
+              const int c0 = 32 * w + 16 * q2;
+              uint32_t words[4] = {0u, 0u, 0u, 0u};
+              if (c0 + 16 <= valid_cols) {
+                const uint4 b = *reinterpret_cast<const uint4 *>(kv + c0);
+                words[0] = b.x, words[1] = b.y, words[2] = b.z, words[3] = b.w;
+              } else if (c0 < valid_cols) {
+                for (int c = c0; c < valid_cols; ++c)
+                  words[(c - c0) >> 2] |= (uint32_t)kv[c] << (8 * ((c - c0) & 3));
+              }
 #pragma unroll
               for (int q4 = 0; q4 < 4; ++q4)
 #pragma unroll
                 for (int by = 0; by < 4; ++by)
-                  if ((words[q4] >> (8 * by)) & 0xFFu) bits |= 1u << (16 * h + 4 * q4 + by);
+                  if ((words[q4] >> (8 * by)) & 0xFFu) bits |= 1u << (16 * q2 + 4 * q4 + by);
             }
             kmask[w] &= bits;
           }
         }
-        const bool full_tile = (kmask[0] & kmask[1] & kmask[2] & kmask[3]) == 0xffffffffu;
+        const bool full_step = (kmask[0] & kmask[1]) == 0xffffffffu;
 
-        ok = __all_sync(0xffffffffu, castdev::mbar_wait(&s_full[ti], j & 1, err));
+        ok = __all_sync(0xffffffffu, castdev::mbar_wait(&s_full[ti * 2 + half], j & 1, err));
         if (!ok) break;
         castdev::tc_fence_after();
-        uint32_t v[128];
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-          castdev::tmem_ld32(s_addr + 32 * w, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * w]));
+        const uint32_t sb = s_addr + 64 * half;
+        uint32_t v[64];
+        castdev::tmem_ld32(sb, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        castdev::tmem_ld32(sb + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         castdev::tmem_wait_ld();
 
-        const float m_tile = mode ? (full_tile ? row_max<true, false>(v, kmask, c2)
+        const float m_step = mode ? (full_step ? row_max<true, false>(v, kmask, c2)
                                                : row_max<true, true>(v, kmask, c2))
-                                  : (full_tile ? row_max<false, false>(v, kmask, c2)
+                                  : (full_step ? row_max<false, false>(v, kmask, c2)
                                                : row_max<false, true>(v, kmask, c2));
-        const bool need = m_tile > m_run + kRescaleLog2;
+        const bool need = m_step > m_run + kRescaleLog2;
         if (__any_sync(0xffffffffu, need)) {
-          const float m_new = fmaxf(m_run, m_tile);
+          const float m_new = fmaxf(m_run, m_step);
           const float alpha = (m_run == -INFINITY) ? (m_new == -INFINITY ? 1.0f : 0.0f)
                                                    : fast_exp2(m_run - m_new);
-          if (j > 0) {
+          if (h > 0) {
+            // O_i += P_i(h-1) V_{h-1} may still be running.  Its barrier is
+            // at most one phase behind: S_i(h), already waited for, was
+            // committed after PV_i(h-2).
+            const int hp = h - 1;
+            ok = __all_sync(0xffffffffu,
+                            castdev::mbar_wait(&pv_done[ti * 2 + (hp & 1)], (hp >> 1) & 1, err));
+            if (!ok) break;
+            castdev::tc_fence_after();
 #pragma unroll 1
             for (int cc = 0; cc < 4; ++cc) {
               uint32_t o[32];
@@ -455,29 +519,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
               castdev::tmem_st32(o_addr + 32 * cc, o);
             }
-            castdev::tmem_wait_st();
           }
           l_run *= alpha;
           m_run = m_new;
         }
         const float base = (m_run == -INFINITY) ? 0.0f : m_run;
-        const float sum = mode ? (full_tile ? row_probs<true, false>(v, kmask, c2, base)
+        const float sum = mode ? (full_step ? row_probs<true, false>(v, kmask, c2, base)
                                             : row_probs<true, true>(v, kmask, c2, base))
-                               : (full_tile ? row_probs<false, false>(v, kmask, c2, base)
+                               : (full_step ? row_probs<false, false>(v, kmask, c2, base)
                                             : row_probs<false, true>(v, kmask, c2, base));
-        castdev::tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        castdev::tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        castdev::tmem_st32(sb, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         l_run += sum;
         castdev::tmem_wait_st();
         castdev::tc_fence_before();
         __syncwarp();
-        if (lane == 0) castdev::mbar_arrive(&p_full[ti]);
+        if (lane == 0) castdev::mbar_arrive(&p_full[ti * 2 + half]);
+        if (half && ++tin == p.k_tiles) {
+          tin = 0;
+          ++jb;
+          c2 = c2_next;
+          c2_next = block_c2(jb + 1);
+        }
       }
     }
     // ------------------------------------------------------------ epilogue
     if (active && ok) {
-      if (n_kv > 0) {
-        ok = __all_sync(0xffffffffu, castdev::mbar_wait(o_final, 0, err));
+      if (n_steps > 0) {
+        // the last PV's commit covers every earlier MMA
+        const int hl = n_steps - 1;
+        ok = __all_sync(0xffffffffu,
+                        castdev::mbar_wait(&pv_done[ti * 2 + (hl & 1)], (hl >> 1) & 1, err));
         castdev::tc_fence_after();
       }
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
@@ -485,7 +556,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t o[32];
-        if (n_kv > 0 && ok) {
+        if (n_steps > 0 && ok) {
           castdev::tmem_ld32(o_addr + 32 * cc, o);
           castdev::tmem_wait_ld();
         } else {
@@ -496,11 +567,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           uint4 w[4];
           uint32_t *wp = reinterpret_cast<uint32_t *>(w);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(o[2 * c]) * inv_l,
-                                                      __uint_as_float(o[2 * c + 1]) * inv_l);
-            wp[c] = *reinterpret_cast<uint32_t *>(&h2);
-          }
+          for (int c = 0; c < 16; ++c)
+            wp[c] = pack_bf16x2(__uint_as_float(o[2 * c]) * inv_l,
+                                __uint_as_float(o[2 * c + 1]) * inv_l);
           uint4 *dst = reinterpret_cast<uint4 *>(orow + 32 * cc);
 #pragma unroll
           for (int c = 0; c < 4; ++c) dst[c] = w[c];

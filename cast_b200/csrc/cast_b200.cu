@@ -344,22 +344,12 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
 
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
-  static int attr_regs = 0;
   std::call_once(attr_once, [] {
     attr_err = cudaFuncSetAttribute(castk::rcsa_attention_kernel,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     castk::AttnSmem::alloc);
-    cudaFuncAttributes fa;
-    if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, castk::rcsa_attention_kernel);
-    if (attr_err == cudaSuccess) attr_regs = fa.numRegs;
   });
   CAST_CUDA_TRY(attr_err);
-  // The kernel moves registers between its warpgroups (setmaxnreg); the
-  // per-CTA pool it launches with must cover the split, or the increase
-  // would never be granted.
-  if (attr_regs * castk::kAttnThreads < castk::kRegPoolNeeded)
-    return fail(CAST_ERR_UNSUPPORTED, "attention kernel built with %d registers/thread; the "
-                "warpgroup register split needs %d per CTA", attr_regs, castk::kRegPoolNeeded);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   castk::rcsa_attention_kernel<<<n_items, castk::kAttnThreads, castk::AttnSmem::alloc, s>>>(
       tm_q8, tm_k8, tm_q16, tm_k16, tm_v, p);

@@ -120,6 +120,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
   }
 }
 
+// Waits for this thread's own asynchronous work (TMA copies, MMAs) tracked by
+// `bar` before the CTA releases the memory it targets.  Bounded by time only:
+// it does not give up early when another wait has failed, because the work it
+// waits for was already issued.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, int *err_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(err_flag, (int)CAST_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ---- TMA (no multicast anywhere in this library) ----
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
