@@ -259,6 +259,80 @@ __device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase,
   return true;
 }
 
+// Packed f32x2 arithmetic (two fp32 lanes per instruction).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// bf16 bits of 2^kRescaleLog2 = 256: a probability above it means the row's
+// running max is stale by more than the lazy-rescale threshold.
+constexpr uint32_t kProbLimitBf16 = 0x4380u;
+
+// Probabilities exp2(S*c2 - base) of a 64-key step in one pass: packed FFMA
+// for the exponent, MUFU exp2, packed row sums, bf16 pairs written in place
+// into v[0..31].  Also returns the largest probability (bf16 bits, both
+// halves) so the caller can tell whether `base` was still a valid max.
+template <bool kInt8, bool kMasked>
+__device__ __forceinline__ float step_probs(uint32_t (&v)[64], const uint32_t (&kmask)[2],
+                                            float c2, float base, uint32_t &pmax) {
+  const float bias = kInt8 ? fmaf(12582912.0f, c2, base) : base;
+  const uint64_t c2x2 = f2_pack(c2, c2);
+  const uint64_t nbx2 = f2_pack(-bias, -bias);
+  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+  uint32_t mx[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const uint32_t a = kInt8 ? v[2 * c] + 0x4B400000u : v[2 * c];
+    const uint32_t b = kInt8 ? v[2 * c + 1] + 0x4B400000u : v[2 * c + 1];
+    float x0, x1;
+    f2_unpack(f2_fma(f2_pack(__uint_as_float(a), __uint_as_float(b)), c2x2, nbx2), x0, x1);
+    float e0 = fast_exp2(x0);
+    float e1 = fast_exp2(x1);
+    if (kMasked) {
+      const uint32_t w = kmask[(2 * c) / 32];
+      e0 = ((w >> ((2 * c) % 32)) & 1u) ? e0 : 0.0f;
+      e1 = ((w >> ((2 * c + 1) % 32)) & 1u) ? e1 : 0.0f;
+    }
+    acc[c & 3] = f2_add(acc[c & 3], f2_pack(e0, e1));
+    const uint32_t pk = pack_bf16x2(e0, e1);
+    mx[c & 3] = bf2_max(mx[c & 3], pk);
+    v[c] = pk;
+  }
+  pmax = bf2_max(bf2_max(mx[0], mx[1]), bf2_max(mx[2], mx[3]));
+  float s0, s1, s2, s3, s4, s5, s6, s7;
+  f2_unpack(acc[0], s0, s1);
+  f2_unpack(acc[1], s2, s3);
+  f2_unpack(acc[2], s4, s5);
+  f2_unpack(acc[3], s6, s7);
+  return ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
+}
+
+template <bool kInt8>
+__device__ __forceinline__ float step_probs_any(uint32_t (&v)[64], const uint32_t (&kmask)[2],
+                                                bool full, float c2, float base, uint32_t &pmax) {
+  return full ? step_probs<kInt8, false>(v, kmask, c2, base, pmax)
+              : step_probs<kInt8, true>(v, kmask, c2, base, pmax);
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 1)
     rcsa_attention_kernel(const __grid_constant__ CUtensorMap tm_q8,
                           const __grid_constant__ CUtensorMap tm_k8,
@@ -492,16 +566,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         castdev::tmem_ld32(sb + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         castdev::tmem_wait_ld();
 
-        const float m_step = mode ? (full_step ? row_max<true, false>(v, kmask, c2)
-                                               : row_max<true, true>(v, kmask, c2))
-                                  : (full_step ? row_max<false, false>(v, kmask, c2)
-                                               : row_max<false, true>(v, kmask, c2));
-        const bool need = m_step > m_run + kRescaleLog2;
-        if (__any_sync(0xffffffffu, need)) {
-          const float m_new = fmaxf(m_run, m_step);
-          const float alpha = (m_run == -INFINITY) ? (m_new == -INFINITY ? 1.0f : 0.0f)
-                                                   : fast_exp2(m_run - m_new);
-          if (h > 0) {
+        // Fast path: exponentials against the running max in one pass.  A
+        // probability above 2^kRescaleLog2 (or no running max yet) sends the
+        // warp to the exact path: true step max, lazy update of the running
+        // max, rescale of O, exponentials again from S.
+        float sum = 0.0f;
+        bool slow = __any_sync(0xffffffffu, m_run == -INFINITY);
+        if (!slow) {
+          uint32_t pmax;
+          sum = mode ? step_probs_any<true>(v, kmask, full_step, c2, m_run, pmax)
+                     : step_probs_any<false>(v, kmask, full_step, c2, m_run, pmax);
+          slow = __any_sync(0xffffffffu, (pmax & 0xFFFFu) > kProbLimitBf16 ||
+                                             (pmax >> 16) > kProbLimitBf16);
+          if (slow) {
+            castdev::tmem_ld32(sb, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+            castdev::tmem_ld32(sb + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+            castdev::tmem_wait_ld();
+          }
+        }
+        if (slow) {
+          const float m_step = mode ? (full_step ? row_max<true, false>(v, kmask, c2)
+                                                 : row_max<true, true>(v, kmask, c2))
+                                    : (full_step ? row_max<false, false>(v, kmask, c2)
+                                                 : row_max<false, true>(v, kmask, c2));
+          float o_scale = 1.0f;
+          if (m_step > m_run + kRescaleLog2 || m_run == -INFINITY) {
+            const float m_new = fmaxf(m_run, m_step);
+            o_scale = (m_run == -INFINITY) ? (m_new == -INFINITY ? 1.0f : 0.0f)
+                                           : fast_exp2(m_run - m_new);
+            l_run *= o_scale;
+            m_run = m_new;
+          }
+          if (h > 0 && __any_sync(0xffffffffu, o_scale != 1.0f)) {
             // O_i += P_i(h-1) V_{h-1} may still be running.  Its barrier is
             // at most one phase behind: S_i(h), already waited for, was
             // committed after PV_i(h-2).
@@ -516,18 +612,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               castdev::tmem_ld32(o_addr + 32 * cc, o);
               castdev::tmem_wait_ld();
 #pragma unroll
-              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * o_scale);
               castdev::tmem_st32(o_addr + 32 * cc, o);
             }
           }
-          l_run *= alpha;
-          m_run = m_new;
+          uint32_t pmax_unused;
+          const float base = (m_run == -INFINITY) ? 0.0f : m_run;
+          sum = mode ? step_probs_any<true>(v, kmask, full_step, c2, base, pmax_unused)
+                     : step_probs_any<false>(v, kmask, full_step, c2, base, pmax_unused);
         }
-        const float base = (m_run == -INFINITY) ? 0.0f : m_run;
-        const float sum = mode ? (full_step ? row_probs<true, false>(v, kmask, c2, base)
-                                            : row_probs<true, true>(v, kmask, c2, base))
-                               : (full_step ? row_probs<false, false>(v, kmask, c2, base)
-                                            : row_probs<false, true>(v, kmask, c2, base));
         castdev::tmem_st32(sb, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         l_run += sum;
         castdev::tmem_wait_st();
