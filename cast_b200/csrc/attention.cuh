@@ -36,6 +36,7 @@
 #pragma once
 
 #include <climits>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -500,27 +501,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float qscale = mode ? p.q_scales[row_item] : 1.0f;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
-    // QK^T scale of list entry jb in log2 units (int8: q_scale * k_scale)
-    auto block_c2 = [&](int jb) {
-      float c = p.sm_scale_log2;
-      if (mode && jb < n_blocks) {
-        const int b = blist[jb];
-        if (b >= 0 && b < p.nkb) c *= qscale * p.k_scales[(size_t)bh * p.nkb + b];
-      }
-      return c;
-    };
-    if (active) {
-      // loop-carried position: list entry jb, 128-key tile tin inside it; the
-      // next entry's scale is loaded one entry ahead
-      int jb = 0, tin = 0;
-      float c2 = block_c2(0), c2_next = block_c2(1);
+    // The step loop, compiled once per QK^T precision so each copy holds only
+    // its own code.
+    auto run_steps = [&](auto int8_tag) {
+      constexpr bool kInt8 = decltype(int8_tag)::value;
+      // Per list entry: first key row, keys inside the block (clipped to Lk)
+      // and the QK^T scale in log2 units (int8: q_scale * k_scale); the next
+      // entry's values are fetched one entry ahead.
+      struct Entry {
+        int krow0, nvalid;
+        float c2;
+      };
+      auto fetch = [&](int jb) {
+        Entry e{0, 0, p.sm_scale_log2};
+        if (jb < n_blocks) {
+          const int blk = blist[jb];
+          if (blk >= 0 && blk < p.nkb) {
+            e.krow0 = blk * p.k_block;
+            e.nvalid = min(p.k_block, p.Lk - e.krow0);
+            if (kInt8) e.c2 *= qscale * p.k_scales[(size_t)bh * p.nkb + blk];
+          }
+        }
+        return e;
+      };
+      Entry cur = fetch(0), nxt = fetch(1);
+      const int block_keys = p.k_tiles * 128;
+      int jb = 0, koff = 0;  // list entry, key offset of this step inside it
       for (int h = 0; h < n_steps; ++h) {
-        const int j = h >> 1, half = h & 1;
-        const int blk = blist[jb];
-        const bool blk_ok = blk >= 0 && blk < p.nkb;
-        const int koff = tin * 128 + 64 * half;
-        const int krow = blk_ok ? blk * p.k_block + koff : 0;
-        const int valid_cols = blk_ok ? max(0, min(64, min(p.k_block - koff, p.Lk - krow))) : 0;
+        const int half = h & 1;
+        const float c2 = cur.c2;
+        const int valid_cols = max(0, min(64, cur.nvalid - koff));
+        const int krow = cur.krow0 + koff;
         // Key mask of this step: columns >= valid_cols, and key_valid == 0.
         uint32_t kmask[2];
 #pragma unroll
@@ -557,7 +568,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const bool full_step = (kmask[0] & kmask[1]) == 0xffffffffu;
 
-        ok = __all_sync(0xffffffffu, castdev::mbar_wait(&s_full[ti * 2 + half], j & 1, err));
+        ok = __all_sync(0xffffffffu, castdev::mbar_wait(&s_full[ti * 2 + half], (h >> 1) & 1, err));
         if (!ok) break;
         castdev::tc_fence_after();
         const uint32_t sb = s_addr + 64 * half;
@@ -574,8 +585,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         bool slow = __any_sync(0xffffffffu, m_run == -INFINITY);
         if (!slow) {
           uint32_t pmax;
-          sum = mode ? step_probs_any<true>(v, kmask, full_step, c2, m_run, pmax)
-                     : step_probs_any<false>(v, kmask, full_step, c2, m_run, pmax);
+          sum = step_probs_any<kInt8>(v, kmask, full_step, c2, m_run, pmax);
           slow = __any_sync(0xffffffffu, (pmax & 0xFFFFu) > kProbLimitBf16 ||
                                              (pmax >> 16) > kProbLimitBf16);
           if (slow) {
@@ -584,11 +594,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             castdev::tmem_wait_ld();
           }
         }
-        if (slow) {
-          const float m_step = mode ? (full_step ? row_max<true, false>(v, kmask, c2)
-                                                 : row_max<true, true>(v, kmask, c2))
-                                    : (full_step ? row_max<false, false>(v, kmask, c2)
-                                                 : row_max<false, true>(v, kmask, c2));
+        if (__builtin_expect(slow, 0)) {
+          const float m_step = full_step ? row_max<kInt8, false>(v, kmask, c2)
+                                         : row_max<kInt8, true>(v, kmask, c2);
           float o_scale = 1.0f;
           if (m_step > m_run + kRescaleLog2 || m_run == -INFINITY) {
             const float m_new = fmaxf(m_run, m_step);
@@ -618,8 +626,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           uint32_t pmax_unused;
           const float base = (m_run == -INFINITY) ? 0.0f : m_run;
-          sum = mode ? step_probs_any<true>(v, kmask, full_step, c2, base, pmax_unused)
-                     : step_probs_any<false>(v, kmask, full_step, c2, base, pmax_unused);
+          sum = step_probs_any<kInt8>(v, kmask, full_step, c2, base, pmax_unused);
         }
         castdev::tmem_st32(sb, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         l_run += sum;
@@ -627,13 +634,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         castdev::tc_fence_before();
         __syncwarp();
         if (lane == 0) castdev::mbar_arrive(&p_full[ti * 2 + half]);
-        if (half && ++tin == p.k_tiles) {
-          tin = 0;
+          koff += 64;
+        if (koff == block_keys) {
+          koff = 0;
           ++jb;
-          c2 = c2_next;
-          c2_next = block_c2(jb + 1);
+          cur = nxt;
+          nxt = fetch(jb + 1);
         }
       }
+    };
+    if (active) {
+      if (mode)
+        run_steps(std::integral_constant<bool, true>{});
+      else
+        run_steps(std::integral_constant<bool, false>{});
     }
     // ------------------------------------------------------------ epilogue
     if (active && ok) {
