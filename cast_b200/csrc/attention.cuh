@@ -279,27 +279,23 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-// bf16 bits of 2^kRescaleLog2 = 256: a probability above it means the row's
-// running max is stale by more than the lazy-rescale threshold.
-constexpr uint32_t kProbLimitBf16 = 0x4380u;
+// The fast path accepts a step whose probabilities (against a running max
+// that may be stale) sum to at most 2^kFastSumLog2: each is then at most
+// 2^16, far from overflow in bf16 and in the fp32 sums and accumulators, and
+// the final normalisation does not depend on the scale.  A larger sum (or
+// inf) sends the warp to the exact path.
+constexpr float kFastSumLimit = 65536.0f;
 
 // Probabilities exp2(S*c2 - base) of a 64-key step in one pass: packed FFMA
 // for the exponent, MUFU exp2, packed row sums, bf16 pairs written in place
-// into v[0..31].  Also returns the largest probability (bf16 bits, both
-// halves) so the caller can tell whether `base` was still a valid max.
+// into v[0..31].  Returns their sum.
 template <bool kInt8, bool kMasked>
 __device__ __forceinline__ float step_probs(uint32_t (&v)[64], const uint32_t (&kmask)[2],
-                                            float c2, float base, uint32_t &pmax) {
+                                            float c2, float base) {
   const float bias = kInt8 ? fmaf(12582912.0f, c2, base) : base;
   const uint64_t c2x2 = f2_pack(c2, c2);
   const uint64_t nbx2 = f2_pack(-bias, -bias);
   uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-  uint32_t mx[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
     const uint32_t a = kInt8 ? v[2 * c] + 0x4B400000u : v[2 * c];
@@ -314,11 +310,8 @@ __device__ __forceinline__ float step_probs(uint32_t (&v)[64], const uint32_t (&
       e1 = ((w >> ((2 * c + 1) % 32)) & 1u) ? e1 : 0.0f;
     }
     acc[c & 3] = f2_add(acc[c & 3], f2_pack(e0, e1));
-    const uint32_t pk = pack_bf16x2(e0, e1);
-    mx[c & 3] = bf2_max(mx[c & 3], pk);
-    v[c] = pk;
+    v[c] = pack_bf16x2(e0, e1);
   }
-  pmax = bf2_max(bf2_max(mx[0], mx[1]), bf2_max(mx[2], mx[3]));
   float s0, s1, s2, s3, s4, s5, s6, s7;
   f2_unpack(acc[0], s0, s1);
   f2_unpack(acc[1], s2, s3);
@@ -329,9 +322,9 @@ __device__ __forceinline__ float step_probs(uint32_t (&v)[64], const uint32_t (&
 
 template <bool kInt8>
 __device__ __forceinline__ float step_probs_any(uint32_t (&v)[64], const uint32_t (&kmask)[2],
-                                                bool full, float c2, float base, uint32_t &pmax) {
-  return full ? step_probs<kInt8, false>(v, kmask, c2, base, pmax)
-              : step_probs<kInt8, true>(v, kmask, c2, base, pmax);
+                                                bool full, float c2, float base) {
+  return full ? step_probs<kInt8, false>(v, kmask, c2, base)
+              : step_probs<kInt8, true>(v, kmask, c2, base);
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -578,16 +571,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         castdev::tmem_wait_ld();
 
         // Fast path: exponentials against the running max in one pass.  A
-        // probability above 2^kRescaleLog2 (or no running max yet) sends the
-        // warp to the exact path: true step max, lazy update of the running
-        // max, rescale of O, exponentials again from S.
+        // step sum above kFastSumLimit (or no running max yet) sends the warp
+        // to the exact path: true step max, lazy update of the running max,
+        // rescale of O, exponentials again from S.
         float sum = 0.0f;
         bool slow = __any_sync(0xffffffffu, m_run == -INFINITY);
         if (!slow) {
-          uint32_t pmax;
-          sum = step_probs_any<kInt8>(v, kmask, full_step, c2, m_run, pmax);
-          slow = __any_sync(0xffffffffu, (pmax & 0xFFFFu) > kProbLimitBf16 ||
-                                             (pmax >> 16) > kProbLimitBf16);
+          sum = step_probs_any<kInt8>(v, kmask, full_step, c2, m_run);
+          slow = __any_sync(0xffffffffu, !(sum <= kFastSumLimit));
           if (slow) {
             castdev::tmem_ld32(sb, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
             castdev::tmem_ld32(sb + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
@@ -624,9 +615,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               castdev::tmem_st32(o_addr + 32 * cc, o);
             }
           }
-          uint32_t pmax_unused;
           const float base = (m_run == -INFINITY) ? 0.0f : m_run;
-          sum = step_probs_any<kInt8>(v, kmask, full_step, c2, base, pmax_unused);
+          sum = step_probs_any<kInt8>(v, kmask, full_step, c2, base);
         }
         castdev::tmem_st32(sb, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         l_run += sum;
