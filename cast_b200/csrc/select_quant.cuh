@@ -53,6 +53,53 @@ __device__ __forceinline__ int quant_code(float x, float s, float inv_s) {
   return max(-127, min(127, c));
 }
 
+// Packed f32x2 helpers (two fp32 lanes per instruction, IEEE round-to-nearest).
+__device__ __forceinline__ uint64_t q2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t q2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t q2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t q2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Codes of 8 values as 8 bytes, equal to quant_code() for every input of a
+// block with amax >= 2^-90:  q0 = RN(x * inv), r = x - q0*s (exact, FMA),
+// q1 = RN(q0 + r*inv) is the correctly rounded x/s (Markstein's correction
+// step with inv = RN(1/s)); rint(q1) comes from the 1.5*2^23 shift, whose low
+// byte is the code (|x| <= amax keeps |code| <= 127, so nothing is clamped).
+// Checked against IEEE division for every bf16 amax and every bf16 x with
+// |x| <= amax (tests/quant_fastpath_exhaustive.c); blocks with amax < 2^-90,
+// where the residual could be subnormal, use quant_code().
+__device__ __forceinline__ uint2 quant8_fast(const float (&f)[8], uint64_t invx2, uint64_t negsx2) {
+  const uint64_t magic = q2_pack(12582912.0f, 12582912.0f);
+  uint32_t t[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t x = q2_pack(f[2 * i], f[2 * i + 1]);
+    const uint64_t q0 = q2_mul(x, invx2);
+    const uint64_t r = q2_fma(q0, negsx2, x);
+    const uint64_t tt = q2_add(q2_fma(r, invx2, q0), magic);
+    t[2 * i] = (uint32_t)tt;
+    t[2 * i + 1] = (uint32_t)(tt >> 32);
+  }
+  const uint32_t lo = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
+  const uint32_t hi = __byte_perm(__byte_perm(t[4], t[5], 0x0040), __byte_perm(t[6], t[7], 0x0040), 0x5410);
+  return make_uint2(lo, hi);
+}
+
 __device__ __forceinline__ float quant_scale_of(float amax) {
   return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
 }
@@ -74,7 +121,7 @@ __device__ __forceinline__ double warp_dot(const double *a, const double *b, int
 // Threads: 16 row slots x D/8 column groups (8 bf16 = 16 bytes each).
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(kSumLanes *(D / 8))
+__global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
     pool_quant_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                       const __nv_bfloat16 *__restrict__ v, int Lq, int Lk, int block, int nqb,
                       int nkb, int8_t *q_codes, float *q_scales, int8_t *k_codes,
@@ -87,6 +134,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8))
   __shared__ float wmax[kThreads / 32];
   __shared__ float wsq[kThreads / 32];
   __shared__ float s_scale;
+  __shared__ float s_amax;
   __shared__ double s_denom;
 
   const int tid = threadIdx.x;
@@ -172,6 +220,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8))
     }
     const float sc = quant_scale_of(m);
     s_scale = sc;
+    s_amax = m;
     if (scales) scales[(size_t)bh * nb + blk] = sc;
     if (block_rms && pool) {
       const int row0 = which == 0 ? 0 : nqb;
@@ -208,10 +257,13 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8))
   if (codes) {
     const float sc = s_scale;
     const float inv = __frcp_rn(sc);
+    const bool fast = s_amax >= 0x1p-90f;  // block-uniform
+    const uint64_t invx2 = q2_pack(inv, inv), negsx2 = q2_pack(-sc, -sc);
     int8_t *cbase = codes + ((size_t)bh * L + b0) * D + grp * 8;
     auto quant8 = [&](const uint4 &raw) {
       float f[8];
       bf16x8_to_f32(raw, f);
+      if (fast) return quant8_fast(f, invx2, negsx2);
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) lo |= (uint32_t)(quant_code(f[i], sc, inv) & 0xFF) << (8 * i);
@@ -341,7 +393,7 @@ __global__ void __launch_bounds__(128)
 // grid = (nblocks, B*H).
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(kSumLanes *(D / 8))
+__global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
     pool_grid_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                      int T, int Hl, int Wl, int tt, int th, int tw, int nh, int nw, int nblocks,
                      double *pooled /*[BH, 2, nblocks, D]*/) {

@@ -5,6 +5,7 @@ import json
 import os
 
 import numpy as np
+import pytest
 import torch
 
 from cast_b200 import workloads
@@ -126,3 +127,20 @@ def test_par_known_answer_identities():
     exp = (1 - a) * left * np.exp(1j * a * theta)[:, None] + a * right * np.exp(-1j * (1 - a) * theta)[:, None]
     np.testing.assert_allclose(m1, exp, atol=1e-12)
     assert opar.ola_normalization(22, 40, opar.overlap_window()).min() > 1e-8
+
+
+def test_fast_quantiser_matches_ieee_division_exhaustively(tmp_path):
+    """The kernel's division-free quantiser (Markstein-corrected quotient)
+    gives the defined code for every bf16 amax and bf16 |x| <= amax."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = os.path.join(os.path.dirname(__file__), "quant_fastpath_exhaustive.c")
+    exe = str(tmp_path / "quant_fastpath_exhaustive")
+    subprocess.run([cc, "-O2", "-ffp-contract=off", "-o", exe, src, "-lm"], check=True)
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "mismatches 0" in res.stdout and "out of range 0" in res.stdout
