@@ -4,8 +4,9 @@
 //
 // Fixed arithmetic order (mirrored by the CPU oracle so that indices and
 // codes compare bit-exactly):
-//   * block sums in float64, row r of a block accumulated into partial
-//     r % kSumLanes in increasing r, partials added in order 0..15;
+//   * block sums: row r of a block accumulated into partial r % kSumLanes in
+//     increasing r in float32 (IEEE adds from 0), partials widened to float64
+//     and added in order 0..15;
 //   * ||mean||^2 and every pooled dot product: lane l (of 32) sums the
 //     products of dims d = l, l+32, ... in increasing d (multiply and add
 //     rounded separately), then an xor-butterfly over 16, 8, 4, 2, 1;
@@ -129,7 +130,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
                       float *block_rms) {
   constexpr int kGroups = D / 8;
   constexpr int kThreads = kSumLanes * kGroups;
-  __shared__ double red[kSumLanes][D];
+  __shared__ float red[kSumLanes][D];
   __shared__ double mean_s[D];
   __shared__ float wmax[kThreads / 32];
   __shared__ float wsq[kThreads / 32];
@@ -162,9 +163,9 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   const int rows = min(block, L - b0);
   const __nv_bfloat16 *base = X + ((size_t)bh * L + b0) * D + grp * 8;
 
-  double acc[8];
+  float acc[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.0;
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
   float amax = 0.0f, sq = 0.0f;
   const bool pool = which != 2;
 
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
       bf16x8_to_f32(raw[u], f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        if (pool) acc[i] = __dadd_rn(acc[i], (double)f[i]);
+        if (pool) acc[i] = __fadd_rn(acc[i], f[i]);
         amax = fmaxf(amax, fabsf(f[i]));
         sq = fmaf(f[i], f[i], sq);
       }
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
     bf16x8_to_f32(ldg_nc_v4(base + (size_t)r * D), f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      if (pool) acc[i] = __dadd_rn(acc[i], (double)f[i]);
+      if (pool) acc[i] = __fadd_rn(acc[i], f[i]);
       amax = fmaxf(amax, fabsf(f[i]));
       sq = fmaf(f[i], f[i], sq);
     }
@@ -230,9 +231,9 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   }
   if (pool) {
     if (tid < D) {
-      double t = red[0][tid];
+      double t = (double)red[0][tid];
 #pragma unroll
-      for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, red[p][tid]);
+      for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, (double)red[p][tid]);
       mean_s[tid] = __ddiv_rn(t, (double)max(rows, 1));
     }
     __syncthreads();
@@ -398,7 +399,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
                      int T, int Hl, int Wl, int tt, int th, int tw, int nh, int nw, int nblocks,
                      double *pooled /*[BH, 2, nblocks, D]*/) {
   constexpr int kGroups = D / 8;
-  __shared__ double red[kSumLanes][D];
+  __shared__ float red[kSumLanes][D];
   __shared__ double mean_s[D];
   __shared__ double s_denom;
   const int tid = threadIdx.x, grp = tid % kGroups, slot = tid / kGroups;
@@ -409,9 +410,9 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   const int L = T * Hl * Wl;
   const int bt = blk / (nh * nw), bhh = (blk / nw) % nh, bw = blk % nw;
   const int S = tt * th * tw;
-  double acc[8];
+  float acc[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.0;
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
   for (int r = slot; r < S; r += kSumLanes) {
     const int it = r / (th * tw), ih = (r / tw) % th, iw = r % tw;
     const int t = bt * tt + it, h = bhh * th + ih, w = bw * tw + iw;
@@ -419,16 +420,16 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
       float f[8];
       bf16x8_to_f32(ldg_nc_v4(X + ((size_t)bh * L + ((size_t)t * Hl + h) * Wl + w) * D + grp * 8), f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __dadd_rn(acc[i], (double)f[i]);
+      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], f[i]);
     }
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) red[slot][grp * 8 + i] = acc[i];
   __syncthreads();
   if (tid < D) {
-    double t = red[0][tid];
+    double t = (double)red[0][tid];
 #pragma unroll
-    for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, red[p][tid]);
+    for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, (double)red[p][tid]);
     mean_s[tid] = __ddiv_rn(t, (double)S);
   }
   __syncthreads();

@@ -6,10 +6,10 @@ never imported by the product package.
 Arithmetic contract shared with the CUDA kernels (so that block indices and
 int8 codes can be compared bit-exactly):
 
-* Block sums are accumulated in float64 over the block's rows in block-linear
-  order, interleaved over ``SUM_LANES`` partial sums (row ``r`` goes to
-  partial ``r % SUM_LANES``), and the partials are then added in order
-  ``0..SUM_LANES-1``.  Every addition is a correctly rounded IEEE float64 add.
+* Block sums: row ``r`` of a block goes to partial ``r % SUM_LANES``; each
+  partial accumulates its rows in increasing order in float32 (correctly
+  rounded IEEE float32 adds, starting from 0), then the partials are widened
+  to float64 and added in order ``0..SUM_LANES-1`` (IEEE float64 adds).
 * Pooled vectors follow ``F.normalize(mean, dim=-1)``
   (``proposed/qk_uncertainty_tangent_attention.py:1021-1022``):
   ``mean = sum / count``; ``ss = lane_tree_sum(mean*mean)``;
@@ -94,7 +94,8 @@ def grid_block_index(
 
 
 def block_sums(x: np.ndarray, index: np.ndarray, valid: np.ndarray | None = None):
-    """Float64 per-block sums with the interleaved fixed order.
+    """Per-block sums with the interleaved fixed order (float32 partials,
+    float64 combination; see the module docstring).
 
     ``x``: ``[..., L, D]`` float32 holding bf16-representable values.
     ``index``: ``[NB, S]`` token index per row (-1 = padding).
@@ -105,22 +106,23 @@ def block_sums(x: np.ndarray, index: np.ndarray, valid: np.ndarray | None = None
     lead = x.shape[:-2]
     nb, s = index.shape
     d = x.shape[-1]
-    x64 = x.astype(np.float64)
+    x32 = x.astype(np.float32)
     rows = -(-s // SUM_LANES) * SUM_LANES
-    gathered = np.zeros(lead + (nb, rows, d), dtype=np.float64)
+    gathered = np.zeros(lead + (nb, rows, d), dtype=np.float32)
     ok = index >= 0
     if valid is not None:
         ok = ok & np.where(index >= 0, valid[np.clip(index, 0, None)], False)
     safe = np.clip(index, 0, None)
-    g = x64[..., safe.reshape(-1), :].reshape(lead + (nb, s, d))
-    g = np.where(ok[..., None], g, 0.0)
+    g = x32[..., safe.reshape(-1), :].reshape(lead + (nb, s, d))
+    g = np.where(ok[..., None], g, np.float32(0.0))
     gathered[..., :s, :] = g
-    partial = np.zeros(lead + (nb, SUM_LANES, d), dtype=np.float64)
+    partial = np.zeros(lead + (nb, SUM_LANES, d), dtype=np.float32)
     for step in range(rows // SUM_LANES):
         partial = partial + gathered[..., step * SUM_LANES:(step + 1) * SUM_LANES, :]
-    total = partial[..., 0, :].copy()
+    wide = partial.astype(np.float64)
+    total = wide[..., 0, :].copy()
     for p in range(1, SUM_LANES):
-        total = total + partial[..., p, :]
+        total = total + wide[..., p, :]
     count = ok.sum(axis=1)
     return total, count
 

@@ -59,7 +59,10 @@ def _errs(out, ref):
     return float(d.max()), float(d.mean())
 
 
-@pytest.mark.parametrize("block,nq,nh,budget", [(128, 2, 6, 3), (880, 2, 5, 2), (64, 2, 8, 4)])
+# 1040-row blocks leave rows for the loop after the 8-deep unrolled loads
+# (16 row partials x 8 rows per step)
+@pytest.mark.parametrize("block,nq,nh,budget", [(128, 2, 6, 3), (880, 2, 5, 2), (64, 2, 8, 4),
+                                                (1040, 2, 4, 2)])
 def test_select_quant_bitexact(cuda, block, nq, nh, budget):
     q, k, v = _rand_problem(2, nq, nh, block, seed=block)
     sel = rcsa.select_quant(q.cuda(), k.cuda(), block_size=block, budget=budget, policy="int8")
