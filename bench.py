@@ -39,7 +39,7 @@ HIST, CUR = 32, 4
 # DRAM bytes (read + write) of one attention launch on the full config-2
 # workload, from the ncu launch list in profiles/launches_rcsa_config2_auto.md
 # (auto policy); other policies have no capture.
-ATTN_TRAFFIC_BYTES = {"auto": 701.3e6}
+ATTN_TRAFFIC_BYTES = {"auto": 696.0e6}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
