@@ -60,8 +60,8 @@ constexpr float kRescaleLog2 = 8.0f;
 struct AttnSmem {
   static constexpr int bars = 229376;  // 224 KB: past the largest layout
   // barriers: q_full, k_full[4], k_empty[4], v_full[3], v_empty[3],
-  //           s_full[2][2], p_full[2][2], pv_done[2][2], mma_drain[2]
-  static constexpr int n_bars = 1 + 2 * kMaxKStages + 2 * kVStages + 4 + 4 + 4 + 2;
+  //           s_full[2][2], p_full[2][2], pv_done[2][2], mma_drain[2], merge
+  static constexpr int n_bars = 1 + 2 * kMaxKStages + 2 * kVStages + 4 + 4 + 4 + 2 + 1;
   static constexpr int tmem_slot = bars + 8 * n_bars;
   static constexpr int blist = (tmem_slot + 16 + 15) / 16 * 16;
   static constexpr int total = blist + 4 * kMaxBlockList;
@@ -177,6 +177,24 @@ __device__ __forceinline__ DescW desc_words(uint32_t addr, uint32_t lbo) {
   return DescW{(uint32_t)d, (uint32_t)(d >> 32)};
 }
 
+// Position in the shared K/V ring of an issuer's (or softmax warpgroup's)
+// t-th 128-key tile.  Pair items (two query tiles, one key list): both tiles
+// read every ring tile, position t.  Split items (one query tile whose key
+// tiles are split between the two warpgroups, A = the first n_a, B = the
+// last n_b, n_a - n_b in {0, 1}): ring order A0 B0 A1 B1 ... then the rest of
+// A, so warpgroup i's t-th tile sits at 2t + i while t < n_b, and A's tail at
+// n_b + t.
+struct RingMap {
+  int split, i, n_a, n_b;
+  __device__ __forceinline__ int pos(int t) const {
+    return !split ? t : (t < n_b ? 2 * t + i : n_b + t);
+  }
+  // key tile (index into the item's concatenated key list) at ring position r
+  __device__ __forceinline__ int key_tile(int r) const {
+    return !split ? r : (r < 2 * n_b ? ((r & 1) ? n_a + (r >> 1) : (r >> 1)) : r - n_b);
+  }
+};
+
 // The MMA issuer of query tile i (one thread per tile).  Per 64-key step h:
 //   wait P_i(h); O_i += P_i(h) V_h; commit pv_done; then S_i(h+2) into the S
 //   buffer P_i(h) came from (issued after the PV that reads it); commit
@@ -184,8 +202,9 @@ __device__ __forceinline__ DescW desc_words(uint32_t addr, uint32_t lbo) {
 //   their "empty" barriers count one arrival per active tile.
 // Returns false if a wait gave up.
 template <int kInt8>
-__device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase, int n_steps,
-                                           int q_bytes, int k_off, int v_off, uint64_t *q_full,
+__device__ __forceinline__ bool mma_issuer(int i, RingMap ring, uint32_t tmem, uint32_t sbase,
+                                           int n_steps, int q_bytes, int k_off, int v_off,
+                                           uint64_t *q_full,
                                            uint64_t *k_full, uint64_t *k_empty, uint64_t *v_full,
                                            uint64_t *v_empty, uint64_t *s_full, uint64_t *p_full,
                                            uint64_t *pv_done, int *err) {
@@ -194,7 +213,7 @@ __device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase,
   constexpr uint32_t idesc_s = kInt8 ? castdev::make_idesc(2, 1, 1, 0, 0, 128, 64)
                                      : castdev::make_idesc(1, 1, 1, 0, 0, 128, 64);
   constexpr uint32_t idesc_pv = castdev::make_idesc(1, 1, 1, 0, 1, 128, 128);
-  const DescW qd = desc_words(sbase + i * q_bytes, 16);
+  const DescW qd = desc_words(sbase + (ring.split ? 0 : i * q_bytes), 16);
   const DescW kd = desc_words(sbase + k_off, 16);     // + stage * kKBytes + half * 8192
   const DescW vd = desc_words(sbase + v_off, 16384);  // + stage * 32768 + half * 8192
   const uint32_t o_col = tmem + i * 128;
@@ -205,7 +224,7 @@ __device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase,
 
   auto issue_s = [&](int h) {
     const uint32_t d = s_col + (h & 1) * 64;
-    const uint32_t ko = ((h >> 1) & (KS - 1)) * kKBytes + (h & 1) * 8192;
+    const uint32_t ko = (ring.pos(h >> 1) & (KS - 1)) * kKBytes + (h & 1) * 8192;
     if (kInt8) {
 #pragma unroll
       for (int s = 0; s < 4; ++s)
@@ -219,21 +238,23 @@ __device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase,
     }
   };
 
-  if (!castdev::mbar_wait(q_full, 0, err) || !castdev::mbar_wait(&k_full[0], 0, err))
+  const int r0 = ring.pos(0);
+  if (!castdev::mbar_wait(q_full, 0, err) ||
+      !castdev::mbar_wait(&k_full[r0 & (KS - 1)], (r0 / KS) & 1, err))
     return false;
   castdev::tc_fence_after();
   issue_s(0);
   castdev::tc_commit(&my_s_full[0]);
   issue_s(1);
   castdev::tc_commit(&my_s_full[1]);
-  castdev::tc_commit(&k_empty[0]);
+  castdev::tc_commit(&k_empty[r0 & (KS - 1)]);
 
-  int vs = 0;
-  uint32_t vphase = 0;
   for (int h = 0; h < n_steps; ++h) {
     const int half = h & 1;
     const int hn = h + 2;
-    if (!half && !castdev::mbar_wait(&v_full[vs], vphase, err)) return false;
+    const int rv = ring.pos(h >> 1);  // ring position of this step's V tile
+    const int vs = rv % kVStages;
+    if (!half && !castdev::mbar_wait(&v_full[vs], (rv / kVStages) & 1, err)) return false;
     if (!castdev::mbar_wait(&my_p_full[half], (h >> 1) & 1, err)) return false;
     castdev::tc_fence_after();
     const uint32_t vo = vs * 32768 + half * 8192;
@@ -244,8 +265,8 @@ __device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase,
     castdev::tc_commit(&my_pv_done[half]);
     if (hn < n_steps) {
       if (!half) {
-        const int t = hn >> 1;
-        if (!castdev::mbar_wait(&k_full[t & (KS - 1)], (t / KS) & 1, err)) return false;
+        const int rk = ring.pos(hn >> 1);
+        if (!castdev::mbar_wait(&k_full[rk & (KS - 1)], (rk / KS) & 1, err)) return false;
         castdev::tc_fence_after();
       }
       issue_s(hn);
@@ -253,8 +274,7 @@ __device__ __forceinline__ bool mma_issuer(int i, uint32_t tmem, uint32_t sbase,
     }
     if (half) {
       castdev::tc_commit(&v_empty[vs]);
-      if (++vs == kVStages) vs = 0, vphase ^= 1u;
-      if (hn < n_steps) castdev::tc_commit(&k_empty[(hn >> 1) & (KS - 1)]);
+      if (hn < n_steps) castdev::tc_commit(&k_empty[ring.pos(hn >> 1) & (KS - 1)]);
     }
   }
   return true;
@@ -346,6 +366,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t *p_full = s_full + 4;          // [tile * 2 + buffer]
   uint64_t *pv_done = p_full + 4;         // [tile * 2 + buffer]
   uint64_t *mma_drain = pv_done + 4;
+  uint64_t *merge_bar = mma_drain + 2;  // split items: warpgroup 1's partial result is ready
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + AttnSmem::tmem_slot);
   int32_t *blist = reinterpret_cast<int32_t *>(smem + AttnSmem::blist);
   int *err = &g_cast_device_error;
@@ -373,7 +394,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int row_item = bh * p.nqb + qb;
   const int n_blocks = min(max(p.counts[row_item], 0), min(p.max_degree, kMaxBlockList));
   const int n_kv = n_blocks * p.k_tiles;  // 128-key tiles
-  const int n_steps = 2 * n_kv;           // 64-key steps
+  // A single query tile (the last of an odd tile count) splits its key tiles
+  // between the two warpgroups (split item), whose partial results are merged
+  // at the end; a pair gives each warpgroup its own query tile.
+  const bool split = nq == 1 && n_kv >= 2;
+  const int n_a = split ? (n_kv + 1) / 2 : n_kv;  // key tiles of warpgroup / issuer 0
+  const int n_b = split ? n_kv - n_a : n_kv;      // key tiles of warpgroup / issuer 1
+  const int n_groups = split ? 2 : nq;            // active warpgroups and issuers
+  const RingMap ring0{split ? 1 : 0, 0, n_a, n_b};
   const int mode = p.qk_mode ? (int)p.qk_mode[row_item] : p.default_mode;  // 1 = int8
 
   // mode-dependent layout
@@ -387,9 +415,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < AttnSmem::n_bars; ++i) castdev::mbar_init(&bar[i], 1);
     for (int i = 0; i < 4; ++i) castdev::mbar_init(&p_full[i], 4);
-    // a K or V stage is free once every active tile's MMAs have read it
-    for (int i = 0; i < kMaxKStages; ++i) castdev::mbar_init(&k_empty[i], nq);
-    for (int i = 0; i < kVStages; ++i) castdev::mbar_init(&v_empty[i], nq);
+    castdev::mbar_init(merge_bar, 4);
+    // a K or V stage is free once every issuer reading it has done so (both
+    // for a pair, the one owning that ring tile for a split item)
+    for (int i = 0; i < kMaxKStages; ++i) castdev::mbar_init(&k_empty[i], split ? 1 : nq);
+    for (int i = 0; i < kVStages; ++i) castdev::mbar_init(&v_empty[i], split ? 1 : nq);
     castdev::fence_barrier_init();
   }
   if (warp == kMmaWarp) {
@@ -423,9 +453,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         int issued = 0;
-        for (int j = 0; j < n_kv; ++j) {
-          const int blk = blist[j / p.k_tiles];
-          const int tin = j % p.k_tiles;
+        for (int j = 0; j < n_kv; ++j) {  // ring position j
+          const int kt = ring0.key_tile(j);
+          const int blk = blist[kt / p.k_tiles];
+          const int tin = kt % p.k_tiles;
           const int krow = (blk >= 0 && blk < p.nkb) ? blk * p.k_block + tin * 128 : 0;
           const int ks = j % KS;
           if (j >= KS && !castdev::mbar_wait(&k_empty[ks], ((j / KS) - 1) & 1, err)) break;
@@ -448,9 +479,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // ---------------------------------------------------- V producer
       if (lane == 0 && n_kv > 0) {
         int issued = 0;
-        for (int j = 0; j < n_kv; ++j) {
-          const int blk = blist[j / p.k_tiles];
-          const int tin = j % p.k_tiles;
+        for (int j = 0; j < n_kv; ++j) {  // ring position j
+          const int kt = ring0.key_tile(j);
+          const int blk = blist[kt / p.k_tiles];
+          const int tin = kt % p.k_tiles;
           const int krow = (blk >= 0 && blk < p.nkb) ? blk * p.k_block + tin * 128 : 0;
           const int vs = j % kVStages;
           if (j >= kVStages && !castdev::mbar_wait(&v_empty[vs], ((j / kVStages) - 1) & 1, err))
@@ -467,14 +499,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else {
       // ---------------------------------------------------- MMA issuers
       const int i = warp == kMmaWarp ? 0 : 1;
-      if (lane == 0 && n_kv > 0 && i < nq) {
+      if (lane == 0 && n_kv > 0 && i < n_groups) {
         const uint32_t sbase = castdev::smem_u32(smem);
+        const RingMap ring{split ? 1 : 0, i, n_a, n_b};
+        const int steps = 2 * (i == 0 ? n_a : n_b);
         if (mode)
-          mma_issuer<1>(i, tmem, sbase, n_steps, q_bytes, k_off, v_off, q_full, k_full, k_empty,
-                        v_full, v_empty, s_full, p_full, pv_done, err);
+          mma_issuer<1>(i, ring, tmem, sbase, steps, q_bytes, k_off, v_off, q_full, k_full,
+                        k_empty, v_full, v_empty, s_full, p_full, pv_done, err);
         else
-          mma_issuer<0>(i, tmem, sbase, n_steps, q_bytes, k_off, v_off, q_full, k_full, k_empty,
-                        v_full, v_empty, s_full, p_full, pv_done, err);
+          mma_issuer<0>(i, ring, tmem, sbase, steps, q_bytes, k_off, v_off, q_full, k_full,
+                        k_empty, v_full, v_empty, s_full, p_full, pv_done, err);
         // Every MMA this thread issued completes before TMEM is released.
         castdev::tc_commit(&mma_drain[i]);
         castdev::mbar_wait_drain(&mma_drain[i], 0, err);
@@ -487,8 +521,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t o_addr = tmem + lane_off + ti * 128;
     const uint32_t s_addr = tmem + lane_off + 256 + ti * 128;
-    const bool active = ti < nq;
-    const int qrow_in_block = (t0 + ti) * 128 + row;
+    const bool active = ti < n_groups;
+    const int my_steps = 2 * (ti == 0 ? n_a : n_b);           // 64-key steps of this warpgroup
+    const int start_tile = (split && ti == 1) ? n_a : 0;        // its first key tile
+    const int qrow_in_block = (t0 + (split ? 0 : ti)) * 128 + row;
     const int qrow = qb * p.q_block + qrow_in_block;
     const bool row_valid = active && qrow_in_block < p.q_block && qrow < p.Lq;
     const float qscale = mode ? p.q_scales[row_item] : 1.0f;
@@ -517,10 +553,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         return e;
       };
-      Entry cur = fetch(0), nxt = fetch(1);
+      int jb = start_tile / p.k_tiles;            // list entry
+      int koff = (start_tile % p.k_tiles) * 128;  // key offset of this step inside it
+      Entry cur = fetch(jb), nxt = fetch(jb + 1);
       const int block_keys = p.k_tiles * 128;
-      int jb = 0, koff = 0;  // list entry, key offset of this step inside it
-      for (int h = 0; h < n_steps; ++h) {
+      for (int h = 0; h < my_steps; ++h) {
         const int half = h & 1;
         const float c2 = cur.c2;
         const int valid_cols = max(0, min(64, cur.nvalid - koff));
@@ -624,7 +661,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         castdev::tc_fence_before();
         __syncwarp();
         if (lane == 0) castdev::mbar_arrive(&p_full[ti * 2 + half]);
-          koff += 64;
+        koff += 64;
         if (koff == block_keys) {
           koff = 0;
           ++jb;
@@ -640,22 +677,58 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         run_steps(std::integral_constant<bool, false>{});
     }
     // ------------------------------------------------------------ epilogue
-    if (active && ok) {
-      if (n_steps > 0) {
-        // the last PV's commit covers every earlier MMA
-        const int hl = n_steps - 1;
-        ok = __all_sync(0xffffffffu,
-                        castdev::mbar_wait(&pv_done[ti * 2 + (hl & 1)], (hl >> 1) & 1, err));
+    if (active && ok && my_steps > 0) {
+      // the last PV's commit covers every earlier MMA of this tile
+      const int hl = my_steps - 1;
+      ok = __all_sync(0xffffffffu,
+                      castdev::mbar_wait(&pv_done[ti * 2 + (hl & 1)], (hl >> 1) & 1, err));
+      castdev::tc_fence_after();
+    }
+    if (split && ti == 1) {
+      // Split item: leave this half's running max and row sum in the tile's
+      // dead S columns for warpgroup 0, which merges O1 into its result.
+      if (ok) {
+        castdev::tmem_st1(s_addr, __float_as_uint(m_run));
+        castdev::tmem_st1(s_addr + 1, __float_as_uint(l_run));
+        castdev::tmem_wait_st();
+      }
+      castdev::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) castdev::mbar_arrive(merge_bar);
+    } else if (active && ok) {
+      float scale0 = 1.0f, scale1 = 0.0f;
+      const uint32_t o1_addr = tmem + lane_off + 128;
+      if (split) {
+        ok = __all_sync(0xffffffffu, castdev::mbar_wait(merge_bar, 0, err));
         castdev::tc_fence_after();
+        const uint32_t s1_addr = tmem + lane_off + 256 + 128;
+        const float m1 = __uint_as_float(castdev::tmem_ld1(s1_addr));
+        const float l1 = __uint_as_float(castdev::tmem_ld1(s1_addr + 1));
+        castdev::tmem_wait_ld();
+        const float m = fmaxf(m_run, m1);
+        scale0 = m == -INFINITY ? 0.0f : fast_exp2(m_run - m);
+        scale1 = m == -INFINITY ? 0.0f : fast_exp2(m1 - m);
+        l_run = l_run * scale0 + l1 * scale1;
+        m_run = m;
       }
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
       __nv_bfloat16 *orow = p.out + ((size_t)bh * p.Lq + qrow) * 128;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t o[32];
-        if (n_steps > 0 && ok) {
+        if (my_steps > 0 && ok) {
           castdev::tmem_ld32(o_addr + 32 * cc, o);
-          castdev::tmem_wait_ld();
+          if (split) {
+            uint32_t o1[32];
+            castdev::tmem_ld32(o1_addr + 32 * cc, o1);
+            castdev::tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              o[c] = __float_as_uint(fmaf(__uint_as_float(o1[c]), scale1,
+                                          __uint_as_float(o[c]) * scale0));
+          } else {
+            castdev::tmem_wait_ld();
+          }
         } else {
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = 0u;
