@@ -186,15 +186,15 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   CAST_CUDA_TRY(cudaGetLastError());
   const int keep = std::min(budget, nkb - nqb);
   const int maxdeg = keep + nqb;
-  const size_t dsm = sizeof(double) * nkb + nkb + 16;
+  const size_t dsm = (sizeof(double) + 2 * sizeof(float)) * nkb + nkb + 16;
   if (dsm > 48 * 1024) return fail(CAST_ERR_UNSUPPORTED, "too many key blocks (%d)", nkb);
   dim3 g2(nqb, B * H);
   if (D == 128)
-    castk::budget_select_kernel<128><<<g2, 128, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
+    castk::budget_select_kernel<128><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
                                                           budget, maxdeg, sel_idx, sel_cnt,
                                                           qk_mode, policy, int8_tolerance);
   else
-    castk::budget_select_kernel<64><<<g2, 128, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
+    castk::budget_select_kernel<64><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
                                                          budget, maxdeg, sel_idx, sel_cnt, qk_mode,
                                                          policy, int8_tolerance);
   CAST_CUDA_TRY(cudaGetLastError());

@@ -333,23 +333,32 @@ __device__ void warp_topk(const double *score, int n, int k, unsigned char *take
 // grid = (nqb, B*H), 128 threads.  Dynamic smem: nkb doubles + nkb bytes.
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
     budget_select_kernel(const double *__restrict__ pooled, const float *__restrict__ block_rms,
                          const float *__restrict__ q_scales, const float *__restrict__ k_scales,
                          int nqb, int nkb, int budget, int maxdeg, int32_t *sel_idx,
                          int32_t *sel_cnt, uint8_t *qk_mode, int policy, float tol) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  double *score = reinterpret_cast<double *>(dsm);
-  unsigned char *taken = dsm + sizeof(double) * nkb;
+  double *score = reinterpret_cast<double *>(dsm);                   // [nkb]
+  float *k_rms = reinterpret_cast<float *>(score + nkb);             // [nkb]
+  float *k_sc = k_rms + nkb;                                         // [nkb]
+  unsigned char *taken = reinterpret_cast<unsigned char *>(k_sc + nkb);  // [nkb]
   __shared__ double qn[D];
   __shared__ int32_t picks[256];
   const int qb = blockIdx.x, bh = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n_warps = blockDim.x >> 5;
   const double *prow = pooled + (size_t)bh * (nqb + nkb) * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = prow[(size_t)qb * D + d];
+  // per key block RMS and scale for the precision policy, fetched up front
+  if (qk_mode && policy == CAST_POLICY_AUTO)
+    for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) {
+      k_rms[kb] = block_rms[(size_t)bh * (nqb + nkb) + nqb + kb];
+      k_sc[kb] = k_scales[(size_t)bh * nkb + kb];
+    }
   __syncthreads();
   const int nhist = nkb - nqb;
-  for (int kb = warp; kb < nhist; kb += 4) {
+  for (int kb = warp; kb < nhist; kb += n_warps) {
     double s = warp_dot<D>(qn, prow + (size_t)(nqb + kb) * D, lane);
     if (lane == 0) score[kb] = s;
   }
@@ -364,27 +373,28 @@ __global__ void __launch_bounds__(128)
     else if (j < keep + qb + 1) val = nhist + (j - keep);
     out[j] = val;
   }
-  if (threadIdx.x == 0) {
-    sel_cnt[(size_t)bh * nqb + qb] = keep + qb + 1;
-    if (qk_mode) {
-      uint8_t mode = policy == CAST_POLICY_INT8 ? 1 : 0;
-      if (policy == CAST_POLICY_AUTO) {
-        // Predicted logit error of the int8 product (uniform quantisation
-        // noise, variance s^2/12 per element) times the logit spread; int8
-        // only where every selected block stays below the tolerance.
-        const float *rms = block_rms + (size_t)bh * (nqb + nkb);
-        const float rq = rms[qb], sq = q_scales[(size_t)bh * nqb + qb];
-        float worst = 0.0f;
-        for (int j = 0; j < keep + qb + 1; ++j) {
-          const int kb = j < keep ? picks[j] : nhist + (j - keep);
-          const float rk = rms[nqb + kb], sk = k_scales[(size_t)bh * nkb + kb];
-          const float err = sqrtf((sq * sq * rk * rk + sk * sk * rq * rq) * (1.0f / 12.0f));
-          worst = fmaxf(worst, err * rq * rk);
-        }
-        mode = worst <= tol ? 1 : 0;
+  if (threadIdx.x == 0) sel_cnt[(size_t)bh * nqb + qb] = keep + qb + 1;
+  if (qk_mode && warp == 0) {
+    uint8_t mode = policy == CAST_POLICY_INT8 ? 1 : 0;
+    if (policy == CAST_POLICY_AUTO) {
+      // Predicted logit error of the int8 product (uniform quantisation
+      // noise, variance s^2/12 per element) times the logit spread; int8
+      // only where every selected block stays below the tolerance.  One lane
+      // per selected block, then the warp maximum.
+      const float rq = block_rms[(size_t)bh * (nqb + nkb) + qb];
+      const float sq = q_scales[(size_t)bh * nqb + qb];
+      float worst = 0.0f;
+      for (int j = lane; j < keep + qb + 1; j += 32) {
+        const int kb = j < keep ? picks[j] : nhist + (j - keep);
+        const float rk = k_rms[kb], sk = k_sc[kb];
+        const float err = sqrtf((sq * sq * rk * rk + sk * sk * rq * rq) * (1.0f / 12.0f));
+        worst = fmaxf(worst, err * rq * rk);
       }
-      qk_mode[(size_t)bh * nqb + qb] = mode;
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) worst = fmaxf(worst, __shfl_xor_sync(0xffffffffu, worst, s));
+      mode = worst <= tol ? 1 : 0;
     }
+    if (lane == 0) qk_mode[(size_t)bh * nqb + qb] = mode;
   }
 }
 
