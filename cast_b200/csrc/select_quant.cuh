@@ -29,6 +29,39 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 &raw, float (&f)[8]) {
   }
 }
 
+// L2 cache policies: a block's statistics pass marks its lines evict-last so
+// they survive until the quantisation pass re-reads them (evict-first there,
+// and for the codes, which are not re-read by this kernel).
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ldg_nc_v4_hint(const void *p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ uint4 ldg_v4_hint(const void *p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ void stg_v2_hint(void *p, uint2 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v2.u32 [%0], {%1,%2}, %3;" ::"l"(p), "r"(v.x), "r"(v.y),
+               "l"(pol)
+               : "memory");
+}
+
 __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -170,11 +203,13 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   const bool pool = which != 2;
 
   constexpr int kUnroll = 8;
+  const uint64_t keep_pol = l2_evict_last(), drop_pol = l2_evict_first();
   int r = slot;
   for (; r + (kUnroll - 1) * kSumLanes < rows; r += kUnroll * kSumLanes) {
     uint4 raw[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) raw[u] = ldg_nc_v4(base + (size_t)(r + u * kSumLanes) * D);
+    for (int u = 0; u < kUnroll; ++u)
+      raw[u] = ldg_nc_v4_hint(base + (size_t)(r + u * kSumLanes) * D, keep_pol);
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       float f[8];
@@ -189,7 +224,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   }
   for (; r < rows; r += kSumLanes) {
     float f[8];
-    bf16x8_to_f32(ldg_nc_v4(base + (size_t)r * D), f);
+    bf16x8_to_f32(ldg_nc_v4_hint(base + (size_t)r * D, keep_pol), f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (pool) acc[i] = __fadd_rn(acc[i], f[i]);
@@ -277,14 +312,14 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
       uint4 raw[kUnroll];
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u)
-        raw[u] = *reinterpret_cast<const uint4 *>(base + (size_t)(rr + u * kSumLanes) * D);
+        raw[u] = ldg_v4_hint(base + (size_t)(rr + u * kSumLanes) * D, drop_pol);
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u)
-        *reinterpret_cast<uint2 *>(cbase + (size_t)(rr + u * kSumLanes) * D) = quant8(raw[u]);
+        stg_v2_hint(cbase + (size_t)(rr + u * kSumLanes) * D, quant8(raw[u]), drop_pol);
     }
     for (; rr < rows; rr += kSumLanes)
-      *reinterpret_cast<uint2 *>(cbase + (size_t)rr * D) =
-          quant8(*reinterpret_cast<const uint4 *>(base + (size_t)rr * D));
+      stg_v2_hint(cbase + (size_t)rr * D, quant8(ldg_v4_hint(base + (size_t)rr * D, drop_pol)),
+                  drop_pol);
   }
 }
 
