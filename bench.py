@@ -177,6 +177,57 @@ def cpu_baseline_sample():
             "sample": "2 of 24 heads (selection + explicit-softmax attention), median of 3, x12"}
 
 
+def par_measure(dev, peaks, peak_src, steps):
+    """PAR (FC-PASM) on BASELINE config 4: bf16 residual [1, 1+4, 880, 3072]
+    (one memory frame), anchors = current frames 0 and 3, targets 1 and 2.
+    One call replayed from a CUDA graph; GB/s on the algorithmic bytes (read
+    the two anchor frames, write the two target frames)."""
+    import torch
+
+    from cast_b200 import par, workloads
+
+    w = workloads.config4(device=dev)
+    corr = par.FCPASMCorrector()
+    corr.begin_model_call(chunk_index=1, step_index=0)
+    full = w.full_residual.clone()
+    act = w.active_residual.contiguous()
+    frames = tuple(w.active_frames)
+    kw = dict(layer_index=0, full_input=None, full_residual=full, active_residual=act,
+              active_frames=torch.tensor(frames), memory_length=w.memory_length,
+              spatial_height=w.height, spatial_width=w.width, active_frame_values=frames)
+    for _ in range(3):
+        corr.correct(**kw)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        corr.correct(**kw)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        corr.correct(**kw)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    n = max(20, steps)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) / n * 1000.0
+    hw, c = full.shape[-2], full.shape[-1]
+    alg = (2 + 2) * hw * c * full.element_size()
+    gbs = alg / (us * 1e-6) / 1e9
+    del graph
+    return {"workload": "config4: FC-PASM, bf16 residual [1, 1+4, 880 (22x40), 3072], anchors 0 and 3, "
+                        "targets 1 and 2", "us_per_call": us, "algorithmic_bytes": alg,
+            "achieved_gbs": gbs, "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
+            "note": f"HBM peak {peak_src}; CUDA graph replay of one correct() call, device time"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -297,6 +348,7 @@ def main():
         e2e = {"ms": e2e_ms, "h2d": sum(t.numel() * t.element_size() for t in (hq, hk, hv)),
                "d2h": hout.numel() * hout.element_size()}
     clocks = sampler.stop()
+    par_line = par_measure(dev, peaks, peak_src, args.steps) if rank == 0 else None
 
     # ---- max over ranks
     vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms], dtype=torch.float64, device=dev)
@@ -347,6 +399,7 @@ def main():
                      "traffic = ncu DRAM bytes per launch; "
                      f"ops/launch int8 {i8_ops:.4g} bf16 {bf_ops:.4g}"),
         },
+        "par": par_line,
         "gpu_launches": 3 * args.steps,
         "clocks": clocks,
     }
