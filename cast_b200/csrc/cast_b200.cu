@@ -368,7 +368,9 @@ extern "C" size_t cast_par_fcpasm_workspace_bytes(int T, int H, int W, int C) {
   const size_t partials = (size_t)castk::kParMaxPairs * castk::kParTiles * par_chunks(C) * castk::kParPartial;
   const size_t weights = (size_t)nt * castk::kParTiles * castk::kParFreq * 4;
   const size_t pred = (size_t)nt * castk::kParTiles * castk::kParPix * C;
-  return align_up(partials * 4, 256) + align_up(weights * 4, 256) + align_up(pred * 4, 256);
+  const size_t filters = (size_t)nt * castk::kParTiles * castk::kParFilterBytes;
+  return align_up(partials * 4, 256) + align_up(weights * 4, 256) + align_up(pred * 4, 256) +
+         align_up(filters, 1024);
 }
 
 static void fill_par_tables(castk::ParTables &t, float tau_low, float tau_high, float power) {
@@ -508,6 +510,8 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
     p.weights = reinterpret_cast<float *>(ws);
     ws += align_up((size_t)std::min(T, castk::kParMaxTargets) * castk::kParTiles * castk::kParFreq * 16, 256);
     p.pred = reinterpret_cast<float *>(ws);
+    ws += align_up((size_t)std::min(T, castk::kParMaxTargets) * castk::kParTiles * castk::kParPix * C * 4, 256);
+    p.filters = ws;
     p.stats = stats_out;
     fill_par_tables(p.tab, tau_low, tau_high, freq_power);
 
@@ -526,8 +530,34 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
     CAST_CUDA_TRY(cudaGetLastError());
     castk::par_finalize_kernel<<<dim3(castk::kParTiles, p.n_pairs), 128, 0, s>>>(p);
     CAST_CUDA_TRY(cudaGetLastError());
-    castk::par_predict_kernel<<<g1, castk::kParChunk, smem_pred, s>>>(p);
-    CAST_CUDA_TRY(cudaGetLastError());
+    // Tensor-core prediction when every 8-channel group is a 16-byte aligned
+    // copy and a pair's targets fit the TMEM columns; the per-channel DFT
+    // kernel otherwise.
+    int max_per_pair = 0;
+    for (int i = 0; i < p.n_pairs; ++i) {
+      int cnt = 0;
+      for (int t = 0; t < nt; ++t) cnt += p.target_pair[t] == i;
+      max_per_pair = std::max(max_per_pair, cnt);
+    }
+    if (C % 8 == 0 && reinterpret_cast<uintptr_t>(act) % 16 == 0 &&
+        max_per_pair <= castk::kParMmaTargets) {
+      static std::once_flag mma_once;
+      static cudaError_t mma_err = cudaSuccess;
+      std::call_once(mma_once, [] {
+        mma_err = cudaFuncSetAttribute(castk::par_predict_mma_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       castk::ParMmaSmem::alloc);
+      });
+      CAST_CUDA_TRY(mma_err);
+      castk::par_filter_kernel<<<dim3(castk::kParTiles, nt, castk::kParKChunks), 256, 0, s>>>(p);
+      CAST_CUDA_TRY(cudaGetLastError());
+      castk::par_predict_mma_kernel<<<dim3(ceil_div(C, 128), castk::kParTiles, p.n_pairs), 128,
+                                      castk::ParMmaSmem::alloc, s>>>(p);
+      CAST_CUDA_TRY(cudaGetLastError());
+    } else {
+      castk::par_predict_kernel<<<g1, castk::kParChunk, smem_pred, s>>>(p);
+      CAST_CUDA_TRY(cudaGetLastError());
+    }
     castk::par_ola_kernel<<<dim3(H * W, nt), 256, 0, s>>>(p);
     CAST_CUDA_TRY(cudaGetLastError());
   }

@@ -15,6 +15,24 @@
 //                        predicted windowed tiles (workspace)
 //   par_ola_kernel       grid (pixel, target): normalised overlap-add, bf16
 //                        write of the target frame                (writes)
+//
+// Tensor-core prediction (used when C % 8 == 0 and a pair has at most
+// kParMmaTargets targets): the whole per-tile chain analysis window -> rfft2
+// -> per-frequency mix -> irfft2 -> synthesis window is linear in the two
+// anchor tiles and circular in the pixel offset, so a target's predicted
+// tile is pred = F_L l + F_R r with F[p][q] = win[p] win[q] kern[(p - q) mod
+// (11, 10)] and kern[d] = (1/110) sum_f c_kx Re(w_f e^{i w_f . d}) (c_kx = 1
+// for kx = 0, 5, else 2: the c2r rows).
+//   par_filter_kernel    grid (tile, target): kern for L and R from the mix
+//                        weights, then F as bf16 hi + lo (the pair carries
+//                        ~16 significant bits) in the shared-memory image
+//                        the MMA reads
+//   par_predict_mma_kernel grid (128-channel chunk, tile, pair): the anchor
+//                        pixels of the tile gathered by TMA (one 64-channel
+//                        row per load; reflect padding is in the row index),
+//                        D[128 ch x 112 px] = A[128 ch x 224 (L|R px)] F via
+//                        tcgen05.mma (A MN-major, F K-major, fp32 in TMEM),
+//                        then the predicted tiles to the workspace
 #pragma once
 
 #include "common.cuh"
@@ -58,6 +76,7 @@ struct ParParams {
   float *partials;               // [n_pairs, 18, n_chunks, 198]
   float *weights;                // [n_targets, 18, 66, 4]
   float *pred;                   // [n_targets, 18, 110, C]
+  uint8_t *filters;              // [n_targets, 18] F images (hi, lo), kParFilterBytes each
   float *stats;                  // optional, see stats layout in capi
   ParTables tab;
 };
@@ -454,6 +473,229 @@ __global__ void __launch_bounds__(kParChunk) par_predict_kernel(const ParParams 
     }
     float *dst = p.pred + ((size_t)tg * kParTiles + tile) * kParPix * p.C + cc;
     irfft2_from_smem(colZ, ld, p.tab, dst, (size_t)p.C, valid);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core prediction.
+constexpr int kParMmaTargets = 4;                // targets per pair (TMEM: 4 x 112 columns)
+constexpr int kParK = 224;                       // L pixels 0..109, R pixels 112..221
+constexpr int kParN = 112;                       // output pixels (110 used)
+constexpr int kParKChunks = 4;                   // 64-element K chunks of the F image
+constexpr int kParFChunkBytes = kParN * 128;     // 14336
+constexpr int kParFHalfBytes = kParKChunks * kParFChunkBytes;  // hi or lo: 57344
+constexpr int kParFilterBytes = 2 * kParFHalfBytes;            // 114688
+constexpr int kParAHalfBytes = kParK * 128;      // 64 channels x 224 rows: 28672
+
+struct ParMmaSmem {
+  static constexpr int a = 0;                          // 2 x kParAHalfBytes
+  static constexpr int b = 2 * kParAHalfBytes;         // kParFilterBytes
+  static constexpr int bars = b + kParFilterBytes;     // a_full, b_full, mma_done[4]
+  static constexpr int tmem_slot = bars + (2 + kParMmaTargets) * 8;
+  static constexpr int total = tmem_slot + 16;
+  static constexpr int alloc = total + 1024;
+};
+
+// grid (tile, target, K chunk), 256 threads.
+__global__ void __launch_bounds__(256) par_filter_kernel(const ParParams p) {
+  __shared__ float wl_re[kParFreq], wl_im[kParFreq], wr_re[kParFreq], wr_im[kParFreq];
+  __shared__ float kern[2][kParPix];
+  const int tile = blockIdx.x, tg = blockIdx.y, t = threadIdx.x;
+  const float *w = p.weights + ((size_t)tg * kParTiles + tile) * kParFreq * 4;
+  if (t < kParFreq) {
+    wl_re[t] = w[4 * t];
+    wl_im[t] = w[4 * t + 1];
+    wr_re[t] = w[4 * t + 2];
+    wr_im[t] = w[4 * t + 3];
+  }
+  __syncthreads();
+  if (t < 2 * kParPix) {
+    const int side = t / kParPix, d = t % kParPix;
+    const int dy = d / kParTW, dx = d % kParTW;
+    const float *are = side ? wr_re : wl_re, *aim = side ? wr_im : wl_im;
+    float acc = 0.0f;
+    for (int ky = 0; ky < kParTH; ++ky) {
+      const int my = (ky * dy) % kParTH;
+      const float cy = p.tab.ch[my], sy = p.tab.shh[my];
+      for (int kx = 0; kx < kParWF; ++kx) {
+        const int mx = (kx * dx) % kParTW;
+        const float cx = p.tab.cw[mx], sx = p.tab.sw[mx];
+        // e^{i(2pi ky dy/11 + 2pi kx dx/10)}
+        const float er = cy * cx - sy * sx, ei = sy * cx + cy * sx;
+        const int f = ky * kParWF + kx;
+        const float re = are[f] * er - aim[f] * ei;
+        acc += (kx == 0 || kx == kParWF - 1) ? re : 2.0f * re;
+      }
+    }
+    kern[side][d] = acc * (1.0f / (float)kParPix);
+  }
+  __syncthreads();
+  // F image: element (n, k) at chunk k/64, row n, 16-byte group (k%64)/8
+  // swizzled by n & 7 (128-byte swizzle, K-major).
+  uint8_t *img = p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes;
+  const int kc0 = blockIdx.z;  // this CTA's 64-element K chunk
+  const int g_end = min(8, kParK / 8 - kc0 * 8);
+  for (int e = t; e < kParN * g_end; e += blockDim.x) {
+    const int n = e / g_end, g = kc0 * 8 + e % g_end;  // 8 consecutive k
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      float v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int k = g * 8 + j + u;
+        float f = 0.0f;
+        const int side = k < kParN ? 0 : 1;
+        const int q = k - side * kParN;
+        if (n < kParPix && q < kParPix) {
+          const int dy = (n / kParTW - q / kParTW + kParTH) % kParTH;
+          const int dx = (n % kParTW - q % kParTW + kParTW) % kParTW;
+          f = p.tab.win[n] * p.tab.win[q] * kern[side][dy * kParTW + dx];
+        }
+        v[u] = f;
+      }
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[0], v[1]);
+      const float2 hf = __bfloat1622float2(h);
+      const __nv_bfloat162 l = __floats2bfloat162_rn(v[0] - hf.x, v[1] - hf.y);
+      hi[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+      lo[j / 2] = *reinterpret_cast<const uint32_t *>(&l);
+    }
+    const int kc = g / 8, grp = g % 8;
+    const size_t off = (size_t)kc * kParFChunkBytes + (size_t)n * 128 + ((grp ^ (n & 7)) * 16);
+    *reinterpret_cast<uint4 *>(img + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(img + kParFHalfBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+// grid (chunk of 128 channels, tile, pair), 128 threads.
+__global__ void __launch_bounds__(128, 1)
+    par_predict_mma_kernel(const ParParams p) {
+  extern __shared__ uint8_t par_smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(par_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ParMmaSmem::bars);
+  uint64_t *b_full = bars + 1;
+  uint64_t *mma_done = bars + 2;  // one per target of the pair: each completes once
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + ParMmaSmem::tmem_slot);
+  int *err = &g_cast_device_error;
+  const int chunk = blockIdx.x, tile = blockIdx.y, pair = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gy = tile / kParGW, gx = tile % kParGW;
+
+  if (threadIdx.x == 0) {
+    castdev::mbar_init(b_full, 1);
+    for (int i = 0; i < kParMmaTargets; ++i) castdev::mbar_init(&mma_done[i], 1);
+    castdev::fence_barrier_init();
+  }
+  if (warp == 0) {
+    castdev::tmem_alloc(tmem_slot, 512);
+    castdev::tmem_relinquish();
+  }
+  // zero K padding rows 110, 111, 222, 223 of both channel halves
+  if (threadIdx.x < 2 * 4 * 8) {
+    const int h = threadIdx.x / 32, r = (threadIdx.x / 8) % 4, c16 = threadIdx.x % 8;
+    const int row = r < 2 ? kParPix + r : kParN + kParPix + (r - 2);
+    *reinterpret_cast<uint4 *>(smem + ParMmaSmem::a + h * kParAHalfBytes + row * 128 + c16 * 16) =
+        make_uint4(0u, 0u, 0u, 0u);
+  }
+
+  // A: 2 anchors x 110 pixels x 128 channels, 16-byte cp.async copies by all
+  // threads into the 128-byte-swizzled MN-major layout (channels beyond C
+  // are zero-filled); the reflect padding is in the source row.
+  {
+    const uint32_t a_s = castdev::smem_u32(smem + ParMmaSmem::a);
+    for (int e = threadIdx.x; e < 2 * kParPix * 16; e += blockDim.x) {
+      const int g16 = e % 16, pix = e / 16;  // 16 groups of 8 channels per pixel
+      const int side = pix / kParPix, q = pix % kParPix;
+      const int frame_row = side ? p.pair_right[pair] : p.pair_left[pair];
+      const int y = reflect_idx(gy * kParStride + q / kParTW - kParPadH, kParH);
+      const int x = reflect_idx(gx * kParStride + q % kParTW - kParPadW, kParW);
+      const int krow = side * kParN + q, h = g16 / 8, g = g16 % 8;
+      const int c0 = chunk * 128 + g16 * 8;
+      const uint32_t dst = a_s + h * kParAHalfBytes + krow * 128 + ((g ^ (krow & 7)) * 16);
+      const __nv_bfloat16 *src = p.active + ((size_t)frame_row * p.HW + y * kParW + x) * p.C + c0;
+      const uint32_t bytes = c0 < p.C ? 16u : 0u;  // zero-fill past C
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
+                   "l"(c0 < p.C ? src : p.active), "r"(bytes)
+                   : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  }
+
+  // the cp.async writes and the zero rows are generic-proxy writes the MMAs
+  // (async proxy) read
+  castdev::fence_proxy_async_smem();
+  __syncthreads();
+  castdev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const uint32_t sbase = castdev::smem_u32(smem);
+  constexpr uint32_t idesc = castdev::make_idesc(1, 1, 1, 1, 0, 128, kParN);
+  int local = 0;  // this target's index among the pair's targets (TMEM columns)
+  int b_loads = 0;
+  bool ok = true;
+  for (int tg = 0; tg < p.n_targets; ++tg) {
+    if (p.target_pair[tg] != pair) continue;
+    const uint32_t d_col = tmem + local * kParN;
+    if (threadIdx.x == 0 && ok) {
+      // the previous target's MMAs have finished reading B
+      if (local > 0) ok = castdev::mbar_wait(&mma_done[local - 1], 0, err);
+      if (ok) {
+        castdev::mbar_arrive_expect_tx(b_full, kParFilterBytes);
+        castdev::bulk_load(smem + ParMmaSmem::b,
+                           p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes,
+                           kParFilterBytes, b_full);
+        ++b_loads;
+      }
+      if (ok) ok = castdev::mbar_wait(b_full, local & 1, err);
+      if (ok) {
+        castdev::tc_fence_after();
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {  // F hi, then F lo
+#pragma unroll
+          for (int s = 0; s < kParK / 16; ++s) {
+            const uint64_t ad = castdev::smem_desc_sw128(sbase + ParMmaSmem::a + 2048 * s,
+                                                         kParAHalfBytes, 1024);
+            const uint64_t bd = castdev::smem_desc_sw128(
+                sbase + ParMmaSmem::b + half * kParFHalfBytes + (s >> 2) * kParFChunkBytes +
+                    (s & 3) * 32,
+                16, 1024);
+            castdev::mma_f16_ss(d_col, ad, bd, idesc, (half | s) != 0);
+          }
+        }
+        castdev::tc_commit(&mma_done[local]);
+      }
+    }
+    // epilogue: this target's 110 predicted pixels for the warp's 32 channels
+    const bool done = __all_sync(0xffffffffu, castdev::mbar_wait(&mma_done[local], 0, err));
+    castdev::tc_fence_after();
+    const int c = chunk * 128 + warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float *dst = p.pred + ((size_t)tg * kParTiles + tile) * kParPix * p.C + c;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t v[32];
+      if (cc < 3) {
+        castdev::tmem_ld32(tmem + lane_off + local * kParN + 32 * cc, v);
+      } else {
+        castdev::tmem_ld16(tmem + lane_off + local * kParN + 96, *reinterpret_cast<uint32_t(*)[16]>(v));
+      }
+      castdev::tmem_wait_ld();
+      const int n_cols = cc < 3 ? 32 : kParPix - 96;
+      if (done && c < p.C) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < n_cols) dst[(size_t)(32 * cc + j) * p.C] = __uint_as_float(v[j]);
+      }
+    }
+    ++local;
+  }
+  // every TMA copy and MMA of this CTA has completed before TMEM is released
+  if (threadIdx.x == 0 && b_loads > 0) castdev::mbar_wait_drain(b_full, (b_loads - 1) & 1, err);
+  __syncthreads();
+  if (warp == 0) {
+    castdev::tc_fence_after();
+    castdev::tmem_dealloc(tmem, 512);
   }
 }
 
