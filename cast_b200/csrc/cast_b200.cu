@@ -370,7 +370,7 @@ extern "C" size_t cast_par_fcpasm_workspace_bytes(int T, int H, int W, int C) {
   const size_t pred = (size_t)nt * castk::kParTiles * castk::kParPix * C;
   const size_t filters = (size_t)nt * castk::kParTiles * castk::kParFilterBytes;
   return align_up(partials * 4, 256) + align_up(weights * 4, 256) + align_up(pred * 4, 256) +
-         align_up(filters, 1024);
+         align_up(filters, 1024) + align_up(castk::kParDftBytes, 1024);
 }
 
 static void fill_par_tables(castk::ParTables &t, float tau_low, float tau_high, float power) {
@@ -391,6 +391,10 @@ static void fill_par_tables(castk::ParTables &t, float tau_low, float tau_high, 
   for (int k = 0; k < castk::kParTH; ++k) {
     t.ch[k] = (float)std::cos(2.0 * pi * k / castk::kParTH);
     t.shh[k] = (float)std::sin(2.0 * pi * k / castk::kParTH);
+  }
+  for (int m = 0; m < castk::kParPix; ++m) {
+    t.c110[m] = (float)std::cos(2.0 * pi * m / castk::kParPix);
+    t.s110[m] = (float)std::sin(2.0 * pi * m / castk::kParPix);
   }
   double fy[castk::kParTH], fx[castk::kParWF], rmax = 0.0;
   for (int k = 0; k < castk::kParTH; ++k) {
@@ -482,7 +486,8 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
   const size_t need = cast_par_fcpasm_workspace_bytes(T, H, W, C);
   if (!workspace || workspace_bytes < need)
     return fail(CAST_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
-  int st = current_device_sm100(nullptr);
+  int num_sms = 0;
+  int st = current_device_sm100(&num_sms);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const size_t frame_bytes = (size_t)H * W * C * 2;
@@ -512,6 +517,8 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
     p.pred = reinterpret_cast<float *>(ws);
     ws += align_up((size_t)std::min(T, castk::kParMaxTargets) * castk::kParTiles * castk::kParPix * C * 4, 256);
     p.filters = ws;
+    ws += align_up((size_t)std::min(T, castk::kParMaxTargets) * castk::kParTiles * castk::kParFilterBytes, 1024);
+    p.dft = ws;
     p.stats = stats_out;
     fill_par_tables(p.tab, tau_low, tau_high, freq_power);
 
@@ -525,30 +532,47 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
         aerr = cudaFuncSetAttribute(castk::par_predict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_pred);
     });
     CAST_CUDA_TRY(aerr);
-    dim3 g1(p.n_chunks, castk::kParTiles, p.n_pairs);
-    castk::par_stats_kernel<<<g1, castk::kParChunk, smem_stats, s>>>(p);
-    CAST_CUDA_TRY(cudaGetLastError());
-    castk::par_finalize_kernel<<<dim3(castk::kParTiles, p.n_pairs), 128, 0, s>>>(p);
-    CAST_CUDA_TRY(cudaGetLastError());
-    // Tensor-core prediction when every 8-channel group is a 16-byte aligned
-    // copy and a pair's targets fit the TMEM columns; the per-channel DFT
-    // kernel otherwise.
+    // Tensor-core paths when every 8-channel group is a 16-byte aligned copy
+    // (statistics and prediction) and a pair's targets fit the TMEM columns
+    // (prediction); the per-channel DFT kernels otherwise.
+    const bool mma_ok = C % 8 == 0 && reinterpret_cast<uintptr_t>(act) % 16 == 0;
     int max_per_pair = 0;
     for (int i = 0; i < p.n_pairs; ++i) {
       int cnt = 0;
       for (int t = 0; t < nt; ++t) cnt += p.target_pair[t] == i;
       max_per_pair = std::max(max_per_pair, cnt);
     }
-    if (C % 8 == 0 && reinterpret_cast<uintptr_t>(act) % 16 == 0 &&
-        max_per_pair <= castk::kParMmaTargets) {
+    if (mma_ok) {
       static std::once_flag mma_once;
       static cudaError_t mma_err = cudaSuccess;
       std::call_once(mma_once, [] {
         mma_err = cudaFuncSetAttribute(castk::par_predict_mma_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        castk::ParMmaSmem::alloc);
+        if (mma_err == cudaSuccess)
+          mma_err = cudaFuncSetAttribute(castk::par_stats_mma_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         castk::ParStatSmem::alloc);
       });
       CAST_CUDA_TRY(mma_err);
+    }
+    dim3 g1(p.n_chunks, castk::kParTiles, p.n_pairs);
+    if (mma_ok) {
+      p.n_stat_chunks = ceil_div(C, 128);
+      castk::par_dft_kernel<<<ceil_div(castk::kParN * (castk::kParN / 8), 256), 256, 0, s>>>(p);
+      CAST_CUDA_TRY(cudaGetLastError());
+      const int n_items = p.n_stat_chunks * castk::kParTiles * p.n_pairs;
+      castk::par_stats_mma_kernel<<<std::min(n_items, num_sms), castk::kParStatThreads,
+                                    castk::ParStatSmem::alloc, s>>>(p);
+    } else {
+      p.n_stat_chunks = p.n_chunks;
+      castk::par_stats_kernel<<<g1, castk::kParChunk, smem_stats, s>>>(p);
+    }
+    CAST_CUDA_TRY(cudaGetLastError());
+    const bool predict_mma = mma_ok && max_per_pair <= castk::kParMmaTargets;
+    castk::par_finalize_kernel<<<dim3(castk::kParTiles, p.n_pairs), castk::kParFinalizeThreads, 0, s>>>(p);
+    CAST_CUDA_TRY(cudaGetLastError());
+    if (predict_mma) {
       castk::par_filter_kernel<<<dim3(castk::kParTiles, nt, castk::kParKChunks), 256, 0, s>>>(p);
       CAST_CUDA_TRY(cudaGetLastError());
       castk::par_predict_mma_kernel<<<dim3(ceil_div(C, 128), castk::kParTiles, p.n_pairs), 128,

@@ -23,10 +23,10 @@
 // tile is pred = F_L l + F_R r with F[p][q] = win[p] win[q] kern[(p - q) mod
 // (11, 10)] and kern[d] = (1/110) sum_f c_kx Re(w_f e^{i w_f . d}) (c_kx = 1
 // for kx = 0, 5, else 2: the c2r rows).
-//   par_filter_kernel    grid (tile, target): kern for L and R from the mix
-//                        weights, then F as bf16 hi + lo (the pair carries
-//                        ~16 significant bits) in the shared-memory image
-//                        the MMA reads
+//   par_filter_kernel    grid (tile, target, K chunk): kern for L and R from
+//                        the mix weights, then F as bf16 hi + lo (the pair
+//                        carries ~16 significant bits) in the shared-memory
+//                        image the MMA reads
 //   par_predict_mma_kernel grid (128-channel chunk, tile, pair): the anchor
 //                        pixels of the tile gathered by TMA (one 64-channel
 //                        row per load; reflect padding is in the row index),
@@ -59,12 +59,15 @@ struct ParTables {
   float thr[kParFreq];    // tau_low + (tau_high - tau_low) * r^p
   float fy[kParTH];       // 2*pi*fftfreq(11)
   float fx[kParWF];       // 2*pi*rfftfreq(10)
+  float c110[kParPix];    // cos(2*pi*m/110): angle of bin (ky, kx) at pixel
+  float s110[kParPix];    // (i, j) is 2*pi*((10 ky i + 11 kx j) mod 110)/110
 };
 
 struct ParParams {
   const __nv_bfloat16 *active;  // [A, HW, C]
   __nv_bfloat16 *full;          // [T, HW, C]
   int C, HW, n_chunks;
+  int n_stat_chunks;            // chunks of `partials` (64 or 128 channels each)
   int n_pairs, n_targets;
   int pair_left[kParMaxPairs], pair_right[kParMaxPairs];  // rows of `active`
   int target_pair[kParMaxTargets];                        // index into pairs
@@ -77,6 +80,7 @@ struct ParParams {
   float *weights;                // [n_targets, 18, 66, 4]
   float *pred;                   // [n_targets, 18, 110, C]
   uint8_t *filters;              // [n_targets, 18] F images (hi, lo), kParFilterBytes each
+  uint8_t *dft;                  // windowed rfft2 matrix image (hi, lo), kParDftBytes
   float *stats;                  // optional, see stats layout in capi
   ParTables tab;
 };
@@ -85,6 +89,48 @@ __device__ __forceinline__ int reflect_idx(int i, int n) {
   if (i < 0) i = -i;
   if (i >= n) i = 2 * (n - 1) - i;
   return i;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core prediction.
+constexpr int kParMmaTargets = 4;                // targets per pair (TMEM: 4 x 112 columns)
+constexpr int kParK = 224;                       // L pixels 0..109, R pixels 112..221
+constexpr int kParN = 112;                       // output pixels (110 used)
+constexpr int kParKChunks = 4;                   // 64-element K chunks of the F image
+constexpr int kParFChunkBytes = kParN * 128;     // 14336
+constexpr int kParFHalfBytes = kParKChunks * kParFChunkBytes;  // hi or lo: 57344
+constexpr int kParFilterBytes = 2 * kParFHalfBytes;            // 114688
+constexpr int kParAHalfBytes = kParK * 128;      // 64 channels x 224 rows: 28672
+
+struct ParMmaSmem {
+  static constexpr int a = 0;                          // 2 x kParAHalfBytes
+  static constexpr int b = 2 * kParAHalfBytes;         // kParFilterBytes
+  static constexpr int bars = b + kParFilterBytes;     // a_full, b_full, mma_done[4]
+  static constexpr int tmem_slot = bars + (2 + kParMmaTargets) * 8;
+  static constexpr int total = tmem_slot + 16;
+  static constexpr int alloc = total + 1024;
+};
+
+// Kernel parameters live in the constant bank, which serves a warp one
+// distinct address at a time; kernels that index the tables per lane read a
+// shared-memory copy, made here with warp-uniform parameter reads.
+__device__ __forceinline__ void par_tables_to_smem(const ParTables &src, ParTables &dst) {
+  constexpr int n = (int)(sizeof(ParTables) / 4);
+  const float *sp = reinterpret_cast<const float *>(&src);
+  float *dp = reinterpret_cast<float *>(&dst);
+  const int lane = threadIdx.x & 31;
+  for (int base = (threadIdx.x >> 5) * 32; base < n; base += blockDim.x) {
+    float mine = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      if (base + k < n) {
+        const float v = sp[base + k];
+        mine = lane == k ? v : mine;
+      }
+    }
+    if (base + lane < n) dp[base + lane] = mine;
+  }
+  __syncthreads();
 }
 
 // Spectra live in shared memory, one column per thread (channel): entry e of
@@ -292,18 +338,101 @@ __global__ void __launch_bounds__(kParChunk) par_stats_kernel(const ParParams p)
   }
 }
 
+// K chunks kc0 .. kc1-1 of the F image of target tg at `tile`, from its mix
+// weights (all threads of the block): kern for L and R, then F as bf16 hi +
+// lo (the pair carries ~16 significant bits) in the shared-memory image the
+// MMA reads.
+struct ParFilterSmem {
+  float wl_re[kParFreq], wl_im[kParFreq], wr_re[kParFreq], wr_im[kParFreq];
+  float kern[2][kParPix];
+};
+__device__ __forceinline__ void par_build_filter(const ParParams &p, const ParTables &tab, int tile, int tg,
+                                                 int kc0, int kc1, ParFilterSmem &fs) {
+  float *wl_re = fs.wl_re, *wl_im = fs.wl_im, *wr_re = fs.wr_re, *wr_im = fs.wr_im;
+  float(*kern)[kParPix] = fs.kern;
+  const int t = threadIdx.x;
+  const float *w = p.weights + ((size_t)tg * kParTiles + tile) * kParFreq * 4;
+  __syncthreads();  // the previous target's reads of fs are done
+  if (t < kParFreq) {
+    wl_re[t] = w[4 * t];
+    wl_im[t] = w[4 * t + 1];
+    wr_re[t] = w[4 * t + 2];
+    wr_im[t] = w[4 * t + 3];
+  }
+  __syncthreads();
+  if (t < 2 * kParPix) {
+    const int side = t / kParPix, d = t % kParPix;
+    const int dy = d / kParTW, dx = d % kParTW;
+    const float *are = side ? wr_re : wl_re, *aim = side ? wr_im : wl_im;
+    float acc = 0.0f;
+    for (int ky = 0; ky < kParTH; ++ky) {
+      const int my = (ky * dy) % kParTH;
+      const float cy = tab.ch[my], sy = tab.shh[my];
+      for (int kx = 0; kx < kParWF; ++kx) {
+        const int mx = (kx * dx) % kParTW;
+        const float cx = tab.cw[mx], sx = tab.sw[mx];
+        // e^{i(2pi ky dy/11 + 2pi kx dx/10)}
+        const float er = cy * cx - sy * sx, ei = sy * cx + cy * sx;
+        const int f = ky * kParWF + kx;
+        const float re = are[f] * er - aim[f] * ei;
+        acc += (kx == 0 || kx == kParWF - 1) ? re : 2.0f * re;
+      }
+    }
+    kern[side][d] = acc * (1.0f / (float)kParPix);
+  }
+  __syncthreads();
+  // F image: element (n, k) at chunk k/64, row n, 16-byte group (k%64)/8
+  // swizzled by n & 7 (128-byte swizzle, K-major).
+  uint8_t *img = p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes;
+  const int g0 = kc0 * 8, ng = min(kc1 * 8, kParK / 8) - g0;
+  for (int e = t; e < kParN * ng; e += blockDim.x) {
+    const int n = e / ng, g = g0 + e % ng;  // 8 consecutive k
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      float v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int k = g * 8 + j + u;
+        float f = 0.0f;
+        const int side = k < kParN ? 0 : 1;
+        const int q = k - side * kParN;
+        if (n < kParPix && q < kParPix) {
+          const int dy = (n / kParTW - q / kParTW + kParTH) % kParTH;
+          const int dx = (n % kParTW - q % kParTW + kParTW) % kParTW;
+          f = tab.win[n] * tab.win[q] * kern[side][dy * kParTW + dx];
+        }
+        v[u] = f;
+      }
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[0], v[1]);
+      const float2 hf = __bfloat1622float2(h);
+      const __nv_bfloat162 l = __floats2bfloat162_rn(v[0] - hf.x, v[1] - hf.y);
+      hi[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+      lo[j / 2] = *reinterpret_cast<const uint32_t *>(&l);
+    }
+    const int kc = g / 8, grp = g % 8;
+    const size_t off = (size_t)kc * kParFChunkBytes + (size_t)n * 128 + ((grp ^ (n & 7)) * 16);
+    *reinterpret_cast<uint4 *>(img + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(img + kParFHalfBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
 // ---------------------------------------------------------------------------
-// One CTA per (tile, pair), 128 threads.
-__global__ void __launch_bounds__(128) par_finalize_kernel(const ParParams p) {
+// One CTA per (tile, pair), kParFinalizeThreads threads.
+constexpr int kParFinalizeThreads = 256;
+__global__ void __launch_bounds__(kParFinalizeThreads) par_finalize_kernel(const __grid_constant__ ParParams p) {
+  __shared__ ParTables tab;
+  par_tables_to_smem(p.tab, tab);
   __shared__ float part[kParPartial];
   __shared__ float unit_re[kParFreq], unit_im[kParFreq], coh[kParFreq], wgt[kParFreq];
   __shared__ float theta[kParFreq], corr[kParPix];
   __shared__ float s_base, s_denom, s_conf, s_dx, s_dy, s_ramp;
   const int tile = blockIdx.x, pair = blockIdx.y, t = threadIdx.x;
-  const float *src = p.partials + ((size_t)pair * kParTiles + tile) * p.n_chunks * kParPartial;
+  const float *src = p.partials + ((size_t)pair * kParTiles + tile) * p.n_stat_chunks * kParPartial;
   for (int r = t; r < kParPartial; r += blockDim.x) {
     float acc = 0.0f;
-    for (int ch = 0; ch < p.n_chunks; ++ch) acc += src[(size_t)ch * kParPartial + r];
+#pragma unroll 8
+    for (int ch = 0; ch < p.n_stat_chunks; ++ch) acc += src[(size_t)ch * kParPartial + r];
     part[r] = acc;
   }
   __syncthreads();
@@ -348,7 +477,7 @@ __global__ void __launch_bounds__(128) par_finalize_kernel(const ParParams p) {
     float acc = 0.0f;
     for (int ky = 0; ky < kParTH; ++ky) {
       const int my = (ky * y) % kParTH;
-      const float ey_c = p.tab.ch[my], ey_s = p.tab.shh[my];
+      const float ey_c = tab.ch[my], ey_s = tab.shh[my];
       for (int kx = 0; kx < kParWF; ++kx) {
         const int f = ky * kParWF + kx;
         const float vr = unit_re[f] * coh[f], vi = unit_im[f] * coh[f];
@@ -360,21 +489,33 @@ __global__ void __launch_bounds__(128) par_finalize_kernel(const ParParams p) {
           acc += (x & 1) ? -zr : zr;
         } else {
           const int mx = (kx * x) % kParTW;
-          acc += 2.0f * (zr * p.tab.cw[mx] - zi * p.tab.sw[mx]);
+          acc += 2.0f * (zr * tab.cw[mx] - zi * tab.sw[mx]);
         }
       }
     }
     corr[t] = acc * (1.0f / (float)(kParTH * kParTW));
   }
   __syncthreads();
-  if (t == 0) {
-    int best = 0;
-    float bv = corr[0];
-    for (int i = 1; i < kParPix; ++i)
+  if (t < 32) {
+    // first index of the maximum: each lane scans i = t, t + 32, ... in
+    // order, then a shuffle tree keeps the larger value, the smaller index
+    // on ties
+    int best = t;
+    float bv = corr[t];
+    for (int i = t + 32; i < kParPix; i += 32)
       if (corr[i] > bv) {
         bv = corr[i];
         best = i;
       }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, best, o);
+      if (ov > bv || (ov == bv && oi < best)) {
+        bv = ov;
+        best = oi;
+      }
+    }
     const int py = best / kParTW, px = best % kParTW;
     auto sub = [](float before, float middle, float after) {
       const float den = before - 2.0f * middle + after;
@@ -384,15 +525,17 @@ __global__ void __launch_bounds__(128) par_finalize_kernel(const ParParams p) {
     const float xr = corr[py * kParTW + (px + 1) % kParTW];
     const float yu = corr[((py + kParTH - 1) % kParTH) * kParTW + px];
     const float yd = corr[((py + 1) % kParTH) * kParTW + px];
-    s_dx = (float)(px >= (kParTW + 1) / 2 ? px - kParTW : px) + sub(xl, bv, xr);
-    s_dy = (float)(py >= (kParTH + 1) / 2 ? py - kParTH : py) + sub(yu, bv, yd);
+    if (t == 0) {
+      s_dx = (float)(px >= (kParTW + 1) / 2 ? px - kParTW : px) + sub(xl, bv, xr);
+      s_dy = (float)(py >= (kParTH + 1) / 2 ? py - kParTH : py) + sub(yu, bv, yd);
+    }
   }
   __syncthreads();
   if (t < 32) {
     float acc = 0.0f;
     for (int f = t; f < kParFreq; f += 32) {
       const int ky = f / kParWF, kx = f % kParWF;
-      const float ang = -(s_dy * p.tab.fy[ky] + s_dx * p.tab.fx[kx]);
+      const float ang = -(s_dy * tab.fy[ky] + s_dx * tab.fx[kx]);
       float sa, ca;
       sincosf(ang, &sa, &ca);
       // Re(unit * conj(exp(i ang)))
@@ -412,7 +555,7 @@ __global__ void __launch_bounds__(128) par_finalize_kernel(const ParParams p) {
   }
   __syncthreads();
   if (t < kParFreq) {
-    const float z = (s_conf - p.tab.thr[t]) / p.temperature;
+    const float z = (s_conf - tab.thr[t]) / p.temperature;
     const float g = 1.0f / (1.0f + expf(-z));
     for (int tg = 0; tg < p.n_targets; ++tg) {
       if (p.target_pair[tg] != pair) continue;
@@ -440,6 +583,16 @@ __global__ void __launch_bounds__(128) par_finalize_kernel(const ParParams p) {
       }
     }
   }
+}
+
+// grid (tile, target, K chunk), 256 threads: the F images for the
+// tensor-core prediction (spread over many SMs: building them is
+// instruction-bound).
+__global__ void __launch_bounds__(256) par_filter_kernel(const __grid_constant__ ParParams p) {
+  __shared__ ParTables tab;
+  __shared__ ParFilterSmem fs;
+  par_tables_to_smem(p.tab, tab);
+  par_build_filter(p, tab, blockIdx.x, blockIdx.y, blockIdx.z, blockIdx.z + 1, fs);
 }
 
 // ---------------------------------------------------------------------------
@@ -476,95 +629,38 @@ __global__ void __launch_bounds__(kParChunk) par_predict_kernel(const ParParams 
   }
 }
 
-// ---------------------------------------------------------------------------
-// Tensor-core prediction.
-constexpr int kParMmaTargets = 4;                // targets per pair (TMEM: 4 x 112 columns)
-constexpr int kParK = 224;                       // L pixels 0..109, R pixels 112..221
-constexpr int kParN = 112;                       // output pixels (110 used)
-constexpr int kParKChunks = 4;                   // 64-element K chunks of the F image
-constexpr int kParFChunkBytes = kParN * 128;     // 14336
-constexpr int kParFHalfBytes = kParKChunks * kParFChunkBytes;  // hi or lo: 57344
-constexpr int kParFilterBytes = 2 * kParFHalfBytes;            // 114688
-constexpr int kParAHalfBytes = kParK * 128;      // 64 channels x 224 rows: 28672
-
-struct ParMmaSmem {
-  static constexpr int a = 0;                          // 2 x kParAHalfBytes
-  static constexpr int b = 2 * kParAHalfBytes;         // kParFilterBytes
-  static constexpr int bars = b + kParFilterBytes;     // a_full, b_full, mma_done[4]
-  static constexpr int tmem_slot = bars + (2 + kParMmaTargets) * 8;
-  static constexpr int total = tmem_slot + 16;
-  static constexpr int alloc = total + 1024;
-};
-
-// grid (tile, target, K chunk), 256 threads.
-__global__ void __launch_bounds__(256) par_filter_kernel(const ParParams p) {
-  __shared__ float wl_re[kParFreq], wl_im[kParFreq], wr_re[kParFreq], wr_im[kParFreq];
-  __shared__ float kern[2][kParPix];
-  const int tile = blockIdx.x, tg = blockIdx.y, t = threadIdx.x;
-  const float *w = p.weights + ((size_t)tg * kParTiles + tile) * kParFreq * 4;
-  if (t < kParFreq) {
-    wl_re[t] = w[4 * t];
-    wl_im[t] = w[4 * t + 1];
-    wr_re[t] = w[4 * t + 2];
-    wr_im[t] = w[4 * t + 3];
+// The two anchor tiles of (pair, tile), channels chunk*128 .. +127, into the
+// 128-byte-swizzled MN-major A image at `a`: K row side*112 + q holds pixel q
+// of the reflect-padded 11x10 tile (side 0 = left anchor), the two 64-channel
+// halves kParAHalfBytes apart.  16-byte cp.async copies spread over the
+// block; channels at or beyond C read as zero, rows 110, 111, 222, 223 are
+// zeroed.  Returns once this thread's copies have landed: the caller fences
+// (generic -> async proxy) and synchronises the block.
+__device__ __forceinline__ void par_gather_anchors(const ParParams &p, int pair, int tile, int chunk,
+                                                   uint8_t *a) {
+  const int gy = tile / kParGW, gx = tile % kParGW;
+  for (int e = threadIdx.x; e < 2 * 4 * 8; e += blockDim.x) {
+    const int h = e / 32, r = (e / 8) % 4, c16 = e % 8;
+    const int row = r < 2 ? kParPix + r : kParN + kParPix + (r - 2);
+    *reinterpret_cast<uint4 *>(a + h * kParAHalfBytes + row * 128 + c16 * 16) = make_uint4(0u, 0u, 0u, 0u);
   }
-  __syncthreads();
-  if (t < 2 * kParPix) {
-    const int side = t / kParPix, d = t % kParPix;
-    const int dy = d / kParTW, dx = d % kParTW;
-    const float *are = side ? wr_re : wl_re, *aim = side ? wr_im : wl_im;
-    float acc = 0.0f;
-    for (int ky = 0; ky < kParTH; ++ky) {
-      const int my = (ky * dy) % kParTH;
-      const float cy = p.tab.ch[my], sy = p.tab.shh[my];
-      for (int kx = 0; kx < kParWF; ++kx) {
-        const int mx = (kx * dx) % kParTW;
-        const float cx = p.tab.cw[mx], sx = p.tab.sw[mx];
-        // e^{i(2pi ky dy/11 + 2pi kx dx/10)}
-        const float er = cy * cx - sy * sx, ei = sy * cx + cy * sx;
-        const int f = ky * kParWF + kx;
-        const float re = are[f] * er - aim[f] * ei;
-        acc += (kx == 0 || kx == kParWF - 1) ? re : 2.0f * re;
-      }
-    }
-    kern[side][d] = acc * (1.0f / (float)kParPix);
+  const uint32_t a_s = castdev::smem_u32(a);
+  for (int e = threadIdx.x; e < 2 * kParPix * 16; e += blockDim.x) {
+    const int g16 = e % 16, pix = e / 16;  // 16 groups of 8 channels per pixel
+    const int side = pix / kParPix, q = pix % kParPix;
+    const int frame_row = side ? p.pair_right[pair] : p.pair_left[pair];
+    const int y = reflect_idx(gy * kParStride + q / kParTW - kParPadH, kParH);
+    const int x = reflect_idx(gx * kParStride + q % kParTW - kParPadW, kParW);
+    const int krow = side * kParN + q, h = g16 / 8, g = g16 % 8;
+    const int c0 = chunk * 128 + g16 * 8;
+    const uint32_t dst = a_s + h * kParAHalfBytes + krow * 128 + ((g ^ (krow & 7)) * 16);
+    const __nv_bfloat16 *src = p.active + ((size_t)frame_row * p.HW + y * kParW + x) * p.C + c0;
+    const uint32_t bytes = c0 < p.C ? 16u : 0u;  // zero-fill past C
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
+                 "l"(c0 < p.C ? src : p.active), "r"(bytes)
+                 : "memory");
   }
-  __syncthreads();
-  // F image: element (n, k) at chunk k/64, row n, 16-byte group (k%64)/8
-  // swizzled by n & 7 (128-byte swizzle, K-major).
-  uint8_t *img = p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes;
-  const int kc0 = blockIdx.z;  // this CTA's 64-element K chunk
-  const int g_end = min(8, kParK / 8 - kc0 * 8);
-  for (int e = t; e < kParN * g_end; e += blockDim.x) {
-    const int n = e / g_end, g = kc0 * 8 + e % g_end;  // 8 consecutive k
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      float v[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int k = g * 8 + j + u;
-        float f = 0.0f;
-        const int side = k < kParN ? 0 : 1;
-        const int q = k - side * kParN;
-        if (n < kParPix && q < kParPix) {
-          const int dy = (n / kParTW - q / kParTW + kParTH) % kParTH;
-          const int dx = (n % kParTW - q % kParTW + kParTW) % kParTW;
-          f = p.tab.win[n] * p.tab.win[q] * kern[side][dy * kParTW + dx];
-        }
-        v[u] = f;
-      }
-      const __nv_bfloat162 h = __floats2bfloat162_rn(v[0], v[1]);
-      const float2 hf = __bfloat1622float2(h);
-      const __nv_bfloat162 l = __floats2bfloat162_rn(v[0] - hf.x, v[1] - hf.y);
-      hi[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
-      lo[j / 2] = *reinterpret_cast<const uint32_t *>(&l);
-    }
-    const int kc = g / 8, grp = g % 8;
-    const size_t off = (size_t)kc * kParFChunkBytes + (size_t)n * 128 + ((grp ^ (n & 7)) * 16);
-    *reinterpret_cast<uint4 *>(img + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4 *>(img + kParFHalfBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // grid (chunk of 128 channels, tile, pair), 128 threads.
@@ -580,47 +676,35 @@ __global__ void __launch_bounds__(128, 1)
   int *err = &g_cast_device_error;
   const int chunk = blockIdx.x, tile = blockIdx.y, pair = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gy = tile / kParGW, gx = tile % kParGW;
+
+  // this pair's targets in order (at most kParMmaTargets, checked by the host)
+  int tgs[kParMmaTargets];
+  int n_loc = 0;
+  for (int tg = 0; tg < p.n_targets; ++tg)
+    if (p.target_pair[tg] == pair && n_loc < kParMmaTargets) tgs[n_loc++] = tg;
+  // F of target `local` into B (thread 0); B is free: the MMAs of the
+  // previous target have completed
+  int b_loads = 0;
+  auto load_f = [&](int local) {
+    castdev::mbar_arrive_expect_tx(b_full, kParFilterBytes);
+    castdev::bulk_load(smem + ParMmaSmem::b,
+                       p.filters + ((size_t)tgs[local] * kParTiles + tile) * kParFilterBytes,
+                       kParFilterBytes, b_full);
+    ++b_loads;
+  };
 
   if (threadIdx.x == 0) {
     castdev::mbar_init(b_full, 1);
     for (int i = 0; i < kParMmaTargets; ++i) castdev::mbar_init(&mma_done[i], 1);
     castdev::fence_barrier_init();
+    if (n_loc > 0) load_f(0);  // lands under the anchor gather
   }
   if (warp == 0) {
     castdev::tmem_alloc(tmem_slot, 512);
     castdev::tmem_relinquish();
   }
-  // zero K padding rows 110, 111, 222, 223 of both channel halves
-  if (threadIdx.x < 2 * 4 * 8) {
-    const int h = threadIdx.x / 32, r = (threadIdx.x / 8) % 4, c16 = threadIdx.x % 8;
-    const int row = r < 2 ? kParPix + r : kParN + kParPix + (r - 2);
-    *reinterpret_cast<uint4 *>(smem + ParMmaSmem::a + h * kParAHalfBytes + row * 128 + c16 * 16) =
-        make_uint4(0u, 0u, 0u, 0u);
-  }
 
-  // A: 2 anchors x 110 pixels x 128 channels, 16-byte cp.async copies by all
-  // threads into the 128-byte-swizzled MN-major layout (channels beyond C
-  // are zero-filled); the reflect padding is in the source row.
-  {
-    const uint32_t a_s = castdev::smem_u32(smem + ParMmaSmem::a);
-    for (int e = threadIdx.x; e < 2 * kParPix * 16; e += blockDim.x) {
-      const int g16 = e % 16, pix = e / 16;  // 16 groups of 8 channels per pixel
-      const int side = pix / kParPix, q = pix % kParPix;
-      const int frame_row = side ? p.pair_right[pair] : p.pair_left[pair];
-      const int y = reflect_idx(gy * kParStride + q / kParTW - kParPadH, kParH);
-      const int x = reflect_idx(gx * kParStride + q % kParTW - kParPadW, kParW);
-      const int krow = side * kParN + q, h = g16 / 8, g = g16 % 8;
-      const int c0 = chunk * 128 + g16 * 8;
-      const uint32_t dst = a_s + h * kParAHalfBytes + krow * 128 + ((g ^ (krow & 7)) * 16);
-      const __nv_bfloat16 *src = p.active + ((size_t)frame_row * p.HW + y * kParW + x) * p.C + c0;
-      const uint32_t bytes = c0 < p.C ? 16u : 0u;  // zero-fill past C
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
-                   "l"(c0 < p.C ? src : p.active), "r"(bytes)
-                   : "memory");
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  }
+  par_gather_anchors(p, pair, tile, chunk, smem + ParMmaSmem::a);
 
   // the cp.async writes and the zero rows are generic-proxy writes the MMAs
   // (async proxy) read
@@ -631,22 +715,12 @@ __global__ void __launch_bounds__(128, 1)
 
   const uint32_t sbase = castdev::smem_u32(smem);
   constexpr uint32_t idesc = castdev::make_idesc(1, 1, 1, 1, 0, 128, kParN);
-  int local = 0;  // this target's index among the pair's targets (TMEM columns)
-  int b_loads = 0;
-  bool ok = true;
-  for (int tg = 0; tg < p.n_targets; ++tg) {
-    if (p.target_pair[tg] != pair) continue;
+  bool ok = true;  // thread 0's view
+  for (int local = 0; local < n_loc; ++local) {
+    const int tg = tgs[local];
     const uint32_t d_col = tmem + local * kParN;
-    if (threadIdx.x == 0 && ok) {
-      // the previous target's MMAs have finished reading B
-      if (local > 0) ok = castdev::mbar_wait(&mma_done[local - 1], 0, err);
-      if (ok) {
-        castdev::mbar_arrive_expect_tx(b_full, kParFilterBytes);
-        castdev::bulk_load(smem + ParMmaSmem::b,
-                           p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes,
-                           kParFilterBytes, b_full);
-        ++b_loads;
-      }
+    int done_i = 1;
+    if (threadIdx.x == 0) {
       if (ok) ok = castdev::mbar_wait(b_full, local & 1, err);
       if (ok) {
         castdev::tc_fence_after();
@@ -664,11 +738,17 @@ __global__ void __launch_bounds__(128, 1)
           }
         }
         castdev::tc_commit(&mma_done[local]);
+        ok = castdev::mbar_wait(&mma_done[local], 0, err);
       }
+      // the next target's F lands under this target's epilogue
+      if (ok && local + 1 < n_loc) load_f(local + 1);
+      done_i = ok;
     }
-    // epilogue: this target's 110 predicted pixels for the warp's 32 channels
-    const bool done = __all_sync(0xffffffffu, castdev::mbar_wait(&mma_done[local], 0, err));
+    // one thread polls the barriers, the others sleep in the block barrier
+    // (polling warps would take shared-memory bandwidth from the MMAs)
+    const bool done = __syncthreads_and(done_i) != 0;
     castdev::tc_fence_after();
+    // epilogue: this target's 110 predicted pixels for the warp's 32 channels
     const int c = chunk * 128 + warp * 32 + lane;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     float *dst = p.pred + ((size_t)tg * kParTiles + tile) * kParPix * p.C + c;
@@ -688,10 +768,307 @@ __global__ void __launch_bounds__(128, 1)
           if (j < n_cols) dst[(size_t)(32 * cc + j) * p.C] = __uint_as_float(v[j]);
       }
     }
-    ++local;
   }
   // every TMA copy and MMA of this CTA has completed before TMEM is released
   if (threadIdx.x == 0 && b_loads > 0) castdev::mbar_wait_drain(b_full, (b_loads - 1) & 1, err);
+  __syncthreads();
+  if (warp == 0) {
+    castdev::tc_fence_after();
+    castdev::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core statistics.  The windowed rfft2 of a tile is a fixed linear map
+// of its 110 pixels, X[f] = sum_q win[q] x[q] e^{-i w_f . q}.  The input is
+// real, so along kx = 0 and kx = 5 the bins of ky and 11 - ky are complex
+// conjugates and bins (0, 0), (0, 5) are real: 110 independent real values.
+// With the channels as M each anchor's independent spectrum is one GEMM,
+// S[128 ch x 112] = A[128 ch x 112 px] Dft, the Dft columns (bf16 hi + lo)
+//   2b, 2b+1  re, im of complex bin b: b < 44 -> (ky = b % 11, kx = 1 + b / 11),
+//             44 <= b < 54 -> (ky = 1 + (b - 44) % 5, kx = b < 49 ? 0 : 5)
+//   108, 109  bins (0, 0) and (0, 5) (real)
+//   110, 111  zero.
+// The per-bin products R conj(L), |R conj(L)| and their channel sums are the
+// epilogue; the mirrored bins take the conjugate of their partner's sums.
+constexpr int kParDftChunkBytes = kParN * 128;             // one 64-pixel K chunk: 14336
+constexpr int kParDftHalfBytes = 2 * kParDftChunkBytes;    // hi or lo: 28672
+constexpr int kParDftBytes = 2 * kParDftHalfBytes;         // 57344
+constexpr int kParCplx = 54;                               // independent complex bins
+constexpr int kParStatVals = 3 * 48 + 24;                  // per-warp sums staged per item
+
+struct ParStatSmem {
+  static constexpr int a = 0;                          // 2 buffers x 2 x kParAHalfBytes
+  static constexpr int b = 4 * kParAHalfBytes;         // kParDftBytes
+  static constexpr int wsum = b + kParDftBytes;        // [4 warps][kParStatVals] floats
+  static constexpr int bars = wsum + 4 * kParStatVals * 4;  // b_full, mma_done[2]
+  static constexpr int tmem_slot = bars + 24;
+  static constexpr int total = tmem_slot + 8;
+  static constexpr int alloc = total + 1024;
+};
+
+// (ky, kx) of independent complex bin b (layout above).
+__device__ __forceinline__ void par_cplx_bin(int b, int &ky, int &kx) {
+  if (b < 44) {
+    ky = b % kParTH;
+    kx = 1 + b / kParTH;
+  } else {
+    ky = 1 + (b - 44) % 5;
+    kx = b < 49 ? 0 : kParWF - 1;
+  }
+}
+
+// One thread per (Dft column n, 8 consecutive pixels): element (n, q) at K
+// chunk q/64, row n, 16-byte group (q%64)/8 swizzled by n & 7; hi at 0, lo
+// at kParDftHalfBytes.
+__global__ void __launch_bounds__(256) par_dft_kernel(const __grid_constant__ ParParams p) {
+  __shared__ ParTables tab;
+  par_tables_to_smem(p.tab, tab);
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= kParN * (kParN / 8)) return;
+  const int n = e / (kParN / 8), g = e % (kParN / 8);
+  int ky = 0, kx = 0;
+  if (n < 2 * kParCplx) par_cplx_bin(n >> 1, ky, kx);
+  else kx = n == 2 * kParCplx ? 0 : kParWF - 1;
+  const bool im = n < 2 * kParCplx && (n & 1);
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    float v[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int q = g * 8 + j + u;
+      float val = 0.0f;
+      if (n < 2 * kParCplx + 2 && q < kParPix) {
+        const int m = (10 * ky * (q / kParTW) + 11 * kx * (q % kParTW)) % kParPix;
+        val = tab.win[q] * (im ? -tab.s110[m] : tab.c110[m]);
+      }
+      v[u] = val;
+    }
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[0], v[1]);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(v[0] - hf.x, v[1] - hf.y);
+    hi[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+    lo[j / 2] = *reinterpret_cast<const uint32_t *>(&l);
+  }
+  const int kc = g / 8, grp = g % 8;
+  const size_t off = (size_t)kc * kParDftChunkBytes + (size_t)n * 128 + ((grp ^ (n & 7)) * 16);
+  *reinterpret_cast<uint4 *>(p.dft + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4 *>(p.dft + kParDftHalfBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+// One halving step of a warp reduce-scatter: lanes with bit OFF set keep the
+// upper half of v[0..N), the others the lower half, each adding its
+// partner's copy of the kept half.
+template <int N, int OFF>
+__device__ __forceinline__ void par_rs_step(float *v, int lane) {
+  constexpr int H = N / 2;
+  const bool up = (lane & OFF) != 0;
+#pragma unroll
+  for (int i = 0; i < H; ++i) {
+    const float send = up ? v[i] : v[H + i];
+    const float keep = up ? v[H + i] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+  }
+}
+
+// Warp sums of v[0..48): lane L ends with the sums of values base .. base+2,
+// base = 24 [L&16] + 12 [L&8] + 6 [L&4] + 3 [L&2]; stored by even lanes.
+__device__ __forceinline__ void par_warp_sum48(float (&v)[48], int lane, float *out) {
+  par_rs_step<48, 16>(v, lane);
+  par_rs_step<24, 8>(v, lane);
+  par_rs_step<12, 4>(v, lane);
+  par_rs_step<6, 2>(v, lane);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], 1);
+  const int base = ((lane & 16) ? 24 : 0) + ((lane & 8) ? 12 : 0) + ((lane & 4) ? 6 : 0) + ((lane & 2) ? 3 : 0);
+  if ((lane & 1) == 0) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) out[base + i] = v[i];
+  }
+}
+
+// Warp sums of v[0..24): base = 12 [L&16] + 6 [L&8] + 3 [L&4]; stored by
+// lanes with L & 3 == 0.
+__device__ __forceinline__ void par_warp_sum24(float (&v)[24], int lane, float *out) {
+  par_rs_step<24, 16>(v, lane);
+  par_rs_step<12, 8>(v, lane);
+  par_rs_step<6, 4>(v, lane);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    v[i] += __shfl_xor_sync(0xffffffffu, v[i], 2);
+    v[i] += __shfl_xor_sync(0xffffffffu, v[i], 1);
+  }
+  const int base = ((lane & 16) ? 12 : 0) + ((lane & 8) ? 6 : 0) + ((lane & 4) ? 3 : 0);
+  if ((lane & 3) == 0) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) out[base + i] = v[i];
+  }
+}
+
+// Persistent: grid <= number of items (chunk of 128 channels, tile, pair),
+// kParStatThreads threads; CTA i takes items i, i + grid, ...  Two A buffers
+// and two TMEM halves: the gather of the next item runs under this item's
+// MMAs and epilogue.  Warp w reads TMEM lanes 32 (w % 4) .. +31 (channels)
+// and column group w / 4.  Writes the partials of each item's chunk (sums
+// over its channels: lane butterflies, then the four lane quarters in order).
+constexpr int kParStatThreads = 512;
+__global__ void __launch_bounds__(kParStatThreads, 1) par_stats_mma_kernel(const __grid_constant__ ParParams p) {
+  extern __shared__ uint8_t par_smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(par_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *b_full = reinterpret_cast<uint64_t *>(smem + ParStatSmem::bars);
+  uint64_t *mma_done = b_full + 1;  // per TMEM half
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + ParStatSmem::tmem_slot);
+  float *wsum = reinterpret_cast<float *>(smem + ParStatSmem::wsum);
+  int *err = &g_cast_device_error;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_items = p.n_stat_chunks * kParTiles * p.n_pairs;
+
+  if (threadIdx.x == 0) {
+    castdev::mbar_init(b_full, 1);
+    castdev::mbar_init(&mma_done[0], 1);
+    castdev::mbar_init(&mma_done[1], 1);
+    castdev::fence_barrier_init();
+    castdev::mbar_arrive_expect_tx(b_full, kParDftBytes);
+    castdev::bulk_load(smem + ParStatSmem::b, p.dft, kParDftBytes, b_full);
+  }
+  if (warp == 0) {
+    castdev::tmem_alloc(tmem_slot, 512);
+    castdev::tmem_relinquish();
+  }
+  auto gather = [&](int it, int buf) {
+    const int chunk = it % p.n_stat_chunks, tile = (it / p.n_stat_chunks) % kParTiles;
+    const int pair = it / (p.n_stat_chunks * kParTiles);
+    par_gather_anchors(p, pair, tile, chunk, smem + ParStatSmem::a + buf * 2 * kParAHalfBytes);
+  };
+  const uint32_t sbase = castdev::smem_u32(smem);
+  auto issue = [&](int buf, uint32_t tmem) {  // thread 0
+    castdev::tc_fence_after();
+    constexpr uint32_t idesc = castdev::make_idesc(1, 1, 1, 1, 0, 128, kParN);
+    const uint32_t a0 = sbase + ParStatSmem::a + buf * 2 * kParAHalfBytes;
+#pragma unroll 1
+    for (int side = 0; side < 2; ++side) {  // left anchor -> columns 0.., right -> 112..
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {  // Dft hi, then Dft lo
+#pragma unroll
+        for (int s = 0; s < kParN / 16; ++s) {
+          const uint64_t ad =
+              castdev::smem_desc_sw128(a0 + 2048 * (side * (kParN / 16) + s), kParAHalfBytes, 1024);
+          const uint64_t bd = castdev::smem_desc_sw128(
+              sbase + ParStatSmem::b + half * kParDftHalfBytes + (s >> 2) * kParDftChunkBytes + (s & 3) * 32,
+              16, 1024);
+          castdev::mma_f16_ss(tmem + buf * 2 * kParN + side * kParN, ad, bd, idesc, (half | s) != 0);
+        }
+      }
+    }
+    castdev::tc_commit(&mma_done[buf]);
+  };
+
+  int it = blockIdx.x;
+  gather(it, 0);
+  castdev::fence_proxy_async_smem();
+  __syncthreads();
+  castdev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  if (threadIdx.x == 0) {
+    ok = castdev::mbar_wait(b_full, 0, err);
+    if (ok) issue(0, tmem);
+  }
+  ok = __syncthreads_and(ok);
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  for (int k = 0; ok && it < n_items; ++k, it += gridDim.x) {
+    const int buf = k & 1;
+    const int next = it + gridDim.x;
+    if (next < n_items) gather(next, buf ^ 1);  // cp.async: lands under this item's work
+    // one thread polls the barrier, the others sleep in the block barrier:
+    // polling warps would take shared-memory bandwidth from the MMAs
+    int done_i = 1;
+    if (threadIdx.x == 0) done_i = castdev::mbar_wait(&mma_done[buf], (k >> 1) & 1, err);
+    const bool done = __syncthreads_and(done_i) != 0;
+    castdev::tc_fence_after();
+    const int grp = warp >> 2;
+    float *wout = wsum + (warp & 3) * kParStatVals;
+    const uint32_t tl = tmem + lane_off + buf * 2 * kParN;
+    if (grp < 3) {  // complex bins 16 grp .. 16 grp + 15
+      uint32_t l[32], r[32];
+      castdev::tmem_ld32(tl + 32 * grp, l);
+      castdev::tmem_ld32(tl + kParN + 32 * grp, r);
+      castdev::tmem_wait_ld();
+      float v[48];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float lr = __uint_as_float(l[2 * j]), li = __uint_as_float(l[2 * j + 1]);
+        const float rr = __uint_as_float(r[2 * j]), ri = __uint_as_float(r[2 * j + 1]);
+        const float cre = rr * lr + ri * li, cim = ri * lr - rr * li;
+        v[3 * j] = cre;
+        v[3 * j + 1] = cim;
+        v[3 * j + 2] = sqrtf(cre * cre + cim * cim);
+      }
+      par_warp_sum48(v, lane, wout + 48 * grp);
+    } else {  // complex bins 48..53, then the real bins (0, 0) and (0, 5)
+      uint32_t l[16], r[16];
+      castdev::tmem_ld16(tl + 96, l);
+      castdev::tmem_ld16(tl + kParN + 96, r);
+      castdev::tmem_wait_ld();
+      float v[24];
+#pragma unroll
+      for (int j = 0; j < 6; ++j) {
+        const float lr = __uint_as_float(l[2 * j]), li = __uint_as_float(l[2 * j + 1]);
+        const float rr = __uint_as_float(r[2 * j]), ri = __uint_as_float(r[2 * j + 1]);
+        const float cre = rr * lr + ri * li, cim = ri * lr - rr * li;
+        v[3 * j] = cre;
+        v[3 * j + 1] = cim;
+        v[3 * j + 2] = sqrtf(cre * cre + cim * cim);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float cre = __uint_as_float(r[12 + j]) * __uint_as_float(l[12 + j]);
+        v[18 + 2 * j] = cre;
+        v[19 + 2 * j] = sqrtf(cre * cre);
+      }
+      v[22] = v[23] = 0.0f;
+      par_warp_sum24(v, lane, wout + 144);
+    }
+    castdev::tc_fence_before();
+    __syncthreads();
+    if (done) {
+      const int chunk = it % p.n_stat_chunks, tile = (it / p.n_stat_chunks) % kParTiles;
+      const int pair = it / (p.n_stat_chunks * kParTiles);
+      float *dst = p.partials + (((size_t)pair * kParTiles + tile) * p.n_stat_chunks + chunk) * kParPartial;
+      for (int r = threadIdx.x; r < kParPartial; r += blockDim.x) {
+        const int qn = r / kParFreq, f = r % kParFreq, ky = f / kParWF, kx = f % kParWF;
+        int vi = -1;
+        float sign = 1.0f;
+        if (kx >= 1 && kx <= 4) {
+          const int b = (kx - 1) * kParTH + ky;
+          vi = b < 48 ? 48 * (b / 16) + 3 * (b % 16) + qn : 144 + 3 * (b - 48) + qn;
+        } else if (ky == 0) {
+          vi = qn == 1 ? -1 : 144 + 18 + (kx ? 2 : 0) + (qn ? 1 : 0);
+        } else {
+          const int kk = ky <= 5 ? ky : kParTH - ky;
+          if (ky > 5 && qn == 1) sign = -1.0f;
+          const int b = 44 + (kx ? 5 : 0) + kk - 1;
+          vi = b < 48 ? 48 * (b / 16) + 3 * (b % 16) + qn : 144 + 3 * (b - 48) + qn;
+        }
+        float acc = 0.0f;
+        if (vi >= 0) {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) acc += wsum[w * kParStatVals + vi];
+        }
+        dst[r] = sign * acc;
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    castdev::fence_proxy_async_smem();
+    bool step_ok = done;
+    ok = __syncthreads_and(step_ok);  // also orders the wsum reads before the next item's writes
+    if (ok && threadIdx.x == 0 && next < n_items) issue(buf ^ 1, tmem);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  // the bulk copy has landed before TMEM is released and the block exits
+  if (threadIdx.x == 0) castdev::mbar_wait_drain(b_full, 0, err);
   __syncthreads();
   if (warp == 0) {
     castdev::tc_fence_after();
