@@ -73,6 +73,24 @@ int make_map_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, i
   return CAST_OK;
 }
 
+// 4-D tiled map over a dense [d3][d2][d1][d0] tensor, box (box0, box1, box2, 1).
+int make_map_4d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes,
+                uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint32_t box0, uint32_t box1,
+                uint32_t box2, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc;
+  int st = get_encode_tiled(&enc);
+  if (st) return st;
+  cuuint64_t dims[4] = {d0, d1, d2, d3};
+  cuuint64_t strides[3] = {d0 * elem_bytes, d0 * d1 * elem_bytes, d0 * d1 * d2 * elem_bytes};
+  cuuint32_t box[4] = {box0, box1, box2, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype, 4, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CAST_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return CAST_OK;
+}
+
 }  // namespace cast
 
 using namespace cast;
@@ -575,8 +593,15 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
     if (predict_mma) {
       castk::par_filter_kernel<<<dim3(castk::kParTiles, nt, castk::kParKChunks), 256, 0, s>>>(p);
       CAST_CUDA_TRY(cudaGetLastError());
-      castk::par_predict_mma_kernel<<<dim3(ceil_div(C, 128), castk::kParTiles, p.n_pairs), 128,
-                                      castk::ParMmaSmem::alloc, s>>>(p);
+      // anchor frames as (channel, column, row, frame); one box of 64 channels
+      // x 10 columns x 11 rows per tile, side and channel half
+      CUtensorMap tm_act;
+      if ((st = make_map_4d(&tm_act, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, W, H, n_active, 64,
+                            castk::kParTW, castk::kParTH, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+      const int n_units = nt * castk::kParTiles * ceil_div(C, 128);
+      castk::par_predict_mma_kernel<<<std::min(n_units, num_sms), castk::kParPredThreads,
+                                      castk::ParMmaSmem::alloc, s>>>(tm_act, p);
       CAST_CUDA_TRY(cudaGetLastError());
     } else {
       castk::par_predict_kernel<<<g1, castk::kParChunk, smem_pred, s>>>(p);

@@ -1,8 +1,8 @@
 // Phase-Aware Reconstruction (FC-PASM reference numerics) for sm_100a.
 //
 // Restates proposed/matrix_world_spectral_residual.py:2771-3662 with the
-// factory knobs.  The 11x10 tile transforms are small direct real DFTs done in
-// registers (one thread per channel); nothing here is GEMM-shaped.
+// factory knobs.  Per-channel path (any C): the 11x10 tile transforms are
+// small direct real DFTs in registers (one thread per channel).
 //
 //   par_stats_kernel     grid (chunk, tile, pair): windowed reflect-padded
 //                        anchor tiles -> rfft2 -> per-chunk channel sums of
@@ -16,23 +16,34 @@
 //   par_ola_kernel       grid (pixel, target): normalised overlap-add, bf16
 //                        write of the target frame                (writes)
 //
-// Tensor-core prediction (used when C % 8 == 0 and a pair has at most
-// kParMmaTargets targets): the whole per-tile chain analysis window -> rfft2
-// -> per-frequency mix -> irfft2 -> synthesis window is linear in the two
-// anchor tiles and circular in the pixel offset, so a target's predicted
-// tile is pred = F_L l + F_R r with F[p][q] = win[p] win[q] kern[(p - q) mod
-// (11, 10)] and kern[d] = (1/110) sum_f c_kx Re(w_f e^{i w_f . d}) (c_kx = 1
-// for kx = 0, 5, else 2: the c2r rows).
+// Tensor-core paths (used when C % 8 == 0 and the anchors are 16-byte
+// aligned; the prediction also needs at most kParMmaTargets targets per
+// pair).  The statistics' rfft2 is a fixed linear map of a tile's pixels,
+// and the whole prediction chain analysis window -> rfft2 -> per-frequency
+// mix -> irfft2 -> synthesis window is linear in the two anchor tiles and
+// circular in the pixel offset: a target's predicted tile is
+// pred = F_L l + F_R r with F[p][q] = win[p] win[q] kern[(p - q) mod (11, 10)]
+// and kern[d] = (1/110) sum_f c_kx Re(w_f e^{i w_f . d}) (c_kx = 1 for
+// kx = 0, 5, else 2: the c2r rows).  Both become GEMMs with the channels as M.
+//   par_dft_kernel       the windowed rfft2 matrix (110 independent real
+//                        columns) as a bf16 hi + lo K-major image
+//   par_stats_mma_kernel persistent over (128-channel chunk, tile, pair):
+//                        anchor tiles gathered with cp.async into two
+//                        buffers, spectra by tcgen05.mma into two TMEM
+//                        halves, R conj(L) and |R conj(L)| summed over the
+//                        chunk's channels by warp butterflies -> partials
+//   par_finalize_kernel  as above
 //   par_filter_kernel    grid (tile, target, K chunk): kern for L and R from
 //                        the mix weights, then F as bf16 hi + lo (the pair
 //                        carries ~16 significant bits) in the shared-memory
-//                        image the MMA reads
-//   par_predict_mma_kernel grid (128-channel chunk, tile, pair): the anchor
-//                        pixels of the tile gathered by TMA (one 64-channel
-//                        row per load; reflect padding is in the row index),
-//                        D[128 ch x 112 px] = A[128 ch x 224 (L|R px)] F via
-//                        tcgen05.mma (A MN-major, F K-major, fp32 in TMEM),
-//                        then the predicted tiles to the workspace
+//                        image the MMA reads, in the slot order of the
+//                        prediction's TMA boxes
+//   par_predict_mma_kernel persistent over (target, tile, 128-channel
+//                        chunk): one TMA box per anchor and channel half,
+//                        D[128 ch x 112 px] = A[128 ch x 224 (L|R slots)] F
+//                        via tcgen05.mma (A MN-major, F K-major, fp32 in
+//                        TMEM), then the predicted tiles to the workspace
+//   par_ola_kernel       as above
 #pragma once
 
 #include "common.cuh"
@@ -85,6 +96,7 @@ struct ParParams {
   ParTables tab;
 };
 
+
 __device__ __forceinline__ int reflect_idx(int i, int n) {
   if (i < 0) i = -i;
   if (i >= n) i = 2 * (n - 1) - i;
@@ -102,14 +114,35 @@ constexpr int kParFHalfBytes = kParKChunks * kParFChunkBytes;  // hi or lo: 5734
 constexpr int kParFilterBytes = 2 * kParFHalfBytes;            // 114688
 constexpr int kParAHalfBytes = kParK * 128;      // 64 channels x 224 rows: 28672
 
+// Prediction: two A buffers (2 x kParAHalfBytes each), one F image, then
+// a_full[2], b_full, mma_done[2], tmem_free[2] and the TMEM slot.
 struct ParMmaSmem {
-  static constexpr int a = 0;                          // 2 x kParAHalfBytes
-  static constexpr int b = 2 * kParAHalfBytes;         // kParFilterBytes
-  static constexpr int bars = b + kParFilterBytes;     // a_full, b_full, mma_done[4]
-  static constexpr int tmem_slot = bars + (2 + kParMmaTargets) * 8;
-  static constexpr int total = tmem_slot + 16;
+  static constexpr int a = 0;
+  static constexpr int b = 4 * kParAHalfBytes;
+  static constexpr int bars = b + kParFilterBytes;
+  static constexpr int tmem_slot = bars + 7 * 8;
+  static constexpr int total = tmem_slot + 8;
   static constexpr int alloc = total + 1024;
 };
+static_assert(ParMmaSmem::alloc <= 227 * 1024, "prediction shared memory");
+constexpr int kParEpiWarps = 8;                          // 2 per TMEM lane quarter
+constexpr int kParPredThreads = (kParEpiWarps + 1) * 32;  // + the producer / MMA warp
+constexpr int kParGatherBytes = 2 * 2 * kParPix * 128;     // both anchors, both channel halves
+
+// The tensor-core paths load a tile as one TMA box of 11 frame rows x 10
+// frame columns, clamped into the frame: every reflected pixel the tile
+// needs lies inside it.  Tile pixel (i, j) sits in box slot (r, s) =
+// (reflect(y) - y0, reflect(x) - x0); at the frame edges two tile pixels can
+// share a slot and some slots are unused, which the F and Dft images absorb
+// (coefficients of pixels sharing a slot are summed, unused slots are zero).
+__host__ __device__ __forceinline__ int par_box_y0(int gy) {
+  const int y = gy * kParStride - kParPadH;
+  return y < 0 ? 0 : (y > kParH - kParTH ? kParH - kParTH : y);
+}
+__host__ __device__ __forceinline__ int par_box_x0(int gx) {
+  const int x = gx * kParStride - kParPadW;
+  return x < 0 ? 0 : (x > kParW - kParTW ? kParW - kParTW : x);
+}
 
 // Kernel parameters live in the constant bank, which serves a warp one
 // distinct address at a time; kernels that index the tables per lane read a
@@ -343,50 +376,65 @@ __global__ void __launch_bounds__(kParChunk) par_stats_kernel(const ParParams p)
 // lo (the pair carries ~16 significant bits) in the shared-memory image the
 // MMA reads.
 struct ParFilterSmem {
-  float wl_re[kParFreq], wl_im[kParFreq], wr_re[kParFreq], wr_im[kParFreq];
+  float w[kParFreq][4];                   // wl_re, wl_im, wr_re, wr_im per bin
+  float zr[2][kParTH][kParTW], zi[2][kParTH][kParTW];
   float kern[2][kParPix];
+  uint32_t slot[kParPix];  // tile pixels in box slot: i0 | i1 << 4 | j0 << 8 | j1 << 12 | rows << 16 | cols << 20
 };
 __device__ __forceinline__ void par_build_filter(const ParParams &p, const ParTables &tab, int tile, int tg,
                                                  int kc0, int kc1, ParFilterSmem &fs) {
-  float *wl_re = fs.wl_re, *wl_im = fs.wl_im, *wr_re = fs.wr_re, *wr_im = fs.wr_im;
-  float(*kern)[kParPix] = fs.kern;
   const int t = threadIdx.x;
   const float *w = p.weights + ((size_t)tg * kParTiles + tile) * kParFreq * 4;
   __syncthreads();  // the previous target's reads of fs are done
-  if (t < kParFreq) {
-    wl_re[t] = w[4 * t];
-    wl_im[t] = w[4 * t + 1];
-    wr_re[t] = w[4 * t + 2];
-    wr_im[t] = w[4 * t + 3];
+  for (int e = t; e < kParFreq * 4; e += blockDim.x) fs.w[e / 4][e % 4] = w[e];
+  if (t < kParPix) {  // which tile rows / columns land in box slot t
+    const int gy = tile / kParGW, gx = tile % kParGW, r = t / kParTW, sx = t % kParTW;
+    uint32_t rows = 0, cols = 0, packed = 0;
+    for (int i = 0; i < kParTH; ++i)
+      if (reflect_idx(gy * kParStride + i - kParPadH, kParH) - par_box_y0(gy) == r && rows < 2)
+        packed |= (uint32_t)i << (4 * rows++);
+    for (int j = 0; j < kParTW; ++j)
+      if (reflect_idx(gx * kParStride + j - kParPadW, kParW) - par_box_x0(gx) == sx && cols < 2)
+        packed |= (uint32_t)j << (8 + 4 * cols++);
+    fs.slot[t] = packed | rows << 16 | cols << 20;
   }
   __syncthreads();
+  // kern[d] = (1/110) sum_f c_kx Re(w_f e^{i(2 pi ky dy / 11 + 2 pi kx dx / 10)}),
+  // c_kx = 1 for kx = 0, 5 and 2 otherwise: first over kx per (ky, dx) ...
   if (t < 2 * kParPix) {
-    const int side = t / kParPix, d = t % kParPix;
-    const int dy = d / kParTW, dx = d % kParTW;
-    const float *are = side ? wr_re : wl_re, *aim = side ? wr_im : wl_im;
-    float acc = 0.0f;
-    for (int ky = 0; ky < kParTH; ++ky) {
-      const int my = (ky * dy) % kParTH;
-      const float cy = tab.ch[my], sy = tab.shh[my];
-      for (int kx = 0; kx < kParWF; ++kx) {
-        const int mx = (kx * dx) % kParTW;
-        const float cx = tab.cw[mx], sx = tab.sw[mx];
-        // e^{i(2pi ky dy/11 + 2pi kx dx/10)}
-        const float er = cy * cx - sy * sx, ei = sy * cx + cy * sx;
-        const int f = ky * kParWF + kx;
-        const float re = are[f] * er - aim[f] * ei;
-        acc += (kx == 0 || kx == kParWF - 1) ? re : 2.0f * re;
-      }
+    const int side = t / kParPix, ky = (t % kParPix) / kParTW, dx = t % kParTW;
+    float zr = 0.0f, zi = 0.0f;
+#pragma unroll
+    for (int kx = 0; kx < kParWF; ++kx) {
+      const int m = (kx * dx) % kParTW;
+      const float c = (kx == 0 || kx == kParWF - 1) ? 1.0f : 2.0f;
+      const float wr = c * fs.w[ky * kParWF + kx][2 * side], wi = c * fs.w[ky * kParWF + kx][2 * side + 1];
+      zr += wr * tab.cw[m] - wi * tab.sw[m];
+      zi += wr * tab.sw[m] + wi * tab.cw[m];
     }
-    kern[side][d] = acc * (1.0f / (float)kParPix);
+    fs.zr[side][ky][dx] = zr;
+    fs.zi[side][ky][dx] = zi;
   }
   __syncthreads();
-  // F image: element (n, k) at chunk k/64, row n, 16-byte group (k%64)/8
+  // ... then over ky per (dy, dx)
+  if (t < 2 * kParPix) {
+    const int side = t / kParPix, dy = (t % kParPix) / kParTW, dx = t % kParTW;
+    float acc = 0.0f;
+#pragma unroll
+    for (int ky = 0; ky < kParTH; ++ky) {
+      const int m = (ky * dy) % kParTH;
+      acc += fs.zr[side][ky][dx] * tab.ch[m] - fs.zi[side][ky][dx] * tab.shh[m];
+    }
+    fs.kern[side][t % kParPix] = acc * (1.0f / (float)kParPix);
+  }
+  __syncthreads();
+// F image: element (n, k) at chunk k/64, row n, 16-byte group (k%64)/8
   // swizzled by n & 7 (128-byte swizzle, K-major).
   uint8_t *img = p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes;
   const int g0 = kc0 * 8, ng = min(kc1 * 8, kParK / 8) - g0;
   for (int e = t; e < kParN * ng; e += blockDim.x) {
     const int n = e / ng, g = g0 + e % ng;  // 8 consecutive k
+    const int ny = n / kParTW, nx = n % kParTW;
     uint32_t hi[4], lo[4];
 #pragma unroll
     for (int j = 0; j < 8; j += 2) {
@@ -396,11 +444,25 @@ __device__ __forceinline__ void par_build_filter(const ParParams &p, const ParTa
         const int k = g * 8 + j + u;
         float f = 0.0f;
         const int side = k < kParN ? 0 : 1;
-        const int q = k - side * kParN;
-        if (n < kParPix && q < kParPix) {
-          const int dy = (n / kParTW - q / kParTW + kParTH) % kParTH;
-          const int dx = (n % kParTW - q % kParTW + kParTW) % kParTW;
-          f = tab.win[n] * tab.win[q] * kern[side][dy * kParTW + dx];
+        const int slot = k - side * kParN;  // box slot r * 10 + s
+        if (n < kParPix && slot < kParPix) {
+          // sum over the (at most 2 x 2) tile pixels in this slot
+          const uint32_t sm = fs.slot[slot];
+          const int rows = (sm >> 16) & 3, cols = (sm >> 20) & 3;
+#pragma unroll
+          for (int a = 0; a < 2; ++a) {
+            const int i = (sm >> (4 * a)) & 15;
+            int dy = ny - i;
+            dy += dy < 0 ? kParTH : 0;
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              const int j = (sm >> (8 + 4 * b)) & 15;
+              int dx = nx - j;
+              dx += dx < 0 ? kParTW : 0;
+              if (a < rows && b < cols) f += tab.win[i * kParTW + j] * fs.kern[side][dy * kParTW + dx];
+            }
+          }
+          f *= tab.win[n];
         }
         v[u] = f;
       }
@@ -663,118 +725,176 @@ __device__ __forceinline__ void par_gather_anchors(const ParParams &p, int pair,
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-// grid (chunk of 128 channels, tile, pair), 128 threads.
-__global__ void __launch_bounds__(128, 1)
-    par_predict_mma_kernel(const ParParams p) {
+// Persistent tensor-core prediction.  Units (target, tile, chunk of 128
+// channels) in that order; CTA c takes the contiguous range
+// [c U / grid, (c + 1) U / grid), so F (per target and tile) changes at most
+// a few times per CTA and stays resident in between.  Warp kParEpiWarps
+// gathers the anchor tiles by TMA into two A buffers (one 64 x 10 x 11 box
+// per anchor and channel half; slot order as par_box_y0 / par_box_x0) and
+// issues the MMAs into two TMEM halves (lane 0); warps 0 .. 7 move D to the workspace (warp w:
+// TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..).  Every wait is bounded;
+// a failed wait stops the warp's loop and sets the device error.
+__global__ void __launch_bounds__(kParPredThreads, 1)
+    par_predict_mma_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ ParParams p) {
   extern __shared__ uint8_t par_smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(par_smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ParMmaSmem::bars);
-  uint64_t *b_full = bars + 1;
-  uint64_t *mma_done = bars + 2;  // one per target of the pair: each completes once
+  uint64_t *a_full = bars, *b_full = bars + 2, *mma_done = bars + 3, *tmem_free = bars + 5;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + ParMmaSmem::tmem_slot);
   int *err = &g_cast_device_error;
-  const int chunk = blockIdx.x, tile = blockIdx.y, pair = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // this pair's targets in order (at most kParMmaTargets, checked by the host)
-  int tgs[kParMmaTargets];
-  int n_loc = 0;
-  for (int tg = 0; tg < p.n_targets; ++tg)
-    if (p.target_pair[tg] == pair && n_loc < kParMmaTargets) tgs[n_loc++] = tg;
-  // F of target `local` into B (thread 0); B is free: the MMAs of the
-  // previous target have completed
-  int b_loads = 0;
-  auto load_f = [&](int local) {
-    castdev::mbar_arrive_expect_tx(b_full, kParFilterBytes);
-    castdev::bulk_load(smem + ParMmaSmem::b,
-                       p.filters + ((size_t)tgs[local] * kParTiles + tile) * kParFilterBytes,
-                       kParFilterBytes, b_full);
-    ++b_loads;
-  };
+  const int nch = (p.C + 127) / 128;
+  const int n_units = p.n_targets * kParTiles * nch;
+  const int u0 = (int)((long long)blockIdx.x * n_units / gridDim.x);
+  const int u1 = (int)((long long)(blockIdx.x + 1) * n_units / gridDim.x);
+  const int n = u1 - u0;
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      castdev::mbar_init(&a_full[i], 1);
+      castdev::mbar_init(&mma_done[i], 1);
+      castdev::mbar_init(&tmem_free[i], kParEpiWarps);
+    }
     castdev::mbar_init(b_full, 1);
-    for (int i = 0; i < kParMmaTargets; ++i) castdev::mbar_init(&mma_done[i], 1);
     castdev::fence_barrier_init();
-    if (n_loc > 0) load_f(0);  // lands under the anchor gather
   }
-  if (warp == 0) {
-    castdev::tmem_alloc(tmem_slot, 512);
+  if (warp == kParEpiWarps) {
+    castdev::tmem_alloc(tmem_slot, 256);
     castdev::tmem_relinquish();
   }
-
-  par_gather_anchors(p, pair, tile, chunk, smem + ParMmaSmem::a);
-
-  // the cp.async writes and the zero rows are generic-proxy writes the MMAs
-  // (async proxy) read
+  // K padding rows 110, 111, 222, 223 of both channel halves of both buffers
+  // (the gather never writes them)
+  for (int e = threadIdx.x; e < 2 * 2 * 4 * 8; e += blockDim.x) {
+    const int buf = e / 64, h = (e / 32) % 2, r = (e / 8) % 4, c16 = e % 8;
+    const int row = r < 2 ? kParPix + r : kParN + kParPix + (r - 2);
+    *reinterpret_cast<uint4 *>(smem + ParMmaSmem::a + buf * 2 * kParAHalfBytes + h * kParAHalfBytes +
+                               row * 128 + c16 * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
   castdev::fence_proxy_async_smem();
   __syncthreads();
   castdev::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const uint32_t sbase = castdev::smem_u32(smem);
-  constexpr uint32_t idesc = castdev::make_idesc(1, 1, 1, 1, 0, 128, kParN);
-  bool ok = true;  // thread 0's view
-  for (int local = 0; local < n_loc; ++local) {
-    const int tg = tgs[local];
-    const uint32_t d_col = tmem + local * kParN;
-    int done_i = 1;
-    if (threadIdx.x == 0) {
-      if (ok) ok = castdev::mbar_wait(b_full, local & 1, err);
-      if (ok) {
-        castdev::tc_fence_after();
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {  // F hi, then F lo
-#pragma unroll
-          for (int s = 0; s < kParK / 16; ++s) {
-            const uint64_t ad = castdev::smem_desc_sw128(sbase + ParMmaSmem::a + 2048 * s,
-                                                         kParAHalfBytes, 1024);
-            const uint64_t bd = castdev::smem_desc_sw128(
-                sbase + ParMmaSmem::b + half * kParFHalfBytes + (s >> 2) * kParFChunkBytes +
-                    (s & 3) * 32,
-                16, 1024);
-            castdev::mma_f16_ss(d_col, ad, bd, idesc, (half | s) != 0);
-          }
-        }
-        castdev::tc_commit(&mma_done[local]);
-        ok = castdev::mbar_wait(&mma_done[local], 0, err);
+  if (warp == kParEpiWarps) {
+    // ---- producer / MMA issuer ------------------------------------------
+    const uint32_t sbase = castdev::smem_u32(smem);
+    constexpr uint32_t idesc = castdev::make_idesc(1, 1, 1, 1, 0, 128, kParN);
+    int g_issued[2] = {0, 0}, g_waited[2] = {0, 0};  // gathers per A buffer
+    int f_loads = 0, f_waited = 0;
+    // all of the issuer's work is lane 0's; the other lanes wait at the shuffles
+    auto gather = [&](int k) {  // unit u0 + k into buffer k & 1: one box per anchor and channel half
+      const int u = u0 + k, buf = k & 1;
+      const int grp = u / nch, chunk = u % nch, tile = grp % kParTiles, tg = grp / kParTiles;
+      const int pair = p.target_pair[tg], gy = tile / kParGW, gx = tile % kParGW;
+      castdev::mbar_arrive_expect_tx(&a_full[buf], kParGatherBytes);
+      for (int e = 0; e < 4; ++e) {
+        const int h = e & 1, side = e >> 1;
+        castdev::tma_load_4d(smem + ParMmaSmem::a + buf * 2 * kParAHalfBytes + h * kParAHalfBytes + side * kParN * 128,
+                             &tm_act, &a_full[buf], chunk * 128 + h * 64, par_box_x0(gx), par_box_y0(gy),
+                             side ? p.pair_right[pair] : p.pair_left[pair]);
       }
-      // the next target's F lands under this target's epilogue
-      if (ok && local + 1 < n_loc) load_f(local + 1);
-      done_i = ok;
+      ++g_issued[buf];
+    };
+    auto load_f = [&](int k) {
+      const int grp = (u0 + k) / nch, tile = grp % kParTiles, tg = grp / kParTiles;
+      castdev::mbar_arrive_expect_tx(b_full, kParFilterBytes);
+      castdev::bulk_load(smem + ParMmaSmem::b, p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes,
+                         kParFilterBytes, b_full);
+      ++f_loads;
+    };
+    bool ok = true;
+    if (lane == 0 && n > 0) {
+      castdev::tma_prefetch_desc(&tm_act);
+      load_f(0);
+      gather(0);
+      if (n > 1) gather(1);
     }
-    // one thread polls the barriers, the others sleep in the block barrier
-    // (polling warps would take shared-memory bandwidth from the MMAs)
-    const bool done = __syncthreads_and(done_i) != 0;
-    castdev::tc_fence_after();
-    // epilogue: this target's 110 predicted pixels for the warp's 32 channels
-    const int c = chunk * 128 + warp * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    float *dst = p.pred + ((size_t)tg * kParTiles + tile) * kParPix * p.C + c;
+    for (int k = 0; k < n && ok; ++k) {
+      const int buf = k & 1;
+      if (lane == 0) {
+        if (k >= 1) {
+          // unit k - 1's MMAs have completed: its A buffer takes unit k + 1,
+          // and B may take a new F
+          ok = castdev::mbar_wait(&mma_done[(k - 1) & 1], ((k - 1) >> 1) & 1, err);
+          if (ok && k + 1 < n) gather(k + 1);
+          if (ok && (u0 + k) / nch != (u0 + k - 1) / nch) load_f(k);
+        }
+        if (ok && f_waited < f_loads) {
+          ok = castdev::mbar_wait(b_full, (f_loads - 1) & 1, err);
+          f_waited = f_loads;
+        }
+        if (ok) {
+          ok = castdev::mbar_wait(&a_full[buf], (k >> 1) & 1, err);
+          ++g_waited[buf];
+        }
+        if (ok && k >= 2) ok = castdev::mbar_wait(&tmem_free[buf], ((k - 2) >> 1) & 1, err);
+        if (ok) {
+          castdev::tc_fence_after();
+          const uint32_t a0 = sbase + ParMmaSmem::a + buf * 2 * kParAHalfBytes;
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t v[32];
-      if (cc < 3) {
-        castdev::tmem_ld32(tmem + lane_off + local * kParN + 32 * cc, v);
-      } else {
-        castdev::tmem_ld16(tmem + lane_off + local * kParN + 96, *reinterpret_cast<uint32_t(*)[16]>(v));
+          for (int half = 0; half < 2; ++half) {  // F hi, then F lo
+#pragma unroll
+            for (int s = 0; s < kParK / 16; ++s) {
+              const uint64_t ad = castdev::smem_desc_sw128(a0 + 2048 * s, kParAHalfBytes, 1024);
+              const uint64_t bd = castdev::smem_desc_sw128(
+                  sbase + ParMmaSmem::b + half * kParFHalfBytes + (s >> 2) * kParFChunkBytes + (s & 3) * 32,
+                  16, 1024);
+              castdev::mma_f16_ss(tmem + buf * kParN, ad, bd, idesc, (half | s) != 0);
+            }
+          }
+          castdev::tc_commit(&mma_done[buf]);
+        }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    // nothing the TMA unit writes may be in flight when the block exits
+    if (lane == 0) {
+      for (int b2 = 0; b2 < 2; ++b2)
+        if (g_issued[b2] > g_waited[b2]) castdev::mbar_wait_drain(&a_full[b2], (g_issued[b2] - 1) & 1, err);
+      if (f_loads > f_waited) castdev::mbar_wait_drain(b_full, (f_loads - 1) & 1, err);
+      if (n > 0) {  // the last MMAs have completed before TMEM is released
+        castdev::mbar_wait_drain(&mma_done[(n - 1) & 1], ((n - 1) >> 1) & 1, err);
+        if (n > 1) castdev::mbar_wait_drain(&mma_done[(n - 2) & 1], ((n - 2) >> 1) & 1, err);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: D -> predicted tiles (fp32, workspace) -----------------
+    const int q = warp & 3, colh = warp >> 2;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    for (int k = 0; k < n; ++k) {
+      const int buf = k & 1, u = u0 + k;
+      const int grp = u / nch, chunk = u % nch, tile = grp % kParTiles, tg = grp / kParTiles;
+      int okw = 1;
+      if (lane == 0) okw = castdev::mbar_wait(&mma_done[buf], (k >> 1) & 1, err);
+      if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+      castdev::tc_fence_after();
+      uint32_t v0[32], v1[32];
+      const uint32_t col = tmem + lane_off + buf * kParN + 64 * colh;
+      castdev::tmem_ld32(col, v0);
+      if (colh == 0) castdev::tmem_ld32(col + 32, v1);
+      else castdev::tmem_ld16(col + 32, *reinterpret_cast<uint32_t(*)[16]>(v1));
       castdev::tmem_wait_ld();
-      const int n_cols = cc < 3 ? 32 : kParPix - 96;
-      if (done && c < p.C) {
+      castdev::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) castdev::mbar_arrive(&tmem_free[buf]);
+      const int c = chunk * 128 + q * 32 + lane;
+      if (c < p.C) {
+        float *dst = p.pred + (((size_t)tg * kParTiles + tile) * kParPix + 64 * colh) * p.C + c;
+        const int n_cols = colh == 0 ? 64 : kParPix - 64;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dst[(size_t)j * p.C] = __uint_as_float(v0[j]);
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (j < n_cols) dst[(size_t)(32 * cc + j) * p.C] = __uint_as_float(v[j]);
+          if (32 + j < n_cols) dst[(size_t)(32 + j) * p.C] = __uint_as_float(v1[j]);
       }
     }
   }
-  // every TMA copy and MMA of this CTA has completed before TMEM is released
-  if (threadIdx.x == 0 && b_loads > 0) castdev::mbar_wait_drain(b_full, (b_loads - 1) & 1, err);
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kParEpiWarps) {
     castdev::tc_fence_after();
-    castdev::tmem_dealloc(tmem, 512);
+    castdev::tmem_dealloc(tmem, 256);
   }
 }
 
