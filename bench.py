@@ -37,9 +37,9 @@ METRIC = "RCSA int8 sparse-attn µs/call & % tensor-core peak; scaling at 1/2/4/
 BLOCK, BUDGET, HEADS, D = 880, 8, 24, 128
 HIST, CUR = 32, 4
 # DRAM bytes (read + write) of one attention launch on the full config-2
-# workload, from the ncu launch list in profiles/launches_rcsa_config2_auto.md
-# (auto policy); other policies have no capture.
-ATTN_TRAFFIC_BYTES = {"auto": 696.0e6}
+# workload (auto policy), from the single-pass ncu capture in
+# profiles/rcsa_attention_config2_traffic.md; other policies have no capture.
+ATTN_TRAFFIC_BYTES = {"auto": 712.4e6}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
