@@ -68,6 +68,38 @@ def test_par_config4_full_vs_restatement(cuda):
     assert np.abs(sample - g["sample"]).max() < 2e-3
 
 
+def _vs_restatement(wl):
+    out, _ = _run_gpu(wl)
+    ref = opar.correct(wl.full_residual.float().numpy(), wl.active_residual.float().numpy(),
+                       wl.active_frames, wl.memory_length, 22, 40)
+    ref_t = torch.from_numpy(ref).to(torch.bfloat16).float()
+    return (out.float() - ref_t).abs()
+
+
+@pytest.mark.parametrize("channels", [60, 200])
+def test_par_channel_edges(cuda, channels):
+    """C = 60 (C % 8 != 0) takes the per-channel DFT kernels; C = 200 the
+    tensor-core kernels with a ragged second 128-channel chunk (zero-filled
+    loads, masked stores)."""
+    d = _vs_restatement(workloads.config4(channels=channels))
+    print(f"C={channels}: max {float(d.max()):.3e} mean {float(d.mean()):.3e}")
+    assert float(d.max()) < 2e-3 and float(d.mean()) < MEAN_ABS
+
+
+def test_par_two_anchor_pairs(cuda):
+    """One memory frame, anchors at current frames 0, 3 | 4, 7 (the segment
+    boundary is 4): pairs (0, 3) with targets 1, 2 and (4, 7) with targets
+    5, 6 -- two pairs' statistics and four targets' F images and predicted
+    tiles in the persistent kernels' orderings; C = 136 leaves an 8-channel
+    second chunk."""
+    g = torch.Generator().manual_seed(11)
+    full = (torch.randn(1, 9, 880, 136, generator=g) * 0.02).to(torch.bfloat16)
+    wl = workloads.PARWorkload("two_pairs", full, [0, 1, 4, 5, 8], 1, 22, 40)
+    d = _vs_restatement(wl)
+    print(f"two pairs: max {float(d.max()):.3e} mean {float(d.mean()):.3e}")
+    assert float(d.max()) < 2e-3 and float(d.mean()) < MEAN_ABS
+
+
 def test_par_injected_confidence_exercises_phase(cuda):
     """Config 4's c~U(0,1) mode: per-tile confidence injected (the reference's
     precomputed_tile_confidence), g from the same sigmoid; compared with the
