@@ -388,7 +388,7 @@ extern "C" size_t cast_par_fcpasm_workspace_bytes(int T, int H, int W, int C) {
   const size_t pred = (size_t)nt * castk::kParTiles * castk::kParPix * C;
   const size_t filters = (size_t)nt * castk::kParTiles * castk::kParFilterBytes;
   return align_up(partials * 4, 256) + align_up(weights * 4, 256) + align_up(pred * 4, 256) +
-         align_up(filters, 1024) + align_up(castk::kParDftBytes, 1024);
+         align_up(filters, 1024) + align_up((size_t)castk::kParClasses * castk::kParDftBytes, 1024);
 }
 
 static void fill_par_tables(castk::ParTables &t, float tau_low, float tau_high, float power) {
@@ -409,10 +409,6 @@ static void fill_par_tables(castk::ParTables &t, float tau_low, float tau_high, 
   for (int k = 0; k < castk::kParTH; ++k) {
     t.ch[k] = (float)std::cos(2.0 * pi * k / castk::kParTH);
     t.shh[k] = (float)std::sin(2.0 * pi * k / castk::kParTH);
-  }
-  for (int m = 0; m < castk::kParPix; ++m) {
-    t.c110[m] = (float)std::cos(2.0 * pi * m / castk::kParPix);
-    t.s110[m] = (float)std::sin(2.0 * pi * m / castk::kParPix);
   }
   double fy[castk::kParTH], fx[castk::kParWF], rmax = 0.0;
   for (int k = 0; k < castk::kParTH; ++k) {
@@ -575,13 +571,45 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
       CAST_CUDA_TRY(mma_err);
     }
     dim3 g1(p.n_chunks, castk::kParTiles, p.n_pairs);
+    // anchor frames as (channel, column, row, frame); one box of 64 channels
+    // x 10 columns x 11 rows per tile, anchor and channel half
+    CUtensorMap tm_act;
+    if (mma_ok && (st = make_map_4d(&tm_act, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, W, H, n_active, 64,
+                                    castk::kParTW, castk::kParTH, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
     if (mma_ok) {
       p.n_stat_chunks = ceil_div(C, 128);
-      castk::par_dft_kernel<<<ceil_div(castk::kParN * (castk::kParN / 8), 256), 256, 0, s>>>(p);
+      // CTAs per tile class in proportion to its items, at least one each
+      int n_cls[castk::kParClasses], g_cls[castk::kParClasses];
+      long long total = 0;
+      for (int c = 0; c < castk::kParClasses; ++c) {
+        n_cls[c] = castk::par_class_tiles(c) * p.n_pairs * p.n_stat_chunks;
+        total += n_cls[c];
+      }
+      const int grid = (int)std::max<long long>(castk::kParClasses, std::min<long long>(num_sms, total));
+      int sum = 0;
+      for (int c = 0; c < castk::kParClasses; ++c) {
+        g_cls[c] = (int)std::max<long long>(1, (long long)grid * n_cls[c] / total);
+        sum += g_cls[c];
+      }
+      while (sum > grid) {  // take from the class with the most CTAs
+        int big = 0;
+        for (int c = 1; c < castk::kParClasses; ++c) big = g_cls[c] > g_cls[big] ? c : big;
+        --g_cls[big];
+        --sum;
+      }
+      while (sum < grid) {  // give to the class with the most items per CTA
+        int need = 0;
+        for (int c = 1; c < castk::kParClasses; ++c)
+          need = (long long)n_cls[c] * g_cls[need] > (long long)n_cls[need] * g_cls[c] ? c : need;
+        ++g_cls[need];
+        ++sum;
+      }
+      p.stat_cta_start[0] = 0;
+      for (int c = 0; c < castk::kParClasses; ++c) p.stat_cta_start[c + 1] = p.stat_cta_start[c] + g_cls[c];
+      castk::par_dft_kernel<<<dim3(ceil_div(castk::kParN * (castk::kParN / 8), 256), castk::kParClasses), 256, 0, s>>>(p);
       CAST_CUDA_TRY(cudaGetLastError());
-      const int n_items = p.n_stat_chunks * castk::kParTiles * p.n_pairs;
-      castk::par_stats_mma_kernel<<<std::min(n_items, num_sms), castk::kParStatThreads,
-                                    castk::ParStatSmem::alloc, s>>>(p);
+      castk::par_stats_mma_kernel<<<grid, castk::kParStatThreads, castk::ParStatSmem::alloc, s>>>(tm_act, p);
     } else {
       p.n_stat_chunks = p.n_chunks;
       castk::par_stats_kernel<<<g1, castk::kParChunk, smem_stats, s>>>(p);
@@ -593,12 +621,6 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
     if (predict_mma) {
       castk::par_filter_kernel<<<dim3(castk::kParTiles, nt, castk::kParKChunks), 256, 0, s>>>(p);
       CAST_CUDA_TRY(cudaGetLastError());
-      // anchor frames as (channel, column, row, frame); one box of 64 channels
-      // x 10 columns x 11 rows per tile, side and channel half
-      CUtensorMap tm_act;
-      if ((st = make_map_4d(&tm_act, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, W, H, n_active, 64,
-                            castk::kParTW, castk::kParTH, CU_TENSOR_MAP_SWIZZLE_128B)))
-        return st;
       const int n_units = nt * castk::kParTiles * ceil_div(C, 128);
       castk::par_predict_mma_kernel<<<std::min(n_units, num_sms), castk::kParPredThreads,
                                       castk::ParMmaSmem::alloc, s>>>(tm_act, p);

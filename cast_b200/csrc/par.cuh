@@ -25,12 +25,12 @@
 // pred = F_L l + F_R r with F[p][q] = win[p] win[q] kern[(p - q) mod (11, 10)]
 // and kern[d] = (1/110) sum_f c_kx Re(w_f e^{i w_f . d}) (c_kx = 1 for
 // kx = 0, 5, else 2: the c2r rows).  Both become GEMMs with the channels as M.
-//   par_dft_kernel       the windowed rfft2 matrix (110 independent real
-//                        columns) as a bf16 hi + lo K-major image
-//   par_stats_mma_kernel persistent over (128-channel chunk, tile, pair):
-//                        anchor tiles gathered with cp.async into two
-//                        buffers, spectra by tcgen05.mma into two TMEM
-//                        halves, R conj(L) and |R conj(L)| summed over the
+//   par_stats_mma_kernel persistent, CTAs per tile class: the class's
+//                        windowed rfft2 matrix (110 independent real
+//                        columns, reflect slots folded in) built in shared
+//                        memory as a bf16 hi + lo image, anchor tiles by TMA
+//                        into two buffers, spectra by tcgen05.mma into two
+//                        TMEM halves, R conj(L) and |R conj(L)| summed over a
 //                        chunk's channels by warp butterflies -> partials
 //   par_finalize_kernel  as above
 //   par_filter_kernel    grid (tile, target, K chunk): kern for L and R from
@@ -70,8 +70,6 @@ struct ParTables {
   float thr[kParFreq];    // tau_low + (tau_high - tau_low) * r^p
   float fy[kParTH];       // 2*pi*fftfreq(11)
   float fx[kParWF];       // 2*pi*rfftfreq(10)
-  float c110[kParPix];    // cos(2*pi*m/110): angle of bin (ky, kx) at pixel
-  float s110[kParPix];    // (i, j) is 2*pi*((10 ky i + 11 kx j) mod 110)/110
 };
 
 struct ParParams {
@@ -91,7 +89,8 @@ struct ParParams {
   float *weights;                // [n_targets, 18, 66, 4]
   float *pred;                   // [n_targets, 18, 110, C]
   uint8_t *filters;              // [n_targets, 18] F images (hi, lo), kParFilterBytes each
-  uint8_t *dft;                  // windowed rfft2 matrix image (hi, lo), kParDftBytes
+  int stat_cta_start[10];        // tensor-core statistics: first CTA of each tile class (9 = grid)
+  uint8_t *dft;                  // per tile class: windowed rfft2 matrix image (hi, lo), kParDftBytes each
   float *stats;                  // optional, see stats layout in capi
   ParTables tab;
 };
@@ -142,6 +141,31 @@ __host__ __device__ __forceinline__ int par_box_y0(int gy) {
 __host__ __device__ __forceinline__ int par_box_x0(int gx) {
   const int x = gx * kParStride - kParPadW;
   return x < 0 ? 0 : (x > kParW - kParTW ? kParW - kParTW : x);
+}
+
+// Tile rows (bits 0-7, 4 each) and tile columns (bits 8-15) whose pixels sit
+// in box slot `slot` of tile (gy, gx), with their counts in bits 16-17 and
+// 20-21: at most two of each.
+__device__ __forceinline__ uint32_t par_slot_word(int gy, int gx, int slot) {
+  const int r = slot / kParTW, sx = slot % kParTW;
+  uint32_t rows = 0, cols = 0, packed = 0;
+  for (int i = 0; i < kParTH; ++i)
+    if (reflect_idx(gy * kParStride + i - kParPadH, kParH) - par_box_y0(gy) == r && rows < 2)
+      packed |= (uint32_t)i << (4 * rows++);
+  for (int j = 0; j < kParTW; ++j)
+    if (reflect_idx(gx * kParStride + j - kParPadW, kParW) - par_box_x0(gx) == sx && cols < 2)
+      packed |= (uint32_t)j << (8 + 4 * cols++);
+  return packed | rows << 16 | cols << 20;
+}
+
+// Tile classes: the slot mapping depends only on the tile row gy and on
+// whether the tile column is the first, an inner one or the last.
+// class = 3 gy + (gx == 0 ? 0 : gx == 5 ? 2 : 1); classes 3 gy + 1 hold 4
+// tiles, the others 1.
+__host__ __device__ __forceinline__ int par_class_tiles(int cls) { return cls % 3 == 1 ? kParGW - 2 : 1; }
+__host__ __device__ __forceinline__ int par_class_tile(int cls, int i) {
+  const int gy = cls / 3, c = cls % 3;
+  return gy * kParGW + (c == 0 ? 0 : (c == 2 ? kParGW - 1 : 1 + i));
 }
 
 // Kernel parameters live in the constant bank, which serves a warp one
@@ -387,17 +411,7 @@ __device__ __forceinline__ void par_build_filter(const ParParams &p, const ParTa
   const float *w = p.weights + ((size_t)tg * kParTiles + tile) * kParFreq * 4;
   __syncthreads();  // the previous target's reads of fs are done
   for (int e = t; e < kParFreq * 4; e += blockDim.x) fs.w[e / 4][e % 4] = w[e];
-  if (t < kParPix) {  // which tile rows / columns land in box slot t
-    const int gy = tile / kParGW, gx = tile % kParGW, r = t / kParTW, sx = t % kParTW;
-    uint32_t rows = 0, cols = 0, packed = 0;
-    for (int i = 0; i < kParTH; ++i)
-      if (reflect_idx(gy * kParStride + i - kParPadH, kParH) - par_box_y0(gy) == r && rows < 2)
-        packed |= (uint32_t)i << (4 * rows++);
-    for (int j = 0; j < kParTW; ++j)
-      if (reflect_idx(gx * kParStride + j - kParPadW, kParW) - par_box_x0(gx) == sx && cols < 2)
-        packed |= (uint32_t)j << (8 + 4 * cols++);
-    fs.slot[t] = packed | rows << 16 | cols << 20;
-  }
+  if (t < kParPix) fs.slot[t] = par_slot_word(tile / kParGW, tile % kParGW, t);
   __syncthreads();
   // kern[d] = (1/110) sum_f c_kx Re(w_f e^{i(2 pi ky dy / 11 + 2 pi kx dx / 10)}),
   // c_kx = 1 for kx = 0, 5 and 2 otherwise: first over kx per (ky, dx) ...
@@ -691,40 +705,6 @@ __global__ void __launch_bounds__(kParChunk) par_predict_kernel(const ParParams 
   }
 }
 
-// The two anchor tiles of (pair, tile), channels chunk*128 .. +127, into the
-// 128-byte-swizzled MN-major A image at `a`: K row side*112 + q holds pixel q
-// of the reflect-padded 11x10 tile (side 0 = left anchor), the two 64-channel
-// halves kParAHalfBytes apart.  16-byte cp.async copies spread over the
-// block; channels at or beyond C read as zero, rows 110, 111, 222, 223 are
-// zeroed.  Returns once this thread's copies have landed: the caller fences
-// (generic -> async proxy) and synchronises the block.
-__device__ __forceinline__ void par_gather_anchors(const ParParams &p, int pair, int tile, int chunk,
-                                                   uint8_t *a) {
-  const int gy = tile / kParGW, gx = tile % kParGW;
-  for (int e = threadIdx.x; e < 2 * 4 * 8; e += blockDim.x) {
-    const int h = e / 32, r = (e / 8) % 4, c16 = e % 8;
-    const int row = r < 2 ? kParPix + r : kParN + kParPix + (r - 2);
-    *reinterpret_cast<uint4 *>(a + h * kParAHalfBytes + row * 128 + c16 * 16) = make_uint4(0u, 0u, 0u, 0u);
-  }
-  const uint32_t a_s = castdev::smem_u32(a);
-  for (int e = threadIdx.x; e < 2 * kParPix * 16; e += blockDim.x) {
-    const int g16 = e % 16, pix = e / 16;  // 16 groups of 8 channels per pixel
-    const int side = pix / kParPix, q = pix % kParPix;
-    const int frame_row = side ? p.pair_right[pair] : p.pair_left[pair];
-    const int y = reflect_idx(gy * kParStride + q / kParTW - kParPadH, kParH);
-    const int x = reflect_idx(gx * kParStride + q % kParTW - kParPadW, kParW);
-    const int krow = side * kParN + q, h = g16 / 8, g = g16 % 8;
-    const int c0 = chunk * 128 + g16 * 8;
-    const uint32_t dst = a_s + h * kParAHalfBytes + krow * 128 + ((g ^ (krow & 7)) * 16);
-    const __nv_bfloat16 *src = p.active + ((size_t)frame_row * p.HW + y * kParW + x) * p.C + c0;
-    const uint32_t bytes = c0 < p.C ? 16u : 0u;  // zero-fill past C
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
-                 "l"(c0 < p.C ? src : p.active), "r"(bytes)
-                 : "memory");
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-}
-
 // Persistent tensor-core prediction.  Units (target, tile, chunk of 128
 // channels) in that order; CTA c takes the contiguous range
 // [c U / grid, (c + 1) U / grid), so F (per target and tile) changes at most
@@ -911,21 +891,28 @@ __global__ void __launch_bounds__(kParPredThreads, 1)
 //   110, 111  zero.
 // The per-bin products R conj(L), |R conj(L)| and their channel sums are the
 // epilogue; the mirrored bins take the conjugate of their partner's sums.
-constexpr int kParDftChunkBytes = kParN * 128;             // one 64-pixel K chunk: 14336
+constexpr int kParDftChunkBytes = kParN * 128;             // one 64-slot K chunk: 14336
 constexpr int kParDftHalfBytes = 2 * kParDftChunkBytes;    // hi or lo: 28672
 constexpr int kParDftBytes = 2 * kParDftHalfBytes;         // 57344
 constexpr int kParCplx = 54;                               // independent complex bins
 constexpr int kParStatVals = 3 * 48 + 24;                  // per-warp sums staged per item
+constexpr int kParStatEpiWarps = 16;                       // 4 per TMEM lane quarter
+constexpr int kParStatThreads = (kParStatEpiWarps + 1) * 32;  // + the TMA / MMA warp
+constexpr int kParClasses = 9;
 
+// Statistics: two A buffers, the class's Dft image, per-warp sums, then
+// a_full[2], mma_done[2], tmem_free[2], b_full and the TMEM slot.
 struct ParStatSmem {
-  static constexpr int a = 0;                          // 2 buffers x 2 x kParAHalfBytes
-  static constexpr int b = 4 * kParAHalfBytes;         // kParDftBytes
-  static constexpr int wsum = b + kParDftBytes;        // [4 warps][kParStatVals] floats
-  static constexpr int bars = wsum + 4 * kParStatVals * 4;  // b_full, mma_done[2]
-  static constexpr int tmem_slot = bars + 24;
+  static constexpr int a = 0;
+  static constexpr int b = 4 * kParAHalfBytes;
+  static constexpr int wsum = b + kParDftBytes;             // [4 lane quarters][kParStatVals]
+  static constexpr int bars = wsum + 4 * kParStatVals * 4;
+  static constexpr int tmem_slot = bars + 7 * 8;
   static constexpr int total = tmem_slot + 8;
   static constexpr int alloc = total + 1024;
 };
+static_assert(ParStatSmem::alloc <= 227 * 1024, "statistics shared memory");
+static_assert(ParStatSmem::bars % 8 == 0, "barrier alignment");
 
 // (ky, kx) of independent complex bin b (layout above).
 __device__ __forceinline__ void par_cplx_bin(int b, int &ky, int &kx) {
@@ -936,45 +923,6 @@ __device__ __forceinline__ void par_cplx_bin(int b, int &ky, int &kx) {
     ky = 1 + (b - 44) % 5;
     kx = b < 49 ? 0 : kParWF - 1;
   }
-}
-
-// One thread per (Dft column n, 8 consecutive pixels): element (n, q) at K
-// chunk q/64, row n, 16-byte group (q%64)/8 swizzled by n & 7; hi at 0, lo
-// at kParDftHalfBytes.
-__global__ void __launch_bounds__(256) par_dft_kernel(const __grid_constant__ ParParams p) {
-  __shared__ ParTables tab;
-  par_tables_to_smem(p.tab, tab);
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= kParN * (kParN / 8)) return;
-  const int n = e / (kParN / 8), g = e % (kParN / 8);
-  int ky = 0, kx = 0;
-  if (n < 2 * kParCplx) par_cplx_bin(n >> 1, ky, kx);
-  else kx = n == 2 * kParCplx ? 0 : kParWF - 1;
-  const bool im = n < 2 * kParCplx && (n & 1);
-  uint32_t hi[4], lo[4];
-#pragma unroll
-  for (int j = 0; j < 8; j += 2) {
-    float v[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int q = g * 8 + j + u;
-      float val = 0.0f;
-      if (n < 2 * kParCplx + 2 && q < kParPix) {
-        const int m = (10 * ky * (q / kParTW) + 11 * kx * (q % kParTW)) % kParPix;
-        val = tab.win[q] * (im ? -tab.s110[m] : tab.c110[m]);
-      }
-      v[u] = val;
-    }
-    const __nv_bfloat162 h = __floats2bfloat162_rn(v[0], v[1]);
-    const float2 hf = __bfloat1622float2(h);
-    const __nv_bfloat162 l = __floats2bfloat162_rn(v[0] - hf.x, v[1] - hf.y);
-    hi[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
-    lo[j / 2] = *reinterpret_cast<const uint32_t *>(&l);
-  }
-  const int kc = g / 8, grp = g % 8;
-  const size_t off = (size_t)kc * kParDftChunkBytes + (size_t)n * 128 + ((grp ^ (n & 7)) * 16);
-  *reinterpret_cast<uint4 *>(p.dft + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-  *reinterpret_cast<uint4 *>(p.dft + kParDftHalfBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 // One halving step of a warp reduce-scatter: lanes with bit OFF set keep the
@@ -989,22 +937,6 @@ __device__ __forceinline__ void par_rs_step(float *v, int lane) {
     const float send = up ? v[i] : v[H + i];
     const float keep = up ? v[H + i] : v[i];
     v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
-  }
-}
-
-// Warp sums of v[0..48): lane L ends with the sums of values base .. base+2,
-// base = 24 [L&16] + 12 [L&8] + 6 [L&4] + 3 [L&2]; stored by even lanes.
-__device__ __forceinline__ void par_warp_sum48(float (&v)[48], int lane, float *out) {
-  par_rs_step<48, 16>(v, lane);
-  par_rs_step<24, 8>(v, lane);
-  par_rs_step<12, 4>(v, lane);
-  par_rs_step<6, 2>(v, lane);
-#pragma unroll
-  for (int i = 0; i < 3; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], 1);
-  const int base = ((lane & 16) ? 24 : 0) + ((lane & 8) ? 12 : 0) + ((lane & 4) ? 6 : 0) + ((lane & 2) ? 3 : 0);
-  if ((lane & 1) == 0) {
-#pragma unroll
-    for (int i = 0; i < 3; ++i) out[base + i] = v[i];
   }
 }
 
@@ -1026,171 +958,314 @@ __device__ __forceinline__ void par_warp_sum24(float (&v)[24], int lane, float *
   }
 }
 
-// Persistent: grid <= number of items (chunk of 128 channels, tile, pair),
-// kParStatThreads threads; CTA i takes items i, i + grid, ...  Two A buffers
-// and two TMEM halves: the gather of the next item runs under this item's
-// MMAs and epilogue.  Warp w reads TMEM lanes 32 (w % 4) .. +31 (channels)
-// and column group w / 4.  Writes the partials of each item's chunk (sums
-// over its channels: lane butterflies, then the four lane quarters in order).
-constexpr int kParStatThreads = 512;
-__global__ void __launch_bounds__(kParStatThreads, 1) par_stats_mma_kernel(const __grid_constant__ ParParams p) {
+// grid (7, tile class), 256 threads, one thread per (column n, 8
+// consecutive box slots): the class's Dft image, element (slot, n) = sum
+// over the tile pixels (i, j) in that slot of win[i][j] e^{-i 2 pi (ky i / 11
+// + kx j / 10)} (re or im by the column layout above), bf16 hi + lo, K-major
+// with the 128-byte swizzle, hi at 0 and lo at kParDftHalfBytes.
+__global__ void __launch_bounds__(256) par_dft_kernel(const __grid_constant__ ParParams p) {
+  __shared__ uint32_t slotw[kParPix];
+  __shared__ float ey_re[kParTH][kParTH], ey_im[kParTH][kParTH], ex_re[kParWF][kParTW], ex_im[kParWF][kParTW];
+  __shared__ float win[kParPix];
+  const int cls = blockIdx.y, t = threadIdx.x;
+  const int t0 = par_class_tile(cls, 0);
+  if (t < kParPix) {
+    slotw[t] = par_slot_word(t0 / kParGW, t0 % kParGW, t);
+    win[t] = p.tab.win[t];
+  }
+  if (t < kParTH * kParTH) {  // e^{-2 pi i ky i / 11}
+    const int m = ((t / kParTH) * (t % kParTH)) % kParTH;
+    double sv, cv;
+    sincospi(2.0 * m / kParTH, &sv, &cv);
+    ey_re[t / kParTH][t % kParTH] = (float)cv;
+    ey_im[t / kParTH][t % kParTH] = (float)-sv;
+  } else if (t < kParTH * kParTH + kParWF * kParTW) {  // e^{-2 pi i kx j / 10}
+    const int e2 = t - kParTH * kParTH, m = ((e2 / kParTW) * (e2 % kParTW)) % kParTW;
+    double sv, cv;
+    sincospi(2.0 * m / kParTW, &sv, &cv);
+    ex_re[e2 / kParTW][e2 % kParTW] = (float)cv;
+    ex_im[e2 / kParTW][e2 % kParTW] = (float)-sv;
+  }
+  __syncthreads();
+  const int e = blockIdx.x * blockDim.x + t;
+  if (e >= kParN * (kParN / 8)) return;
+  const int nn = e % kParN, g = e / kParN;  // a warp takes consecutive columns of one slot group
+  int ky = 0, kx = 0;
+  if (nn < 2 * kParCplx) par_cplx_bin(nn >> 1, ky, kx);
+  else kx = nn == 2 * kParCplx ? 0 : kParWF - 1;
+  const bool im = nn < 2 * kParCplx && (nn & 1);
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    float v[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int slot = g * 8 + j + u;
+      float val = 0.0f;
+      if (nn < 2 * kParCplx + 2 && slot < kParPix) {
+        const uint32_t sw = slotw[slot];
+        const int rows = (sw >> 16) & 3, cols = (sw >> 20) & 3;
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+          for (int b = 0; b < 2; ++b)
+            if (a < rows && b < cols) {
+              const int i = (sw >> (4 * a)) & 15, jj = (sw >> (8 + 4 * b)) & 15;
+              // e^{-i(alpha + beta)}: re = cos(alpha + beta), im = -sin(alpha + beta)
+              const float yr = ey_re[ky][i], yi = ey_im[ky][i], xr = ex_re[kx][jj], xi = ex_im[kx][jj];
+              const float pr = yr * xr - yi * xi, pim = yr * xi + yi * xr;
+              val += win[i * kParTW + jj] * (im ? pim : pr);
+            }
+      }
+      v[u] = val;
+    }
+    const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[0], v[1]);
+    const float2 hf = __bfloat1622float2(h2);
+    const __nv_bfloat162 l2 = __floats2bfloat162_rn(v[0] - hf.x, v[1] - hf.y);
+    hi[j / 2] = *reinterpret_cast<const uint32_t *>(&h2);
+    lo[j / 2] = *reinterpret_cast<const uint32_t *>(&l2);
+  }
+  const int kc = g / 8, grp = g % 8;
+  uint8_t *img = p.dft + (size_t)cls * kParDftBytes;
+  const int off = kc * kParDftChunkBytes + nn * 128 + ((grp ^ (nn & 7)) * 16);
+  *reinterpret_cast<uint4 *>(img + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4 *>(img + kParDftHalfBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+// Persistent statistics.  CTAs are assigned to tile classes
+// (p.stat_cta_start); a class's CTAs take its items (tile of the class, pair,
+// chunk of 128 channels) round-robin.  Each CTA loads its class's Dft image
+// (par_dft_kernel) with one bulk copy.  Warp kParStatEpiWarps gathers the
+// anchor tiles by TMA (one box per anchor and channel half) into two A
+// buffers and issues the MMAs into two TMEM halves; warps 0 .. 15 form the
+// per-bin products and channel sums (warp w: TMEM lanes 32 (w % 4) ..,
+// column group w / 4, in 24-value butterflies (register budget: 17 warps);
+// then the four lane quarters in order) and write the partials of each
+// item's chunk.
+__global__ void __launch_bounds__(kParStatThreads, 1)
+    par_stats_mma_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ ParParams p) {
   extern __shared__ uint8_t par_smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(par_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *b_full = reinterpret_cast<uint64_t *>(smem + ParStatSmem::bars);
-  uint64_t *mma_done = b_full + 1;  // per TMEM half
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ParStatSmem::bars);
+  uint64_t *a_full = bars, *mma_done = bars + 2, *tmem_free = bars + 4, *b_full = bars + 6;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + ParStatSmem::tmem_slot);
   float *wsum = reinterpret_cast<float *>(smem + ParStatSmem::wsum);
   int *err = &g_cast_device_error;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = p.n_stat_chunks * kParTiles * p.n_pairs;
+  const int nch = p.n_stat_chunks;
+
+  // this CTA's class and its share of the class's items
+  int cls = 0;
+  while (cls + 1 < kParClasses && p.stat_cta_start[cls + 1] <= (int)blockIdx.x) ++cls;
+  const int g_cls = p.stat_cta_start[cls + 1] - p.stat_cta_start[cls];
+  const int first = blockIdx.x - p.stat_cta_start[cls];
+  const int per_tile = p.n_pairs * nch;
+  const int n_cls = par_class_tiles(cls) * per_tile;
+  const int n = first < n_cls ? (n_cls - first + g_cls - 1) / g_cls : 0;
+  auto item = [&](int k, int &tile, int &pair, int &chunk) {
+    const int li = first + k * g_cls;
+    tile = par_class_tile(cls, li / per_tile);
+    pair = (li % per_tile) / nch;
+    chunk = li % nch;
+  };
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      castdev::mbar_init(&a_full[i], 1);
+      castdev::mbar_init(&mma_done[i], 1);
+      castdev::mbar_init(&tmem_free[i], 1);
+    }
     castdev::mbar_init(b_full, 1);
-    castdev::mbar_init(&mma_done[0], 1);
-    castdev::mbar_init(&mma_done[1], 1);
     castdev::fence_barrier_init();
-    castdev::mbar_arrive_expect_tx(b_full, kParDftBytes);
-    castdev::bulk_load(smem + ParStatSmem::b, p.dft, kParDftBytes, b_full);
   }
-  if (warp == 0) {
+  if (warp == kParStatEpiWarps) {
     castdev::tmem_alloc(tmem_slot, 512);
     castdev::tmem_relinquish();
   }
-  auto gather = [&](int it, int buf) {
-    const int chunk = it % p.n_stat_chunks, tile = (it / p.n_stat_chunks) % kParTiles;
-    const int pair = it / (p.n_stat_chunks * kParTiles);
-    par_gather_anchors(p, pair, tile, chunk, smem + ParStatSmem::a + buf * 2 * kParAHalfBytes);
-  };
-  const uint32_t sbase = castdev::smem_u32(smem);
-  auto issue = [&](int buf, uint32_t tmem) {  // thread 0
-    castdev::tc_fence_after();
-    constexpr uint32_t idesc = castdev::make_idesc(1, 1, 1, 1, 0, 128, kParN);
-    const uint32_t a0 = sbase + ParStatSmem::a + buf * 2 * kParAHalfBytes;
-#pragma unroll 1
-    for (int side = 0; side < 2; ++side) {  // left anchor -> columns 0.., right -> 112..
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {  // Dft hi, then Dft lo
-#pragma unroll
-        for (int s = 0; s < kParN / 16; ++s) {
-          const uint64_t ad =
-              castdev::smem_desc_sw128(a0 + 2048 * (side * (kParN / 16) + s), kParAHalfBytes, 1024);
-          const uint64_t bd = castdev::smem_desc_sw128(
-              sbase + ParStatSmem::b + half * kParDftHalfBytes + (s >> 2) * kParDftChunkBytes + (s & 3) * 32,
-              16, 1024);
-          castdev::mma_f16_ss(tmem + buf * 2 * kParN + side * kParN, ad, bd, idesc, (half | s) != 0);
-        }
-      }
-    }
-    castdev::tc_commit(&mma_done[buf]);
-  };
-
-  int it = blockIdx.x;
-  gather(it, 0);
+  // K padding rows 110, 111, 222, 223 of both buffers (the gather never writes them)
+  for (int e = threadIdx.x; e < 2 * 2 * 4 * 8; e += blockDim.x) {
+    const int buf = e / 64, h = (e / 32) % 2, r = (e / 8) % 4, c16 = e % 8;
+    const int row = r < 2 ? kParPix + r : kParN + kParPix + (r - 2);
+    *reinterpret_cast<uint4 *>(smem + ParStatSmem::a + buf * 2 * kParAHalfBytes + h * kParAHalfBytes + row * 128 +
+                               c16 * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
   castdev::fence_proxy_async_smem();
   __syncthreads();
   castdev::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
-  if (threadIdx.x == 0) {
-    ok = castdev::mbar_wait(b_full, 0, err);
-    if (ok) issue(0, tmem);
-  }
-  ok = __syncthreads_and(ok);
-  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-  for (int k = 0; ok && it < n_items; ++k, it += gridDim.x) {
-    const int buf = k & 1;
-    const int next = it + gridDim.x;
-    if (next < n_items) gather(next, buf ^ 1);  // cp.async: lands under this item's work
-    // one thread polls the barrier, the others sleep in the block barrier:
-    // polling warps would take shared-memory bandwidth from the MMAs
-    int done_i = 1;
-    if (threadIdx.x == 0) done_i = castdev::mbar_wait(&mma_done[buf], (k >> 1) & 1, err);
-    const bool done = __syncthreads_and(done_i) != 0;
-    castdev::tc_fence_after();
-    const int grp = warp >> 2;
+
+  if (warp == kParStatEpiWarps) {
+    // ---- TMA / MMA issuer (lane 0) ------------------------------------------
+    const uint32_t sbase = castdev::smem_u32(smem);
+    constexpr uint32_t idesc = castdev::make_idesc(1, 1, 1, 1, 0, 128, kParN);
+    int g_issued[2] = {0, 0}, g_waited[2] = {0, 0};
+    auto gather = [&](int k) {
+      int tile, pair, chunk;
+      item(k, tile, pair, chunk);
+      const int buf = k & 1, gy = tile / kParGW, gx = tile % kParGW;
+      castdev::mbar_arrive_expect_tx(&a_full[buf], kParGatherBytes);
+      for (int e = 0; e < 4; ++e) {
+        const int h = e & 1, side = e >> 1;
+        castdev::tma_load_4d(smem + ParStatSmem::a + buf * 2 * kParAHalfBytes + h * kParAHalfBytes + side * kParN * 128,
+                             &tm_act, &a_full[buf], chunk * 128 + h * 64, par_box_x0(gx), par_box_y0(gy),
+                             side ? p.pair_right[pair] : p.pair_left[pair]);
+      }
+      ++g_issued[buf];
+    };
+    bool ok = true;
+    bool b_loaded = false;
+    if (lane == 0 && n > 0) {
+      castdev::tma_prefetch_desc(&tm_act);
+      castdev::mbar_arrive_expect_tx(b_full, kParDftBytes);
+      castdev::bulk_load(smem + ParStatSmem::b, p.dft + (size_t)cls * kParDftBytes, kParDftBytes, b_full);
+      b_loaded = true;
+      gather(0);
+      if (n > 1) gather(1);
+      ok = castdev::mbar_wait(b_full, 0, err);
+      if (ok) b_loaded = false;
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    for (int k = 0; k < n && ok; ++k) {
+      const int buf = k & 1;
+      if (lane == 0) {
+        if (k >= 1) {
+          // unit k - 1's MMAs have completed: its A buffer takes item k + 1
+          ok = castdev::mbar_wait(&mma_done[(k - 1) & 1], ((k - 1) >> 1) & 1, err);
+          if (ok && k + 1 < n) gather(k + 1);
+        }
+        if (ok) {
+          ok = castdev::mbar_wait(&a_full[buf], (k >> 1) & 1, err);
+          ++g_waited[buf];
+        }
+        if (ok && k >= 2) ok = castdev::mbar_wait(&tmem_free[buf], ((k - 2) >> 1) & 1, err);
+        if (ok) {
+          castdev::tc_fence_after();
+          const uint32_t a0 = sbase + ParStatSmem::a + buf * 2 * kParAHalfBytes;
+#pragma unroll 1
+          for (int side = 0; side < 2; ++side) {  // left anchor -> columns 0.., right -> 112..
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {  // Dft hi, then Dft lo
+#pragma unroll
+              for (int s = 0; s < kParN / 16; ++s) {
+                const uint64_t ad =
+                    castdev::smem_desc_sw128(a0 + 2048 * (side * (kParN / 16) + s), kParAHalfBytes, 1024);
+                const uint64_t bd = castdev::smem_desc_sw128(
+                    sbase + ParStatSmem::b + half * kParDftHalfBytes + (s >> 2) * kParDftChunkBytes + (s & 3) * 32,
+                    16, 1024);
+                castdev::mma_f16_ss(tmem + buf * 2 * kParN + side * kParN, ad, bd, idesc, (half | s) != 0);
+              }
+            }
+          }
+          castdev::tc_commit(&mma_done[buf]);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (lane == 0) {  // nothing the TMA unit or the tensor core writes may be in flight at exit
+      if (b_loaded) castdev::mbar_wait_drain(b_full, 0, err);
+      for (int b2 = 0; b2 < 2; ++b2)
+        if (g_issued[b2] > g_waited[b2]) castdev::mbar_wait_drain(&a_full[b2], (g_issued[b2] - 1) & 1, err);
+      if (n > 0) castdev::mbar_wait_drain(&mma_done[(n - 1) & 1], ((n - 1) >> 1) & 1, err);
+      if (n > 1) castdev::mbar_wait_drain(&mma_done[(n - 2) & 1], ((n - 2) >> 1) & 1, err);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue warps (named barrier 1 over kParStatEpiWarps warps) ---------
+    const int et = threadIdx.x;  // 0 .. kParStatEpiWarps * 32 - 1
+    constexpr uint32_t kEpi = kParStatEpiWarps * 32;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     float *wout = wsum + (warp & 3) * kParStatVals;
-    const uint32_t tl = tmem + lane_off + buf * 2 * kParN;
-    if (grp < 3) {  // complex bins 16 grp .. 16 grp + 15
-      uint32_t l[32], r[32];
-      castdev::tmem_ld32(tl + 32 * grp, l);
-      castdev::tmem_ld32(tl + kParN + 32 * grp, r);
-      castdev::tmem_wait_ld();
-      float v[48];
+    for (int k = 0; k < n; ++k) {
+      const int buf = k & 1;
+      int okw = 1;
+      if (lane == 0) okw = castdev::mbar_wait(&mma_done[buf], (k >> 1) & 1, err);
+      const bool done = __shfl_sync(0xffffffffu, okw, 0) != 0;
+      castdev::tc_fence_after();
+      const uint32_t tl = tmem + lane_off + buf * 2 * kParN;
+      const int grp = warp >> 2;
+      if (grp < 3) {  // complex bins 16 grp .. 16 grp + 15, 8 per butterfly
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t l[16], r[16];
+          if (done) {
+            castdev::tmem_ld16(tl + 32 * grp + 16 * hh, l);
+            castdev::tmem_ld16(tl + kParN + 32 * grp + 16 * hh, r);
+            castdev::tmem_wait_ld();
+          }
+          float v[24];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float lr = __uint_as_float(l[2 * j]), li = __uint_as_float(l[2 * j + 1]);
-        const float rr = __uint_as_float(r[2 * j]), ri = __uint_as_float(r[2 * j + 1]);
-        const float cre = rr * lr + ri * li, cim = ri * lr - rr * li;
-        v[3 * j] = cre;
-        v[3 * j + 1] = cim;
-        v[3 * j + 2] = sqrtf(cre * cre + cim * cim);
-      }
-      par_warp_sum48(v, lane, wout + 48 * grp);
-    } else {  // complex bins 48..53, then the real bins (0, 0) and (0, 5)
-      uint32_t l[16], r[16];
-      castdev::tmem_ld16(tl + 96, l);
-      castdev::tmem_ld16(tl + kParN + 96, r);
-      castdev::tmem_wait_ld();
-      float v[24];
-#pragma unroll
-      for (int j = 0; j < 6; ++j) {
-        const float lr = __uint_as_float(l[2 * j]), li = __uint_as_float(l[2 * j + 1]);
-        const float rr = __uint_as_float(r[2 * j]), ri = __uint_as_float(r[2 * j + 1]);
-        const float cre = rr * lr + ri * li, cim = ri * lr - rr * li;
-        v[3 * j] = cre;
-        v[3 * j + 1] = cim;
-        v[3 * j + 2] = sqrtf(cre * cre + cim * cim);
-      }
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float cre = __uint_as_float(r[12 + j]) * __uint_as_float(l[12 + j]);
-        v[18 + 2 * j] = cre;
-        v[19 + 2 * j] = sqrtf(cre * cre);
-      }
-      v[22] = v[23] = 0.0f;
-      par_warp_sum24(v, lane, wout + 144);
-    }
-    castdev::tc_fence_before();
-    __syncthreads();
-    if (done) {
-      const int chunk = it % p.n_stat_chunks, tile = (it / p.n_stat_chunks) % kParTiles;
-      const int pair = it / (p.n_stat_chunks * kParTiles);
-      float *dst = p.partials + (((size_t)pair * kParTiles + tile) * p.n_stat_chunks + chunk) * kParPartial;
-      for (int r = threadIdx.x; r < kParPartial; r += blockDim.x) {
-        const int qn = r / kParFreq, f = r % kParFreq, ky = f / kParWF, kx = f % kParWF;
-        int vi = -1;
-        float sign = 1.0f;
-        if (kx >= 1 && kx <= 4) {
-          const int b = (kx - 1) * kParTH + ky;
-          vi = b < 48 ? 48 * (b / 16) + 3 * (b % 16) + qn : 144 + 3 * (b - 48) + qn;
-        } else if (ky == 0) {
-          vi = qn == 1 ? -1 : 144 + 18 + (kx ? 2 : 0) + (qn ? 1 : 0);
-        } else {
-          const int kk = ky <= 5 ? ky : kParTH - ky;
-          if (ky > 5 && qn == 1) sign = -1.0f;
-          const int b = 44 + (kx ? 5 : 0) + kk - 1;
-          vi = b < 48 ? 48 * (b / 16) + 3 * (b % 16) + qn : 144 + 3 * (b - 48) + qn;
+          for (int j = 0; j < 8; ++j) {
+            const float lr = __uint_as_float(l[2 * j]), li = __uint_as_float(l[2 * j + 1]);
+            const float rr = __uint_as_float(r[2 * j]), ri = __uint_as_float(r[2 * j + 1]);
+            const float cre = rr * lr + ri * li, cim = ri * lr - rr * li;
+            v[3 * j] = cre;
+            v[3 * j + 1] = cim;
+            v[3 * j + 2] = sqrtf(cre * cre + cim * cim);
+          }
+          par_warp_sum24(v, lane, wout + 48 * grp + 24 * hh);
         }
-        float acc = 0.0f;
-        if (vi >= 0) {
-#pragma unroll
-          for (int w = 0; w < 4; ++w) acc += wsum[w * kParStatVals + vi];
+      } else {  // complex bins 48..53, then the real bins (0, 0) and (0, 5)
+        uint32_t l[16], r[16];
+        if (done) {
+          castdev::tmem_ld16(tl + 96, l);
+          castdev::tmem_ld16(tl + kParN + 96, r);
+          castdev::tmem_wait_ld();
         }
-        dst[r] = sign * acc;
+        float v[24];
+#pragma unroll
+        for (int j = 0; j < 6; ++j) {
+          const float lr = __uint_as_float(l[2 * j]), li = __uint_as_float(l[2 * j + 1]);
+          const float rr = __uint_as_float(r[2 * j]), ri = __uint_as_float(r[2 * j + 1]);
+          const float cre = rr * lr + ri * li, cim = ri * lr - rr * li;
+          v[3 * j] = cre;
+          v[3 * j + 1] = cim;
+          v[3 * j + 2] = sqrtf(cre * cre + cim * cim);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float cre = __uint_as_float(r[12 + j]) * __uint_as_float(l[12 + j]);
+          v[18 + 2 * j] = cre;
+          v[19 + 2 * j] = sqrtf(cre * cre);
+        }
+        v[22] = v[23] = 0.0f;
+        par_warp_sum24(v, lane, wout + 144);
       }
+      castdev::tc_fence_before();
+      castdev::named_bar_sync(1, kEpi);  // TMEM half read, per-quarter sums staged
+      if (et == 0) castdev::mbar_arrive(&tmem_free[buf]);
+      if (done) {
+        int tile, pair, chunk;
+        item(k, tile, pair, chunk);
+        float *dst = p.partials + (((size_t)pair * kParTiles + tile) * nch + chunk) * kParPartial;
+        for (int r = et; r < kParPartial; r += kEpi) {
+          const int qn = r / kParFreq, f = r % kParFreq, ky = f / kParWF, kx = f % kParWF;
+          int vi = -1;
+          float sign = 1.0f;
+          if (kx >= 1 && kx <= 4) {
+            const int b = (kx - 1) * kParTH + ky;
+            vi = b < 48 ? 48 * (b / 16) + 3 * (b % 16) + qn : 144 + 3 * (b - 48) + qn;
+          } else if (ky == 0) {
+            vi = qn == 1 ? -1 : 144 + 18 + (kx ? 2 : 0) + (qn ? 1 : 0);
+          } else {
+            const int kk = ky <= 5 ? ky : kParTH - ky;
+            if (ky > 5 && qn == 1) sign = -1.0f;
+            const int b = 44 + (kx ? 5 : 0) + kk - 1;
+            vi = b < 48 ? 48 * (b / 16) + 3 * (b % 16) + qn : 144 + 3 * (b - 48) + qn;
+          }
+          float acc = 0.0f;
+          if (vi >= 0) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) acc += wsum[w * kParStatVals + vi];
+          }
+          dst[r] = sign * acc;
+        }
+      }
+      castdev::named_bar_sync(1, kEpi);  // sums read before the next item's staging
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    castdev::fence_proxy_async_smem();
-    bool step_ok = done;
-    ok = __syncthreads_and(step_ok);  // also orders the wsum reads before the next item's writes
-    if (ok && threadIdx.x == 0 && next < n_items) issue(buf ^ 1, tmem);
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  // the bulk copy has landed before TMEM is released and the block exits
-  if (threadIdx.x == 0) castdev::mbar_wait_drain(b_full, 0, err);
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kParStatEpiWarps) {
     castdev::tc_fence_after();
     castdev::tmem_dealloc(tmem, 512);
   }
