@@ -380,6 +380,34 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
 // ===========================================================================
 static int par_chunks(int C) { return ceil_div(C, castk::kParChunk); }
 
+// Per device: the class rfft2 images in castk::g_par_dft (built once), and a
+// side stream with two events on which the active-frame copies run beside
+// the PAR kernels.  g_par_mutex serialises each call's launch sequence, so
+// concurrent callers never interleave on the shared stream and events (nor
+// pull the side stream into another caller's stream capture).
+static constexpr int kParMaxDevices = 64;
+static std::mutex g_par_mutex;
+static bool g_par_dft_built[kParMaxDevices] = {};
+static void *g_par_dft_ptr[kParMaxDevices] = {};
+static cudaStream_t g_par_side[kParMaxDevices] = {};
+static cudaEvent_t g_par_fork[kParMaxDevices] = {}, g_par_join[kParMaxDevices] = {};
+
+// Creates the current device's side stream and events, and looks up the
+// image array; with g_par_mutex held.
+static int par_device_state(int *dev_out) {
+  int dev = 0;
+  CAST_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kParMaxDevices) return fail(CAST_ERR_UNSUPPORTED, "device %d", dev);
+  if (!g_par_side[dev]) {
+    CAST_CUDA_TRY(cudaStreamCreateWithFlags(&g_par_side[dev], cudaStreamNonBlocking));
+    CAST_CUDA_TRY(cudaEventCreateWithFlags(&g_par_fork[dev], cudaEventDisableTiming));
+    CAST_CUDA_TRY(cudaEventCreateWithFlags(&g_par_join[dev], cudaEventDisableTiming));
+  }
+  if (!g_par_dft_ptr[dev]) CAST_CUDA_TRY(cudaGetSymbolAddress(&g_par_dft_ptr[dev], castk::g_par_dft));
+  *dev_out = dev;
+  return CAST_OK;
+}
+
 extern "C" size_t cast_par_fcpasm_workspace_bytes(int T, int H, int W, int C) {
   if (T <= 0 || H != castk::kParH || W != castk::kParW || C <= 0) return 0;
   const int nt = std::min(T, castk::kParMaxTargets);
@@ -388,7 +416,7 @@ extern "C" size_t cast_par_fcpasm_workspace_bytes(int T, int H, int W, int C) {
   const size_t pred = (size_t)nt * castk::kParTiles * castk::kParPix * C;
   const size_t filters = (size_t)nt * castk::kParTiles * castk::kParFilterBytes;
   return align_up(partials * 4, 256) + align_up(weights * 4, 256) + align_up(pred * 4, 256) +
-         align_up(filters, 1024) + align_up((size_t)castk::kParClasses * castk::kParDftBytes, 1024);
+         align_up(filters, 1024);
 }
 
 static void fill_par_tables(castk::ParTables &t, float tau_low, float tau_high, float power) {
@@ -508,6 +536,26 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
   __nv_bfloat16 *full = static_cast<__nv_bfloat16 *>(full_residual);
   const __nv_bfloat16 *act = static_cast<const __nv_bfloat16 *>(active_residual);
 
+  std::lock_guard<std::mutex> lock(g_par_mutex);
+  int dev = 0;
+  if ((st = par_device_state(&dev))) return st;
+  // corrected[:, active_frames] = active_residual: independent of the target
+  // frames, so with targets present the copies run on the side stream beside
+  // the PAR kernels and `s` waits for them at the end
+  const bool fork = nt > 0;
+  cudaStream_t cs = s;
+  if (fork) {
+    CAST_CUDA_TRY(cudaEventRecord(g_par_fork[dev], s));
+    CAST_CUDA_TRY(cudaStreamWaitEvent(g_par_side[dev], g_par_fork[dev], 0));
+    cs = g_par_side[dev];
+  }
+  for (int i = 0; i < n_active; ++i) {
+    void *dst = full + (size_t)active_frames[i] * H * W * C;
+    const void *src = act + (size_t)i * H * W * C;
+    if (dst != src) CAST_CUDA_TRY(cudaMemcpyAsync(dst, src, frame_bytes, cudaMemcpyDeviceToDevice, cs));
+  }
+  if (fork) CAST_CUDA_TRY(cudaEventRecord(g_par_join[dev], cs));
+
   if (nt > 0) {
     p.active = act;
     p.full = full;
@@ -531,8 +579,7 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
     p.pred = reinterpret_cast<float *>(ws);
     ws += align_up((size_t)std::min(T, castk::kParMaxTargets) * castk::kParTiles * castk::kParPix * C * 4, 256);
     p.filters = ws;
-    ws += align_up((size_t)std::min(T, castk::kParMaxTargets) * castk::kParTiles * castk::kParFilterBytes, 1024);
-    p.dft = ws;
+    p.dft = static_cast<uint8_t *>(g_par_dft_ptr[dev]);
     p.stats = stats_out;
     fill_par_tables(p.tab, tau_low, tau_high, freq_power);
 
@@ -607,8 +654,22 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
       }
       p.stat_cta_start[0] = 0;
       for (int c = 0; c < castk::kParClasses; ++c) p.stat_cta_start[c + 1] = p.stat_cta_start[c] + g_cls[c];
-      castk::par_dft_kernel<<<dim3(ceil_div(castk::kParN * (castk::kParN / 8), 256), castk::kParClasses), 256, 0, s>>>(p);
-      CAST_CUDA_TRY(cudaGetLastError());
+      const dim3 dft_grid(ceil_div(castk::kParN * (castk::kParN / 8), 256), castk::kParClasses);
+      if (!g_par_dft_built[dev]) {
+        cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+        CAST_CUDA_TRY(cudaStreamIsCapturing(s, &capture));
+        if (capture == cudaStreamCaptureStatusNone) {
+          // once per device, on the private stream (no wait on the caller's)
+          castk::par_dft_kernel<<<dft_grid, 256, 0, g_par_side[dev]>>>(p);
+          CAST_CUDA_TRY(cudaGetLastError());
+          CAST_CUDA_TRY(cudaStreamSynchronize(g_par_side[dev]));
+          g_par_dft_built[dev] = true;
+        } else {
+          // inside a capture nothing may synchronise: the graph builds them
+          castk::par_dft_kernel<<<dft_grid, 256, 0, s>>>(p);
+          CAST_CUDA_TRY(cudaGetLastError());
+        }
+      }
       castk::par_stats_mma_kernel<<<grid, castk::kParStatThreads, castk::ParStatSmem::alloc, s>>>(tm_act, p);
     } else {
       p.n_stat_chunks = p.n_chunks;
@@ -632,12 +693,7 @@ extern "C" int cast_par_fcpasm(void *full_residual, const void *active_residual,
     castk::par_ola_kernel<<<dim3(H * W, nt), 256, 0, s>>>(p);
     CAST_CUDA_TRY(cudaGetLastError());
   }
-  // corrected[:, active_frames] = active_residual
-  for (int i = 0; i < n_active; ++i) {
-    void *dst = full + (size_t)active_frames[i] * H * W * C;
-    const void *src = act + (size_t)i * H * W * C;
-    if (dst != src) CAST_CUDA_TRY(cudaMemcpyAsync(dst, src, frame_bytes, cudaMemcpyDeviceToDevice, s));
-  }
+  if (fork) CAST_CUDA_TRY(cudaStreamWaitEvent(s, g_par_join[dev], 0));
   return CAST_OK;
 }
 

@@ -446,8 +446,10 @@ __device__ __forceinline__ void par_build_filter(const ParParams &p, const ParTa
   // swizzled by n & 7 (128-byte swizzle, K-major).
   uint8_t *img = p.filters + ((size_t)tg * kParTiles + tile) * kParFilterBytes;
   const int g0 = kc0 * 8, ng = min(kc1 * 8, kParK / 8) - g0;
+  // a warp takes consecutive output pixels n of one group of 8 K slots: the
+  // slot words and windows are broadcasts, the kern reads consecutive
   for (int e = t; e < kParN * ng; e += blockDim.x) {
-    const int n = e / ng, g = g0 + e % ng;  // 8 consecutive k
+    const int n = e % kParN, g = g0 + e / kParN;  // 8 consecutive k
     const int ny = n / kParTW, nx = n % kParTW;
     uint32_t hi[4], lo[4];
 #pragma unroll
@@ -957,6 +959,11 @@ __device__ __forceinline__ void par_warp_sum24(float (&v)[24], int lane, float *
     for (int i = 0; i < 3; ++i) out[base + i] = v[i];
   }
 }
+
+// The class images depend only on the window and the tile geometry: the host
+// builds them once per device into this array (or, inside a stream capture
+// before that, as part of the captured work).
+__device__ __align__(1024) uint8_t g_par_dft[kParClasses * kParDftBytes];
 
 // grid (7, tile class), 256 threads, one thread per (column n, 8
 // consecutive box slots): the class's Dft image, element (slot, n) = sum
