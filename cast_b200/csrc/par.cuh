@@ -504,6 +504,7 @@ __global__ void __launch_bounds__(kParFinalizeThreads) par_finalize_kernel(const
   __shared__ float part[kParPartial];
   __shared__ float unit_re[kParFreq], unit_im[kParFreq], coh[kParFreq], wgt[kParFreq];
   __shared__ float theta[kParFreq], corr[kParPix];
+  __shared__ float z_re[kParTH][kParWF], z_im[kParTH][kParWF];
   __shared__ float s_base, s_denom, s_conf, s_dx, s_dy, s_ramp;
   const int tile = blockIdx.x, pair = blockIdx.y, t = threadIdx.x;
   const float *src = p.partials + ((size_t)pair * kParTiles + tile) * p.n_stat_chunks * kParPartial;
@@ -549,27 +550,30 @@ __global__ void __launch_bounds__(kParFinalizeThreads) par_finalize_kernel(const
       s_base = fminf(fmaxf(cw / denom, 0.0f), 1.0f);
     }
   }
-  // PHAT correlation: irfft2(unit * coherence, s=(11,10)), one output per thread.
+  // PHAT correlation: irfft2(unit * coherence, s=(11,10)), separably: first
+  // Z[y][kx] = sum_ky v e^{+i 2pi ky y / 11} ...
+  if (t < kParTH * kParWF) {
+    const int y = t / kParWF, kx = t % kParWF;
+    float zr = 0.0f, zi = 0.0f;
+#pragma unroll
+    for (int ky = 0; ky < kParTH; ++ky) {
+      const int my = (ky * y) % kParTH, f = ky * kParWF + kx;
+      const float vr = unit_re[f] * coh[f], vi = unit_im[f] * coh[f];
+      zr += vr * tab.ch[my] - vi * tab.shh[my];
+      zi += vr * tab.shh[my] + vi * tab.ch[my];
+    }
+    z_re[y][kx] = zr;
+    z_im[y][kx] = zi;
+  }
+  __syncthreads();
+  // ... then the c2r rows over kx (imaginary parts of kx = 0 and 5 dropped)
   if (t < kParPix) {
     const int y = t / kParTW, x = t % kParTW;
-    float acc = 0.0f;
-    for (int ky = 0; ky < kParTH; ++ky) {
-      const int my = (ky * y) % kParTH;
-      const float ey_c = tab.ch[my], ey_s = tab.shh[my];
-      for (int kx = 0; kx < kParWF; ++kx) {
-        const int f = ky * kParWF + kx;
-        const float vr = unit_re[f] * coh[f], vi = unit_im[f] * coh[f];
-        // Z contribution: v * e^{+i 2pi ky y/11}
-        const float zr = vr * ey_c - vi * ey_s, zi = vr * ey_s + vi * ey_c;
-        if (kx == 0) {
-          acc += zr;
-        } else if (kx == 5) {
-          acc += (x & 1) ? -zr : zr;
-        } else {
-          const int mx = (kx * x) % kParTW;
-          acc += 2.0f * (zr * tab.cw[mx] - zi * tab.sw[mx]);
-        }
-      }
+    float acc = z_re[y][0] + ((x & 1) ? -z_re[y][kParWF - 1] : z_re[y][kParWF - 1]);
+#pragma unroll
+    for (int kx = 1; kx < kParWF - 1; ++kx) {
+      const int mx = (kx * x) % kParTW;
+      acc += 2.0f * (z_re[y][kx] * tab.cw[mx] - z_im[y][kx] * tab.sw[mx]);
     }
     corr[t] = acc * (1.0f / (float)(kParTH * kParTW));
   }
