@@ -26,14 +26,14 @@ SIGNATURES = {
     "cast_device_error": (c_int, [c_void_p]),
     "cast_rcsa_select_quant": (
         c_int,
-        [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_int, c_float, c_void_p, c_void_p, c_size_t, c_void_p],
     ),
     "cast_rcsa_select_quant_workspace_bytes": (c_size_t, [c_int] * 6),
     "cast_rcsa_select_quant_noalloc": (
         c_int,
-        [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_int, c_float, c_void_p, c_void_p],
     ),

@@ -144,7 +144,8 @@ extern "C" size_t cast_rcsa_select_quant_workspace_bytes(int B, int H, int Lq, i
          2 * align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256);
 }
 
-extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *v, int B, int H,
+extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *v,
+                                      const uint8_t *q_valid, const uint8_t *k_valid, int B, int H,
                                       int Lq, int Lk, int D, int block_size, int budget, int rule,
                                       int32_t *sel_idx, int32_t *sel_cnt, int8_t *q_codes,
                                       float *q_scales, int8_t *k_codes, float *k_scales,
@@ -193,14 +194,24 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   const __nv_bfloat16 *qb = static_cast<const __nv_bfloat16 *>(q);
   const __nv_bfloat16 *kb = static_cast<const __nv_bfloat16 *>(k);
   const __nv_bfloat16 *vb = static_cast<const __nv_bfloat16 *>(v);
-  if (D == 128)
-    castk::pool_quant_kernel<128><<<grid, 256, 0, s>>>(qb, kb, vb, Lq, Lk, block_size, nqb, nkb,
-                                                       q_codes, qs, k_codes, ks, v_codes, v_scales,
-                                                       pooled_out, rms);
+  // the masked variant only when a validity mask is given
+  const bool masked = q_valid || k_valid;
+  if (D == 128 && !masked)
+    castk::pool_quant_kernel<128, false><<<grid, 256, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
+                                                              nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                              v_scales, pooled_out, rms);
+  else if (D == 128)
+    castk::pool_quant_kernel<128, true><<<grid, 256, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
+                                                             nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                             v_scales, pooled_out, rms);
+  else if (!masked)
+    castk::pool_quant_kernel<64, false><<<grid, 128, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
+                                                             nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                             v_scales, pooled_out, rms);
   else
-    castk::pool_quant_kernel<64><<<grid, 128, 0, s>>>(qb, kb, vb, Lq, Lk, block_size, nqb, nkb,
-                                                      q_codes, qs, k_codes, ks, v_codes, v_scales,
-                                                      pooled_out, rms);
+    castk::pool_quant_kernel<64, true><<<grid, 128, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
+                                                            nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                            v_scales, pooled_out, rms);
   CAST_CUDA_TRY(cudaGetLastError());
   const int keep = std::min(budget, nkb - nqb);
   const int maxdeg = keep + nqb;
@@ -729,7 +740,8 @@ static int noalloc_scratch(void **out) {
   return CAST_OK;
 }
 
-extern "C" int cast_rcsa_select_quant_noalloc(const void *q, const void *k, const void *v, int B,
+extern "C" int cast_rcsa_select_quant_noalloc(const void *q, const void *k, const void *v,
+                                              const uint8_t *q_valid, const uint8_t *k_valid, int B,
                                               int H, int Lq, int Lk, int D, int block_size,
                                               int budget, int rule, int32_t *sel_idx,
                                               int32_t *sel_cnt, int8_t *q_codes, float *q_scales,
@@ -748,7 +760,7 @@ extern "C" int cast_rcsa_select_quant_noalloc(const void *q, const void *k, cons
   void *scratch = nullptr;
   st = noalloc_scratch(&scratch);
   if (st) return st;
-  return cast_rcsa_select_quant(q, k, v, B, H, Lq, Lk, D, block_size, budget, rule, sel_idx,
+  return cast_rcsa_select_quant(q, k, v, q_valid, k_valid, B, H, Lq, Lk, D, block_size, budget, rule, sel_idx,
                                 sel_cnt, q_codes, q_scales, k_codes, k_scales, v_codes, v_scales,
                                 qk_mode, policy, int8_tolerance, pooled, scratch,
                                 CAST_NOALLOC_SCRATCH_BYTES, stream);

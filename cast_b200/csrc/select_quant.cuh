@@ -154,10 +154,15 @@ __device__ __forceinline__ double warp_dot(const double *a, const double *b, int
 // grid.x spans [Q blocks | K blocks | V blocks], grid.y = B*H.
 // Threads: 16 row slots x D/8 column groups (8 bf16 = 16 bytes each).
 // ---------------------------------------------------------------------------
-template <int D>
+// kMasked: q_valid / k_valid may be given (token validity of the compact
+// packing; k_valid also covers V).  An invalid token's row is read and
+// replaced by zeros -- exactly the restatement's zero-padded sums -- leaves
+// the block's pooled-mean denominator and RMS count, and gets code 0.
+template <int D, bool kMasked>
 __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
     pool_quant_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
-                      const __nv_bfloat16 *__restrict__ v, int Lq, int Lk, int block, int nqb,
+                      const __nv_bfloat16 *__restrict__ v, const uint8_t *__restrict__ q_valid,
+                      const uint8_t *__restrict__ k_valid, int Lq, int Lk, int block, int nqb,
                       int nkb, int8_t *q_codes, float *q_scales, int8_t *k_codes,
                       float *k_scales, int8_t *v_codes, float *v_scales, double *pooled,
                       float *block_rms) {
@@ -170,6 +175,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   __shared__ float s_scale;
   __shared__ float s_amax;
   __shared__ double s_denom;
+  __shared__ int s_count;  // valid rows of the block
 
   const int tid = threadIdx.x;
   const int grp = tid % kGroups;
@@ -195,6 +201,11 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   const int b0 = blk * block;
   const int rows = min(block, L - b0);
   const __nv_bfloat16 *base = X + ((size_t)bh * L + b0) * D + grp * 8;
+  const uint8_t *vrow = kMasked ? (which == 0 ? q_valid : k_valid) : nullptr;  // may be null
+  if (vrow) vrow += b0;
+  if (tid == 0) s_count = kMasked && vrow ? 0 : rows;
+  __syncthreads();
+  int my_count = 0;  // valid rows among this thread's (column group 0 only)
 
   float acc[8];
 #pragma unroll
@@ -214,6 +225,12 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
     for (int u = 0; u < kUnroll; ++u) {
       float f[8];
       bf16x8_to_f32(raw[u], f);
+      if (kMasked && vrow) {
+        const bool ok = vrow[r + u * kSumLanes] != 0;
+        my_count += ok;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = ok ? f[i] : 0.0f;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         if (pool) acc[i] = __fadd_rn(acc[i], f[i]);
@@ -225,6 +242,12 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   for (; r < rows; r += kSumLanes) {
     float f[8];
     bf16x8_to_f32(ldg_nc_v4_hint(base + (size_t)r * D, keep_pol), f);
+    if (kMasked && vrow) {
+      const bool ok = vrow[r] != 0;
+      my_count += ok;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = ok ? f[i] : 0.0f;
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (pool) acc[i] = __fadd_rn(acc[i], f[i]);
@@ -247,7 +270,9 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
 #pragma unroll
     for (int i = 0; i < 8; ++i) red[slot][grp * 8 + i] = acc[i];
   }
+  if (kMasked && vrow && grp == 0 && my_count) atomicAdd(&s_count, my_count);
   __syncthreads();
+  const int count = s_count;
   if (tid == 0) {
     float m = 0.0f, s2 = 0.0f;
     for (int w = 0; w < kThreads / 32; ++w) {
@@ -261,7 +286,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
     if (block_rms && pool) {
       const int row0 = which == 0 ? 0 : nqb;
       block_rms[(size_t)bh * (nqb + nkb) + row0 + blk] =
-          sqrtf(s2 / (float)max(1, rows * D));
+          sqrtf(s2 / (float)max(1, count * D));
     }
   }
   if (pool) {
@@ -269,7 +294,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
       double t = (double)red[0][tid];
 #pragma unroll
       for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, (double)red[p][tid]);
-      mean_s[tid] = __ddiv_rn(t, (double)max(rows, 1));
+      mean_s[tid] = __ddiv_rn(t, (double)max(count, 1));
     }
     __syncthreads();
     if (tid < 32) {
@@ -314,12 +339,17 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
       for (int u = 0; u < kUnroll; ++u)
         raw[u] = ldg_v4_hint(base + (size_t)(rr + u * kSumLanes) * D, drop_pol);
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-        stg_v2_hint(cbase + (size_t)(rr + u * kSumLanes) * D, quant8(raw[u]), drop_pol);
+      for (int u = 0; u < kUnroll; ++u) {
+        uint2 c = quant8(raw[u]);
+        if (kMasked && vrow && !vrow[rr + u * kSumLanes]) c = make_uint2(0u, 0u);
+        stg_v2_hint(cbase + (size_t)(rr + u * kSumLanes) * D, c, drop_pol);
+      }
     }
-    for (; rr < rows; rr += kSumLanes)
-      stg_v2_hint(cbase + (size_t)rr * D, quant8(ldg_v4_hint(base + (size_t)rr * D, drop_pol)),
-                  drop_pol);
+    for (; rr < rows; rr += kSumLanes) {
+      uint2 c = quant8(ldg_v4_hint(base + (size_t)rr * D, drop_pol));
+      if (kMasked && vrow && !vrow[rr]) c = make_uint2(0u, 0u);
+      stg_v2_hint(cbase + (size_t)rr * D, c, drop_pol);
+    }
   }
 }
 

@@ -95,6 +95,8 @@ def select_quant(
     quantize: bool = True,
     quantize_v: bool = False,
     return_pooled: bool = False,
+    q_valid: torch.Tensor | None = None,
+    k_valid: torch.Tensor | None = None,
     workspace: Workspace | None = None,
 ) -> Selection:
     """Pooled-QK block selection fused with per-block int8 quantisation.
@@ -105,6 +107,11 @@ def select_quant(
     highest pooled cosine (``F.normalize(mean)`` dot product, as
     ``proposed/qk_uncertainty_tangent_attention.py:1021-1042``; ties to the
     lower index), then current blocks ``0..i``.
+    ``q_valid`` / ``k_valid``: optional uint8 ``[Lq]`` / ``[Lk]`` token
+    validity of the compact packing (the same for every (b, h)); invalid
+    tokens count as zero in a block's sums and amax, leave its pooled-mean
+    denominator and get code 0
+    (``proposed/matrix_curvature_phase_frame_weave.py:5696-5699``).
     """
     if policy not in POLICIES:
         raise ValueError(f"policy must be one of {sorted(POLICIES)}")
@@ -116,6 +123,14 @@ def select_quant(
     lk = k.shape[2]
     if k.shape[:2] != (b, h) or k.shape[3] != d:
         raise ValueError(f"k shape {tuple(k.shape)} incompatible with q {tuple(q.shape)}")
+    if q_valid is not None:
+        _need_cuda("q_valid", q_valid, torch.uint8, 1)
+        if q_valid.numel() != lq:
+            raise ValueError("q_valid must have Lq entries")
+    if k_valid is not None:
+        _need_cuda("k_valid", k_valid, torch.uint8, 1)
+        if k_valid.numel() != lk:
+            raise ValueError("k_valid must have Lk entries")
     nqb, nkb = -(-lq // block_size), -(-lk // block_size)
     keep = min(budget, nkb - nqb)
     dev = q.device
@@ -134,7 +149,8 @@ def select_quant(
     ws = (workspace or _default_ws).get(dev, nbytes)
     P = _lib.ptr
     _lib.call(
-        "cast_rcsa_select_quant", P(q), P(k), P(v) if vc is not None else None, b, h, lq, lk, d,
+        "cast_rcsa_select_quant", P(q), P(k), P(v) if vc is not None else None, P(q_valid), P(k_valid),
+        b, h, lq, lk, d,
         block_size, budget, RULE_BUDGET_CAUSAL, P(idx), P(cnt), P(qc), P(qs), P(kc), P(ks), P(vc),
         P(vs), P(mode), POLICIES[policy], float(int8_tolerance), P(pooled), P(ws), ws.numel(),
         _stream(dev),
@@ -295,7 +311,7 @@ class RCSAPlan:
         _need_cuda("k", k, torch.bfloat16, 4)
         P = _lib.ptr
         _lib.call(
-            "cast_rcsa_select_quant", P(q), P(k), None, B, H, Lq, Lk, D, self.block_size,
+            "cast_rcsa_select_quant", P(q), P(k), None, None, None, B, H, Lq, Lk, D, self.block_size,
             self.budget, RULE_BUDGET_CAUSAL, P(self.indices), P(self.counts), P(self.q_codes),
             P(self.q_scales), P(self.k_codes), P(self.k_scales), None, None, P(self.qk_mode),
             POLICIES[self.policy], self.int8_tolerance, None, P(self.workspace),

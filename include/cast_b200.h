@@ -83,6 +83,12 @@ enum cast_qk_policy {
  *   q        bf16 [B,H,Lq,D]   queries of the current chunk
  *   k        bf16 [B,H,Lk,D]   history blocks then the current chunk's blocks
  *   v        bf16 [B,H,Lk,D]   may be NULL (then v_codes/v_scales ignored)
+ *   q_valid  uint8 [Lq], k_valid uint8 [Lk]: token validity of the compact
+ *            packing (proposed/matrix_curvature_phase_frame_weave.py:5696-5699),
+ *            the same for every (b,h); may be NULL (all valid).  Invalid
+ *            tokens count as zero in a block's sums, amax and RMS, are left
+ *            out of its pooled-mean denominator, and get code 0; k_valid also
+ *            applies to v.
  *   sel_idx  int32 [B,H,nQb,maxdeg], maxdeg = min(budget,nKb-nQb)+nQb, -1 pad
  *   sel_cnt  int32 [B,H,nQb]
  *   q_codes  int8 [B,H,Lq,D], q_scales float [B,H,nQb]    (may be NULL)
@@ -94,8 +100,8 @@ enum cast_qk_policy {
  * Quantiser: s = amax/127 (s = 1 if amax == 0),
  *            code = clamp(rint_half_even(x / s), -127, 127), IEEE division.
  */
-CAST_API int cast_rcsa_select_quant(const void *q, const void *k, const void *v, int B, int H, int Lq,
-                           int Lk, int D, int block_size, int budget, int rule,
+CAST_API int cast_rcsa_select_quant(const void *q, const void *k, const void *v, const uint8_t *q_valid,
+                           const uint8_t *k_valid, int B, int H, int Lq, int Lk, int D, int block_size, int budget, int rule,
                            int32_t *sel_idx, int32_t *sel_cnt, int8_t *q_codes, float *q_scales,
                            int8_t *k_codes, float *k_scales, int8_t *v_codes, float *v_scales,
                            uint8_t *qk_mode, int policy, float int8_tolerance, double *pooled,
@@ -128,7 +134,8 @@ CAST_API size_t cast_rcsa_select_quant_workspace_bytes(int B, int H, int Lq, int
  * each other's results.  Issue them on one stream, or order them with events.
  */
 #define CAST_NOALLOC_SCRATCH_BYTES (8u << 20)
-CAST_API int cast_rcsa_select_quant_noalloc(const void *q, const void *k, const void *v, int B, int H,
+CAST_API int cast_rcsa_select_quant_noalloc(const void *q, const void *k, const void *v,
+                                   const uint8_t *q_valid, const uint8_t *k_valid, int B, int H,
                                    int Lq, int Lk, int D, int block_size, int budget, int rule,
                                    int32_t *sel_idx, int32_t *sel_cnt, int8_t *q_codes,
                                    float *q_scales, int8_t *k_codes, float *k_scales,

@@ -263,15 +263,19 @@ def taba_select_from_scores(
     return sel, cnt
 
 
-def rcsa_select(q: np.ndarray, k: np.ndarray, block_size: int, budget: int):
+def rcsa_select(q: np.ndarray, k: np.ndarray, block_size: int, budget: int,
+                q_valid: np.ndarray | None = None, k_valid: np.ndarray | None = None):
     """Full RCSA selection on packed Q ``[B,H,Lq,D]`` / K ``[B,H,Lk,D]``.
 
+    ``q_valid`` / ``k_valid``: optional bool ``[Lq]`` / ``[Lk]`` token
+    validity of the compact packing; invalid tokens count as zero and leave the
+    pooled-mean denominator (``proposed/matrix_curvature_phase_frame_weave.py:5696-5699``).
     Returns ``(sel, cnt, q_norm, k_norm, scores)``.
     """
     qi = contiguous_block_index(q.shape[-2], block_size)
     ki = contiguous_block_index(k.shape[-2], block_size)
-    qs, qc = block_sums(q, qi)
-    ks, kc = block_sums(k, ki)
+    qs, qc = block_sums(q, qi, q_valid)
+    ks, kc = block_sums(k, ki, k_valid)
     qn = pooled_normalized(qs, qc)
     kn = pooled_normalized(ks, kc)
     sc = pooled_scores(qn, kn)

@@ -60,10 +60,10 @@ def test_attention_rejects_null_and_unsupported(lib):
 
 def test_select_quant_validation(lib):
     fake = ctypes.c_void_p(4096)
-    args = [fake, fake, None, 1, 1, 880, 1760, 128, 880, 8, 0, fake, fake] + [None] * 6 + [fake]
+    args = [fake, fake, None, None, None, 1, 1, 880, 1760, 128, 880, 8, 0, fake, fake] + [None] * 6 + [fake]
     st = lib.cast_rcsa_select_quant(*args, 2, 0.025, None, None, 0, None)
     assert st == 1  # auto policy with a qk_mode output needs code buffers
-    args2 = [fake, fake, None, 1, 1, 880, 1760, 96, 880, 8, 0, fake, fake] + [None] * 7
+    args2 = [fake, fake, None, None, None, 1, 1, 880, 1760, 96, 880, 8, 0, fake, fake] + [None] * 7
     st = lib.cast_rcsa_select_quant(*args2, 0, 0.025, None, None, 0, None)
     assert st == 2
     need = lib.cast_rcsa_select_quant_workspace_bytes(1, 24, 3520, 31680, 128, 880)

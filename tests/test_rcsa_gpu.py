@@ -72,6 +72,35 @@ def test_select_quant_bitexact(cuda, block, nq, nh, budget):
     assert bool((sel.qk_mode == 1).all())
 
 
+@pytest.mark.parametrize("d", [128, 64])
+def test_select_quant_valid_mask(cuda, d):
+    """Compact-packing validity (proposed/matrix_curvature_phase_frame_weave.py:5696-5699):
+    padded tokens hold large garbage here, so any leak into the sums, the
+    amax or the pooled-mean denominator changes the selection or the codes."""
+    block, nq, nh, budget = 128, 2, 6, 3
+    q, k, _ = _rand_problem(2, nq, nh, block, d=d, seed=7)
+    g = torch.Generator().manual_seed(8)
+    q_valid = torch.rand(q.shape[2], generator=g) > 0.2
+    k_valid = torch.rand(k.shape[2], generator=g) > 0.2
+    k_valid[2 * block:3 * block] = False  # a fully padded history block
+    q = torch.where(q_valid[None, None, :, None], q, torch.full_like(q, 60.0))
+    k = torch.where(k_valid[None, None, :, None], k, torch.full_like(k, -70.0))
+    sel = rcsa.select_quant(q.cuda(), k.cuda(), block_size=block, budget=budget, policy="int8",
+                            return_pooled=True, q_valid=q_valid.to(torch.uint8).cuda(),
+                            k_valid=k_valid.to(torch.uint8).cuda())
+    torch.cuda.synchronize()
+    qv, kv = q_valid.numpy(), k_valid.numpy()
+    o_sel, o_cnt, qn, kn, _ = orc.rcsa_select(_np(q), _np(k), block, budget, q_valid=qv, k_valid=kv)
+    assert np.array_equal(sel.indices.cpu().numpy(), o_sel)
+    assert np.array_equal(sel.counts.cpu().numpy(), o_cnt)
+    pooled = sel.pooled.cpu().numpy()
+    assert np.array_equal(pooled[:, :, :nq], qn) and np.array_equal(pooled[:, :, nq:], kn)
+    qc, qs = orc.quantize_blocks(_np(q), block, qv)
+    kc, ks = orc.quantize_blocks(_np(k), block, kv)
+    assert np.array_equal(sel.q_scales.cpu().numpy(), qs) and np.array_equal(sel.k_scales.cpu().numpy(), ks)
+    assert np.array_equal(sel.q_codes.cpu().numpy(), qc) and np.array_equal(sel.k_codes.cpu().numpy(), kc)
+
+
 def test_select_quant_d64_config1_golden(cuda):
     w = workloads.config1()
     g = np.load(os.path.join(GOLDEN, "cfg1_select.npz"))

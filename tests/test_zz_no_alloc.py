@@ -49,7 +49,7 @@ def _outputs(q, k, v, block, budget):
 def _args(q, k, v, block, budget, o):
     b, h, lq, d = q.shape
     P = _lib.ptr
-    return [P(q), P(k), P(v), b, h, lq, k.shape[2], d, block, budget, rcsa.RULE_BUDGET_CAUSAL,
+    return [P(q), P(k), P(v), None, None, b, h, lq, k.shape[2], d, block, budget, rcsa.RULE_BUDGET_CAUSAL,
             P(o["idx"]), P(o["cnt"]), P(o["qc"]), P(o["qs"]), P(o["kc"]), P(o["ks"]), P(o["vc"]),
             P(o["vs"]), P(o["mode"]), rcsa.POLICIES["auto"], 0.025, P(o["pooled"])]
 
@@ -99,7 +99,7 @@ def test_noalloc_rejects_oversize_before_launch():
     b, h, lq, lk, d, block = 1, 64, 4096, 65536, 128, 64
     need = lib.cast_rcsa_select_quant_workspace_bytes(b, h, lq, lk, d, block)
     assert need > NOALLOC_SCRATCH_BYTES
-    args = [None, None, None, b, h, lq, lk, d, block, 16, 0] + [None] * 9 + [2, 0.025, None, None]
+    args = [None, None, None, None, None, b, h, lq, lk, d, block, 16, 0] + [None] * 9 + [2, 0.025, None, None]
     status = lib.cast_rcsa_select_quant_noalloc(*args)
     assert status == CAST_ERR_WORKSPACE
     msg = lib.cast_last_error_message().decode()
