@@ -240,6 +240,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--heads", type=int, default=HEADS,
                     help="heads of the config-2 layer (smaller values only for profiling captures)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="BASELINE config 5 instead: 30 layers x 3 denoise steps x 8 rollouts of "
+                         "config-2 layer calls per chunk (a step = one chunk)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -260,6 +263,8 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     peaks, peak_src = load_peaks()
+    if args.sweep:
+        return run_sweep(args, world, rank, local, dev, peaks, peak_src)
 
     head_lo, head_hi = 0, args.heads
     if args.shard == "head" and world > 1:
@@ -408,6 +413,110 @@ def main():
                        "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]}
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline_sample()
+    print(json.dumps(line))
+    return 0
+
+
+SWEEP_LAYERS, SWEEP_STEPS, SWEEP_ROLLOUTS = 30, 3, 8
+
+
+def run_sweep(args, world, rank, local, dev, peaks, peak_src):
+    """per chunk, 30 layers x 3 denoise steps x 8 rollouts
+    = 720 config-2 layer calls (random-init layers: two seeded input sets of
+    the layer shape, alternating, each far larger than L2).  ``--shard head``
+    gives every GPU H/N heads of every call and all-gathers the bf16 head
+    outputs after each call on NCCL's stream (async), overlapped with the next
+    call's selection and attention; ``--shard rollout`` gives every GPU 8/N
+    rollouts with all heads and no collective.  Each layer call is one CUDA
+    graph replay; a ring of three output / gather buffers keeps in-flight
+    gathers off the buffer the next call writes."""
+    import torch
+    import torch.distributed as dist
+
+    from cast_b200 import distributed as cdist
+    from cast_b200 import rcsa, workloads
+
+    head = args.shard == "head"
+    if not head and SWEEP_ROLLOUTS % world:
+        raise SystemExit(f"{SWEEP_ROLLOUTS} rollouts do not split over {world} GPUs")
+    lo, hi = cdist.head_range(args.heads, world, rank) if head else (0, args.heads)
+    calls = SWEEP_LAYERS * SWEEP_STEPS * (SWEEP_ROLLOUTS if head else SWEEP_ROLLOUTS // world)
+    sets = []
+    for i in range(2):
+        w = workloads.config2(heads=args.heads, seed=11 + i + (0 if head else 100 * rank))
+        sets.append(tuple(t[:, lo:hi].contiguous().to(dev) for t in (w.q, w.k, w.v)))
+    b_, h_, lq_, d_ = sets[0][0].shape
+    plan = rcsa.RCSAPlan(b_, h_, lq_, sets[0][1].shape[2], d_, block_size=BLOCK, budget=BUDGET,
+                         policy=args.policy, device=dev)
+    ring = 3
+    outs = [torch.empty_like(sets[0][0]) for _ in range(ring)]
+    gath = [torch.empty((world * b_, h_, lq_, d_), dtype=torch.bfloat16, device=dev)
+            for _ in range(ring)] if head and world > 1 else None
+    graphs = {(si, r): plan.capture(*sets[si], "all", out=outs[r]) for si in range(2) for r in range(ring)}
+    works = [None] * ring
+    stream = torch.cuda.current_stream(dev)
+
+    def chunk():
+        for c in range(calls):
+            r = c % ring
+            if works[r] is not None:  # the gather that last read this slot
+                works[r].wait()
+                works[r] = None
+            graphs[(c % 2, r)].replay()
+            if gath is not None:
+                works[r] = dist.all_gather_into_tensor(gath[r], outs[r], async_op=True)
+        for r in range(ring):
+            if works[r] is not None:
+                works[r].wait()
+                works[r] = None
+
+    for _ in range(args.warmup):
+        chunk()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        chunk()
+    e.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = torch.tensor([a.elapsed_time(e) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_chunk = float(ms.item())
+    sel = plan.selection()
+    i8_ops, bf_ops = attention_ops(sel.counts.cpu(), sel.qk_mode.cpu() if sel.qk_mode is not None else None, BLOCK)
+    p_bf16 = peaks["bf16_tflops_sustained"] * 1e12
+    ideal_ms = calls * (i8_ops / (2.0 * p_bf16) + bf_ops / p_bf16) * 1e3
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "config 5 sweep: ms per chunk (30 layers x 3 denoise steps x 8 rollouts of the config-2 layer)",
+        "value": ms_chunk, "unit": "ms/chunk", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": False, "scaling": "strong", "dtype": "int8+bf16", "vs_baseline": None,
+        "data": "synthetic (two seeded config-2 input sets, alternating per call)",
+        "config": {"workload": "config5", "parallelism": f"{args.shard}-sharded x{world}",
+                   "heads_per_gpu": hi - lo, "calls_per_gpu_per_chunk": calls, "policy": args.policy},
+        "ms_per_layer_call_per_gpu": ms_chunk / calls,
+        "roofline": {"bound": "tensor", "ideal_ms_per_gpu": ideal_ms, "frac": ideal_ms / ms_chunk,
+                     "note": f"selection + attention of every call vs the attention tensor work at the "
+                             f"{peak_src} sustained bf16 peak ({peaks['bf16_tflops_sustained']} TFLOP/s, int8 = 2x)"},
+        "collective": ("all-gather of bf16 head outputs after every call on NCCL's stream, overlapped with "
+                       "the next call" if gath is not None else "none"),
+        "gpu_launches": 3 * calls * args.steps,
+        "clocks": clocks,
+    }
     print(json.dumps(line))
     return 0
 

@@ -318,17 +318,26 @@ class RCSAPlan:
             self.workspace.numel(), _stream(self.device),
         )
 
-    def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """Attention with the last selection; into ``out`` (bf16 ``[B,H,Lq,D]``)
+        when given, else into the plan's own output buffer."""
         B, H, Lq, Lk, D = self.shape
         _need_cuda("v", v, torch.bfloat16, 4)
+        if out is None:
+            out = self.out
+        elif tuple(out.shape) != (B, H, Lq, D):
+            raise ValueError("out shape differs from the plan")
+        else:
+            _need_cuda("out", out, torch.bfloat16, 4)
         P = _lib.ptr
         _lib.call(
             "cast_rcsa_attention", P(q), P(k), P(v), P(self.q_codes), P(self.q_scales),
             P(self.k_codes), P(self.k_scales), P(self.qk_mode), P(self.indices), P(self.counts),
             int(self.indices.shape[-1]), None, B, H, Lq, Lk, D, self.block_size, self.block_size,
-            float(self.sm_scale), P(self.out), None, _stream(self.device),
+            float(self.sm_scale), P(out), None, _stream(self.device),
         )
-        return self.out
+        return out
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         self.select(q, k)
@@ -338,23 +347,24 @@ class RCSAPlan:
         return Selection(self.indices, self.counts, self.q_codes, self.q_scales, self.k_codes,
                          self.k_scales, None, None, self.qk_mode, None)
 
-    def capture(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, parts: str = "all"):
+    def capture(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, parts: str = "all",
+                out: torch.Tensor | None = None):
         """CUDA graph of one call on these input buffers (``parts``: all,
-        select or attend).  Replaying it recomputes from the buffers' current
-        contents."""
+        select or attend; the attention writes ``out`` when given).  Replaying
+        it recomputes from the buffers' current contents."""
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            self._run_parts(q, k, v, parts)  # warm the launch paths on this stream
+            self._run_parts(q, k, v, parts, out)  # warm the launch paths on this stream
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         with torch.cuda.graph(g, stream=s):
-            self._run_parts(q, k, v, parts)
+            self._run_parts(q, k, v, parts, out)
         return g
 
-    def _run_parts(self, q, k, v, parts):
+    def _run_parts(self, q, k, v, parts, out=None):
         if parts in ("all", "select"):
             self.select(q, k)
         if parts in ("all", "attend"):
-            self.attend(q, k, v)
+            self.attend(q, k, v, out)
