@@ -240,6 +240,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--heads", type=int, default=HEADS,
                     help="heads of the config-2 layer (smaller values only for profiling captures)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3],
+                    help="2: the headline layer (default); 3: BASELINE config 3, 128 history frames, "
+                         "anchor-only queries (Lq=1760), budget 16")
     ap.add_argument("--sweep", action="store_true",
                     help="BASELINE config 5 instead: 30 layers x 3 denoise steps x 8 rollouts of "
                          "config-2 layer calls per chunk (a step = one chunk)")
@@ -269,7 +272,11 @@ def main():
     head_lo, head_hi = 0, args.heads
     if args.shard == "head" and world > 1:
         head_lo, head_hi = cdist.head_range(args.heads, world, rank)
-    w = workloads.config2(heads=args.heads, seed=1 + (rank if args.shard == "rollout" else 0))
+    if args.config == 3:
+        w = workloads.config3(heads=args.heads)
+    else:
+        w = workloads.config2(heads=args.heads, seed=1 + (rank if args.shard == "rollout" else 0))
+    budget = w.budget
     q_h = w.q[:, head_lo:head_hi].contiguous()
     k_h = w.k[:, head_lo:head_hi].contiguous()
     v_h = w.v[:, head_lo:head_hi].contiguous()
@@ -280,7 +287,7 @@ def main():
 
     stream = torch.cuda.current_stream(dev)
     b_, h_, lq_, d_ = q.shape
-    plan = rcsa.RCSAPlan(b_, h_, lq_, k.shape[2], d_, block_size=BLOCK, budget=BUDGET,
+    plan = rcsa.RCSAPlan(b_, h_, lq_, k.shape[2], d_, block_size=BLOCK, budget=budget,
                          policy=args.policy, device=dev)
 
     # eager warm-up through the plan (no allocation per call)
@@ -371,6 +378,8 @@ def main():
     achieved = (i8_ops + bf_ops) / (att_ms * 1e-3) / 1e12
     peak_eff = (i8_ops + bf_ops) / t_roof / 1e12
     int8_frac = float(sel.qk_mode.float().mean()) if sel.qk_mode is not None else 0.0
+    sq_read = (q.numel() + k.numel()) * 2
+    sq_bytes = sq_read + (q.numel() + k.numel())  # bf16 read + int8 codes written
 
     if world > 1:
         dist.destroy_process_group()
@@ -382,23 +391,32 @@ def main():
         "higher_is_better": False,
         "scaling": "weak" if args.shard == "rollout" else "strong",
         "vs_baseline": None, "dtype": "int8+bf16" if args.policy != "bf16" else "bf16",
-        "data": "synthetic (seeded config 2: N(0,1)*U(0.5,2) per head)",
+        "data": ("synthetic (seeded config 2: N(0,1)*U(0.5,2) per head)" if args.config == 2 else
+                 "synthetic (seeded config 3: N(0,1)*U(0.5,2) per head, linear drift over history frames)"),
         "config": {
-            "workload": "config2: RCSA layer (select+int8 quant+block-sparse attention), "
-                        "H=24 d128, Lq=3520 (4x880), 32+4 key frames, budget 8, block-causal",
+            "workload": ("config2: RCSA layer (select+int8 quant+block-sparse attention), "
+                         "H=24 d128, Lq=3520 (4x880), 32+4 key frames, budget 8, block-causal"
+                         if args.config == 2 else
+                         "config3: RCSA layer, H=24 d128, 128 history frames + 2 anchors, "
+                         "anchor-only queries Lq=1760 (2x880), budget 16, block-causal"),
             "parallelism": f"{args.shard}-sharded x{world}",
             "policy": args.policy, "int8_row_fraction": int8_frac,
             "heads_per_gpu": head_hi - head_lo,
-            "l2": "inputs larger than L2 (Q+K 216 MB read per step by the selection pass)",
+            "l2": f"inputs larger than L2 (Q+K {sq_read / 1e6:.0f} MB read per step by the selection pass)",
         },
         "attention_us": att_ms * 1000.0,
         "select_quant_us": sel_ms * 1000.0,
+        "select_quant_roofline": {
+            "bound": "hbm", "algorithmic_bytes": sq_bytes, "achieved_gbs": sq_bytes / (sel_ms * 1e-3) / 1e9,
+            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": sq_bytes / (sel_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "note": "selection + quantisation kernels: Q+K bf16 read, int8 codes written (pooled/RMS/scales ignored)",
+        },
         "host_enqueue_us_eager": host_us,
         "timing": "CUDA graph replay of the 3-kernel layer call; events on the replay stream",
         "roofline": {
             "bound": "tensor", "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
             "frac": achieved / peak_eff,
-            "traffic": ATTN_TRAFFIC_BYTES.get(args.policy) if args.heads == HEADS else None,
+            "traffic": ATTN_TRAFFIC_BYTES.get(args.policy) if (args.heads == HEADS and args.config == 2) else None,
             "note": (f"attention kernel; peak = work-weighted harmonic of bf16 {peaks['bf16_tflops']} "
                      f"TFLOP/s ({peak_src} cuBLAS burst) and int8 = 2x bf16 (no measured int8 peak); "
                      "traffic = ncu DRAM bytes per launch; "
@@ -411,7 +429,7 @@ def main():
     if e2e:
         line["e2e"] = {"value": e2e_ms * 1000.0 / calls_per_step, "unit": "us/call",
                        "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]}
-    if not args.no_cpu_baseline and world == 1:
+    if not args.no_cpu_baseline and world == 1 and args.config == 2:
         line["cpu_baseline"] = cpu_baseline_sample()
     print(json.dumps(line))
     return 0

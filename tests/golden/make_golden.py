@@ -23,6 +23,9 @@ Files:
   the explicit-softmax attention output (bf16 path and int8 simulation).
 * ``cfg2_select_h2.npz`` -- config 2, heads 0..1: reference-primitive scores
   and the budget rule's selection.
+* ``cfg3_select_h2.npz`` -- config 3 (anchor queries over 128 history
+  frames, budget 16) generated with 2 heads: reference-primitive scores and
+  the budget rule's selection.
 * ``par_*.npz``          -- ``WorldAlignedSpectralResidualCorrector.correct``
   (``proposed/matrix_world_spectral_residual.py:5283``) with the factory's FC
   knobs on reduced-channel inputs (targets stored as bf16 bits) and its
@@ -130,6 +133,21 @@ def make_cfg2(manifest: dict):
                         scores_f32=scores, selected=sel, counts=cnt)
 
 
+def make_cfg3(manifest: dict):
+    from interaction_accel.methods.proposed.reciprocal_joint_attention import _tile_visual_tensor
+
+    w = workloads.config3(heads=2)
+    manifest["inputs"]["config3_h2"] = {"q": sha(w.q), "k": sha(w.k), "v": sha(w.v)}
+    q, k = w.q, w.k
+    nq, nk = q.shape[2] // 880, k.shape[2] // 880
+    qn = ref_pooled(_tile_visual_tensor, q, nq, (22, 40), (1, 22, 40))
+    kn = ref_pooled(_tile_visual_tensor, k, nk, (22, 40), (1, 22, 40))
+    scores = torch.matmul(qn, kn.transpose(-2, -1)).numpy()
+    sel, cnt = budget_rule(scores, nq, w.budget)
+    np.savez_compressed(os.path.join(HERE, "cfg3_select_h2.npz"),
+                        scores_f32=scores, selected=sel, counts=cnt)
+
+
 def par_corrector():
     from interaction_accel.methods.proposed.matrix_world_spectral_residual import (
         WorldAlignedSpectralResidualCorrector,
@@ -208,16 +226,27 @@ def make_par(manifest: dict):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the CAST src/ directory")
-    ap.add_argument("--skip-cfg4", action="store_true")
+    ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "par"),
+                    help="regenerate these fixtures only; other manifest entries are kept")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     # The reference's PAR path calls torch.cuda.current_stream(); on a CPU-only
     # host that call is replaced by a no-op (proposed/matrix_world_spectral_residual.py:3007).
     torch.cuda.current_stream = lambda *a, **k: None
     manifest = {"inputs": {}, "files": {}}
-    make_cfg1({}, manifest)
-    make_cfg2(manifest)
-    make_par(manifest)
+    mpath = os.path.join(HERE, "MANIFEST.json")
+    if args.only and os.path.exists(mpath):
+        with open(mpath) as fh:
+            manifest = json.load(fh)
+    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "par"))
+    if "cfg1" in todo:
+        make_cfg1({}, manifest)
+    if "cfg2" in todo:
+        make_cfg2(manifest)
+    if "cfg3" in todo:
+        make_cfg3(manifest)
+    if "par" in todo:
+        make_par(manifest)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             with open(os.path.join(HERE, f), "rb") as fh:

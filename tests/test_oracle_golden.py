@@ -34,6 +34,8 @@ def test_workload_generators_reproduce_golden_inputs():
     w = workloads.config1()
     assert _sha(w.meta["q_full"]) == man["config1"]["q_full"]
     assert _sha(w.k) == man["config1"]["k"] and _sha(w.v) == man["config1"]["v"]
+    w3 = workloads.config3(heads=2)
+    assert [_sha(t) for t in (w3.q, w3.k, w3.v)] == [man["config3_h2"][n] for n in "qkv"]
     assert _sha(workloads.config4(channels=64).full_residual) == man["par_c64"]["full_residual"]
     assert _sha(workloads.par_motion(channels=64).full_residual) == man["par_motion_c64"]["full_residual"]
 
@@ -66,6 +68,15 @@ def test_budget_rule_matches_reference_primitives_config2_two_heads():
     q = w.q[:, :2].float().numpy()
     k = w.k[:, :2].float().numpy()
     sel, cnt, _, _, scores = orc.rcsa_select(q, k, 880, 8)
+    assert np.array_equal(sel, g["selected"]) and np.array_equal(cnt, g["counts"])
+    assert np.abs(scores - g["scores_f32"]).max() < 1e-5
+
+
+def test_budget_rule_matches_reference_primitives_config3():
+    """Anchor-only queries over a 128-frame history, budget 16."""
+    g = np.load(os.path.join(GOLDEN, "cfg3_select_h2.npz"))
+    w = workloads.config3(heads=2)
+    sel, cnt, _, _, scores = orc.rcsa_select(w.q.float().numpy(), w.k.float().numpy(), 880, w.budget)
     assert np.array_equal(sel, g["selected"]) and np.array_equal(cnt, g["counts"])
     assert np.abs(scores - g["scores_f32"]).max() < 1e-5
 

@@ -222,6 +222,38 @@ def test_rcsa_config2_two_heads(cuda):
     assert ma < MAX_ABS and aa < MEAN_ABS
 
 
+def test_rcsa_config3_two_heads(cuda):
+    """Config 3 shape (anchor queries 0 and 3 over 128 history frames + the
+    two anchor key frames, budget 16) generated with 2 heads, through the full
+    RCSA call."""
+    w = workloads.config3(heads=2)
+    q, k, v = w.q, w.k, w.v
+    gold = np.load(os.path.join(GOLDEN, "cfg3_select_h2.npz"))
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    results = {}
+    for policy in ("bf16", "auto", "int8"):
+        out, sel = rcsa.rcsa_attention(qd, kd, vd, block_size=880, budget=w.budget, policy=policy)
+        torch.cuda.synchronize()
+        results[policy] = (out, sel)
+    sel = results["int8"][1]
+    o_sel, o_cnt = _check_selection(sel, q, k, 880, w.budget)
+    # the reference's float32 pooled scores give the same selection
+    assert np.array_equal(o_sel, gold["selected"]) and np.array_equal(o_cnt, gold["counts"])
+    assert o_sel.shape == (1, 2, 2, 18)
+    qc, qs, kc, ks = _check_codes(sel, q, k, 880)
+    ref_bf16 = orc.block_sparse_attention(_np(q), _np(k), _np(v), o_sel, o_cnt, 880, 880)
+    ref_int8 = orc.block_sparse_attention(_np(q), _np(k), _np(v), o_sel, o_cnt, 880, 880,
+                                          q_codes=qc, q_scales=qs, k_codes=kc, k_scales=ks)
+    mb, ab = _errs(results["bf16"][0], ref_bf16)
+    mi, ai = _errs(results["int8"][0], ref_int8)
+    ma, aa = _errs(results["auto"][0], ref_bf16)
+    print(f"bf16 {mb:.2e}/{ab:.2e} int8-vs-sim {mi:.2e}/{ai:.2e} auto-vs-bf16 {ma:.2e}/{aa:.2e} "
+          f"modes {results['auto'][1].qk_mode.flatten().tolist()}")
+    assert mb < MAX_ABS and ab < MEAN_ABS
+    assert mi < MAX_ABS and ai < MEAN_ABS
+    assert ma < MAX_ABS and aa < MEAN_ABS
+
+
 def test_rcsa_config2_full_properties(cuda):
     """All 24 heads at full size: structure of the selection, code
     reconstruction bound, finite outputs, and int8/bf16 agreement where the
