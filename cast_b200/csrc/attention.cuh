@@ -51,6 +51,12 @@ constexpr int kMaxKStages = 4;
 constexpr int kVStages = 3;
 constexpr int kMaxBlockList = 256;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kMaxSplitItems = 512;  // items cut into parts in one launch
+constexpr int kMaxItemParts = 64;    // parts of one cut item
+// Partial result of one part: O of both query tiles (fp32, [tile][column]
+// [row], so a warp's 32 rows are contiguous), then per tile the running max
+// and the row sum of its 128 rows.
+constexpr int kPartSlotFloats = 2 * 128 * 128 + 2 * 2 * 128;
 
 // Shared memory (offsets from the 1024-byte aligned base).  The Q and K
 // areas depend on the QK^T precision of the CTA:
@@ -84,7 +90,24 @@ struct AttnParams {
   int n_full_items;      // BH * nqb * full_pairs
   int default_mode;      // used when qk_mode == nullptr
   float sm_scale_log2;
+  // Work split.  CTA x < n_whole runs item x over all its key tiles.  Item
+  // n_whole + s (s < n_split) is cut along its key tiles into the parts
+  // part_first[s] .. part_first[s+1]-1, run by CTAs n_whole + part; part j of
+  // n covers key tiles [j*T/n, (j+1)*T/n) of the T = part_tiles[s] the host
+  // planned, the last part everything from there on.  Each part leaves its
+  // partial result in slot `part` of part_ws; the last part of the item to
+  // finish (counted in part_counter[s], zero between launches) merges them.
+  int n_whole, n_split;
+  int *part_counter;
+  float *part_ws;
+  uint16_t part_first[kMaxSplitItems + 1];
+  uint16_t part_tiles[kMaxSplitItems];
 };
+
+// First key tile of part j of n over T planned tiles.
+__device__ __forceinline__ int part_lo(int j, int T, int n) {
+  return (int)(((long long)j * T) / n);
+}
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -368,15 +391,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t *mma_drain = pv_done + 4;
   uint64_t *merge_bar = mma_drain + 2;  // split items: warpgroup 1's partial result is ready
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + AttnSmem::tmem_slot);
+  volatile uint32_t *part_flag = tmem_slot + 1;  // this CTA merges its cut item
   int32_t *blist = reinterpret_cast<int32_t *>(smem + AttnSmem::blist);
   int *err = &g_cast_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   // ---- work item (full query-tile pairs first, heaviest query blocks first)
+  // and, for a cut item, which part of it
+  int x = blockIdx.x, split_idx = -1, part = 0, n_parts = 1, planned = 0;
+  if (x >= p.n_whole) {
+    const int b = x - p.n_whole;
+    int lo = 0, hi = p.n_split;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if ((int)p.part_first[mid] <= b)
+        lo = mid;
+      else
+        hi = mid;
+    }
+    split_idx = lo;
+    part = b - (int)p.part_first[lo];
+    n_parts = (int)p.part_first[lo + 1] - (int)p.part_first[lo];
+    planned = p.part_tiles[lo];
+    x = p.n_whole + lo;
+  }
   int bh, qb, pair;
   {
-    int x = blockIdx.x;
     if (x < p.n_full_items) {
       pair = x % p.full_pairs;
       const int rest = x / p.full_pairs;
@@ -393,7 +434,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int nq = min(2, p.q_tiles - t0);
   const int row_item = bh * p.nqb + qb;
   const int n_blocks = min(max(p.counts[row_item], 0), min(p.max_degree, kMaxBlockList));
-  const int n_kv = n_blocks * p.k_tiles;  // 128-key tiles
+  const int n_kv_item = n_blocks * p.k_tiles;  // 128-key tiles of the item
+  // This CTA's key tiles [kt_lo, kt_lo + n_kv), and the number of the item's
+  // parts that have any (n_live; 1 = this CTA writes the output itself).
+  int kt_lo = 0, n_kv = n_kv_item, n_live = 1;
+  if (split_idx >= 0) {
+    const int lo = part_lo(part, planned, n_parts);
+    const int hi = part + 1 == n_parts ? INT_MAX : part_lo(part + 1, planned, n_parts);
+    kt_lo = min(lo, n_kv_item);
+    n_kv = min(hi, n_kv_item) - kt_lo;
+    n_live = 0;
+    for (int j = 0; j < n_parts; ++j) n_live += part_lo(j, planned, n_parts) < n_kv_item;
+    if (n_kv_item == 0) {
+      if (part > 0) return;  // part 0 writes the item's (zero) rows
+      n_live = 1;
+    } else if (n_kv == 0) {
+      return;
+    }
+  }
   // A single query tile (the last of an odd tile count) splits its key tiles
   // between the two warpgroups (split item), whose partial results are merged
   // at the end; a pair gives each warpgroup its own query tile.
@@ -454,7 +512,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         int issued = 0;
         for (int j = 0; j < n_kv; ++j) {  // ring position j
-          const int kt = ring0.key_tile(j);
+          const int kt = kt_lo + ring0.key_tile(j);
           const int blk = blist[kt / p.k_tiles];
           const int tin = kt % p.k_tiles;
           const int krow = (blk >= 0 && blk < p.nkb) ? blk * p.k_block + tin * 128 : 0;
@@ -480,7 +538,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0 && n_kv > 0) {
         int issued = 0;
         for (int j = 0; j < n_kv; ++j) {  // ring position j
-          const int kt = ring0.key_tile(j);
+          const int kt = kt_lo + ring0.key_tile(j);
           const int blk = blist[kt / p.k_tiles];
           const int tin = kt % p.k_tiles;
           const int krow = (blk >= 0 && blk < p.nkb) ? blk * p.k_block + tin * 128 : 0;
@@ -523,7 +581,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t s_addr = tmem + lane_off + 256 + ti * 128;
     const bool active = ti < n_groups;
     const int my_steps = 2 * (ti == 0 ? n_a : n_b);           // 64-key steps of this warpgroup
-    const int start_tile = (split && ti == 1) ? n_a : 0;        // its first key tile
+    const int start_tile = kt_lo + ((split && ti == 1) ? n_a : 0);  // its first key tile
     const int qrow_in_block = (t0 + (split ? 0 : ti)) * 128 + row;
     const int qrow = qb * p.q_block + qrow_in_block;
     const bool row_valid = active && qrow_in_block < p.q_block && qrow < p.Lq;
@@ -695,10 +753,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       castdev::tc_fence_before();
       __syncwarp();
       if (lane == 0) castdev::mbar_arrive(merge_bar);
-    } else if (active && ok) {
+    } else if (active) {
       float scale0 = 1.0f, scale1 = 0.0f;
       const uint32_t o1_addr = tmem + lane_off + 128;
-      if (split) {
+      if (split && ok) {
         ok = __all_sync(0xffffffffu, castdev::mbar_wait(merge_bar, 0, err));
         castdev::tc_fence_after();
         const uint32_t s1_addr = tmem + lane_off + 256 + 128;
@@ -711,12 +769,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l_run = l_run * scale0 + l1 * scale1;
         m_run = m;
       }
-      const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-      __nv_bfloat16 *orow = p.out + ((size_t)bh * p.Lq + qrow) * 128;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t o[32];
-        if (my_steps > 0 && ok) {
+      // 32 columns of this row's O (the split halves merged), unnormalised
+      auto load_o = [&](int cc, uint32_t (&o)[32]) {
+        if (my_steps > 0) {
           castdev::tmem_ld32(o_addr + 32 * cc, o);
           if (split) {
             uint32_t o1[32];
@@ -733,20 +788,88 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = 0u;
         }
-        if (row_valid) {
-          uint4 w[4];
-          uint32_t *wp = reinterpret_cast<uint32_t *>(w);
+      };
+      auto store_row = [&](int cc, const float (&o)[32], float inv_l) {
+        uint4 w[4];
+        uint32_t *wp = reinterpret_cast<uint32_t *>(w);
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            wp[c] = pack_bf16x2(__uint_as_float(o[2 * c]) * inv_l,
-                                __uint_as_float(o[2 * c + 1]) * inv_l);
-          uint4 *dst = reinterpret_cast<uint4 *>(orow + 32 * cc);
+        for (int c = 0; c < 16; ++c) wp[c] = pack_bf16x2(o[2 * c] * inv_l, o[2 * c + 1] * inv_l);
+        uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)bh * p.Lq + qrow) * 128 + 32 * cc);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) dst[c] = w[c];
+        for (int c = 0; c < 4; ++c) dst[c] = w[c];
+      };
+      if (n_live == 1) {
+        // the whole item ran here: normalise and write
+        if (ok) {
+          const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t o[32];
+            load_o(cc, o);
+            if (row_valid) store_row(cc, *reinterpret_cast<float(*)[32]>(o), inv_l);
+          }
+          if (row_valid && p.lse)
+            p.lse[(size_t)bh * p.Lq + qrow] = l_run > 0.0f ? m_run + __log2f(l_run) : -INFINITY;
+        }
+      } else {
+        // Cut item: leave this part's O, running max and row sum in its
+        // slot; the item's last part to arrive merges every slot
+        // (O = sum_j O_j 2^(m_j - m), l likewise, m = max_j m_j).
+        const uint32_t n_thr = 128u * (split ? 1u : (uint32_t)nq);
+        const int mo = 2 * 128 * 128 + ti * 256 + row;  // running max of this row in a slot
+        float *slot = p.part_ws + (size_t)(blockIdx.x - p.n_whole) * kPartSlotFloats;
+        if (ok) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t o[32];
+            load_o(cc, o);
+            float *dst = slot + ti * 16384 + 32 * cc * 128 + row;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) dst[c * 128] = __uint_as_float(o[c]);
+          }
+          slot[mo] = m_run;
+          slot[mo + 128] = l_run;
+        }
+        __threadfence();
+        castdev::named_bar_sync(1, n_thr);
+        if (threadIdx.x == 0) {
+          const int prev = atomicAdd(&p.part_counter[split_idx], 1);
+          const uint32_t last = prev == n_live - 1;
+          if (last) atomicExch(&p.part_counter[split_idx], 0);
+          *part_flag = last;
+          __threadfence();
+        }
+        castdev::named_bar_sync(1, n_thr);
+        if (*part_flag) {
+          const float *base = p.part_ws + (size_t)p.part_first[split_idx] * kPartSlotFloats;
+          float m = -INFINITY;
+          for (int j = 0; j < n_live; ++j) m = fmaxf(m, __ldcg(base + (size_t)j * kPartSlotFloats + mo));
+          float l = 0.0f;
+          for (int j = 0; j < n_live; ++j) {
+            const float *sj = base + (size_t)j * kPartSlotFloats;
+            const float mj = __ldcg(sj + mo);
+            if (mj != -INFINITY) l = fmaf(__ldcg(sj + mo + 128), fast_exp2(mj - m), l);
+          }
+          const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            float acc[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) acc[c] = 0.0f;
+            for (int j = 0; j < n_live; ++j) {
+              const float *sj = base + (size_t)j * kPartSlotFloats;
+              const float mj = __ldcg(sj + mo);
+              const float w = mj == -INFINITY ? 0.0f : fast_exp2(mj - m);
+              const float *oj = sj + ti * 16384 + 32 * cc * 128 + row;
+#pragma unroll
+              for (int c = 0; c < 32; ++c) acc[c] = fmaf(__ldcg(oj + c * 128), w, acc[c]);
+            }
+            if (row_valid) store_row(cc, acc, inv_l);
+          }
+          if (row_valid && p.lse)
+            p.lse[(size_t)bh * p.Lq + qrow] = l > 0.0f ? m + __log2f(l) : -INFINITY;
         }
       }
-      if (row_valid && p.lse)
-        p.lse[(size_t)bh * p.Lq + qrow] = l_run > 0.0f ? m_run + __log2f(l_run) : -INFINITY;
     }
   }
 

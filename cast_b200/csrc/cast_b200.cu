@@ -1,8 +1,12 @@
 // Single translation unit of libcast_b200.so: the extern "C" entry points
 // declared in include/cast_b200.h and the host-side launch logic.
+#include <algorithm>
 #include <cstdarg>
 #include <cmath>
+#include <functional>
+#include <map>
 #include <mutex>
+#include <queue>
 #include <vector>
 
 #include "common.cuh"
@@ -287,6 +291,147 @@ extern "C" int cast_taba_select(const void *q, const void *k, int B, int H, int 
 // ===========================================================================
 // block-sparse attention
 // ===========================================================================
+
+// How the attention launch is cut into CTAs.  The kernel runs one CTA per
+// work item (two 128-row query tiles of one (b*h, query block), or one
+// single tile), heaviest first; the hardware hands CTAs to SMs in launch
+// order, so the last wave leaves SMs idle while the longest items finish.
+// The plan keeps the first items whole and cuts the items of the tail along
+// their key tiles into parts whose partial results the kernel merges.  It is
+// chosen by simulating that greedy dispatch over the SMs with the expected
+// per-item work (count_hint, else max_degree key blocks per item): the
+// threshold of tail work per SM below which items are cut, and the part
+// length, are searched for the shortest simulated makespan.
+struct AttnSplitPlan {
+  int n_whole = 0, n_split = 0, n_parts = 0;
+  std::vector<uint16_t> first, tiles;
+  size_t ws_bytes = 0;
+};
+
+static size_t attn_counter_bytes(int n_split) { return ((size_t)n_split * 4 + 255) / 256 * 256; }
+
+static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_tiles,
+                                          int max_degree, const int32_t *count_hint, int n_sms) {
+  using castk::kMaxItemParts;
+  using castk::kMaxSplitItems;
+  const int full_pairs = q_tiles / 2;
+  const int n_full = BH * nqb * full_pairs;
+  const int n_items = n_full + (q_tiles % 2 ? BH * nqb : 0);
+  const int deg = std::min(max_degree, castk::kMaxBlockList);
+  // key tiles (T) and cost per item, in the kernel's item order
+  std::vector<int> T(n_items);
+  std::vector<double> cost(n_items);
+  for (int x = 0; x < n_items; ++x) {
+    int bh, qb;
+    bool pair_item = x < n_full;
+    if (pair_item) {
+      const int rest = x / full_pairs;
+      bh = rest % BH;
+      qb = nqb - 1 - rest / BH;
+    } else {
+      const int y = x - n_full;
+      bh = y % BH;
+      qb = nqb - 1 - y / BH;
+    }
+    const int c = count_hint ? std::min(std::max(count_hint[(size_t)bh * nqb + qb], 0), deg) : deg;
+    T[x] = c * k_tiles;
+    // a single tile splits its key tiles over both softmax warpgroups
+    cost[x] = pair_item || T[x] < 2 ? T[x] : 0.5 * T[x];
+  }
+  // Per-CTA cost in key-tile steps (launch, pipeline fill and drain: ~3
+  // tile steps measured) and per cut part (partial write and merge).
+  const double kCtaCost = 3.0, kPartCost = 0.5;
+  auto simulate = [&](const std::vector<double> &d) {
+    std::priority_queue<double, std::vector<double>, std::greater<double>> sm;
+    for (int i = 0; i < n_sms; ++i) sm.push(0.0);
+    double end = 0.0;
+    for (double w : d) {
+      const double t = sm.top() + w + kCtaCost;
+      sm.pop();
+      sm.push(t);
+      end = std::max(end, t);
+    }
+    return end;
+  };
+  std::vector<double> suffix(n_items + 1, 0.0);
+  for (int x = n_items - 1; x >= 0; --x) suffix[x] = suffix[x + 1] + cost[x];
+
+  AttnSplitPlan best;
+  best.n_whole = n_items;
+  double best_t = simulate(cost);
+  std::vector<double> d;
+  std::vector<int> nparts;
+  for (int thr = 4; thr <= 64; thr += 4) {
+    int X = 0;
+    while (X < n_items && suffix[X] > (double)thr * n_sms) ++X;
+    if (X == n_items || n_items - X > kMaxSplitItems) continue;
+    for (int len = 4; len <= 64; len += 4) {
+      d.assign(cost.begin(), cost.begin() + X);
+      nparts.assign(n_items - X, 1);
+      int total = 0;
+      for (int x = X; x < n_items; ++x) {
+        const int n = std::max(1, std::min({(T[x] + len - 1) / len, kMaxItemParts, T[x]}));
+        nparts[x - X] = n;
+        total += n;
+        for (int j = 0; j < n; ++j) d.push_back(cost[x] / n + (n > 1 ? kPartCost : 0.0));
+      }
+      if (total > 65535) continue;
+      const double t = simulate(d);
+      if (t < best_t - 1e-9) {
+        best_t = t;
+        best.n_whole = X;
+        best.n_split = n_items - X;
+        best.n_parts = total;
+        best.first.assign(1, 0);
+        best.tiles.clear();
+        for (int x = X; x < n_items; ++x) {
+          best.first.push_back((uint16_t)(best.first.back() + nparts[x - X]));
+          best.tiles.push_back((uint16_t)std::min(T[x], 65535));
+        }
+      }
+    }
+  }
+  if (best.n_split > 0)
+    best.ws_bytes = attn_counter_bytes(best.n_split) +
+                    (size_t)best.n_parts * castk::kPartSlotFloats * sizeof(float);
+  return best;
+}
+
+// Plans are cached per (shape, hint, SM count): the search runs once per
+// problem shape.
+static std::mutex g_attn_plan_mutex;
+static std::map<std::vector<int32_t>, AttnSplitPlan> g_attn_plans;
+
+static AttnSplitPlan attention_plan(int BH, int nqb, int q_tiles, int k_tiles, int max_degree,
+                                    const int32_t *count_hint, int n_sms) {
+  std::vector<int32_t> key = {BH, nqb, q_tiles, k_tiles, max_degree, n_sms, count_hint ? 1 : 0};
+  if (count_hint) key.insert(key.end(), count_hint, count_hint + (size_t)BH * nqb);
+  std::lock_guard<std::mutex> lock(g_attn_plan_mutex);
+  auto it = g_attn_plans.find(key);
+  if (it != g_attn_plans.end()) return it->second;
+  if (g_attn_plans.size() >= 64) g_attn_plans.clear();
+  AttnSplitPlan plan = plan_attention_split(BH, nqb, q_tiles, k_tiles, max_degree, count_hint, n_sms);
+  g_attn_plans.emplace(std::move(key), plan);
+  return plan;
+}
+
+static int attention_dims_ok(int B, int H, int Lq, int Lk, int q_block, int k_block, int max_degree) {
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || q_block <= 0 || k_block <= 0 || max_degree <= 0)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
+  return CAST_OK;
+}
+
+extern "C" size_t cast_rcsa_attention_workspace_bytes(int B, int H, int Lq, int Lk, int q_block,
+                                                       int k_block, int max_degree,
+                                                       const int32_t *count_hint) {
+  if (attention_dims_ok(B, H, Lq, Lk, q_block, k_block, max_degree)) return 0;
+  int n_sms = 0;
+  if (current_device_sm100(&n_sms)) return 0;
+  return attention_plan(B * H, ceil_div(Lq, q_block), ceil_div(q_block, 128), ceil_div(k_block, 128),
+                        max_degree, count_hint, n_sms)
+      .ws_bytes;
+}
+
 extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
                                    const int8_t *q_codes, const float *q_scales,
                                    const int8_t *k_codes, const float *k_scales,
@@ -294,11 +439,12 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
                                    const int32_t *counts, int max_degree,
                                    const uint8_t *key_valid, int B, int H, int Lq, int Lk, int D,
                                    int q_block, int k_block, float sm_scale, void *out,
-                                   float *lse, cast_stream_t stream) {
+                                   float *lse, const int32_t *count_hint, void *workspace,
+                                   size_t workspace_bytes, cast_stream_t stream) {
   if (!q || !k || !v || !indices || !counts || !out)
     return fail(CAST_ERR_INVALID_ARGUMENT, "q, k, v, indices, counts and out are required");
-  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || q_block <= 0 || k_block <= 0 || max_degree <= 0)
-    return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
+  int st = attention_dims_ok(B, H, Lq, Lk, q_block, k_block, max_degree);
+  if (st) return st;
   if (D != 128) return fail(CAST_ERR_UNSUPPORTED, "attention head_dim %d (supported: 128)", D);
   if (q_block % 16 || k_block % 16)
     return fail(CAST_ERR_UNSUPPORTED, "block sizes must be multiples of 16 (q %d, k %d)", q_block, k_block);
@@ -312,13 +458,14 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
     return fail(CAST_ERR_INVALID_ARGUMENT, "qk_mode given without int8 codes");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
       (q_codes && !aligned16(q_codes)) || (k_codes && !aligned16(k_codes)) ||
-      (key_valid && !aligned16(key_valid)))
+      (key_valid && !aligned16(key_valid)) || (workspace && !aligned16(workspace)))
     return fail(CAST_ERR_ALIGNMENT, "tensor base pointers must be 16-byte aligned");
   if (!(sm_scale > 0.0f) || !std::isfinite(sm_scale))
     return fail(CAST_ERR_INVALID_ARGUMENT, "sm_scale must be positive and finite");
   if ((long long)B * H * std::max(Lq, Lk) >= (1ll << 31))
     return fail(CAST_ERR_UNSUPPORTED, "B*H*L exceeds the 32-bit TMA coordinate range");
-  int st = current_device_sm100(nullptr);
+  int n_sms = 0;
+  st = current_device_sm100(&n_sms);
   if (st) return st;
 
   const int BH = B * H;
@@ -370,6 +517,30 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   p.default_mode = have_codes ? 1 : 0;
   p.sm_scale_log2 = sm_scale * 1.4426950408889634f;
   const int n_items = p.n_full_items + (p.q_tiles % 2 ? BH * p.nqb : 0);
+  p.n_whole = n_items;
+  p.n_split = 0;
+  p.part_counter = nullptr;
+  p.part_ws = nullptr;
+  memset(p.part_first, 0, sizeof(p.part_first));
+  memset(p.part_tiles, 0, sizeof(p.part_tiles));
+  int grid = n_items;
+  if (workspace) {
+    const AttnSplitPlan plan =
+        attention_plan(BH, p.nqb, p.q_tiles, p.k_tiles, max_degree, count_hint, n_sms);
+    if (workspace_bytes < plan.ws_bytes)
+      return fail(CAST_ERR_INVALID_ARGUMENT, "workspace of %zu bytes < %zu required", workspace_bytes,
+                  plan.ws_bytes);
+    if (plan.n_split > 0) {
+      p.n_whole = plan.n_whole;
+      p.n_split = plan.n_split;
+      p.part_counter = static_cast<int *>(workspace);
+      p.part_ws = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) +
+                                            attn_counter_bytes(plan.n_split));
+      std::copy(plan.first.begin(), plan.first.end(), p.part_first);
+      std::copy(plan.tiles.begin(), plan.tiles.end(), p.part_tiles);
+      grid = plan.n_whole + plan.n_parts;
+    }
+  }
 
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
@@ -380,7 +551,7 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   });
   CAST_CUDA_TRY(attr_err);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  castk::rcsa_attention_kernel<<<n_items, castk::kAttnThreads, castk::AttnSmem::alloc, s>>>(
+  castk::rcsa_attention_kernel<<<grid, castk::kAttnThreads, castk::AttnSmem::alloc, s>>>(
       tm_q8, tm_k8, tm_q16, tm_k16, tm_v, p);
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;

@@ -22,6 +22,8 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 
+import numpy as np
+
 import torch
 
 from . import _lib
@@ -72,15 +74,37 @@ class Workspace:
     def __init__(self):
         self._buf: dict[torch.device, torch.Tensor] = {}
 
-    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+    def get(self, device: torch.device, nbytes: int, zero: bool = False) -> torch.Tensor:
+        """A buffer of at least ``nbytes``; ``zero``: zero-filled when (re)allocated."""
         buf = self._buf.get(device)
         if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            alloc = torch.zeros if zero else torch.empty
+            buf = alloc(max(int(nbytes), 256), dtype=torch.uint8, device=device)
             self._buf[device] = buf
         return buf
 
 
 _default_ws = Workspace()
+# Attention workspaces hold arrival counters that every completed call leaves
+# at zero, so they are zero-filled once and never shared with other kernels.
+_attn_ws = Workspace()
+
+
+def budget_count_hint(B: int, H: int, nqb: int, nkb: int, budget: int) -> np.ndarray:
+    """Key blocks per (b, h, query block) under the historical-budget +
+    block-causal rule: ``min(budget, nkb - nqb)`` history blocks plus current
+    blocks ``0..i`` (host int32 ``[B,H,nQb]``, the attention's balance hint)."""
+    keep = min(budget, nkb - nqb)
+    per_qb = keep + 1 + np.arange(nqb, dtype=np.int32)
+    return np.ascontiguousarray(np.broadcast_to(per_qb, (B, H, nqb)).astype(np.int32))
+
+
+def _attention_workspace(b, h, lq, lk, q_block, k_block, max_degree, hint, device, workspace):
+    nbytes = int(_lib.load().cast_rcsa_attention_workspace_bytes(
+        b, h, lq, lk, q_block, k_block, max_degree, None if hint is None else hint.ctypes.data))
+    if nbytes == 0:
+        return None, 0
+    return (workspace or _attn_ws).get(device, nbytes, zero=True), nbytes
 
 
 def select_quant(
@@ -176,6 +200,9 @@ def block_sparse_attention(
     qk_mode: torch.Tensor | None = None,
     return_lse: bool = False,
     out: torch.Tensor | None = None,
+    count_hint=None,
+    balance: bool = True,
+    workspace: Workspace | None = None,
 ):
     """Block-sparse attention over listed key blocks (tcgen05, sm_100a).
 
@@ -183,6 +210,10 @@ def block_sparse_attention(
     ``indices[b,h,i,:counts[b,h,i]]`` with ``key_valid`` (uint8 ``[Lk]``)
     set.  ``sm_scale`` defaults to ``1/sqrt(D)`` as the reference launch does.
     With int8 codes/scales the QK^T product runs in int8 where ``qk_mode`` is 1.
+    ``balance`` cuts the items that would run last into key-tile parts merged
+    on the device (a zero-filled attention ``workspace``); ``count_hint``
+    (host ints ``[B,H,nQb]``, default ``max_degree``) is the expected
+    ``counts``, used only for that balance.
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
         _need_cuda(name, t, torch.bfloat16, 4)
@@ -197,11 +228,21 @@ def block_sparse_attention(
     if out is None:
         out = torch.empty_like(q)
     lse = torch.empty(b, h, lq, dtype=torch.float32, device=q.device) if return_lse else None
+    max_degree = int(indices.shape[-1])
+    hint, ws, nbytes = None, None, 0
+    if balance:
+        if count_hint is not None:
+            hint = np.ascontiguousarray(np.asarray(count_hint, dtype=np.int32).reshape(-1))
+            if hint.size != b * h * (-(-lq // q_block)):
+                raise ValueError("count_hint must have B*H*nQb entries")
+        ws, nbytes = _attention_workspace(b, h, lq, lk, q_block, k_block, max_degree, hint,
+                                          q.device, workspace)
     P = _lib.ptr
     _lib.call(
         "cast_rcsa_attention", P(q), P(k), P(v), P(q_codes), P(q_scales), P(k_codes), P(k_scales),
-        P(qk_mode), P(indices), P(counts), int(indices.shape[-1]), P(key_valid), b, h, lq, lk, d,
-        q_block, k_block, float(sm_scale), P(out), P(lse), _stream(q.device),
+        P(qk_mode), P(indices), P(counts), max_degree, P(key_valid), b, h, lq, lk, d,
+        q_block, k_block, float(sm_scale), P(out), P(lse),
+        None if hint is None else hint.ctypes.data, P(ws), nbytes, _stream(q.device),
     )
     return (out, lse) if return_lse else out
 
@@ -261,10 +302,13 @@ def rcsa_attention(
     sel = select_quant(q, k, None, block_size=block_size, budget=budget, policy=policy,
                        int8_tolerance=int8_tolerance, quantize=policy != "bf16",
                        workspace=workspace)
+    b, h, lq, _ = q.shape
+    nqb, nkb = -(-lq // block_size), -(-k.shape[2] // block_size)
     out = block_sparse_attention(
         q, k, v, sel.indices, sel.counts, q_block=block_size, k_block=block_size,
         sm_scale=sm_scale, q_codes=sel.q_codes, q_scales=sel.q_scales, k_codes=sel.k_codes,
         k_scales=sel.k_scales, qk_mode=sel.qk_mode,
+        count_hint=budget_count_hint(b, h, nqb, nkb, budget),
     )
     return out, sel
 
@@ -300,6 +344,14 @@ class RCSAPlan:
         self.out = torch.empty(B, H, Lq, D, dtype=torch.bfloat16, device=dev)
         nbytes = _lib.load().cast_rcsa_select_quant_workspace_bytes(B, H, Lq, Lk, D, block_size)
         self.workspace = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+        # attention: expected counts of the rule (balance hint) and its own
+        # zero-filled workspace of arrival counters and partial results
+        self.count_hint = budget_count_hint(B, H, nqb, nkb, budget)
+        with torch.cuda.device(dev):
+            nbytes = int(_lib.load().cast_rcsa_attention_workspace_bytes(
+                B, H, Lq, Lk, block_size, block_size, keep + nqb, self.count_hint.ctypes.data))
+        self.attn_workspace = (torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+                               if nbytes else None)
         self.sm_scale = 1.0 / math.sqrt(D)
         self.device = dev
 
@@ -335,7 +387,10 @@ class RCSAPlan:
             "cast_rcsa_attention", P(q), P(k), P(v), P(self.q_codes), P(self.q_scales),
             P(self.k_codes), P(self.k_scales), P(self.qk_mode), P(self.indices), P(self.counts),
             int(self.indices.shape[-1]), None, B, H, Lq, Lk, D, self.block_size, self.block_size,
-            float(self.sm_scale), P(out), None, _stream(self.device),
+            float(self.sm_scale), P(out), None, self.count_hint.ctypes.data,
+            P(self.attn_workspace),
+            0 if self.attn_workspace is None else self.attn_workspace.numel(),
+            _stream(self.device),
         )
         return out
 

@@ -181,6 +181,16 @@ CAST_API size_t cast_taba_select_workspace_bytes(int B, int H, int T, int Hl, in
  *   indices int32 [B,H,nQb,max_degree]; counts int32 [B,H,nQb]
  *   key_valid uint8 [Lk] or NULL; lse float [B,H,Lq] (log2-domain row
  *   log-sum-exp of the scaled logits) or NULL.
+ *   count_hint int32 [B,H,nQb] in HOST memory, or NULL: the counts the
+ *   caller expects (NULL = max_degree everywhere).  Only the balance of the
+ *   work over the SMs depends on it; the result follows `counts`.
+ *   workspace: device memory of cast_rcsa_attention_workspace_bytes(...)
+ *   bytes (same shape, max_degree and hint), 16-byte aligned, ZERO-FILLED
+ *   before its first use; every completed call leaves it fit for the next.
+ *   With a workspace the items that would run last are cut along their key
+ *   tiles into parts whose partial results (fp32) are merged on the device;
+ *   with NULL every item runs whole.  Calls that share a workspace must not
+ *   overlap on the GPU.
  * Supported: D == 128, q_block and k_block multiples of 16.
  */
 CAST_API int cast_rcsa_attention(const void *q, const void *k, const void *v, const int8_t *q_codes,
@@ -188,7 +198,13 @@ CAST_API int cast_rcsa_attention(const void *q, const void *k, const void *v, co
                         const uint8_t *qk_mode, const int32_t *indices, const int32_t *counts,
                         int max_degree, const uint8_t *key_valid, int B, int H, int Lq, int Lk,
                         int D, int q_block, int k_block, float sm_scale, void *out, float *lse,
+                        const int32_t *count_hint, void *workspace, size_t workspace_bytes,
                         cast_stream_t stream);
+/* Workspace bytes for cast_rcsa_attention on the current device (0: no
+ * item is cut, or the sizes are invalid / no sm_100 device). */
+CAST_API size_t cast_rcsa_attention_workspace_bytes(int B, int H, int Lq, int Lk, int q_block,
+                                                    int k_block, int max_degree,
+                                                    const int32_t *count_hint);
 
 /*
  * Phase-Aware Reconstruction (FC-PASM reference numerics) on one model call.

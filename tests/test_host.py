@@ -43,18 +43,18 @@ def test_status_strings(lib):
 
 def test_attention_rejects_null_and_unsupported(lib):
     st = lib.cast_rcsa_attention(*([None] * 10), 1, None, 1, 1, 128, 128, 128, 128, 128, 0.1,
-                                 None, None, None)
+                                 None, None, None, None, 0, None)
     assert st == 1 and b"required" in lib.cast_last_error_message()
     fake = ctypes.c_void_p(4096)
     st = lib.cast_rcsa_attention(fake, fake, fake, None, None, None, None, None, fake, fake, 1, None,
-                                 1, 1, 128, 128, 64, 128, 128, 0.1, fake, None, None)
+                                 1, 1, 128, 128, 64, 128, 128, 0.1, fake, None, None, None, 0, None)
     assert st == 2 and b"head_dim" in lib.cast_last_error_message()
     st = lib.cast_rcsa_attention(fake, fake, fake, None, None, None, None, None, fake, fake, 1, None,
-                                 1, 1, 128, 128, 128, 100, 128, 0.1, fake, None, None)
+                                 1, 1, 128, 128, 128, 100, 128, 0.1, fake, None, None, None, 0, None)
     assert st == 2 and b"multiples of 16" in lib.cast_last_error_message()
     odd = ctypes.c_void_p(4097)
     st = lib.cast_rcsa_attention(odd, fake, fake, None, None, None, None, None, fake, fake, 1, None,
-                                 1, 1, 128, 128, 128, 128, 128, 0.1, fake, None, None)
+                                 1, 1, 128, 128, 128, 128, 128, 0.1, fake, None, None, None, 0, None)
     assert st == 3
 
 

@@ -192,6 +192,59 @@ def test_longcat_active_dropin_key_valid(cuda):
     assert float(out[0, 0, block:2 * block].abs().max()) == 0.0
 
 
+@pytest.mark.parametrize("mode", ["bf16", "int8"])
+def test_attention_cut_items(cuda, mode):
+    """Items cut along their key tiles (balance=True) against whole items and
+    the oracle: random counts including 0 and max_degree, a fully masked key
+    block, ragged Lk, and count hints that are too small, too large or
+    absent (parts that run past their planned range, or are empty).  Two
+    calls in a row give identical bits (the arrival counters reset)."""
+    block, heads, nqb, nkb = 880, 2, 2, 7
+    g = torch.Generator().manual_seed(21)
+    lk = nkb * block - 300
+    q = torch.randn(1, heads, nqb * block, 128, generator=g).bfloat16()
+    k = torch.randn(1, heads, lk, 128, generator=g).bfloat16()
+    v = torch.randn(1, heads, lk, 128, generator=g).bfloat16()
+    valid = torch.rand(lk, generator=g) > 0.2
+    valid[3 * block:4 * block] = False
+    max_degree = 6
+    idx = torch.full((1, heads, nqb, max_degree), -1, dtype=torch.int32)
+    cnt = torch.tensor([[[0, max_degree], [3, 5]]], dtype=torch.int32)
+    for h in range(heads):
+        for i in range(nqb):
+            idx[0, h, i, :cnt[0, h, i]] = torch.randperm(nkb, generator=g)[:cnt[0, h, i]].to(torch.int32)
+    kw, okw = {}, {}
+    if mode == "int8":
+        kp = torch.cat([k, torch.zeros(1, heads, nkb * block - lk, 128, dtype=k.dtype)], dim=2)
+        sel = rcsa.select_quant(q.cuda(), kp.cuda(), block_size=block, budget=2, policy="int8")
+        kw = dict(q_codes=sel.q_codes, q_scales=sel.q_scales,
+                  k_codes=sel.k_codes[:, :, :lk].contiguous(), k_scales=sel.k_scales)
+        qc, qs = orc.quantize_blocks(_np(q), block)
+        kc, ks = orc.quantize_blocks(_np(kp), block)
+        okw = dict(q_codes=qc, q_scales=qs, k_codes=kc[:, :, :lk], k_scales=ks)
+    ref = orc.block_sparse_attention(_np(q), _np(k), _np(v), idx.numpy(), cnt.numpy(), block, block,
+                                     key_valid=valid.numpy(), **okw)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    common = dict(q_block=block, k_block=block, key_valid=valid.to(torch.uint8).cuda(), return_lse=True, **kw)
+    whole, lse_w = rcsa.block_sparse_attention(qd, kd, vd, idx.cuda(), cnt.cuda(), balance=False, **common)
+    for hint in (None, np.full((1, heads, nqb), 1), np.full((1, heads, nqb), max_degree),
+                 np.array([[[2, 6], [1, 4]]] * 1)):
+        outs = [rcsa.block_sparse_attention(qd, kd, vd, idx.cuda(), cnt.cuda(), count_hint=hint, **common)
+                for _ in range(2)]
+        torch.cuda.synchronize()
+        (o1, l1), (o2, l2) = outs
+        assert torch.equal(o1, o2) and torch.equal(l1, l2)
+        m, a = _errs(o1, ref)
+        print(f"{mode} hint {None if hint is None else hint.ravel().tolist()}: max {m:.2e} mean {a:.2e}")
+        assert m < MAX_ABS and a < MEAN_ABS
+        assert float((o1.float() - whole.float()).abs().max()) < MAX_ABS
+        fin = torch.isfinite(lse_w)
+        assert torch.equal(fin, torch.isfinite(l1))
+        assert float((l1[fin] - lse_w[fin]).abs().max()) < 1e-3
+    # the item with no key block writes zeros
+    assert float(o1[0, 0, :block].abs().max()) == 0.0
+
+
 def test_rcsa_config2_two_heads(cuda):
     """Config 2 shape (880-token frames, 32 history + 4 current, budget 8) on
     heads 0-1 of the seeded config-2 tensors, through the full RCSA call."""
