@@ -245,9 +245,10 @@ __device__ __forceinline__ bool mma_issuer(int i, RingMap ring, uint32_t tmem, u
   uint64_t *my_p_full = p_full + 2 * i;
   uint64_t *my_pv_done = pv_done + 2 * i;
 
-  auto issue_s = [&](int h) {
-    const uint32_t d = s_col + (h & 1) * 64;
-    const uint32_t ko = (ring.pos(h >> 1) & (KS - 1)) * kKBytes + (h & 1) * 8192;
+  // S_i of one half of the key tile at ring position r into S buffer `half`
+  auto issue_s = [&](int r, int half) {
+    const uint32_t d = s_col + half * 64;
+    const uint32_t ko = ((uint32_t)r & (KS - 1)) * kKBytes + half * 8192;
     if (kInt8) {
 #pragma unroll
       for (int s = 0; s < 4; ++s)
@@ -260,45 +261,49 @@ __device__ __forceinline__ bool mma_issuer(int i, RingMap ring, uint32_t tmem, u
       }
     }
   };
+  const int n_tiles = n_steps / 2;
 
-  const int r0 = ring.pos(0);
+  int rk = ring.pos(0);  // ring position of the next key tile to multiply
   if (!castdev::mbar_wait(q_full, 0, err) ||
-      !castdev::mbar_wait(&k_full[r0 & (KS - 1)], (r0 / KS) & 1, err))
+      !castdev::mbar_wait(&k_full[rk & (KS - 1)], (rk / KS) & 1, err))
     return false;
   castdev::tc_fence_after();
-  issue_s(0);
+  issue_s(rk, 0);
   castdev::tc_commit(&my_s_full[0]);
-  issue_s(1);
+  issue_s(rk, 1);
   castdev::tc_commit(&my_s_full[1]);
-  castdev::tc_commit(&k_empty[r0 & (KS - 1)]);
+  castdev::tc_commit(&k_empty[rk & (KS - 1)]);
 
-  for (int h = 0; h < n_steps; ++h) {
-    const int half = h & 1;
-    const int hn = h + 2;
-    const int rv = ring.pos(h >> 1);  // ring position of this step's V tile
+  // Per key tile t: steps 2t and 2t+1 (its two halves).  Ring positions,
+  // stages and phases are worked out once per tile.
+  for (int t = 0; t < n_tiles; ++t) {
+    const int rv = ring.pos(t);  // ring position of this tile's V
     const int vs = rv % kVStages;
-    if (!half && !castdev::mbar_wait(&v_full[vs], (rv / kVStages) & 1, err)) return false;
-    if (!castdev::mbar_wait(&my_p_full[half], (h >> 1) & 1, err)) return false;
-    castdev::tc_fence_after();
-    const uint32_t vo = vs * 32768 + half * 8192;
-    const uint32_t pa = s_col + half * 64;
+    const bool more = t + 1 < n_tiles;
+    if (more) rk = ring.pos(t + 1);
+    if (!castdev::mbar_wait(&v_full[vs], (rv / kVStages) & 1, err)) return false;
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
-      castdev::mma_f16_ts(o_col, pa + 8 * s, vd.at(vo + 2048 * s), idesc_pv, (h | s) != 0);
-    castdev::tc_commit(&my_pv_done[half]);
-    if (hn < n_steps) {
-      if (!half) {
-        const int rk = ring.pos(hn >> 1);
-        if (!castdev::mbar_wait(&k_full[rk & (KS - 1)], (rk / KS) & 1, err)) return false;
-        castdev::tc_fence_after();
+    for (int half = 0; half < 2; ++half) {
+      if (!castdev::mbar_wait(&my_p_full[half], t & 1, err)) return false;
+      castdev::tc_fence_after();
+      const uint32_t vo = vs * 32768 + half * 8192;
+      const uint32_t pa = s_col + half * 64;
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        castdev::mma_f16_ts(o_col, pa + 8 * s, vd.at(vo + 2048 * s), idesc_pv, (t | half | s) != 0);
+      castdev::tc_commit(&my_pv_done[half]);
+      if (more) {
+        // S of the next tile's same half, into the buffer this PV read
+        if (half == 0) {
+          if (!castdev::mbar_wait(&k_full[rk & (KS - 1)], (rk / KS) & 1, err)) return false;
+          castdev::tc_fence_after();
+        }
+        issue_s(rk, half);
+        castdev::tc_commit(&my_s_full[half]);
       }
-      issue_s(hn);
-      castdev::tc_commit(&my_s_full[half]);
     }
-    if (half) {
-      castdev::tc_commit(&v_empty[vs]);
-      if (hn < n_steps) castdev::tc_commit(&k_empty[ring.pos(hn >> 1) & (KS - 1)]);
-    }
+    castdev::tc_commit(&v_empty[vs]);
+    if (more) castdev::tc_commit(&k_empty[rk & (KS - 1)]);
   }
   return true;
 }

@@ -338,9 +338,10 @@ static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_ti
     // a single tile splits its key tiles over both softmax warpgroups
     cost[x] = pair_item || T[x] < 2 ? T[x] : 0.5 * T[x];
   }
-  // Per-CTA cost in key-tile steps (launch, pipeline fill and drain: ~3
-  // tile steps measured) and per cut part (partial write and merge).
-  const double kCtaCost = 3.0, kPartCost = 0.5;
+  // Per-CTA cost in 128-key tile steps (launch, setup, pipeline fill and
+  // drain, epilogue: ~9 us, ~4 tile steps, in CTA timelines on B200) and the
+  // extra cost of a cut part (partial result written and merged: ~2.5).
+  const double kCtaCost = 4.0, kPartCost = 2.5;
   auto simulate = [&](const std::vector<double> &d) {
     std::priority_queue<double, std::vector<double>, std::greater<double>> sm;
     for (int i = 0; i < n_sms; ++i) sm.push(0.0);
@@ -358,7 +359,9 @@ static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_ti
 
   AttnSplitPlan best;
   best.n_whole = n_items;
-  double best_t = simulate(cost);
+  // A cut plan must beat running every item whole by 5 %: the simulation
+  // does not see every cost of the cut parts.
+  double best_t = 0.95 * simulate(cost);
   std::vector<double> d;
   std::vector<int> nparts;
   for (int thr = 4; thr <= 64; thr += 4) {
