@@ -50,6 +50,12 @@ SIGNATURES = {
          c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     ),
     "cast_rcsa_attention_workspace_bytes": (c_size_t, [c_int] * 7 + [c_void_p]),
+    "cast_compact_pack": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
+         c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+    ),
+    "cast_compact_unpack": (c_int, [c_void_p, c_void_p] + [c_int] * 5 + [c_void_p, c_void_p]),
     "cast_par_fcpasm": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float,

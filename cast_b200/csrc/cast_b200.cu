@@ -13,6 +13,7 @@
 #include "select_quant.cuh"
 #include "attention.cuh"
 #include "par.cuh"
+#include "compact.cuh"
 
 namespace cast {
 
@@ -125,7 +126,8 @@ extern "C" int cast_device_error(cast_stream_t stream) {
   int v = 0, zero = 0;
   CAST_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_cast_device_error, sizeof(int)));
   CAST_CUDA_TRY(cudaMemcpyToSymbol(g_cast_device_error, &zero, sizeof(int)));
-  if (v) return fail(v, "a bounded device wait gave up (%s)", cast_status_string(v));
+  if (v) return fail(v, "device-side error: %s (a bounded wait gave up, or an index was out of range)",
+                    cast_status_string(v));
   return CAST_OK;
 }
 
@@ -531,7 +533,7 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
     const AttnSplitPlan plan =
         attention_plan(BH, p.nqb, p.q_tiles, p.k_tiles, max_degree, count_hint, n_sms);
     if (workspace_bytes < plan.ws_bytes)
-      return fail(CAST_ERR_INVALID_ARGUMENT, "workspace of %zu bytes < %zu required", workspace_bytes,
+      return fail(CAST_ERR_WORKSPACE, "workspace of %zu bytes < %zu required", workspace_bytes,
                   plan.ws_bytes);
     if (plan.n_split > 0) {
       p.n_whole = plan.n_whole;
@@ -556,6 +558,69 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   castk::rcsa_attention_kernel<<<grid, castk::kAttnThreads, castk::AttnSmem::alloc, s>>>(
       tm_q8, tm_k8, tm_q16, tm_k16, tm_v, p);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+// ===========================================================================
+// compact-layout packing (+ RoPE phase) and the output scatter
+// ===========================================================================
+static int grid_rows(long long rows, int n_sms) {
+  // enough CTAs of 128 threads to fill every SM several times over
+  return (int)std::min<long long>(rows, (long long)n_sms * 16);
+}
+
+extern "C" int cast_compact_pack(const void *q, const void *k, const void *v, int in_dtype,
+                                 const float *phase, int phase_heads, const int32_t *block_indices,
+                                 int B, int L, int H, int D, int P, void *q_out, void *k_out,
+                                 void *v_out, cast_stream_t stream) {
+  if (!q || !k || !v || !block_indices || !q_out || !k_out || !v_out)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "q, k, v, block_indices and the outputs are required");
+  if (B <= 0 || L <= 0 || H <= 0 || P <= 0) return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
+  if (D != castk::kCompactD) return fail(CAST_ERR_UNSUPPORTED, "compact path head_dim %d (supported: 128)", D);
+  if (in_dtype != 0 && in_dtype != 1)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "in_dtype %d (0 = bf16, 1 = fp32)", in_dtype);
+  if (phase && phase_heads != 1 && phase_heads != H)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "phase_heads %d must be 1 or H = %d", phase_heads, H);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(q_out) || !aligned16(k_out) ||
+      !aligned16(v_out) || (phase && !aligned16(phase)))
+    return fail(CAST_ERR_ALIGNMENT, "tensor base pointers must be 16-byte aligned");
+  int n_sms = 0;
+  int st = current_device_sm100(&n_sms);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = grid_rows((long long)B * P, n_sms);
+  const float2 *ph = reinterpret_cast<const float2 *>(phase);
+  auto *qo = static_cast<__nv_bfloat16 *>(q_out);
+  auto *ko = static_cast<__nv_bfloat16 *>(k_out);
+  auto *vo = static_cast<__nv_bfloat16 *>(v_out);
+  if (in_dtype == 0)
+    castk::compact_pack_kernel<__nv_bfloat16><<<grid, castk::kCompactThreads, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(q), static_cast<const __nv_bfloat16 *>(k),
+        static_cast<const __nv_bfloat16 *>(v), ph, phase_heads, block_indices, B, L, H, P, qo, ko, vo);
+  else
+    castk::compact_pack_kernel<float><<<grid, castk::kCompactThreads, 0, s>>>(
+        static_cast<const float *>(q), static_cast<const float *>(k), static_cast<const float *>(v), ph,
+        phase_heads, block_indices, B, L, H, P, qo, ko, vo);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+extern "C" int cast_compact_unpack(const void *packed, const int32_t *token_to_packed, int B, int L,
+                                   int H, int D, int P, void *out, cast_stream_t stream) {
+  if (!packed || !token_to_packed || !out)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "packed, token_to_packed and out are required");
+  if (B <= 0 || L <= 0 || H <= 0 || P <= 0) return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
+  if (D != castk::kCompactD) return fail(CAST_ERR_UNSUPPORTED, "compact path head_dim %d (supported: 128)", D);
+  if (!aligned16(packed) || !aligned16(out))
+    return fail(CAST_ERR_ALIGNMENT, "tensor base pointers must be 16-byte aligned");
+  int n_sms = 0;
+  int st = current_device_sm100(&n_sms);
+  if (st) return st;
+  castk::compact_unpack_kernel<<<grid_rows((long long)B * L, n_sms), castk::kCompactThreads, 0,
+                                 reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16 *>(packed), token_to_packed, B, L, H, P,
+      static_cast<__nv_bfloat16 *>(out));
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;
 }

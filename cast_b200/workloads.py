@@ -20,6 +20,7 @@ configurations of the hot path:
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field
 
 import torch
@@ -137,3 +138,46 @@ def par_motion(device: str | torch.device = "cpu", channels: int = 64,
         frames.append(crop.permute(0, 2, 3, 1).reshape(1, 880, channels))
     full = torch.stack(frames, 1).to(torch.bfloat16)
     return PARWorkload("par_motion", full.to(device), [0, 1, 4], 1, 22, 40)
+
+
+@dataclass
+class CompactCase:
+    q: torch.Tensor            # bf16 [1, L, H, 128], token order
+    k: torch.Tensor
+    v: torch.Tensor
+    coords: torch.Tensor       # long [L, 3]: compact frame, row, column
+    freqs: torch.Tensor        # complex64 [positions, 64] or [H, positions, 64]
+    memory_length: int
+    memory_latent_idx: list[int]
+    predict_latent_idx: tuple[int, int]
+    block_id: torch.Tensor     # long [L]: compact block of each token
+    n_blocks: int
+    block_size: int
+
+
+def compact_case(per_head_phase: bool = False, heads: int = 2, frames: int = 3,
+                 hw: tuple[int, int] = (4, 8), cell: tuple[int, int, int] = (1, 3, 8),
+                 memory_frames: int = 1, seed: int = 5) -> CompactCase:
+    """A small compact layout in the frame weave's conventions (memory frames
+    first, block cells of (tt, th, tw) that may be ragged, so some packed
+    slots are padding), with seeded q/k/v and a seeded unit-modulus RoPE
+    frequency table."""
+    g = torch.Generator().manual_seed(seed)
+    h0, w0 = hw
+    n = frames * h0 * w0
+    q, k, v = (torch.randn(1, n, heads, 128, generator=g).bfloat16() for _ in range(3))
+    tok = torch.arange(n)
+    t, sp = tok // (h0 * w0), tok % (h0 * w0)
+    hh, ww = sp // w0, sp % w0
+    coords = torch.stack([t, hh, ww], dim=1)
+    shape = (heads, 1024, 64) if per_head_phase else (1024, 64)
+    angles = torch.rand(shape, generator=g) * (2 * math.pi)
+    freqs = torch.polar(torch.ones(shape), angles)
+    tt, th, tw = cell
+    nh, nw = -(-h0 // th), -(-w0 // tw)
+    mem_cells = -(-memory_frames // tt)
+    tcell = torch.where(t < memory_frames, t // tt, mem_cells + (t - memory_frames) // tt)
+    block_id = tcell * nh * nw + (hh // th) * nw + ww // tw
+    n_blocks = (mem_cells + -(-(frames - memory_frames) // tt)) * nh * nw
+    return CompactCase(q, k, v, coords, freqs, memory_frames, [5 + i for i in range(memory_frames)],
+                       (7, 7 + frames - memory_frames), block_id, n_blocks, tt * th * tw)

@@ -207,6 +207,38 @@ CAST_API size_t cast_rcsa_attention_workspace_bytes(int B, int H, int Lq, int Lk
                                                     const int32_t *count_hint);
 
 /*
+ * Compact-layout packing for the compact selection / attention path, with
+ * the RoPE phase applied on the way.  Replaces, for one layer call, the
+ * reference's RoPE rotation MatrixCurvaturePhaseFrameWeave.
+ * _apply_compact_rope_phase (proposed/matrix_curvature_phase_frame_weave.py:
+ * 5565-5574) of q and k, and the packing in _compact_cwca_attention
+ * (:5677-5684: gather by block_indices, transpose, zero the padding) plus the
+ * bf16 cast of the attention launch (proposed/matrix_jit_spatial_acceleration.py:679-681).
+ *   q, k, v       [B,L,H,D] bf16 (in_dtype 0) or fp32 (in_dtype 1), token order
+ *   phase         complex64 [L,phase_heads,D/2] as (re, im) float pairs, or
+ *                 NULL (no rotation); phase_heads 1 or H
+ *   block_indices int32 [P] packed slot -> token, -1 = padding
+ *   q/k/v_out     bf16 [B,H,P,D]: rot(x)[b, block_indices[p], h, :] rounded
+ *                 to bf16, zeros at padding.  The rotation multiplies the
+ *                 (even, odd) pairs by the phase in fp32 with separately
+ *                 rounded products and sums, as a complex64 multiply.
+ * Supported: D == 128.  An index >= L is written as padding and reported by
+ * cast_device_error().
+ */
+CAST_API int cast_compact_pack(const void *q, const void *k, const void *v, int in_dtype,
+                      const float *phase, int phase_heads, const int32_t *block_indices, int B,
+                      int L, int H, int D, int P, void *q_out, void *k_out, void *v_out,
+                      cast_stream_t stream);
+/*
+ * The attention output back in token order (proposed/matrix_curvature_phase_
+ * frame_weave.py:6095): out[b,t,h,:] = packed[b,h,token_to_packed[t],:].
+ *   packed bf16 [B,H,P,D]; token_to_packed int32 [L]; out bf16 [B,L,H,D].
+ * A position outside [0,P) gives zeros and is reported by cast_device_error().
+ */
+CAST_API int cast_compact_unpack(const void *packed, const int32_t *token_to_packed, int B, int L,
+                        int H, int D, int P, void *out, cast_stream_t stream);
+
+/*
  * Phase-Aware Reconstruction (FC-PASM reference numerics) on one model call.
  * Replaces WorldAlignedSpectralResidualCorrector.correct with the factory's
  * FC knobs (proposed/matrix_world_spectral_residual.py:5283-5394 ->

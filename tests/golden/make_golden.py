@@ -26,6 +26,12 @@ Files:
 * ``cfg3_select_h2.npz`` -- config 3 (anchor queries over 128 history
   frames, budget 16) generated with 2 heads: reference-primitive scores and
   the budget rule's selection.
+* ``compact_pack.npz`` -- the compact path's RoPE phase
+  (``MatrixCurvaturePhaseFrameWeave._cached_compact_rope_phase``), rotation
+  (``_apply_compact_rope_phase``), packing and output scatter (the lines of
+  ``_compact_cwca_attention`` :5677-5684 and :6095) on
+  ``workloads.compact_case`` with a shared and a per-head frequency table:
+  SHA-256 of every output (bf16 bits) and of the phases, and the layout.
 * ``par_*.npz``          -- ``WorldAlignedSpectralResidualCorrector.correct``
   (``proposed/matrix_world_spectral_residual.py:5283``) with the factory's FC
   knobs on reduced-channel inputs (targets stored as bf16 bits) and its
@@ -148,6 +154,58 @@ def make_cfg3(manifest: dict):
                         scores_f32=scores, selected=sel, counts=cnt)
 
 
+def make_compact(manifest: dict):
+    from types import SimpleNamespace
+
+    from interaction_accel.methods.proposed.matrix_curvature_phase_frame_weave import (
+        MatrixCurvaturePhaseFrameWeave as Weave,
+    )
+
+    out = {}
+    for tag, per_head in (("shared", False), ("heads", True)):
+        c = workloads.compact_case(per_head_phase=per_head)
+        manifest["inputs"][f"compact_{tag}"] = {"q": sha(c.q), "k": sha(c.k), "v": sha(c.v),
+                                                "freqs": sha(torch.view_as_real(c.freqs))}
+        holder = SimpleNamespace(_compact_rope_phase_key=None, _compact_rope_phase=None)
+        phase = Weave._cached_compact_rope_phase(holder, c.coords, c.freqs, c.memory_length,
+                                                 c.memory_latent_idx, c.predict_latent_idx)
+        q = Weave._apply_compact_rope_phase(c.q, phase)
+        k = Weave._apply_compact_rope_phase(c.k, phase)
+        # layout: the stable grouping of the runtime-optimised layout builder
+        # (proposed/matrix_curvature_phase_frame_weave.py:5269-5304)
+        bid = c.block_id
+        order = torch.argsort(bid, stable=True)
+        sorted_blocks = bid.index_select(0, order)
+        counts = torch.bincount(sorted_blocks, minlength=c.n_blocks)
+        starts = torch.cumsum(counts, dim=0) - counts
+        ranks = torch.arange(order.numel()) - torch.repeat_interleave(starts, counts)
+        block_indices = torch.full((c.n_blocks, c.block_size), -1, dtype=torch.long)
+        block_indices.view(-1)[sorted_blocks * c.block_size + ranks] = order
+        block_valid = block_indices >= 0
+        token_to_packed = torch.empty(bid.numel(), dtype=torch.long)
+        packed_position = torch.arange(c.n_blocks * c.block_size).reshape(c.n_blocks, c.block_size)
+        token_to_packed[block_indices[block_valid]] = packed_position[block_valid]
+        # packing (:5677-5684) and the bf16 cast of the attention launch
+        flat = block_indices.clamp_min(0).reshape(-1)
+        mask = block_valid.reshape(-1)
+        packed = []
+        for x in (q, k, c.v):
+            xp = x[:, flat].transpose(1, 2).contiguous()
+            xp[:, :, ~mask] = 0
+            packed.append(xp.to(torch.bfloat16))
+        # output scatter (:6095) of a seeded attention output
+        g = torch.Generator().manual_seed(11)
+        out_packed = torch.randn(packed[0].shape, generator=g).bfloat16()
+        output = out_packed.transpose(1, 2)[:, token_to_packed]
+        out[f"{tag}_block_indices"] = block_indices.numpy()
+        out[f"{tag}_token_to_packed"] = token_to_packed.numpy()
+        out[f"{tag}_phase_sha"] = np.array(sha(torch.view_as_real(phase.to(torch.complex64)).contiguous()))
+        for name, t in zip(("q", "k", "v"), packed):
+            out[f"{tag}_{name}_sha"] = np.array(sha(t))
+        out[f"{tag}_unpack_sha"] = np.array(sha(output.contiguous()))
+    np.savez_compressed(os.path.join(HERE, "compact_pack.npz"), **out)
+
+
 def par_corrector():
     from interaction_accel.methods.proposed.matrix_world_spectral_residual import (
         WorldAlignedSpectralResidualCorrector,
@@ -226,7 +284,7 @@ def make_par(manifest: dict):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the CAST src/ directory")
-    ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "par"),
+    ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "compact", "par"),
                     help="regenerate these fixtures only; other manifest entries are kept")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
@@ -238,13 +296,15 @@ def main():
     if args.only and os.path.exists(mpath):
         with open(mpath) as fh:
             manifest = json.load(fh)
-    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "par"))
+    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par"))
     if "cfg1" in todo:
         make_cfg1({}, manifest)
     if "cfg2" in todo:
         make_cfg2(manifest)
     if "cfg3" in todo:
         make_cfg3(manifest)
+    if "compact" in todo:
+        make_compact(manifest)
     if "par" in todo:
         make_par(manifest)
     for f in sorted(os.listdir(HERE)):
