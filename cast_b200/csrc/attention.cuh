@@ -98,6 +98,11 @@ struct AttnParams {
   // partial result in slot `part` of part_ws; the last part of the item to
   // finish (counted in part_counter[s], zero between launches) merges them.
   int n_whole, n_split;
+  // Converted pairs (n_conv > 0, no cut items then): the last n_conv pair
+  // items run as single query tiles, after the native single tiles: CTAs
+  // [0, n_full_items - n_conv) pairs, then the n_items - n_full_items
+  // single tiles, then two CTAs per converted pair (tile 2*pair, 2*pair+1).
+  int n_conv, n_items;
   int *part_counter;
   float *part_ws;
   uint16_t part_first[kMaxSplitItems + 1];
@@ -405,7 +410,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // ---- work item (full query-tile pairs first, heaviest query blocks first)
   // and, for a cut item, which part of it
   int x = blockIdx.x, split_idx = -1, part = 0, n_parts = 1, planned = 0;
-  if (x >= p.n_whole) {
+  int conv_tile = -1;  // converted pair: which of its two tiles this CTA runs
+  if (p.n_conv > 0) {
+    const int kept = p.n_full_items - p.n_conv;
+    const int singles = p.n_items - p.n_full_items;
+    if (x >= kept + singles) {
+      const int j = x - kept - singles;
+      x = kept + j / 2;
+      conv_tile = j & 1;
+    } else if (x >= kept) {
+      x = p.n_full_items + (x - kept);
+    }
+  } else if (x >= p.n_whole) {
     const int b = x - p.n_whole;
     int lo = 0, hi = p.n_split;
     while (hi - lo > 1) {
@@ -435,8 +451,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       qb = p.nqb - 1 - x / p.BH;
     }
   }
-  const int t0 = 2 * pair;
-  const int nq = min(2, p.q_tiles - t0);
+  const int t0 = 2 * pair + max(conv_tile, 0);
+  const int nq = conv_tile >= 0 ? 1 : min(2, p.q_tiles - t0);
   const int row_item = bh * p.nqb + qb;
   const int n_blocks = min(max(p.counts[row_item], 0), min(p.max_degree, kMaxBlockList));
   const int n_kv_item = n_blocks * p.k_tiles;  // 128-key tiles of the item

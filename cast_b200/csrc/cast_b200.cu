@@ -306,6 +306,7 @@ extern "C" int cast_taba_select(const void *q, const void *k, int B, int H, int 
 // length, are searched for the shortest simulated makespan.
 struct AttnSplitPlan {
   int n_whole = 0, n_split = 0, n_parts = 0;
+  int n_conv = 0;  // tail pairs run as two single tiles (no cut items then)
   std::vector<uint16_t> first, tiles;
   size_t ws_bytes = 0;
 };
@@ -313,7 +314,8 @@ struct AttnSplitPlan {
 static size_t attn_counter_bytes(int n_split) { return ((size_t)n_split * 4 + 255) / 256 * 256; }
 
 static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_tiles,
-                                          int max_degree, const int32_t *count_hint, int n_sms) {
+                                          int max_degree, const int32_t *count_hint, int n_sms,
+                                          bool allow_cut) {
   using castk::kMaxItemParts;
   using castk::kMaxSplitItems;
   const int full_pairs = q_tiles / 2;
@@ -361,12 +363,27 @@ static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_ti
 
   AttnSplitPlan best;
   best.n_whole = n_items;
-  // A cut plan must beat running every item whole by 5 %: the simulation
-  // does not see every cost of the cut parts.
-  double best_t = 0.95 * simulate(cost);
+  const double t_whole = simulate(cost);
+  double best_t = t_whole;
   std::vector<double> d;
+  // Converted pairs: the last n_conv pair items (the lightest pairs) run as
+  // two single query tiles each, after the native single tiles; a single
+  // tile shares its key tiles between both softmax warpgroups, so each half
+  // costs half the pair.  Taken for a 2 % simulated gain.
+  for (int n_conv = 4; n_conv <= n_full; n_conv += 4) {
+    d.assign(cost.begin(), cost.begin() + (n_full - n_conv));
+    d.insert(d.end(), cost.begin() + n_full, cost.end());
+    for (int x = n_full - n_conv; x < n_full; ++x) d.insert(d.end(), 2, 0.5 * cost[x]);
+    const double t = simulate(d);
+    if (t < 0.98 * t_whole && t < best_t - 1e-9) {
+      best_t = t;
+      best.n_conv = n_conv;
+    }
+  }
+  // Cut items: must beat running every item whole by 5 %, since the
+  // simulation does not see every cost of the cut parts.
   std::vector<int> nparts;
-  for (int thr = 4; thr <= 64; thr += 4) {
+  for (int thr = 4; allow_cut && thr <= 64; thr += 4) {
     int X = 0;
     while (X < n_items && suffix[X] > (double)thr * n_sms) ++X;
     if (X == n_items || n_items - X > kMaxSplitItems) continue;
@@ -382,8 +399,9 @@ static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_ti
       }
       if (total > 65535) continue;
       const double t = simulate(d);
-      if (t < best_t - 1e-9) {
+      if (t < 0.95 * t_whole && t < best_t - 1e-9) {
         best_t = t;
+        best.n_conv = 0;
         best.n_whole = X;
         best.n_split = n_items - X;
         best.n_parts = total;
@@ -395,6 +413,12 @@ static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_ti
         }
       }
     }
+  }
+  if (best.n_conv > 0) {  // the conversion won: no cut items
+    best.n_whole = n_items;
+    best.n_split = best.n_parts = 0;
+    best.first.clear();
+    best.tiles.clear();
   }
   if (best.n_split > 0)
     best.ws_bytes = attn_counter_bytes(best.n_split) +
@@ -408,14 +432,16 @@ static std::mutex g_attn_plan_mutex;
 static std::map<std::vector<int32_t>, AttnSplitPlan> g_attn_plans;
 
 static AttnSplitPlan attention_plan(int BH, int nqb, int q_tiles, int k_tiles, int max_degree,
-                                    const int32_t *count_hint, int n_sms) {
-  std::vector<int32_t> key = {BH, nqb, q_tiles, k_tiles, max_degree, n_sms, count_hint ? 1 : 0};
+                                    const int32_t *count_hint, int n_sms, bool allow_cut) {
+  std::vector<int32_t> key = {BH, nqb, q_tiles, k_tiles, max_degree, n_sms, count_hint ? 1 : 0,
+                              allow_cut ? 1 : 0};
   if (count_hint) key.insert(key.end(), count_hint, count_hint + (size_t)BH * nqb);
   std::lock_guard<std::mutex> lock(g_attn_plan_mutex);
   auto it = g_attn_plans.find(key);
   if (it != g_attn_plans.end()) return it->second;
   if (g_attn_plans.size() >= 64) g_attn_plans.clear();
-  AttnSplitPlan plan = plan_attention_split(BH, nqb, q_tiles, k_tiles, max_degree, count_hint, n_sms);
+  AttnSplitPlan plan =
+      plan_attention_split(BH, nqb, q_tiles, k_tiles, max_degree, count_hint, n_sms, allow_cut);
   g_attn_plans.emplace(std::move(key), plan);
   return plan;
 }
@@ -433,7 +459,7 @@ extern "C" size_t cast_rcsa_attention_workspace_bytes(int B, int H, int Lq, int 
   int n_sms = 0;
   if (current_device_sm100(&n_sms)) return 0;
   return attention_plan(B * H, ceil_div(Lq, q_block), ceil_div(q_block, 128), ceil_div(k_block, 128),
-                        max_degree, count_hint, n_sms)
+                        max_degree, count_hint, n_sms, true)
       .ws_bytes;
 }
 
@@ -522,16 +548,19 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   p.default_mode = have_codes ? 1 : 0;
   p.sm_scale_log2 = sm_scale * 1.4426950408889634f;
   const int n_items = p.n_full_items + (p.q_tiles % 2 ? BH * p.nqb : 0);
+  p.n_items = n_items;
   p.n_whole = n_items;
   p.n_split = 0;
   p.part_counter = nullptr;
   p.part_ws = nullptr;
   memset(p.part_first, 0, sizeof(p.part_first));
   memset(p.part_tiles, 0, sizeof(p.part_tiles));
-  int grid = n_items;
+  // Items are cut only with a workspace; converting tail pairs needs none.
+  const AttnSplitPlan plan = attention_plan(BH, p.nqb, p.q_tiles, p.k_tiles, max_degree, count_hint,
+                                            n_sms, workspace != nullptr);
+  p.n_conv = plan.n_conv;
+  int grid = n_items + plan.n_conv;
   if (workspace) {
-    const AttnSplitPlan plan =
-        attention_plan(BH, p.nqb, p.q_tiles, p.k_tiles, max_degree, count_hint, n_sms);
     if (workspace_bytes < plan.ws_bytes)
       return fail(CAST_ERR_WORKSPACE, "workspace of %zu bytes < %zu required", workspace_bytes,
                   plan.ws_bytes);
