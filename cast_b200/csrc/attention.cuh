@@ -491,7 +491,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int k_off = 2 * q_bytes;
   const int v_off = k_off + KS * k_bytes;
 
-  if (threadIdx.x == 0) {
+  if (warp == kProducerWarp && lane == 0) {
+    // The producer thread initialises the barriers and starts the Q load
+    // before the CTA-wide sync, so the load overlaps the rest of the set-up.
     for (int i = 0; i < AttnSmem::n_bars; ++i) castdev::mbar_init(&bar[i], 1);
     for (int i = 0; i < 4; ++i) castdev::mbar_init(&p_full[i], 4);
     castdev::mbar_init(merge_bar, 4);
@@ -500,18 +502,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; i < kMaxKStages; ++i) castdev::mbar_init(&k_empty[i], split ? 1 : nq);
     for (int i = 0; i < kVStages; ++i) castdev::mbar_init(&v_empty[i], split ? 1 : nq);
     castdev::fence_barrier_init();
+    castdev::tma_prefetch_desc(mode ? &tm_q8 : &tm_q16);
+    castdev::tma_prefetch_desc(mode ? &tm_k8 : &tm_k16);
+    castdev::tma_prefetch_desc(&tm_v);
+    if (n_kv > 0) {
+      const int qrow0 = qb * p.q_block + t0 * 128;
+      castdev::mbar_arrive_expect_tx(q_full, nq * q_bytes);
+      for (int i = 0; i < nq; ++i) {
+        uint8_t *qd = smem + q_off + i * q_bytes;
+        if (mode) {
+          castdev::tma_load_3d(qd, &tm_q8, q_full, 0, qrow0 + i * 128, bh);
+        } else {
+          castdev::tma_load_3d(qd, &tm_q16, q_full, 0, qrow0 + i * 128, bh);
+          castdev::tma_load_3d(qd + 16384, &tm_q16, q_full, 64, qrow0 + i * 128, bh);
+        }
+      }
+    }
   }
   if (warp == kMmaWarp) {
     castdev::tmem_alloc(tmem_slot, 512);
     castdev::tmem_relinquish();
   }
-  for (int j = threadIdx.x; j < n_blocks; j += blockDim.x)
+  // the whole list row (not only `counts` entries), so these loads need not
+  // wait for the count
+  for (int j = threadIdx.x; j < min(p.max_degree, kMaxBlockList); j += blockDim.x)
     blist[j] = p.indices[(size_t)row_item * p.max_degree + j];
-  if (warp == kProducerWarp && lane == 0) {
-    castdev::tma_prefetch_desc(mode ? &tm_q8 : &tm_q16);
-    castdev::tma_prefetch_desc(mode ? &tm_k8 : &tm_k16);
-    castdev::tma_prefetch_desc(&tm_v);
-  }
   __syncthreads();
   castdev::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -519,18 +534,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp >= 8) {
     if (warp == kProducerWarp) {
       // ---------------------------------------------------- Q + K producer
-      if (lane == 0 && n_kv > 0) {
-        const int qrow0 = qb * p.q_block + t0 * 128;
-        castdev::mbar_arrive_expect_tx(q_full, nq * q_bytes);
-        for (int i = 0; i < nq; ++i) {
-          uint8_t *qd = smem + q_off + i * q_bytes;
-          if (mode) {
-            castdev::tma_load_3d(qd, &tm_q8, q_full, 0, qrow0 + i * 128, bh);
-          } else {
-            castdev::tma_load_3d(qd, &tm_q16, q_full, 0, qrow0 + i * 128, bh);
-            castdev::tma_load_3d(qd + 16384, &tm_q16, q_full, 64, qrow0 + i * 128, bh);
-          }
-        }
+      if (lane == 0 && n_kv > 0) {  // (Q is already on its way)
         int issued = 0;
         for (int j = 0; j < n_kv; ++j) {  // ring position j
           const int kt = kt_lo + ring0.key_tile(j);
