@@ -17,6 +17,7 @@ _lock = threading.Lock()
 _lib = None
 
 c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+c_longlong = ctypes.c_longlong
 
 # name -> (restype, argtypes); mirrors include/cast_b200.h
 SIGNATURES = {
@@ -56,6 +57,11 @@ SIGNATURES = {
          c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     ),
     "cast_compact_unpack": (c_int, [c_void_p, c_void_p] + [c_int] * 5 + [c_void_p, c_void_p]),
+    "cast_barycentric_pair_write": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_longlong, c_int,
+         c_void_p],
+    ),
     "cast_par_fcpasm": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float,

@@ -14,6 +14,7 @@
 #include "attention.cuh"
 #include "par.cuh"
 #include "compact.cuh"
+#include "barycentric.cuh"
 
 namespace cast {
 
@@ -650,6 +651,36 @@ extern "C" int cast_compact_unpack(const void *packed, const int32_t *token_to_p
                                  reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16 *>(packed), token_to_packed, B, L, H, P,
       static_cast<__nv_bfloat16 *>(out));
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+// ===========================================================================
+// control-barycentric two-anchor writer
+// ===========================================================================
+extern "C" int cast_barycentric_pair_write(const float *active_residual, const float *weights,
+                                           const int32_t *source_pairs, const int32_t *target_frames,
+                                           float *output, int A, int T, int N, long long spatial_channels,
+                                           int arithmetic_mode, cast_stream_t stream) {
+  if (!active_residual || !weights || !source_pairs || !target_frames || !output)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "all tensors are required");
+  if (A <= 0 || T <= 0 || N <= 0 || spatial_channels <= 0)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
+  if (N > 65535) return fail(CAST_ERR_UNSUPPORTED, "%d target rows (at most 65535)", N);
+  if (arithmetic_mode < 0 || arithmetic_mode > 3)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "arithmetic_mode %d (0..3)", arithmetic_mode);
+  if (!aligned16(active_residual) || !aligned16(output))
+    return fail(CAST_ERR_ALIGNMENT, "tensor base pointers must be 16-byte aligned");
+  int n_sms = 0;
+  int st = current_device_sm100(&n_sms);
+  if (st) return st;
+  const long long vec = (spatial_channels & 3) == 0 ? spatial_channels / 4 : spatial_channels;
+  // about 8 CTAs per SM over all target rows
+  const long long want = std::max<long long>(1, (long long)n_sms * 8 / N);
+  const int gx = (int)std::min<long long>(std::min(want, (vec + castk::kBaryThreads - 1) / castk::kBaryThreads), 65535);
+  castk::barycentric_pair_kernel<<<dim3(gx, N), castk::kBaryThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      active_residual, weights, source_pairs, target_frames, output, spatial_channels, A, T,
+      arithmetic_mode == 0 ? 2 : arithmetic_mode);
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;
 }

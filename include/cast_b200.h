@@ -239,6 +239,27 @@ CAST_API int cast_compact_unpack(const void *packed, const int32_t *token_to_pac
                         int H, int D, int P, void *out, cast_stream_t stream);
 
 /*
+ * Two-anchor residual writer of the control-barycentric reconstruction.
+ * Replaces direct_control_barycentric_pair_write (proposed/matrix_control_
+ * barycentric_pair_kernel.py:22-204), which the frame weave's control-
+ * barycentric lift calls with arithmetic_mode "left_then_right_fma"
+ * (proposed/matrix_curvature_phase_frame_weave.py:4278-4286).
+ *   active_residual fp32 [A, spatial_channels]   (the reference's [1,A,S,C])
+ *   weights         fp32 [N, 2]; source_pairs int32 [N, 2] (slots in [0,A));
+ *   target_frames   int32 [N] (frames in [0,T)); output fp32 [T, spatial_channels]
+ *   output[target[n]] = mix(active[pair[n][0]], w[n][0], active[pair[n][1]], w[n][1])
+ * arithmetic_mode: 1 separate RN(RN(l*wl) + RN(r*wr)); 2 left_then_right_fma
+ * FMA(r, wr, RN(l*wl)); 3 right_then_left_fma FMA(l, wl, RN(r*wr)); 0
+ * "fused" (the reference leaves its rounding to the compiler) runs as 2.
+ * Rows whose slots or frame are out of range are skipped and reported by
+ * cast_device_error().
+ */
+CAST_API int cast_barycentric_pair_write(const float *active_residual, const float *weights,
+                                const int32_t *source_pairs, const int32_t *target_frames,
+                                float *output, int A, int T, int N, long long spatial_channels,
+                                int arithmetic_mode, cast_stream_t stream);
+
+/*
  * Phase-Aware Reconstruction (FC-PASM reference numerics) on one model call.
  * Replaces WorldAlignedSpectralResidualCorrector.correct with the factory's
  * FC knobs (proposed/matrix_world_spectral_residual.py:5283-5394 ->

@@ -1,0 +1,76 @@
+"""Control-barycentric two-anchor writer on the GPU
+(cast_barycentric_pair_write) against the CPU oracle: bit-exact fp32."""
+
+import numpy as np
+import pytest
+import torch
+
+from cast_b200 import barycentric
+from oracle import barycentric as ob
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(A, T, S, C, seed):
+    g = torch.Generator().manual_seed(seed)
+    active = torch.randn(1, A, S, C, generator=g)
+    targets = torch.tensor([1, 2, 5, 6], dtype=torch.int32)[: T - 4 if T > 8 else 4]
+    pairs = torch.tensor([[0, 1], [0, 1], [2, 3], [3, 4]], dtype=torch.int32)[: targets.numel()]
+    weights = torch.softmax(torch.randn(1, targets.numel(), 2, generator=g), dim=-1)
+    return active, weights, pairs, targets
+
+
+@pytest.mark.parametrize("mode", ["fused", "separate", "left_then_right_fma", "right_then_left_fma"])
+@pytest.mark.parametrize("S,C", [(880, 64), (7, 5)])
+def test_pair_write_matches_oracle(cuda, mode, S, C):
+    active, weights, pairs, targets = _case(5, 8, S, C, seed=S + C)
+    out = torch.full((1, 8, S, C), 7.0)
+    ref = ob.pair_write(active[0].reshape(5, -1).numpy(), weights[0].numpy(), pairs.numpy(),
+                        targets.numpy(), out[0].reshape(8, -1).numpy().copy(), ob.MODES[mode])
+    got = barycentric.direct_control_barycentric_pair_write(
+        active.cuda(), weights.cuda(), pairs.cuda(), targets.cuda(), out.cuda(), arithmetic_mode=mode)
+    torch.cuda.synchronize()
+    got = got[0].reshape(8, -1).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    # frames that are not targets keep their contents
+    assert (got[[0, 3, 4, 7]] == 7.0).all()
+
+
+def test_pair_write_checks_like_the_reference(cuda):
+    active, weights, pairs, targets = _case(3, 8, 7, 5, seed=1)  # 3 anchors: refused
+    out = torch.zeros(1, 8, 7, 5, device="cuda")
+    with pytest.raises(ValueError, match="4/5/6"):
+        barycentric.direct_control_barycentric_pair_write(active.cuda(), weights.cuda(), pairs.cuda(),
+                                                          targets.cuda(), out)
+
+
+def test_pair_write_config4_scale_rate(cuda):
+    """Config 4's residual frame (880 x 3072 fp32) with two targets between
+    anchors: bit-exact, and the HBM rate (inputs larger than L2)."""
+    g = torch.Generator().manual_seed(3)
+    active = torch.randn(1, 4, 880, 3072, generator=g).cuda()
+    weights = torch.softmax(torch.randn(1, 2, 2, generator=g), dim=-1).cuda()
+    pairs = torch.tensor([[0, 1], [0, 1]], dtype=torch.int32).cuda()
+    targets = torch.tensor([1, 2], dtype=torch.int32).cuda()
+    out = torch.zeros(1, 5, 880, 3072, device="cuda")
+    barycentric.direct_control_barycentric_pair_write(active, weights, pairs, targets, out,
+                                                      arithmetic_mode="left_then_right_fma")
+    torch.cuda.synchronize()
+    ref = ob.pair_write(active[0].reshape(4, -1).cpu().numpy(), weights[0].cpu().numpy(),
+                        pairs.cpu().numpy(), targets.cpu().numpy(),
+                        np.zeros((5, 880 * 3072), np.float32), 2)
+    assert np.array_equal(out[0].reshape(5, -1).cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    flush = torch.empty(64 << 20, dtype=torch.int32, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(5):
+        flush.zero_()
+        e0.record()
+        barycentric.direct_control_barycentric_pair_write(active, weights, pairs, targets, out,
+                                                          arithmetic_mode="left_then_right_fma")
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1000.0)
+    us = sorted(ts)[len(ts) // 2]
+    nbytes = 2 * 3 * 880 * 3072 * 4  # per target: two frames read, one written
+    print(f"barycentric pair write (2 targets, 880x3072 fp32): {us:.1f} us, {nbytes / us / 1e3:.0f} GB/s")
