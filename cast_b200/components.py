@@ -13,7 +13,10 @@ Matrix DiT attention hook keep their call signatures:
   numerics) -> :class:`cast_b200.par.FCPASMCorrector` with the corrector's
   own FC knobs;
 * ``attention_compiler.select`` (TABA pooled-QK selection) -> the CUDA
-  selection given the compiler's compiled row degrees.
+  selection given the compiler's compiled row degrees;
+* the frame weave's ``direct_control_barycentric_pair_write`` (the
+  control-barycentric lift's two-anchor writer) ->
+  :func:`cast_b200.barycentric.direct_control_barycentric_pair_write`.
 
 The reference package itself (its orchestration, CAFS, degree budgets, the
 memory compiler) is not part of this repository; it is imported from the
@@ -24,7 +27,7 @@ from __future__ import annotations
 
 import importlib
 
-from . import rcsa
+from . import barycentric, rcsa
 from .par import FCPASMCorrector
 from .select import TABASelector
 
@@ -51,6 +54,10 @@ def install_kernels() -> None:
     if "longcat_asymmetric" not in _PATCHED:
         _PATCHED["longcat_asymmetric"] = weave.MatrixCausalFrameLayerRelay._longcat_asymmetric
         weave.MatrixCausalFrameLayerRelay._longcat_asymmetric = staticmethod(rcsa.longcat_asymmetric)
+    if "pair_write" not in _PATCHED:
+        # the weave calls the writer through its own module-level name
+        _PATCHED["pair_write"] = weave.direct_control_barycentric_pair_write
+        weave.direct_control_barycentric_pair_write = barycentric.direct_control_barycentric_pair_write
 
 
 def uninstall_kernels() -> None:
@@ -62,6 +69,9 @@ def uninstall_kernels() -> None:
         weave = _ref("matrix_curvature_phase_frame_weave")
         weave.MatrixCausalFrameLayerRelay._longcat_asymmetric = staticmethod(
             _PATCHED.pop("longcat_asymmetric"))
+    if "pair_write" in _PATCHED:
+        weave = _ref("matrix_curvature_phase_frame_weave")
+        weave.direct_control_barycentric_pair_write = _PATCHED.pop("pair_write")
 
 
 def corrector_from_reference(ref_corrector) -> FCPASMCorrector:
