@@ -666,7 +666,6 @@ extern "C" int cast_barycentric_pair_write(const float *active_residual, const f
     return fail(CAST_ERR_INVALID_ARGUMENT, "all tensors are required");
   if (A <= 0 || T <= 0 || N <= 0 || spatial_channels <= 0)
     return fail(CAST_ERR_INVALID_ARGUMENT, "non-positive size");
-  if (N > 65535) return fail(CAST_ERR_UNSUPPORTED, "%d target rows (at most 65535)", N);
   if (arithmetic_mode < 0 || arithmetic_mode > 3)
     return fail(CAST_ERR_INVALID_ARGUMENT, "arithmetic_mode %d (0..3)", arithmetic_mode);
   if (!aligned16(active_residual) || !aligned16(output))
@@ -675,11 +674,11 @@ extern "C" int cast_barycentric_pair_write(const float *active_residual, const f
   int st = current_device_sm100(&n_sms);
   if (st) return st;
   const long long vec = (spatial_channels & 3) == 0 ? spatial_channels / 4 : spatial_channels;
-  // about 8 CTAs per SM over all target rows
-  const long long want = std::max<long long>(1, (long long)n_sms * 8 / N);
-  const int gx = (int)std::min<long long>(std::min(want, (vec + castk::kBaryThreads - 1) / castk::kBaryThreads), 65535);
-  castk::barycentric_pair_kernel<<<dim3(gx, N), castk::kBaryThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      active_residual, weights, source_pairs, target_frames, output, spatial_channels, A, T,
+  // 4 CTAs per SM, grid-strided over the frame (every CTA walks all rows)
+  const int grid = (int)std::min<long long>((long long)n_sms * 4,
+                                            (vec + castk::kBaryThreads - 1) / castk::kBaryThreads);
+  castk::barycentric_pair_kernel<<<grid, castk::kBaryThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      active_residual, weights, source_pairs, target_frames, output, spatial_channels, A, T, N,
       arithmetic_mode == 0 ? 2 : arithmetic_mode);
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;

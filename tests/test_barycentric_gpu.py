@@ -60,17 +60,29 @@ def test_pair_write_config4_scale_rate(cuda):
                         pairs.cpu().numpy(), targets.cpu().numpy(),
                         np.zeros((5, 880 * 3072), np.float32), 2)
     assert np.array_equal(out[0].reshape(5, -1).cpu().numpy().view(np.uint32), ref.view(np.uint32))
-    flush = torch.empty(64 << 20, dtype=torch.int32, device="cuda")
+    # four input/output sets in turn (4 x 54 MB, more than L2), back to back
+    sets = [(torch.randn_like(active), torch.zeros_like(out)) for _ in range(4)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ts = []
-    for _ in range(5):
-        flush.zero_()
-        e0.record()
-        barycentric.direct_control_barycentric_pair_write(active, weights, pairs, targets, out,
+    for a_, o_ in sets:
+        barycentric.direct_control_barycentric_pair_write(a_, weights, pairs, targets, o_,
                                                           arithmetic_mode="left_then_right_fma")
-        e1.record()
-        torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1) * 1000.0)
-    us = sorted(ts)[len(ts) // 2]
-    nbytes = 2 * 3 * 880 * 3072 * 4  # per target: two frames read, one written
+    # one CUDA graph of 20 launches, so host enqueue time does not show
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for r in range(20):
+            a_, o_ = sets[r % 4]
+            barycentric.direct_control_barycentric_pair_write(a_, weights, pairs, targets, o_,
+                                                              arithmetic_mode="left_then_right_fma")
+    graph.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / 20
+    # algorithmic: the two shared anchor frames read once, two targets written
+    nbytes = 4 * 880 * 3072 * 4
     print(f"barycentric pair write (2 targets, 880x3072 fp32): {us:.1f} us, {nbytes / us / 1e3:.0f} GB/s")
