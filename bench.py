@@ -35,6 +35,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "RCSA int8 sparse-attn µs/call & % tensor-core peak; scaling at 1/2/4/8 B200"
 BLOCK, BUDGET, HEADS, D = 880, 8, 24, 128
+# kernels of one layer call: pooling + quantisation, selection, attention, and
+# under the auto policy the code pass for the blocks int8 query blocks read
+KERNELS_PER_CALL = {"auto": 4, "int8": 3, "bf16": 3}
 HIST, CUR = 32, 4
 # DRAM bytes (read + write) of one attention launch on the full config-2
 # workload (auto policy), from the single-pass ncu capture in
@@ -379,7 +382,22 @@ def main():
     peak_eff = (i8_ops + bf_ops) / t_roof / 1e12
     int8_frac = float(sel.qk_mode.float().mean()) if sel.qk_mode is not None else 0.0
     sq_read = (q.numel() + k.numel()) * 2
-    sq_bytes = sq_read + (q.numel() + k.numel())  # bf16 read + int8 codes written
+    if args.policy == "auto" and sel.qk_mode is not None:
+        # codes only for the blocks the int8 query blocks read, which the code
+        # pass reads again (bf16) and writes (int8)
+        mode, idx, cnt = sel.qk_mode.cpu(), sel.indices.cpu(), sel.counts.cpu()
+        coded = 0
+        for b in range(mode.shape[0]):
+            for h in range(mode.shape[1]):
+                kset = set()
+                for i in range(mode.shape[2]):
+                    if mode[b, h, i]:
+                        coded += 1
+                        kset.update(int(x) for x in idx[b, h, i, :cnt[b, h, i]])
+                coded += len(kset)
+        sq_bytes = sq_read + coded * BLOCK * d_ * 3
+    else:
+        sq_bytes = sq_read + (q.numel() + k.numel())  # bf16 read + int8 codes written
 
     if world > 1:
         dist.destroy_process_group()
@@ -409,10 +427,13 @@ def main():
         "select_quant_roofline": {
             "bound": "hbm", "algorithmic_bytes": sq_bytes, "achieved_gbs": sq_bytes / (sel_ms * 1e-3) / 1e9,
             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": sq_bytes / (sel_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-            "note": "selection + quantisation kernels: Q+K bf16 read, int8 codes written (pooled/RMS/scales ignored)",
+            "note": ("selection + quantisation kernels: Q+K bf16 read once; int8 codes written for every block "
+                     "(int8/bf16 policy) or, under auto, only for the blocks int8 query blocks read (those read "
+                     "again); pooled/RMS/scales ignored"),
         },
         "host_enqueue_us_eager": host_us,
-        "timing": "CUDA graph replay of the 3-kernel layer call; events on the replay stream",
+        "timing": (f"CUDA graph replay of the {KERNELS_PER_CALL[args.policy]}-kernel layer call; "
+                   "events on the replay stream"),
         "roofline": {
             "bound": "tensor", "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
             "frac": achieved / peak_eff,
@@ -423,7 +444,7 @@ def main():
                      f"ops/launch int8 {i8_ops:.4g} bf16 {bf_ops:.4g}"),
         },
         "par": par_line,
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": KERNELS_PER_CALL[args.policy] * args.steps,
         "clocks": clocks,
     }
     if e2e:
@@ -532,7 +553,7 @@ def run_sweep(args, world, rank, local, dev, peaks, peak_src):
                              f"{peak_src} sustained bf16 peak ({peaks['bf16_tflops_sustained']} TFLOP/s, int8 = 2x)"},
         "collective": ("all-gather of bf16 head outputs after every call on NCCL's stream, overlapped with "
                        "the next call" if gath is not None else "none"),
-        "gpu_launches": 3 * calls * args.steps,
+        "gpu_launches": KERNELS_PER_CALL[args.policy] * calls * args.steps,
         "clocks": clocks,
     }
     print(json.dumps(line))

@@ -203,21 +203,25 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   const __nv_bfloat16 *vb = static_cast<const __nv_bfloat16 *>(v);
   // the masked variant only when a validity mask is given
   const bool masked = q_valid || k_valid;
+  // Auto policy: codes only for the blocks the int8 query blocks read,
+  // written after the selection (kernel 3); V codes keep the fused pass.
+  const bool lazy = policy == CAST_POLICY_AUTO && qk_mode && !v_codes;
+  int8_t *qc1 = lazy ? nullptr : q_codes, *kc1 = lazy ? nullptr : k_codes;
   if (D == 128 && !masked)
     castk::pool_quant_kernel<128, false><<<grid, 256, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
-                                                              nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                              nqb, nkb, qc1, qs, kc1, ks, v_codes,
                                                               v_scales, pooled_out, rms);
   else if (D == 128)
     castk::pool_quant_kernel<128, true><<<grid, 256, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
-                                                             nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                             nqb, nkb, qc1, qs, kc1, ks, v_codes,
                                                              v_scales, pooled_out, rms);
   else if (!masked)
     castk::pool_quant_kernel<64, false><<<grid, 128, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
-                                                             nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                             nqb, nkb, qc1, qs, kc1, ks, v_codes,
                                                              v_scales, pooled_out, rms);
   else
     castk::pool_quant_kernel<64, true><<<grid, 128, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
-                                                            nqb, nkb, q_codes, qs, k_codes, ks, v_codes,
+                                                            nqb, nkb, qc1, qs, kc1, ks, v_codes,
                                                             v_scales, pooled_out, rms);
   CAST_CUDA_TRY(cudaGetLastError());
   const int keep = std::min(budget, nkb - nqb);
@@ -234,6 +238,23 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
                                                          budget, maxdeg, sel_idx, sel_cnt, qk_mode,
                                                          policy, int8_tolerance);
   CAST_CUDA_TRY(cudaGetLastError());
+  if (lazy) {
+    dim3 g3(nqb + nkb, B * H);
+#define CAST_QUANT_NEEDED(DD, MM, TT)                                                                \
+  castk::quant_needed_kernel<DD, MM><<<g3, TT, 0, s>>>(qb, kb, q_valid, k_valid, Lq, Lk, block_size, \
+                                                       nqb, nkb, sel_idx, sel_cnt, maxdeg, qk_mode,  \
+                                                       q_codes, qs, k_codes, ks)
+    if (D == 128 && !masked)
+      CAST_QUANT_NEEDED(128, false, 256);
+    else if (D == 128)
+      CAST_QUANT_NEEDED(128, true, 256);
+    else if (!masked)
+      CAST_QUANT_NEEDED(64, false, 128);
+    else
+      CAST_QUANT_NEEDED(64, true, 128);
+#undef CAST_QUANT_NEEDED
+    CAST_CUDA_TRY(cudaGetLastError());
+  }
   return CAST_OK;
 }
 

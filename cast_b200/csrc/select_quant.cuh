@@ -149,6 +149,48 @@ __device__ __forceinline__ double warp_dot(const double *a, const double *b, int
   return part;
 }
 
+// The int8 codes of one block (second pass): each thread takes rows slot,
+// slot + 16, ... of its 8-column group; `fast` selects the division-free
+// path (exact for blocks with amax >= 2^-90), else the IEEE division;
+// padding rows (vrow[r] == 0) get code 0.
+template <int D, bool kMasked>
+__device__ __forceinline__ void write_block_codes(const __nv_bfloat16 *base, int8_t *cbase, int rows,
+                                                  int slot, const uint8_t *vrow, float sc, bool fast,
+                                                  uint64_t drop_pol) {
+  constexpr int kUnroll = 8;
+  const float inv = __frcp_rn(sc);
+  const uint64_t invx2 = q2_pack(inv, inv), negsx2 = q2_pack(-sc, -sc);
+  auto quant8 = [&](const uint4 &raw) {
+    float f[8];
+    bf16x8_to_f32(raw, f);
+    if (fast) return quant8_fast(f, invx2, negsx2);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) lo |= (uint32_t)(quant_code(f[i], sc, inv) & 0xFF) << (8 * i);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hi |= (uint32_t)(quant_code(f[4 + i], sc, inv) & 0xFF) << (8 * i);
+    return make_uint2(lo, hi);
+  };
+  int rr = slot;
+  for (; rr + (kUnroll - 1) * kSumLanes < rows; rr += kUnroll * kSumLanes) {
+    uint4 raw[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      raw[u] = ldg_v4_hint(base + (size_t)(rr + u * kSumLanes) * D, drop_pol);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      uint2 c = quant8(raw[u]);
+      if (kMasked && vrow && !vrow[rr + u * kSumLanes]) c = make_uint2(0u, 0u);
+      stg_v2_hint(cbase + (size_t)(rr + u * kSumLanes) * D, c, drop_pol);
+    }
+  }
+  for (; rr < rows; rr += kSumLanes) {
+    uint2 c = quant8(ldg_v4_hint(base + (size_t)rr * D, drop_pol));
+    if (kMasked && vrow && !vrow[rr]) c = make_uint2(0u, 0u);
+    stg_v2_hint(cbase + (size_t)rr * D, c, drop_pol);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 1: per-(bh, block) pooled statistics and int8 codes.
 // grid.x spans [Q blocks | K blocks | V blocks], grid.y = B*H.
@@ -315,42 +357,63 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
   }
 
   // Second pass: int8 codes (the block was just read; these loads hit L2).
-  if (codes) {
-    const float sc = s_scale;
-    const float inv = __frcp_rn(sc);
-    const bool fast = s_amax >= 0x1p-90f;  // block-uniform
-    const uint64_t invx2 = q2_pack(inv, inv), negsx2 = q2_pack(-sc, -sc);
-    int8_t *cbase = codes + ((size_t)bh * L + b0) * D + grp * 8;
-    auto quant8 = [&](const uint4 &raw) {
-      float f[8];
-      bf16x8_to_f32(raw, f);
-      if (fast) return quant8_fast(f, invx2, negsx2);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) lo |= (uint32_t)(quant_code(f[i], sc, inv) & 0xFF) << (8 * i);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) hi |= (uint32_t)(quant_code(f[4 + i], sc, inv) & 0xFF) << (8 * i);
-      return make_uint2(lo, hi);
-    };
-    int rr = slot;
-    for (; rr + (kUnroll - 1) * kSumLanes < rows; rr += kUnroll * kSumLanes) {
-      uint4 raw[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-        raw[u] = ldg_v4_hint(base + (size_t)(rr + u * kSumLanes) * D, drop_pol);
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        uint2 c = quant8(raw[u]);
-        if (kMasked && vrow && !vrow[rr + u * kSumLanes]) c = make_uint2(0u, 0u);
-        stg_v2_hint(cbase + (size_t)(rr + u * kSumLanes) * D, c, drop_pol);
+  if (codes)
+    write_block_codes<D, kMasked>(base, codes + ((size_t)bh * L + b0) * D + grp * 8, rows, slot, vrow,
+                                  s_scale, s_amax >= 0x1p-90f, drop_pol);
+}
+
+// Kernel 3 (auto policy): int8 codes only for the blocks an int8 query block
+// reads -- its own Q block and every K block it selected; the other code
+// bytes are left as they are.  grid = (nqb + nkb, B*H), the threads of
+// kernel 1; each CTA first decides from qk_mode / sel_idx whether its block
+// is needed, and exits if not.  The scale is kernel 1's.  The division-free
+// path is taken for scale >= 2^-96, which implies amax >= 127 * 2^-96 *
+// (1 - 2^-24) > 2^-90 (where it is exact); smaller blocks use the division,
+// so the codes equal kernel 1's fused second pass bit for bit.
+template <int D, bool kMasked>
+__global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
+    quant_needed_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
+                        const uint8_t *__restrict__ q_valid, const uint8_t *__restrict__ k_valid,
+                        int Lq, int Lk, int block, int nqb, int nkb,
+                        const int32_t *__restrict__ sel_idx, const int32_t *__restrict__ sel_cnt,
+                        int maxdeg, const uint8_t *__restrict__ qk_mode, int8_t *q_codes,
+                        const float *__restrict__ q_scales, int8_t *k_codes,
+                        const float *__restrict__ k_scales) {
+  constexpr int kGroups = D / 8;
+  __shared__ int s_need;
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.y;
+  const bool is_q = (int)blockIdx.x < nqb;
+  const int blk = is_q ? blockIdx.x : blockIdx.x - nqb;
+  if (tid < 32) {
+    bool need = false;
+    if (is_q) {
+      need = tid == 0 && qk_mode[(size_t)bh * nqb + blk] != 0;
+    } else {
+      for (int qb = 0; qb < nqb; ++qb) {
+        if (!qk_mode[(size_t)bh * nqb + qb]) continue;
+        const int cnt = min(max(sel_cnt[(size_t)bh * nqb + qb], 0), maxdeg);
+        const int32_t *row = sel_idx + ((size_t)bh * nqb + qb) * maxdeg;
+        for (int j = tid; j < cnt; j += 32) need |= row[j] == blk;
       }
     }
-    for (; rr < rows; rr += kSumLanes) {
-      uint2 c = quant8(ldg_v4_hint(base + (size_t)rr * D, drop_pol));
-      if (kMasked && vrow && !vrow[rr]) c = make_uint2(0u, 0u);
-      stg_v2_hint(cbase + (size_t)rr * D, c, drop_pol);
-    }
+    need = __any_sync(0xffffffffu, need);
+    if (tid == 0) s_need = need;
   }
+  __syncthreads();
+  if (!s_need) return;
+  const int grp = tid % kGroups, slot = tid / kGroups;
+  const __nv_bfloat16 *X = is_q ? q : k;
+  const int L = is_q ? Lq : Lk;
+  const int b0 = blk * block;
+  const int rows = min(block, L - b0);
+  const uint8_t *vrow = kMasked ? (is_q ? q_valid : k_valid) : nullptr;
+  if (vrow) vrow += b0;
+  const float sc = is_q ? q_scales[(size_t)bh * nqb + blk] : k_scales[(size_t)bh * nkb + blk];
+  int8_t *codes = is_q ? q_codes : k_codes;
+  write_block_codes<D, kMasked>(X + ((size_t)bh * L + b0) * D + grp * 8,
+                                codes + ((size_t)bh * L + b0) * D + grp * 8, rows, slot, vrow, sc,
+                                sc >= 0x1p-96f, l2_evict_first());
 }
 
 // ---------------------------------------------------------------------------

@@ -99,6 +99,11 @@ enum cast_qk_policy {
  *            then they live only in the workspace)
  * Quantiser: s = amax/127 (s = 1 if amax == 0),
  *            code = clamp(rint_half_even(x / s), -127, 127), IEEE division.
+ * Scales are written for every block.  Codes: for every block, except under
+ * CAST_POLICY_AUTO with qk_mode given and no v_codes, where only the blocks
+ * an int8 query block reads get codes -- each int8 query block's own Q
+ * block and the K blocks it selected -- and the other code bytes are left as
+ * they were (the attention never reads them).
  */
 CAST_API int cast_rcsa_select_quant(const void *q, const void *k, const void *v, const uint8_t *q_valid,
                            const uint8_t *k_valid, int B, int H, int Lq, int Lk, int D, int block_size, int budget, int rule,

@@ -101,6 +101,43 @@ def test_select_quant_valid_mask(cuda, d):
     assert np.array_equal(sel.q_codes.cpu().numpy(), qc) and np.array_equal(sel.k_codes.cpu().numpy(), kc)
 
 
+@pytest.mark.parametrize("masked", [False, True])
+def test_auto_policy_codes_where_read(cuda, masked):
+    """Auto policy: codes are written after the selection, only for the
+    blocks an int8 query block reads (its own Q block, the K blocks it
+    selected); there they equal the int8 policy's codes bit for bit, and the
+    scales equal for every block."""
+    w = workloads.config2(heads=4)
+    q, k = w.q.cuda(), w.k.cuda()
+    kw = {}
+    if masked:
+        g = torch.Generator().manual_seed(3)
+        kw = dict(q_valid=(torch.rand(q.shape[2], generator=g) > 0.1).to(torch.uint8).cuda(),
+                  k_valid=(torch.rand(k.shape[2], generator=g) > 0.1).to(torch.uint8).cuda())
+    auto = rcsa.select_quant(q, k, block_size=880, budget=8, policy="auto", **kw)
+    full = rcsa.select_quant(q, k, block_size=880, budget=8, policy="int8", **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(auto.indices, full.indices) and torch.equal(auto.counts, full.counts)
+    assert torch.equal(auto.q_scales, full.q_scales) and torch.equal(auto.k_scales, full.k_scales)
+    mode = auto.qk_mode.cpu()
+    assert bool(mode.any()) and not bool(mode.all())
+    idx, cnt = auto.indices.cpu(), auto.counts.cpu()
+    n_q = n_k = 0
+    for h in range(4):
+        needed = set()
+        for qb in range(4):
+            if mode[0, h, qb]:
+                sl = slice(qb * 880, (qb + 1) * 880)
+                assert torch.equal(auto.q_codes[0, h, sl], full.q_codes[0, h, sl])
+                needed.update(int(x) for x in idx[0, h, qb, :cnt[0, h, qb]])
+                n_q += 1
+        for kb in sorted(needed):
+            sl = slice(kb * 880, (kb + 1) * 880)
+            assert torch.equal(auto.k_codes[0, h, sl], full.k_codes[0, h, sl])
+            n_k += 1
+    print(f"auto policy: {n_q} int8 query blocks, {n_k} K blocks quantised of {4 * 36}")
+
+
 def test_select_quant_d64_config1_golden(cuda):
     w = workloads.config1()
     g = np.load(os.path.join(GOLDEN, "cfg1_select.npz"))
@@ -328,8 +365,12 @@ def test_rcsa_config2_full_properties(cuda):
         assert bool((hist >= 0).all()) and bool((hist < 32).all())
         assert bool((hist.sort(dim=-1).values.diff(dim=-1) > 0).all())
         assert bool((idx[0, :, i, 8:9 + i] == torch.arange(32, 33 + i)).all())
+    # under the auto policy only int8 query blocks have Q codes
     deq = sel.q_codes.float() * sel.q_scales.repeat_interleave(880, dim=2)[..., None]
-    assert float((deq - w.q.float()).abs().max()) <= float(sel.q_scales.max()) * 0.5 + 1e-6
+    int8_rows = sel.qk_mode.bool().repeat_interleave(880, dim=2)[..., None]
+    err = torch.where(int8_rows, (deq - w.q.float()).abs(), torch.zeros_like(deq))
+    assert bool(sel.qk_mode.any())
+    assert float(err.max()) <= float(sel.q_scales.max()) * 0.5 + 1e-6
     assert bool(torch.isfinite(out_a.float()).all())
     diff = (out_a.float() - out_b.float()).abs()
     assert float(diff.mean()) < MEAN_ABS and float(diff.max()) < MAX_ABS
