@@ -180,6 +180,76 @@ def cpu_baseline_sample():
             "sample": "2 of 24 heads (selection + explicit-softmax attention), median of 3, x12"}
 
 
+def _graph_us(fn, n, dev):
+    """Mean device time of fn() replayed from a CUDA graph, n replays."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        fn()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del graph
+    return a.elapsed_time(b) / n * 1000.0
+
+
+def compact_measure(dev, peaks, steps):
+    """The compact path's packing with the RoPE phase at config-2 compact
+    scale (31,680 tokens of 36 frames x 22x40, 24 heads, 880-token frame
+    blocks; q/k/v 195 MB each, larger than L2), and the control-barycentric
+    pair writer on config 4's frame (880 x 3072 fp32, targets 1 and 2 between
+    anchors 0 and 3).  Graph replay; GB/s on the algorithmic bytes."""
+    import numpy as np
+    import torch
+
+    from cast_b200 import barycentric, compact, workloads
+
+    c = workloads.compact_case(heads=24, frames=36, hw=(22, 40), cell=(1, 22, 40), seed=9)
+    order = torch.argsort(c.block_id, stable=True)  # frame blocks: full, no padding
+    idx = order.to(torch.int32).to(dev)
+    g = torch.Generator().manual_seed(9)
+    phase = torch.polar(torch.ones(c.q.shape[1], 1, 64), torch.rand(c.q.shape[1], 1, 64, generator=g))
+    qd, kd, vd, ph = c.q.to(dev), c.k.to(dev), c.v.to(dev), phase.to(dev)
+    out = compact.pack(qd, kd, vd, idx, ph)
+    n = max(10, steps)
+    us_pack = _graph_us(lambda: compact.pack(qd, kd, vd, idx, ph, out=out), n, dev)
+    pack_bytes = 6 * qd.numel() * 2
+    act = torch.randn(1, 4, 880, 3072, generator=g).to(dev)
+    wts = torch.softmax(torch.randn(1, 2, 2, generator=g), dim=-1).to(dev)
+    prs = torch.tensor([[0, 1], [0, 1]], dtype=torch.int32, device=dev)
+    tgs = torch.tensor([1, 2], dtype=torch.int32, device=dev)
+    full = torch.zeros(1, 5, 880, 3072, device=dev)
+    us_pair = _graph_us(lambda: barycentric.direct_control_barycentric_pair_write(
+        act, wts, prs, tgs, full, arithmetic_mode="left_then_right_fma"), n, dev)
+    pair_bytes = 4 * 880 * 3072 * 4  # two shared anchor frames read, two targets written
+    del np
+    return {
+        "compact_pack": {"us_per_call": us_pack, "algorithmic_bytes": pack_bytes,
+                         "achieved_gbs": pack_bytes / us_pack / 1e3,
+                         "frac": pack_bytes / us_pack / 1e3 / peaks["hbm_gbs"],
+                         "workload": "31,680 tokens x 24 heads x 128, bf16, RoPE phase, 880-token blocks"},
+        "pair_write": {"us_per_call": us_pair, "algorithmic_bytes": pair_bytes,
+                       "achieved_gbs": pair_bytes / us_pair / 1e3,
+                       "frac": pair_bytes / us_pair / 1e3 / peaks["hbm_gbs"],
+                       "workload": "config-4 frame 880 x 3072 fp32, targets 1, 2 between anchors 0, 3; "
+                                   "graph of one call (L2 holds the 43 MB, an upper bound)"},
+        "note": "HBM peak measured; CUDA graph replay, device time",
+    }
+
+
 def par_measure(dev, peaks, peak_src, steps):
     """PAR (FC-PASM) on BASELINE config 4: bf16 residual [1, 1+4, 880, 3072]
     (one memory frame), anchors = current frames 0 and 3, targets 1 and 2.
@@ -364,6 +434,7 @@ def main():
                "d2h": hout.numel() * hout.element_size()}
     clocks = sampler.stop()
     par_line = par_measure(dev, peaks, peak_src, args.steps) if rank == 0 else None
+    compact_line = compact_measure(dev, peaks, args.steps) if rank == 0 else None
 
     # ---- max over ranks
     vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms], dtype=torch.float64, device=dev)
@@ -444,6 +515,7 @@ def main():
                      f"ops/launch int8 {i8_ops:.4g} bf16 {bf_ops:.4g}"),
         },
         "par": par_line,
+        "compact_and_lift": compact_line,
         "gpu_launches": KERNELS_PER_CALL[args.policy] * args.steps,
         "clocks": clocks,
     }
