@@ -226,17 +226,36 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   CAST_CUDA_TRY(cudaGetLastError());
   const int keep = std::min(budget, nkb - nqb);
   const int maxdeg = keep + nqb;
-  const size_t dsm = (sizeof(double) + 2 * sizeof(float)) * nkb + nkb + 16;
-  if (dsm > 48 * 1024) return fail(CAST_ERR_UNSUPPORTED, "too many key blocks (%d)", nkb);
+  // Selection kernel shared memory: sort keys over the next power of two of
+  // the history blocks, key-block RMS and scales, and (when they fit in
+  // 160 KB) the history's pooled vectors staged by asynchronous copies.
+  const int nhist = nkb - nqb;
+  int pw = 1;
+  while (pw < nhist) pw <<= 1;
+  const size_t dsm_base = (sizeof(double) + sizeof(int32_t)) * pw + 2 * sizeof(float) * nkb + 16;
+  const size_t stage_bytes = (size_t)nhist * D * sizeof(double);
+  const bool stage_k = stage_bytes <= 160 * 1024;
+  const size_t dsm = dsm_base + (stage_k ? stage_bytes : 0);
+  if (dsm > 200 * 1024) return fail(CAST_ERR_UNSUPPORTED, "too many key blocks (%d)", nkb);
+  static std::once_flag bsel_once;
+  static cudaError_t bsel_err = cudaSuccess;
+  std::call_once(bsel_once, [] {
+    bsel_err = cudaFuncSetAttribute(castk::budget_select_kernel<128>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (bsel_err == cudaSuccess)
+      bsel_err = cudaFuncSetAttribute(castk::budget_select_kernel<64>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  CAST_CUDA_TRY(bsel_err);
   dim3 g2(nqb, B * H);
   if (D == 128)
     castk::budget_select_kernel<128><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
                                                           budget, maxdeg, sel_idx, sel_cnt,
-                                                          qk_mode, policy, int8_tolerance);
+                                                          qk_mode, policy, int8_tolerance, stage_k);
   else
     castk::budget_select_kernel<64><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
                                                          budget, maxdeg, sel_idx, sel_cnt, qk_mode,
-                                                         policy, int8_tolerance);
+                                                         policy, int8_tolerance, stage_k);
   CAST_CUDA_TRY(cudaGetLastError());
   if (lazy) {
     dim3 g3(nqb + nkb, B * H);

@@ -456,6 +456,45 @@ __device__ void warp_topk(const double *score, int n, int k, unsigned char *take
   }
 }
 
+// 16-byte asynchronous copy global -> shared (no registers, many in flight).
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(castdev::smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Sorts the n keys (sk[i], si[i]) of the CTA in place into `better` order
+// (score descending, index ascending), a bitonic network over P = the next
+// power of two (the tail padded with -inf).  The order is total, so the first
+// k entries are exactly the ones warp_topk picks, in the same order.
+__device__ void cta_sort_better(double *sk, int32_t *si, int n, int P) {
+  for (int i = n + threadIdx.x; i < P; i += blockDim.x) {
+    sk[i] = -INFINITY;
+    si[i] = 0x7fffffff;
+  }
+  __syncthreads();
+  for (int kk = 2; kk <= P; kk <<= 1)
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int l = i ^ j;
+        if (l > i) {
+          const bool i_first = (i & kk) == 0;
+          const bool l_better = better(sk[l], si[l], sk[i], si[i]);
+          if (i_first == l_better) {  // out of order: swap
+            const double td = sk[i];
+            sk[i] = sk[l];
+            sk[l] = td;
+            const int32_t ti = si[i];
+            si[i] = si[l];
+            si[l] = ti;
+          }
+        }
+      }
+      __syncthreads();
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 2: budget + block-causal selection and the int8/bf16 QK^T policy.
 // grid = (nqb, B*H), 128 threads.  Dynamic smem: nkb doubles + nkb bytes.
@@ -465,18 +504,28 @@ __global__ void __launch_bounds__(256)
     budget_select_kernel(const double *__restrict__ pooled, const float *__restrict__ block_rms,
                          const float *__restrict__ q_scales, const float *__restrict__ k_scales,
                          int nqb, int nkb, int budget, int maxdeg, int32_t *sel_idx,
-                         int32_t *sel_cnt, uint8_t *qk_mode, int policy, float tol) {
+                         int32_t *sel_cnt, uint8_t *qk_mode, int policy, float tol, bool stage_k) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  double *score = reinterpret_cast<double *>(dsm);                   // [nkb]
-  float *k_rms = reinterpret_cast<float *>(score + nkb);             // [nkb]
+  const int nhist = nkb - nqb;
+  int P = 1;
+  while (P < nhist) P <<= 1;
+  // dynamic shared memory: the history's pooled vectors when they fit
+  // (stage_k), the sort keys, then RMS and scales of the key blocks
+  double *kst = reinterpret_cast<double *>(dsm);                     // [nhist][D] or none
+  double *score = kst + (stage_k ? (size_t)nhist * D : 0);           // [P]
+  int32_t *sidx = reinterpret_cast<int32_t *>(score + P);            // [P]
+  float *k_rms = reinterpret_cast<float *>(sidx + P);                // [nkb]
   float *k_sc = k_rms + nkb;                                         // [nkb]
-  unsigned char *taken = reinterpret_cast<unsigned char *>(k_sc + nkb);  // [nkb]
   __shared__ double qn[D];
   __shared__ int32_t picks[256];
   const int qb = blockIdx.x, bh = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n_warps = blockDim.x >> 5;
   const double *prow = pooled + (size_t)bh * (nqb + nkb) * D;
+  if (stage_k) {  // the history's pooled vectors, all copies in flight at once
+    const double *src = prow + (size_t)nqb * D;
+    for (int e = threadIdx.x * 2; e < nhist * D; e += blockDim.x * 2) cp_async16(kst + e, src + e);
+  }
   for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = prow[(size_t)qb * D + d];
   // per key block RMS and scale for the precision policy, fetched up front
   if (qk_mode && policy == CAST_POLICY_AUTO)
@@ -484,15 +533,20 @@ __global__ void __launch_bounds__(256)
       k_rms[kb] = block_rms[(size_t)bh * (nqb + nkb) + nqb + kb];
       k_sc[kb] = k_scales[(size_t)bh * nkb + kb];
     }
+  if (stage_k) cp_async_wait_all();
   __syncthreads();
-  const int nhist = nkb - nqb;
   for (int kb = warp; kb < nhist; kb += n_warps) {
-    double s = warp_dot<D>(qn, prow + (size_t)(nqb + kb) * D, lane);
-    if (lane == 0) score[kb] = s;
+    const double *b = stage_k ? kst + (size_t)kb * D : prow + (size_t)(nqb + kb) * D;
+    double s = warp_dot<D>(qn, b, lane);
+    if (lane == 0) {
+      score[kb] = s;
+      sidx[kb] = kb;
+    }
   }
   __syncthreads();
   const int keep = min(budget, nhist);
-  if (warp == 0) warp_topk(score, nhist, keep, taken, picks, lane);
+  cta_sort_better(score, sidx, nhist, P);
+  for (int j = threadIdx.x; j < keep; j += blockDim.x) picks[j] = sidx[j];
   __syncthreads();
   int32_t *out = sel_idx + ((size_t)bh * nqb + qb) * maxdeg;
   for (int j = threadIdx.x; j < maxdeg; j += blockDim.x) {
