@@ -148,7 +148,8 @@ extern "C" size_t cast_rcsa_select_quant_workspace_bytes(int B, int H, int Lq, i
   const int nqb = ceil_div(Lq, block_size), nkb = ceil_div(Lk, block_size);
   // pooled vectors, block RMS, and the q/k scales when the caller passes none
   return sq_pooled_bytes(B, H, nqb, nkb, D) + sq_rms_bytes(B, H, nqb, nkb) +
-         2 * align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256);
+         2 * align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256) +
+         align_up((size_t)B * H * (nqb + nkb), 256);  // need flags of the auto policy's code pass
 }
 
 extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *v,
@@ -182,7 +183,8 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   const size_t need = cast_rcsa_select_quant_workspace_bytes(B, H, Lq, Lk, D, block_size);
   if (!workspace || workspace_bytes < need)
     return fail(CAST_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
-  int st = current_device_sm100(nullptr);
+  int n_sms = 0;
+  int st = current_device_sm100(&n_sms);
   if (st) return st;
 
   uint8_t *ws = static_cast<uint8_t *>(workspace);
@@ -193,6 +195,8 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   float *qs = q_scales ? q_scales : reinterpret_cast<float *>(ws);
   ws += align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256);
   float *ks = k_scales ? k_scales : reinterpret_cast<float *>(ws);
+  ws += align_up((size_t)B * H * (nqb + nkb) * sizeof(float), 256);
+  uint8_t *need_flags = ws;
   double *pooled_out = pooled ? pooled : pooled_ws;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -207,22 +211,23 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   // written after the selection (kernel 3); V codes keep the fused pass.
   const bool lazy = policy == CAST_POLICY_AUTO && qk_mode && !v_codes;
   int8_t *qc1 = lazy ? nullptr : q_codes, *kc1 = lazy ? nullptr : k_codes;
+  uint8_t *nf = lazy ? need_flags : nullptr;
   if (D == 128 && !masked)
     castk::pool_quant_kernel<128, false><<<grid, 256, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
                                                               nqb, nkb, qc1, qs, kc1, ks, v_codes,
-                                                              v_scales, pooled_out, rms);
+                                                              v_scales, pooled_out, rms, nf);
   else if (D == 128)
     castk::pool_quant_kernel<128, true><<<grid, 256, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
                                                              nqb, nkb, qc1, qs, kc1, ks, v_codes,
-                                                             v_scales, pooled_out, rms);
+                                                             v_scales, pooled_out, rms, nf);
   else if (!masked)
     castk::pool_quant_kernel<64, false><<<grid, 128, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
                                                              nqb, nkb, qc1, qs, kc1, ks, v_codes,
-                                                             v_scales, pooled_out, rms);
+                                                             v_scales, pooled_out, rms, nf);
   else
     castk::pool_quant_kernel<64, true><<<grid, 128, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
                                                             nqb, nkb, qc1, qs, kc1, ks, v_codes,
-                                                            v_scales, pooled_out, rms);
+                                                            v_scales, pooled_out, rms, nf);
   CAST_CUDA_TRY(cudaGetLastError());
   const int keep = std::min(budget, nkb - nqb);
   const int maxdeg = keep + nqb;
@@ -251,18 +256,18 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   if (D == 128)
     castk::budget_select_kernel<128><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
                                                           budget, maxdeg, sel_idx, sel_cnt,
-                                                          qk_mode, policy, int8_tolerance, stage_k);
+                                                          qk_mode, policy, int8_tolerance, stage_k, nf);
   else
     castk::budget_select_kernel<64><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nqb, nkb,
                                                          budget, maxdeg, sel_idx, sel_cnt, qk_mode,
-                                                         policy, int8_tolerance, stage_k);
+                                                         policy, int8_tolerance, stage_k, nf);
   CAST_CUDA_TRY(cudaGetLastError());
   if (lazy) {
-    dim3 g3(nqb + nkb, B * H);
+    const int g3 = B * H * (nqb + nkb);  // one CTA per block; unmarked ones exit at once
 #define CAST_QUANT_NEEDED(DD, MM, TT)                                                                \
   castk::quant_needed_kernel<DD, MM><<<g3, TT, 0, s>>>(qb, kb, q_valid, k_valid, Lq, Lk, block_size, \
-                                                       nqb, nkb, sel_idx, sel_cnt, maxdeg, qk_mode,  \
-                                                       q_codes, qs, k_codes, ks)
+                                                       nqb, nkb, B * H, need_flags, q_codes, qs,     \
+                                                       k_codes, ks)
     if (D == 128 && !masked)
       CAST_QUANT_NEEDED(128, false, 256);
     else if (D == 128)

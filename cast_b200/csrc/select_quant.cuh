@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
                       const uint8_t *__restrict__ k_valid, int Lq, int Lk, int block, int nqb,
                       int nkb, int8_t *q_codes, float *q_scales, int8_t *k_codes,
                       float *k_scales, int8_t *v_codes, float *v_scales, double *pooled,
-                      float *block_rms) {
+                      float *block_rms, uint8_t *need_flags) {
   constexpr int kGroups = D / 8;
   constexpr int kThreads = kSumLanes * kGroups;
   __shared__ float red[kSumLanes][D];
@@ -330,6 +330,8 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
       block_rms[(size_t)bh * (nqb + nkb) + row0 + blk] =
           sqrtf(s2 / (float)max(1, count * D));
     }
+    // the block is not needed until an int8 query block marks it
+    if (need_flags && pool) need_flags[(size_t)bh * (nqb + nkb) + (which == 0 ? 0 : nqb) + blk] = 0;
   }
   if (pool) {
     if (tid < D) {
@@ -363,57 +365,44 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
 }
 
 // Kernel 3 (auto policy): int8 codes only for the blocks an int8 query block
-// reads -- its own Q block and every K block it selected; the other code
-// bytes are left as they are.  grid = (nqb + nkb, B*H), the threads of
-// kernel 1; each CTA first decides from qk_mode / sel_idx whether its block
-// is needed, and exits if not.  The scale is kernel 1's.  The division-free
-// path is taken for scale >= 2^-96, which implies amax >= 127 * 2^-96 *
-// (1 - 2^-24) > 2^-90 (where it is exact); smaller blocks use the division,
-// so the codes equal kernel 1's fused second pass bit for bit.
+// reads -- its own Q block and every K block it selected, which the
+// selection kernel marked in need_flags ([B*H][nQb + nKb], cleared by kernel
+// 1); the other code bytes are left as they are.  The grid strides over the
+// flags (blocks in (bh, block) order; launched with one CTA per block, so
+// an unmarked block's CTA exits after one byte) and codes the marked blocks
+// with kernel 1's scale.  The division-free path is taken for
+// scale >= 2^-96, which implies amax >= 127 * 2^-96 * (1 - 2^-24) > 2^-90
+// (where it is exact); smaller blocks use the division, so the codes equal
+// kernel 1's fused second pass bit for bit.
 template <int D, bool kMasked>
 __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
     quant_needed_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                         const uint8_t *__restrict__ q_valid, const uint8_t *__restrict__ k_valid,
-                        int Lq, int Lk, int block, int nqb, int nkb,
-                        const int32_t *__restrict__ sel_idx, const int32_t *__restrict__ sel_cnt,
-                        int maxdeg, const uint8_t *__restrict__ qk_mode, int8_t *q_codes,
+                        int Lq, int Lk, int block, int nqb, int nkb, int BH,
+                        const uint8_t *__restrict__ need_flags, int8_t *q_codes,
                         const float *__restrict__ q_scales, int8_t *k_codes,
                         const float *__restrict__ k_scales) {
   constexpr int kGroups = D / 8;
-  __shared__ int s_need;
   const int tid = threadIdx.x;
-  const int bh = blockIdx.y;
-  const bool is_q = (int)blockIdx.x < nqb;
-  const int blk = is_q ? blockIdx.x : blockIdx.x - nqb;
-  if (tid < 32) {
-    bool need = false;
-    if (is_q) {
-      need = tid == 0 && qk_mode[(size_t)bh * nqb + blk] != 0;
-    } else {
-      for (int qb = 0; qb < nqb; ++qb) {
-        if (!qk_mode[(size_t)bh * nqb + qb]) continue;
-        const int cnt = min(max(sel_cnt[(size_t)bh * nqb + qb], 0), maxdeg);
-        const int32_t *row = sel_idx + ((size_t)bh * nqb + qb) * maxdeg;
-        for (int j = tid; j < cnt; j += 32) need |= row[j] == blk;
-      }
-    }
-    need = __any_sync(0xffffffffu, need);
-    if (tid == 0) s_need = need;
-  }
-  __syncthreads();
-  if (!s_need) return;
   const int grp = tid % kGroups, slot = tid / kGroups;
-  const __nv_bfloat16 *X = is_q ? q : k;
-  const int L = is_q ? Lq : Lk;
-  const int b0 = blk * block;
-  const int rows = min(block, L - b0);
-  const uint8_t *vrow = kMasked ? (is_q ? q_valid : k_valid) : nullptr;
-  if (vrow) vrow += b0;
-  const float sc = is_q ? q_scales[(size_t)bh * nqb + blk] : k_scales[(size_t)bh * nkb + blk];
-  int8_t *codes = is_q ? q_codes : k_codes;
-  write_block_codes<D, kMasked>(X + ((size_t)bh * L + b0) * D + grp * 8,
-                                codes + ((size_t)bh * L + b0) * D + grp * 8, rows, slot, vrow, sc,
-                                sc >= 0x1p-96f, l2_evict_first());
+  const int per = nqb + nkb;
+  for (int id = blockIdx.x; id < BH * per; id += gridDim.x) {
+    if (!need_flags[id]) continue;  // block-uniform
+    const int bh = id / per, x = id % per;
+    const bool is_q = x < nqb;
+    const int blk = is_q ? x : x - nqb;
+    const __nv_bfloat16 *X = is_q ? q : k;
+    const int L = is_q ? Lq : Lk;
+    const int b0 = blk * block;
+    const int rows = min(block, L - b0);
+    const uint8_t *vrow = kMasked ? (is_q ? q_valid : k_valid) : nullptr;
+    if (vrow) vrow += b0;
+    const float sc = is_q ? q_scales[(size_t)bh * nqb + blk] : k_scales[(size_t)bh * nkb + blk];
+    int8_t *codes = is_q ? q_codes : k_codes;
+    write_block_codes<D, kMasked>(X + ((size_t)bh * L + b0) * D + grp * 8,
+                                  codes + ((size_t)bh * L + b0) * D + grp * 8, rows, slot, vrow, sc,
+                                  sc >= 0x1p-96f, l2_evict_first());
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -504,7 +493,8 @@ __global__ void __launch_bounds__(256)
     budget_select_kernel(const double *__restrict__ pooled, const float *__restrict__ block_rms,
                          const float *__restrict__ q_scales, const float *__restrict__ k_scales,
                          int nqb, int nkb, int budget, int maxdeg, int32_t *sel_idx,
-                         int32_t *sel_cnt, uint8_t *qk_mode, int policy, float tol, bool stage_k) {
+                         int32_t *sel_cnt, uint8_t *qk_mode, int policy, float tol, bool stage_k,
+                         uint8_t *need_flags) {
   extern __shared__ __align__(16) unsigned char dsm[];
   const int nhist = nkb - nqb;
   int P = 1;
@@ -577,6 +567,11 @@ __global__ void __launch_bounds__(256)
       mode = worst <= tol ? 1 : 0;
     }
     if (lane == 0) qk_mode[(size_t)bh * nqb + qb] = mode;
+    if (need_flags && mode) {  // this query block and every K block it reads need codes
+      uint8_t *nf = need_flags + (size_t)bh * (nqb + nkb);
+      if (lane == 0) nf[qb] = 1;
+      for (int j = lane; j < keep + qb + 1; j += 32) nf[nqb + (j < keep ? picks[j] : nhist + (j - keep))] = 1;
+    }
   }
 }
 
