@@ -165,32 +165,6 @@ __device__ __forceinline__ float row_max(const uint32_t (&v)[64], const uint32_t
   }
 }
 
-// Probabilities exp2(S*c2 - base) of the step (masked keys 0), packed bf16
-// pairs written in place into v[0..31].  Returns their sum.  For s32 scores
-// the int->float conversion is folded into the FFMA:
-// float(S) = as_float(S + 0x4B400000) - 1.5*2^23, exact for |S| < 2^22.
-template <bool kInt8, bool kMasked>
-__device__ __forceinline__ float row_probs(uint32_t (&v)[64], const uint32_t (&kmask)[2],
-                                           float c2, float base) {
-  const float bias = kInt8 ? fmaf(12582912.0f, c2, base) : base;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    const uint32_t a = kInt8 ? v[2 * c] + 0x4B400000u : v[2 * c];
-    const uint32_t b = kInt8 ? v[2 * c + 1] + 0x4B400000u : v[2 * c + 1];
-    float e0 = fast_exp2(fmaf(__uint_as_float(a), c2, -bias));
-    float e1 = fast_exp2(fmaf(__uint_as_float(b), c2, -bias));
-    if (kMasked) {
-      const uint32_t w = kmask[(2 * c) / 32];
-      e0 = ((w >> ((2 * c) % 32)) & 1u) ? e0 : 0.0f;
-      e1 = ((w >> ((2 * c + 1) % 32)) & 1u) ? e1 : 0.0f;
-    }
-    acc[c & 3] += e0 + e1;
-    v[c] = pack_bf16x2(e0, e1);
-  }
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
-}
-
 // Shared-memory descriptor as (lo, hi) words: hi is fixed by the LBO/SBO
 // strides, and lo = start>>4 | LBO>>4 << 16, so an operand `off` bytes further
 // on is lo + off/16 (smem addresses stay below 2^18, so nothing carries).
@@ -341,7 +315,9 @@ constexpr float kFastSumLimit = 65536.0f;
 
 // Probabilities exp2(S*c2 - base) of a 64-key step in one pass: packed FFMA
 // for the exponent, MUFU exp2, packed row sums, bf16 pairs written in place
-// into v[0..31].  Returns their sum.
+// into v[0..31].  Returns their sum.  For s32 scores the int->float
+// conversion is folded into the FFMA: float(S) = as_float(S + 0x4B400000) -
+// 1.5*2^23, exact for |S| < 2^22.
 template <bool kInt8, bool kMasked>
 __device__ __forceinline__ float step_probs(uint32_t (&v)[64], const uint32_t (&kmask)[2],
                                             float c2, float base) {
