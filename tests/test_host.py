@@ -91,3 +91,44 @@ def test_python_wrappers_refuse_cpu_tensors():
     q = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         rcsa.select_quant(q, q, block_size=128, budget=1)
+
+
+def test_compact_and_pair_writer_validation(lib):
+    fake = ctypes.c_void_p(4096)
+    # compact packing: head_dim other than 128, bad dtype code, bad phase heads
+    st = lib.cast_compact_pack(fake, fake, fake, 0, None, 1, fake, 1, 8, 2, 64, 8, fake, fake, fake, None)
+    assert st == 2 and b"head_dim" in lib.cast_last_error_message()
+    st = lib.cast_compact_pack(fake, fake, fake, 7, None, 1, fake, 1, 8, 2, 128, 8, fake, fake, fake, None)
+    assert st == 1 and b"in_dtype" in lib.cast_last_error_message()
+    st = lib.cast_compact_pack(fake, fake, fake, 0, fake, 3, fake, 1, 8, 2, 128, 8, fake, fake, fake, None)
+    assert st == 1 and b"phase_heads" in lib.cast_last_error_message()
+    st = lib.cast_compact_unpack(None, fake, 1, 8, 2, 128, 8, fake, None)
+    assert st == 1
+    # pair writer: unknown arithmetic mode, misaligned frames
+    st = lib.cast_barycentric_pair_write(fake, fake, fake, fake, fake, 4, 5, 2, 880 * 64, 9, None)
+    assert st == 1 and b"arithmetic_mode" in lib.cast_last_error_message()
+    odd = ctypes.c_void_p(4097)
+    st = lib.cast_barycentric_pair_write(odd, fake, fake, fake, fake, 4, 5, 2, 880 * 64, 2, None)
+    assert st == 3
+
+
+def test_pair_writer_wrapper_checks_like_the_reference():
+    import torch
+
+    from cast_b200 import barycentric
+
+    act = torch.zeros(1, 4, 8, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        barycentric.direct_control_barycentric_pair_write(
+            act, torch.zeros(1, 2, 2), torch.zeros(2, 2, dtype=torch.int32),
+            torch.zeros(2, dtype=torch.int32), torch.zeros(1, 5, 8, 4))
+
+
+def test_compact_wrapper_refuses_cpu_tensors():
+    import torch
+
+    from cast_b200 import compact
+
+    x = torch.zeros(1, 8, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        compact.pack(x, x, x, torch.zeros(8, dtype=torch.int32))
