@@ -423,3 +423,73 @@ class RCSAPlan:
             self.select(q, k)
         if parts in ("all", "attend"):
             self.attend(q, k, v, out)
+
+
+class RCSAHostPlan:
+    """An RCSA layer call whose inputs and output live in pinned host memory.
+
+    The heads are split into ``groups`` contiguous groups, each with its own
+    :class:`RCSAPlan`.  Group g's host-to-device copy runs on one copy stream,
+    its selection + attention on the caller's stream once that copy is in,
+    and its device-to-host copy on a second copy stream once its attention is
+    done -- so the copies of one group overlap the compute of another, and
+    the two copy directions overlap each other.  The call returns with the
+    output copy ordered before anything the caller enqueues next on its
+    stream.  Batch size 1 (a head slice of ``[1,H,L,D]`` is contiguous).
+    """
+
+    def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int,
+                 budget: int, policy: str = "auto", groups: int = 4,
+                 int8_tolerance: float = DEFAULT_INT8_TOLERANCE, device=None):
+        if B != 1:
+            raise ValueError("RCSAHostPlan takes batch size 1 (contiguous head slices)")
+        dev = torch.device(device if device is not None else "cuda")
+        groups = max(1, min(int(groups), H))
+        bounds = [H * g // groups for g in range(groups + 1)]
+        self.heads = [(bounds[g], bounds[g + 1]) for g in range(groups)]
+        self.plans = [RCSAPlan(B, h1 - h0, Lq, Lk, D, block_size=block_size, budget=budget,
+                               policy=policy, int8_tolerance=int8_tolerance, device=dev)
+                      for h0, h1 in self.heads]
+        self.q = torch.empty(B, H, Lq, D, dtype=torch.bfloat16, device=dev)
+        self.k = torch.empty(B, H, Lk, D, dtype=torch.bfloat16, device=dev)
+        self.v = torch.empty(B, H, Lk, D, dtype=torch.bfloat16, device=dev)
+        self.out = torch.empty(B, H, Lq, D, dtype=torch.bfloat16, device=dev)
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.shape = (B, H, Lq, Lk, D)
+        self.device = dev
+
+    def __call__(self, hq: torch.Tensor, hk: torch.Tensor, hv: torch.Tensor,
+                 hout: torch.Tensor) -> torch.Tensor:
+        """``hq``/``hk``/``hv``/``hout``: pinned host bf16 tensors of the plan's
+        shapes; the attention output lands in ``hout``."""
+        B, H, Lq, Lk, D = self.shape
+        for name, t, L in (("q", hq, Lq), ("k", hk, Lk), ("v", hv, Lk), ("out", hout, Lq)):
+            if t.is_cuda or t.dtype != torch.bfloat16 or tuple(t.shape) != (B, H, L, D):
+                raise ValueError(f"{name} must be a host bf16 tensor of shape {(B, H, L, D)}")
+            if not t.is_pinned():
+                raise ValueError(f"{name} must be in pinned host memory")
+        cur = torch.cuda.current_stream(self.device)
+        # the previous call's compute and copies are done with the buffers
+        self.h2d.wait_stream(cur)
+        self.d2h.wait_stream(cur)
+        ready = []
+        with torch.cuda.stream(self.h2d):
+            for h0, h1 in self.heads:
+                for dst, src in ((self.q, hq), (self.k, hk), (self.v, hv)):
+                    dst[:, h0:h1].copy_(src[:, h0:h1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self.h2d)
+                ready.append(ev)
+        for (h0, h1), plan, ev in zip(self.heads, self.plans, ready):
+            cur.wait_event(ev)
+            q, k, v = self.q[:, h0:h1], self.k[:, h0:h1], self.v[:, h0:h1]
+            plan.select(q, k)
+            plan.attend(q, k, v, out=self.out[:, h0:h1])
+            done = torch.cuda.Event()
+            done.record(cur)
+            self.d2h.wait_event(done)
+            with torch.cuda.stream(self.d2h):
+                hout[:, h0:h1].copy_(self.out[:, h0:h1], non_blocking=True)
+        cur.wait_stream(self.d2h)
+        return hout

@@ -422,3 +422,28 @@ def test_taba_select_ragged_grid_bitexact(cuda, block_shape):
     assert np.array_equal(scores.cpu().numpy(), o_sc)
     assert np.array_equal(idx.cpu().numpy(), o_sel)
     assert np.array_equal(cnt.cpu().numpy(), o_cnt)
+
+
+def test_host_plan_matches_device_plan(cuda):
+    """RCSAHostPlan (pinned host inputs, head groups with overlapped copies)
+    gives the device plan's selection and, within the attention bars, its
+    output; two calls in a row give the same bits."""
+    w = workloads.config2(heads=4)
+    hq, hk, hv = (t.pin_memory() for t in (w.q, w.k, w.v))
+    hout = torch.empty(w.q.shape, dtype=torch.bfloat16).pin_memory()
+    hp = rcsa.RCSAHostPlan(1, 4, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8,
+                           groups=3, device="cuda")
+    hp(hq, hk, hv, hout)
+    torch.cuda.synchronize()
+    first = hout.clone()
+    hp(hq, hk, hv, hout)
+    torch.cuda.synchronize()
+    assert torch.equal(first, hout)
+    dp = rcsa.RCSAPlan(1, 4, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8, device="cuda")
+    ref = dp(w.q.cuda(), w.k.cuda(), w.v.cuda())
+    torch.cuda.synchronize()
+    for (h0, h1), plan in zip(hp.heads, hp.plans):
+        assert torch.equal(plan.indices, dp.indices[:, h0:h1])
+        assert torch.equal(plan.qk_mode, dp.qk_mode[:, h0:h1])
+    d = (hout.float() - ref.float().cpu()).abs()
+    assert float(d.max()) < MAX_ABS and float(d.mean()) < MEAN_ABS
