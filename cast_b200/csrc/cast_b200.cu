@@ -15,6 +15,7 @@
 #include "par.cuh"
 #include "compact.cuh"
 #include "barycentric.cuh"
+#include "swap_router.cuh"
 
 namespace cast {
 
@@ -725,6 +726,117 @@ extern "C" int cast_barycentric_pair_write(const float *active_residual, const f
   castk::barycentric_pair_kernel<<<grid, castk::kBaryThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       active_residual, weights, source_pairs, target_frames, output, spatial_channels, A, T, N,
       arithmetic_mode == 0 ? 2 : arithmetic_mode);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+// ===========================================================================
+// FC-PASM swap router
+// ===========================================================================
+struct SwapLayout {
+  size_t cand, proxy, err, limit, best, obj, ctl, total;
+};
+
+static bool swap_shape(int B, int H, int Q, int K, int D, int S, int M, int mult, int historical,
+                       int same_bank, int G, castk::SwapShape *p) {
+  if (B <= 0 || H <= 0 || Q <= 0 || K <= 0 || D <= 0 || S <= 0 || M < 0 || M >= Q || mult < 1 ||
+      G < 2 || (G & 1) || D % G)
+    return false;
+  p->B = B, p->H = H, p->Q = Q, p->K = K, p->D = D, p->S = S, p->M = M, p->R = Q - M, p->G = G;
+  p->cand_blocks = historical ? M : K;
+  p->Lc = (int)std::min<long long>(p->cand_blocks, (long long)mult * S);
+  p->mult = mult, p->historical = historical ? 1 : 0, p->same_bank = same_bank ? 1 : 0;
+  return p->cand_blocks > 0;
+}
+
+static SwapLayout swap_layout(const castk::SwapShape &p) {
+  const size_t rows = (size_t)p.B * p.H * p.R, bh = (size_t)p.B * p.H;
+  SwapLayout l;
+  l.cand = 0;
+  l.proxy = l.cand + align_up(rows * p.Lc * sizeof(int), 256);
+  l.err = l.proxy + align_up(rows * p.Lc * p.G * sizeof(float), 256);
+  l.limit = l.err + align_up(rows * p.G * sizeof(float), 256);
+  l.best = l.limit + align_up(rows * sizeof(int), 256);
+  l.obj = l.best + align_up(bh * sizeof(castk::SwapBest), 256);
+  l.ctl = l.obj + align_up(2 * bh * sizeof(double), 256);
+  l.total = l.ctl + 256;
+  return l;
+}
+
+extern "C" size_t cast_swap_route_workspace_bytes(int B, int H, int Q, int K, int D, int S,
+                                                  int memory_blocks, int candidate_multiplier,
+                                                  int historical_only, int sketch_groups) {
+  castk::SwapShape p;
+  if (!swap_shape(B, H, Q, K, D, S, memory_blocks, candidate_multiplier, historical_only, 0,
+                  sketch_groups, &p))
+    return 0;
+  return swap_layout(p).total;
+}
+
+extern "C" int cast_swap_route(const float *score, const float *pooled_value, long long *selected,
+                               const long long *counts, const uint8_t *local, const uint8_t *row_gate,
+                               const float *coefficient, const float *hessian, int B, int H, int Q,
+                               int K, int D, int S, int memory_blocks, int candidate_multiplier,
+                               int num_swap_rounds, float swap_eps, int sketch_groups,
+                               int max_swaps_per_call, int historical_only, int same_bank_only,
+                               double *stats, void *workspace, size_t workspace_bytes,
+                               cast_stream_t stream) {
+  if (!score || !pooled_value || !selected || !counts || !local || !coefficient || !hessian || !stats)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "score, pooled_value, selected, counts, local, "
+                                           "coefficient, hessian and stats are required");
+  castk::SwapShape p;
+  if (!swap_shape(B, H, Q, K, D, S, memory_blocks, candidate_multiplier, historical_only,
+                  same_bank_only, sketch_groups, &p))
+    return fail(CAST_ERR_INVALID_ARGUMENT,
+                "invalid shape (B=%d H=%d Q=%d K=%d D=%d S=%d memory_blocks=%d multiplier=%d "
+                "sketch_groups=%d historical_only=%d)",
+                B, H, Q, K, D, S, memory_blocks, candidate_multiplier, sketch_groups, historical_only);
+  if (num_swap_rounds < 0 || num_swap_rounds > 2)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "num_swap_rounds %d (0..2)", num_swap_rounds);
+  if (max_swaps_per_call < 0) return fail(CAST_ERR_INVALID_ARGUMENT, "negative max_swaps_per_call");
+  if (!(swap_eps >= 0.f) || std::isinf(swap_eps))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "swap_eps must be finite and non-negative");
+  const size_t sm1 = (size_t)(2 * K + D + 32) * sizeof(float) + (size_t)(2 * p.Lc + S) * sizeof(int);
+  const size_t sm2 = (size_t)2 * p.R * p.G * sizeof(float);
+  if (sm1 > 48 * 1024 || sm2 > 48 * 1024)
+    return fail(CAST_ERR_UNSUPPORTED, "too large for one CTA (K=%d S=%d rows=%d sketch_groups=%d)", K,
+                S, p.R, p.G);
+  const SwapLayout lay = swap_layout(p);
+  if (!workspace || workspace_bytes < lay.total)
+    return fail(CAST_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, lay.total);
+  if (!aligned16(workspace)) return fail(CAST_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  char *ws = static_cast<char *>(workspace);
+  int *cand = reinterpret_cast<int *>(ws + lay.cand);
+  float *proxy = reinterpret_cast<float *>(ws + lay.proxy);
+  float *err = reinterpret_cast<float *>(ws + lay.err);
+  int *limit = reinterpret_cast<int *>(ws + lay.limit);
+  auto *best = reinterpret_cast<castk::SwapBest *>(ws + lay.best);
+  double *obj = reinterpret_cast<double *>(ws + lay.obj);
+  auto *ctl = reinterpret_cast<castk::SwapCtl *>(ws + lay.ctl);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int rows = B * H * p.R, bh = B * H;
+  castk::swap_proxy_kernel<<<rows, castk::kSwapProxyThreads, sm1, s>>>(
+      score, pooled_value, selected, counts, local, p, 1e-6f, cand, proxy, err, limit, ctl);
+  CAST_CUDA_TRY(cudaGetLastError());
+  // rounds: the first also records the objective before any swap; a last
+  // pass records the objective after and writes the stats
+  if (num_swap_rounds == 0) {
+    castk::swap_round_kernel<<<bh, castk::kSwapRoundThreads, sm2, s>>>(
+        selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
+        ctl, stats, 0, 0, 0, swap_eps, max_swaps_per_call);
+    CAST_CUDA_TRY(cudaGetLastError());
+  }
+  for (int r = 0; r < num_swap_rounds; ++r) {
+    castk::swap_round_kernel<<<bh, castk::kSwapRoundThreads, sm2, s>>>(
+        selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
+        ctl, stats, 1, r == 0 ? 0 : -1, 0, swap_eps, max_swaps_per_call);
+    CAST_CUDA_TRY(cudaGetLastError());
+  }
+  castk::swap_round_kernel<<<bh, castk::kSwapRoundThreads, sm2, s>>>(
+      selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
+      ctl, stats, 0, 1, 1, swap_eps, max_swaps_per_call);
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;
 }

@@ -1,0 +1,384 @@
+"""FC-PASM fixed-budget swap router on the B200 kernels.
+
+Mirrors ``FCPASMSwapRoutingConfig`` and ``FCPASMLocalCoordinateSwapRouter``
+(``proposed/fc_pasm_swap_routing.py:23-62`` and ``:109-1115``): the same
+constructor, ``refine`` keywords, fallback records, checks and error
+messages.  ``refine`` keeps the reference's gates on the host and runs its
+numeric body -- candidates, omission proxies, quadratic terms, the swap
+rounds -- in ``cast_swap_route`` (one proxy launch, one launch per round and
+one closing launch, no host synchronisation between them).
+
+The transport operators of the objective (:116-268) are built here, once per
+(anchor pair, exponent, grid) and cached in the transport entry, the way the
+reference caches them (``_attention_operator_cache``): a bilinear lift of the
+attention-grid basis maps, the sqrt-Hann overlapping analysis of the FC-PASM
+reconstruction, the per-frequency phase exp(i x g theta), overlap-add and
+block pooling; ``quadratic_terms`` folds them into one coefficient vector and
+one Hessian over the current rows.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+_OP_CACHE_KEY = "_cast_b200_operator_cache"
+
+
+@dataclass(frozen=True)
+class FCPASMSwapRoutingConfig:
+    candidate_multiplier: int = 2
+    num_swap_rounds: int = 1
+    swap_eps: float = 1e-6
+    lambda_anchor: float = 1.0
+    lambda_reconstruction: float = 1.0
+    sketch_groups: int = 16
+    require_fc_transport: bool = False
+    min_transport_affinity: float = 0.0
+    min_pair_transport_affinity: float = 0.0
+    max_swaps_per_call: int = 0
+    active_layers: tuple[int, ...] = ()
+    historical_only: bool = False
+    same_bank_only: bool = False
+
+    def __post_init__(self) -> None:
+        if self.candidate_multiplier < 1:
+            raise ValueError("candidate multiplier must be positive")
+        if self.num_swap_rounds not in {0, 1, 2}:
+            raise ValueError("FC-PASM routing supports zero to two swap rounds")
+        if not math.isfinite(self.swap_eps) or self.swap_eps < 0.0:
+            raise ValueError("swap epsilon must be finite and non-negative")
+        if self.lambda_anchor < 0.0 or self.lambda_reconstruction < 0.0:
+            raise ValueError("routing objective weights must be non-negative")
+        if self.lambda_anchor + self.lambda_reconstruction <= 0.0:
+            raise ValueError("routing objective must contain a positive term")
+        if self.sketch_groups < 2 or self.sketch_groups % 2:
+            raise ValueError("routing sketch groups must be a positive even number")
+        if not 0.0 <= self.min_transport_affinity <= 1.0:
+            raise ValueError("minimum FC transport affinity must be in [0, 1]")
+        if not 0.0 <= self.min_pair_transport_affinity <= 1.0:
+            raise ValueError("minimum pair FC transport affinity must be in [0, 1]")
+        if self.max_swaps_per_call < 0:
+            raise ValueError("maximum swaps per call must be non-negative")
+        if any(layer < 0 for layer in self.active_layers):
+            raise ValueError("routing active layers must be non-negative")
+        if self.historical_only and self.same_bank_only:
+            raise ValueError("historical-only routing already fixes the KV bank")
+
+
+def _hann_sqrt(n_y: int, n_x: int, device) -> torch.Tensor:
+    wy = torch.hann_window(n_y, periodic=False, device=device, dtype=torch.float32)
+    wx = torch.hann_window(n_x, periodic=False, device=device, dtype=torch.float32)
+    return (wy[:, None] * wx[None, :]).clamp_min(0.0).sqrt()
+
+
+def transport_operator(transport: dict | None, pair: tuple[int, int], *, spatial_shape: tuple[int, int],
+                       exponent: float, device) -> tuple[torch.Tensor, bool]:
+    """The [output, input] operator on the ``spatial_shape`` attention grid
+    that moves a block map along the FC-PASM transport of ``pair`` by
+    ``exponent`` (identity, False when the pair has no usable sketch)."""
+    gh, gw = int(spatial_shape[0]), int(spatial_shape[1])
+    n = gh * gw
+    eye = torch.eye(n, device=device, dtype=torch.float32)
+    entry = transport.get("pairs", {}).get(pair) if transport is not None else None
+    if not isinstance(entry, dict):
+        return eye, False
+    theta, aff = entry.get("theta"), entry.get("affinity")
+    if not (isinstance(theta, torch.Tensor) and isinstance(aff, torch.Tensor)
+            and theta.ndim == 3 and aff.shape == theta.shape):
+        return eye, False
+    cache = entry.setdefault(_OP_CACHE_KEY, {})
+    key = (gh, gw, round(float(exponent), 12), str(device))
+    if isinstance(cache.get(key), torch.Tensor):
+        return cache[key].to(device), True
+    oh, ow = (int(v) for v in transport["output_shape"])
+    th_, tw_ = (int(v) for v in transport["transport_shape"])
+    wh, ww = (int(v) for v in transport["window_shape"])
+    sh, sw = (int(v) for v in transport["stride"])
+    ph, pw = (int(v) for v in transport["padding"])
+    gy, gx = (int(v) for v in transport["tile_grid"])
+    tiles_n = gy * gx
+    if theta.shape[0] != tiles_n:
+        raise RuntimeError("FC routing frequency tiles do not match the OLA grid")
+    win = _hann_sqrt(wh, ww, device)
+    # analysis: each basis map lifted to the latent grid, windowed tiles
+    lifted = F.interpolate(eye.reshape(n, 1, gh, gw), size=(oh, ow), mode="bilinear", align_corners=False)
+    cols = F.unfold(F.pad(lifted, (pw, pw, ph, ph), mode="reflect"), kernel_size=(wh, ww), stride=(sh, sw))
+    tiles = cols.transpose(1, 2).reshape(n * tiles_n, 1, wh, ww) * win
+    pooled = (th_, tw_) != (wh, ww)
+    if pooled:
+        tiles = F.avg_pool2d(tiles, 2, 2, ceil_mode=True, count_include_pad=False)
+    spec = torch.fft.rfft2(tiles.reshape(n, tiles_n, th_, tw_))
+    theta = theta.to(device=device, dtype=torch.float32)
+    aff = aff.to(device=device, dtype=torch.float32)
+    if theta.shape[-2:] != spec.shape[-2:]:
+        raise RuntimeError("FC routing frequency operator has an invalid shape")
+    rot = torch.polar(torch.ones_like(theta), float(exponent) * aff * theta)
+    moved = torch.fft.irfft2(spec * rot[None], s=(th_, tw_))
+    still = torch.fft.irfft2(spec, s=(th_, tw_))
+    if pooled:
+        moved, still = (F.interpolate(x.reshape(n * tiles_n, 1, th_, tw_), size=(wh, ww), mode="bilinear",
+                                      align_corners=False) for x in (moved, still))
+    # synthesis: windowed overlap-add normalised by the summed squared window
+    size = (oh + 2 * ph, ow + 2 * pw)
+    norm = F.fold((win * win).reshape(-1, 1).expand(-1, tiles_n)[None], size, (wh, ww), stride=(sh, sw))
+    norm = norm[:, :, ph:ph + oh, pw:pw + ow].clamp_min(1e-8)
+
+    def ola(x):
+        folded = F.fold((x.reshape(n, tiles_n, wh, ww) * win).reshape(n, tiles_n, -1).transpose(1, 2),
+                        size, (wh, ww), stride=(sh, sw))
+        return folded[:, :, ph:ph + oh, pw:pw + ow] / norm
+
+    bh, bw = math.ceil(oh / gh), math.ceil(ow / gw)
+    delta = F.avg_pool2d(ola(moved) - ola(still), (bh, bw), (bh, bw), ceil_mode=True, count_include_pad=False)
+    if delta.shape[-2:] != (gh, gw):
+        raise RuntimeError("FC routing operator did not return the attention grid")
+    op = (eye + delta.reshape(n, n)).transpose(0, 1).contiguous()
+    cache[key] = op
+    return op, True
+
+
+def quadratic_terms(*, temporal_cells: int, spatial: int, exact_frames: tuple[int, ...],
+                    temporal_group_size: int, current_boundary: int, transport: dict | None,
+                    lambda_anchor: float, lambda_reconstruction: float, device):
+    """(coefficient [R], Hessian [R,R], transport used) of the routing
+    objective over the current rows: anchor rows weighted by their cell's
+    Exact-anchor count, and for every skipped target t between anchors l < r
+    of one segment, |A_t e_l + B_t e_r|^2 with A_t = (1-a) M(a),
+    B_t = a M(-(1-a)), a = (t-l)/(r-l) (:414-548)."""
+    cells, sp = temporal_cells, spatial
+    grid = ((int(transport.get("attention_spatial_h", 1)), int(transport.get("attention_spatial_w", sp)))
+            if transport is not None else (1, sp))
+    cell_of = {int(f): min(int(f) // int(temporal_group_size), cells - 1) for f in exact_frames}
+    count = torch.zeros(cells, dtype=torch.float32)
+    for f in exact_frames:
+        count[cell_of[int(f)]] += 1.0
+    coef = (count * float(lambda_anchor)).repeat_interleave(sp).to(device)
+    hess = torch.zeros(cells * sp, cells * sp, dtype=torch.float32, device=device)
+    used = False
+    lam = float(lambda_reconstruction)
+    for left, right in zip(exact_frames, exact_frames[1:]):
+        if (left < current_boundary) != (right < current_boundary):
+            continue
+        lc, rc = cell_of[int(left)], cell_of[int(right)]
+        ls, rs = slice(lc * sp, (lc + 1) * sp), slice(rc * sp, (rc + 1) * sp)
+        for target in range(left + 1, right):
+            a = float(target - left) / float(right - left)
+            m_l, f_l = transport_operator(transport, (int(left), int(right)), spatial_shape=grid,
+                                          exponent=a, device=device)
+            m_r, f_r = transport_operator(transport, (int(left), int(right)), spatial_shape=grid,
+                                          exponent=-(1.0 - a), device=device)
+            used = used or f_l or f_r
+            A, Bm = (1.0 - a) * m_l, a * m_r
+            if lc == rc:
+                C = A + Bm
+                hess[ls, ls] += lam * (C.transpose(0, 1) @ C)
+            else:
+                hess[ls, ls] += lam * (A.transpose(0, 1) @ A)
+                hess[rs, rs] += lam * (Bm.transpose(0, 1) @ Bm)
+                hess[ls, rs] += lam * (A.transpose(0, 1) @ Bm)
+                hess[rs, ls] += lam * (Bm.transpose(0, 1) @ A)
+    return coef.contiguous(), hess.contiguous(), used
+
+
+def _mean_affinity(entry) -> float:
+    if not isinstance(entry, dict):
+        return 0.0
+    v = entry.get("mean_affinity", 0.0)
+    return float(v.detach().float().item()) if isinstance(v, torch.Tensor) else float(v)
+
+
+class FCPASMLocalCoordinateSwapRouter:
+    """Refine compact pooled-Q/K routes without changing the row budgets."""
+
+    def __init__(self, config) -> None:
+        self.config = config
+        self._records: list[dict[str, Any]] = []
+        self._ws: torch.Tensor | None = None
+
+    def _fallback(self, layer_index: int, reason: str, baseline, **extra):
+        record = {"layer_index": int(layer_index), "status": "independent_topk_fallback",
+                  "fallback_reason": reason, "swap_count": 0, **extra, "fixed_budget": True}
+        self._records.append(record)
+        return baseline, record
+
+    def _workspace(self, nbytes: int, device) -> torch.Tensor:
+        if self._ws is None or self._ws.numel() < nbytes or self._ws.device != device:
+            self._ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+        return self._ws
+
+    def refine(self, *, score, pooled_value, selected, counts, local, memory_blocks, spatial_shape,
+               exact_current_frames, temporal_group_size, current_boundary, transport, layer_index):
+        """Zero, one or two single-swap rounds on the device (:616-1077)."""
+        cfg = self.config
+        if score.ndim != 4 or pooled_value.ndim != 4:
+            raise ValueError("routing requires BHQK score and BHKD pooled values")
+        if score.shape[:2] != pooled_value.shape[:2] or score.shape[-1] != pooled_value.shape[-2]:
+            raise ValueError("routing score/value layouts differ")
+        if selected.shape[:3] != score.shape[:3] or counts.shape != score.shape[:3]:
+            raise ValueError("routing selection/count layouts differ")
+        if local.shape != score.shape[-2:]:
+            raise ValueError("routing local stencil has invalid shape")
+        score = score.detach()
+        pooled_value = pooled_value.detach()
+        baseline = selected.clone()
+        if cfg.active_layers and layer_index not in cfg.active_layers:
+            return self._fallback(layer_index, "layer_not_enabled", baseline)
+        B, H, Q, K = score.shape
+        current_rows = Q - int(memory_blocks)
+        spatial = int(spatial_shape[0] * spatial_shape[1])
+        if current_rows <= 0 or current_rows % spatial:
+            return self._fallback(layer_index, "no_rectangular_current_rows", baseline, fc_cache_used=False)
+        cells = current_rows // spatial
+        frames = tuple(int(f) for f in exact_current_frames)
+        if tuple(sorted(set(frames))) != frames:
+            raise ValueError("routing Exact Current frames must be unique and chronological")
+        same_seg = [(l, r) for l, r in zip(frames, frames[1:])
+                    if (l < current_boundary) == (r < current_boundary)]
+        has_skipped = any(r - l > 1 for l, r in same_seg)
+        if cfg.num_swap_rounds == 0 or len(frames) < 2 or not has_skipped:
+            reason = ("zero_swap_rounds" if cfg.num_swap_rounds == 0
+                      else "fewer_than_two_exact_anchors" if len(frames) < 2 else "no_skipped_frames")
+            return self._fallback(layer_index, reason, baseline, fc_cache_used=False)
+        pairs = transport.get("pairs", {}) if isinstance(transport, dict) else {}
+        matching = [pairs[(l, r)] for l, r in same_seg
+                    if r - l > 1 and isinstance(pairs.get((l, r)), dict)
+                    and isinstance(pairs[(l, r)].get("theta"), torch.Tensor)]
+        match_aff = max((_mean_affinity(e) for e in matching), default=0.0)
+        strong = bool(matching) and match_aff >= cfg.min_transport_affinity
+        if cfg.require_fc_transport and not strong:
+            reason = ("weak_previous_layer_fc_transport" if matching
+                      else "missing_previous_layer_fc_transport")
+            return self._fallback(layer_index, reason, baseline, matching_transport_affinity=match_aff,
+                                  fc_cache_used=False, g0_fallback=True)
+        row_gate = None
+        gate_cells = 0
+        if cfg.min_pair_transport_affinity > 0.0:
+            gate = [False] * cells
+            for l, r in same_seg:
+                if r - l <= 1 or _mean_affinity(pairs.get((l, r))) < cfg.min_pair_transport_affinity:
+                    continue
+                for t in range(l + 1, r):
+                    c = min(t // int(temporal_group_size), cells - 1)
+                    gate_cells += not gate[c]
+                    gate[c] = True
+            if not any(gate):
+                return self._fallback(layer_index, "no_strong_transport_pair_cells", baseline,
+                                      matching_transport_affinity=match_aff,
+                                      min_pair_transport_affinity=cfg.min_pair_transport_affinity,
+                                      pair_gate_cells=0, fc_cache_used=bool(matching))
+            row_gate = torch.tensor(gate, dtype=torch.uint8).repeat_interleave(spatial).to(score.device)
+        dev = score.device
+        if dev.type != "cuda":
+            raise ValueError("the swap router runs on a CUDA device")
+        slot = torch.arange(selected.shape[-1], device=dev)
+        valid = slot[None, None, None] < counts[..., None]
+        hist_sel = valid & (selected < memory_blocks)
+        hist_counts = hist_sel.sum(-1)
+        swappable = (hist_sel if cfg.historical_only else valid).sum(-1)
+        if int(swappable.max().item()) == 0:
+            return self._fallback(layer_index, "no_swappable_kv_selected", baseline)
+        coef, hess, cache_used = quadratic_terms(
+            temporal_cells=cells, spatial=spatial, exact_frames=frames,
+            temporal_group_size=int(temporal_group_size), current_boundary=int(current_boundary),
+            transport=transport, lambda_anchor=cfg.lambda_anchor,
+            lambda_reconstruction=cfg.lambda_reconstruction, device=dev)
+        cache_used = cache_used or bool(matching)
+        sel = selected.to(torch.int64).contiguous()
+        S = sel.shape[-1]
+        D = pooled_value.shape[-1]
+        if D % cfg.sketch_groups:
+            raise ValueError("value width must be divisible by sketch groups")
+        lib = _lib.load()
+        nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, D, S, int(memory_blocks),
+                                                     cfg.candidate_multiplier, int(cfg.historical_only),
+                                                     cfg.sketch_groups)
+        ws = self._workspace(nbytes, dev)
+        stats = torch.empty(4, dtype=torch.float64, device=dev)
+        sc = score.float().contiguous()
+        pv = pooled_value.float().contiguous()
+        cn = counts.to(torch.int64).contiguous()
+        lo = local.to(torch.uint8).contiguous()
+        _lib.call("cast_swap_route", sc.data_ptr(), pv.data_ptr(), sel.data_ptr(), cn.data_ptr(),
+                  lo.data_ptr(), _lib.ptr(row_gate), coef.data_ptr(), hess.data_ptr(), B, H, Q, K, D, S,
+                  int(memory_blocks), cfg.candidate_multiplier, cfg.num_swap_rounds, float(cfg.swap_eps),
+                  cfg.sketch_groups, cfg.max_swaps_per_call, int(cfg.historical_only),
+                  int(cfg.same_bank_only), stats.data_ptr(), ws.data_ptr(), ws.numel(),
+                  torch.cuda.current_stream(dev).cuda_stream)
+        if sel.data_ptr() != selected.data_ptr():
+            selected.copy_(sel)
+        swaps, before, after, gained = (float(v) for v in stats.cpu())
+        swaps = int(swaps)
+        final_hist = ((selected < memory_blocks) & valid).sum(-1)
+        nonhist = lambda t: torch.where(valid & (t >= memory_blocks), t, K).sort(dim=-1).values  # noqa: E731
+        unchanged = bool(torch.equal(nonhist(selected), nonhist(baseline)))
+        if cfg.same_bank_only and not torch.equal(hist_counts, final_hist):
+            raise RuntimeError("same-bank FC-PASM routing changed Memory KV counts")
+        if cfg.historical_only and not torch.equal(final_hist, hist_counts):
+            raise RuntimeError("FC-PASM routing changed a historical-KV row budget")
+        if cfg.historical_only and not unchanged:
+            raise RuntimeError("FC-PASM routing modified Current-KV support")
+        if after > before + 1e-5 * max(abs(before), 1.0):
+            raise RuntimeError("FC-PASM swap increased its refinement objective")
+        terms = sum(max(0, r - l - 1) for l, r in same_seg)
+        f64 = lambda v: torch.tensor(v, dtype=torch.float32)  # noqa: E731
+        record = {
+            "layer_index": int(layer_index), "status": "refined",
+            "candidate_multiplier": cfg.candidate_multiplier,
+            "candidate_max": min(memory_blocks if cfg.historical_only else K,
+                                 cfg.candidate_multiplier * int(swappable.max().item())),
+            "swap_rounds": cfg.num_swap_rounds, "max_swaps_per_call": cfg.max_swaps_per_call,
+            "swap_count": swaps, "objective_before": f64(before), "objective_after": f64(after),
+            "objective_improvement": f64(before - after),
+            "average_swap_improvement": f64(gained / swaps if swaps else 0.0),
+            "anchor_term_weight": cfg.lambda_anchor,
+            "reconstruction_term_weight": cfg.lambda_reconstruction,
+            "reconstruction_terms": terms, "fc_cache_used": cache_used,
+            "matching_transport_affinity": match_aff,
+            "min_pair_transport_affinity": cfg.min_pair_transport_affinity,
+            "pair_gate_cells": gate_cells, "g0_fallback": not cache_used, "fixed_budget": True,
+            "historical_only": cfg.historical_only, "same_bank_only": cfg.same_bank_only,
+            "historical_budget_before": int(hist_counts.sum().item()),
+            "historical_budget_after": int(final_hist.sum().item()),
+            "current_kv_support_unchanged": unchanged,
+            "minimum_k": int(counts.min().item()), "maximum_k": int(counts.max().item()),
+            "budget_before": int(counts.sum().item()), "budget_after": int(counts.sum().item()),
+            "unique_indices": True, "local_support_preserved": True,
+        }
+        self._records.append(record)
+        return selected, record
+
+    def summary(self) -> dict[str, Any]:
+        rows = []
+        for raw in self._records:
+            row = {}
+            for k, v in raw.items():
+                if isinstance(v, torch.Tensor):
+                    c = v.detach().float().cpu()
+                    row[k] = float(c.item()) if c.numel() == 1 else [float(x) for x in c.flatten().tolist()]
+                else:
+                    row[k] = v
+            rows.append(row)
+        c = self.config
+        return {"routing_mode": "fc_pasm_swap",
+                "config": {"candidate_multiplier": c.candidate_multiplier,
+                           "num_swap_rounds": c.num_swap_rounds, "swap_eps": c.swap_eps,
+                           "lambda_anchor": c.lambda_anchor,
+                           "lambda_reconstruction": c.lambda_reconstruction,
+                           "sketch_groups": c.sketch_groups,
+                           "require_fc_transport": c.require_fc_transport,
+                           "min_transport_affinity": c.min_transport_affinity,
+                           "min_pair_transport_affinity": c.min_pair_transport_affinity,
+                           "max_swaps_per_call": c.max_swaps_per_call,
+                           "active_layers": list(c.active_layers),
+                           "historical_only": c.historical_only, "same_bank_only": c.same_bank_only},
+                "records": rows}
+
+    def reset(self) -> None:
+        self._records.clear()

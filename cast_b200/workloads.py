@@ -181,3 +181,72 @@ def compact_case(per_head_phase: bool = False, heads: int = 2, frames: int = 3,
     n_blocks = (mem_cells + -(-(frames - memory_frames) // tt)) * nh * nw
     return CompactCase(q, k, v, coords, freqs, memory_frames, [5 + i for i in range(memory_frames)],
                        (7, 7 + frames - memory_frames), block_id, n_blocks, tt * th * tw)
+
+
+@dataclass
+class SwapCase:
+    score: torch.Tensor          # float32 [B, H, Q, K], local entries lowered by 1e6
+    pooled_value: torch.Tensor   # float32 [B, H, K, D]
+    selected: torch.Tensor       # long [B, H, Q, S]: local keys, then the best others
+    counts: torch.Tensor         # long [B, H, Q]
+    local: torch.Tensor          # bool [Q, K]
+    memory_blocks: int
+    spatial_shape: tuple[int, int]
+    exact_frames: tuple[int, ...]
+    temporal_group_size: int
+    current_boundary: int
+    transport: dict | None
+
+
+def swap_case(*, heads: int = 3, memory_blocks: int = 6, cells: int = 4,
+              spatial_shape: tuple[int, int] = (2, 4), dim: int = 64, width: int = 10,
+              exact_frames: tuple[int, ...] = (0, 3), transport: bool = False,
+              ragged: bool = True, temporal_group_size: int = 1, seed: int = 11) -> SwapCase:
+    """Pooled block scores and values in the layout the swap router reads at
+    its call site: memory blocks first, then ``cells`` temporal cells of
+    ``nh x nw`` current blocks; each current row's local stencil is the
+    current blocks of its own cell, each memory row's its own block.  The
+    selection holds every local key then the best-scoring others (ragged
+    counts when ``ragged``).  With ``transport`` a seeded FC-PASM endpoint
+    sketch (22x40 latent, 11x10 windows, stride 8, padding (4, 5), 2x2
+    transport pooling) is attached for every skipped anchor pair."""
+    g = torch.Generator().manual_seed(seed)
+    nh, nw = spatial_shape
+    sp = nh * nw
+    Q = K = memory_blocks + cells * sp
+    raw = torch.randn(1, heads, Q, K, generator=g) * 2.0
+    local = torch.zeros(Q, K, dtype=torch.bool)
+    for m in range(memory_blocks):
+        local[m, m] = True
+    for c in range(cells):
+        rows = slice(memory_blocks + c * sp, memory_blocks + (c + 1) * sp)
+        local[rows, rows] = True
+    forced = raw + local[None, None].float() * 1e6
+    order = torch.argsort(forced, dim=-1, descending=True, stable=True)
+    selected = order[..., :width].clone()
+    n_local = local.sum(-1)
+    if ragged:
+        extra = torch.randint(0, 3, (1, heads, Q), generator=g)
+        counts = torch.clamp(torch.full((1, heads, Q), width) - extra, min=0)
+        counts = torch.maximum(counts, n_local[None, None] + 1)
+    else:
+        counts = torch.full((1, heads, Q), width)
+    pad = torch.gather(selected, -1, (counts - 1)[..., None])
+    slot = torch.arange(width)[None, None, None]
+    selected = torch.where(slot < counts[..., None], selected, pad)
+    value = torch.randn(1, heads, K, dim, generator=g)
+    tr = None
+    if transport:
+        patches, fh, fw = 18, 6, 3
+        pairs = {}
+        for left, right in zip(exact_frames, exact_frames[1:]):
+            if right - left > 1:
+                theta = (torch.rand(patches, fh, fw, generator=g) * 2 - 1) * math.pi
+                aff = torch.sigmoid(torch.randn(patches, fh, fw, generator=g) + 1.0)
+                pairs[(int(left), int(right))] = {"theta": theta, "affinity": aff,
+                                                  "mean_affinity": aff.mean()}
+        tr = {"tile_grid": (3, 6), "output_shape": (22, 40), "transport_shape": (6, 5),
+              "window_shape": (11, 10), "stride": (8, 8), "padding": (4, 5), "pairs": pairs,
+              "attention_spatial_h": nh, "attention_spatial_w": nw}
+    return SwapCase(raw - local[None, None].float() * 1e6, value, selected, counts, local,
+                    memory_blocks, (nh, nw), tuple(exact_frames), temporal_group_size, 4, tr)

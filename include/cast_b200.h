@@ -265,6 +265,43 @@ CAST_API int cast_barycentric_pair_write(const float *active_residual, const flo
                                 int arithmetic_mode, cast_stream_t stream);
 
 /*
+ * FC-PASM fixed-budget swap router: the numeric body of
+ * FCPASMLocalCoordinateSwapRouter.refine (proposed/fc_pasm_swap_routing.py:
+ * 616-1077, called at proposed/matrix_curvature_phase_frame_weave.py:6040)
+ * after its fallback gates.  Rows are pooled query blocks, memory blocks
+ * first; the R = Q - memory_blocks current rows are searched.
+ *   score        fp32 [B,H,Q,K] (as the call site passes it: local entries
+ *                lowered by 1e6); pooled_value fp32 [B,H,K,D]
+ *   selected     int64 [B,H,Q,S], rewritten IN PLACE by the accepted swaps;
+ *                counts int64 [B,H,Q] (valid slots per row); local uint8 [Q,K]
+ *   row_gate     uint8 [R] or NULL: rows a swap may touch (the per-pair
+ *                transport-affinity gate, :785-820)
+ *   coefficient  fp32 [R], hessian fp32 [R,R]: the objective
+ *                J(e) = sum_r coefficient[r] |e_r|^2 + e^T hessian e over the
+ *                current rows' sketched errors (anchor term and transport
+ *                reconstruction terms, _objective_terms :414-548)
+ *   stats        fp64 [4] device: swaps made, objective before, objective
+ *                after, summed improvement
+ * Candidates are the top min(cand_blocks, multiplier*S) blocks of
+ * score + 1e6*local (cand_blocks = memory_blocks if historical_only else K),
+ * which holds every row's valid candidates of the reference's top-k.  Each
+ * round accepts at most one swap over the whole call (the first minimum in
+ * (b, h, row, slot, candidate) order) when it beats -swap_eps and the cap
+ * allows.  A selected key outside [0,K) is skipped and reported by
+ * cast_device_error().  Launches: 2 + num_swap_rounds (3 when 0 rounds).
+ */
+CAST_API int cast_swap_route(const float *score, const float *pooled_value, long long *selected,
+                    const long long *counts, const uint8_t *local, const uint8_t *row_gate,
+                    const float *coefficient, const float *hessian, int B, int H, int Q, int K,
+                    int D, int S, int memory_blocks, int candidate_multiplier, int num_swap_rounds,
+                    float swap_eps, int sketch_groups, int max_swaps_per_call, int historical_only,
+                    int same_bank_only, double *stats, void *workspace, size_t workspace_bytes,
+                    cast_stream_t stream);
+CAST_API size_t cast_swap_route_workspace_bytes(int B, int H, int Q, int K, int D, int S,
+                                       int memory_blocks, int candidate_multiplier,
+                                       int historical_only, int sketch_groups);
+
+/*
  * Phase-Aware Reconstruction (FC-PASM reference numerics) on one model call.
  * Replaces WorldAlignedSpectralResidualCorrector.correct with the factory's
  * FC knobs (proposed/matrix_world_spectral_residual.py:5283-5394 ->

@@ -37,6 +37,13 @@ Files:
   knobs on reduced-channel inputs (targets stored as bf16 bits) and its
   endpoint statistics; ``par_cfg4_summary.npz`` summarises the full
   C=3072 config-4 output (strided sample + per-frame sums).
+* ``swap_*.npz``         -- ``FCPASMLocalCoordinateSwapRouter.refine``
+  (``proposed/fc_pasm_swap_routing.py:616-1077``) on ``workloads.swap_case``
+  inputs under five configurations (identity transport, the factory's
+  production knobs with an FC sketch, two rounds, historical-only, the
+  per-pair affinity gate): the selection after, swap count, objective before
+  and after, and the transport operators (``_transport_matrix`` :116-268) the
+  objective used.
 * ``MANIFEST.json``      -- SHA-256 of every fixture and of every regenerated
   input (mirrors the hash manifest idea of ``scripts/check_release.py:19-26``).
 """
@@ -281,10 +288,69 @@ def make_par(manifest: dict):
     )
 
 
+SWAP_CASES = {
+    # name: (swap_case kwargs, router config kwargs)
+    "identity_two_rounds": (dict(transport=False), dict(num_swap_rounds=2)),
+    "fc_production": (dict(transport=True), dict(
+        num_swap_rounds=1, swap_eps=0.10, max_swaps_per_call=1, same_bank_only=True,
+        require_fc_transport=True, min_transport_affinity=0.5, active_layers=(22, 26))),
+    "fc_two_rounds": (dict(transport=True), dict(num_swap_rounds=2)),
+    "historical_only": (dict(transport=False, seed=14), dict(num_swap_rounds=2, historical_only=True)),
+    "pair_gate": (dict(transport=True, exact_frames=(0, 3, 6), temporal_group_size=2, seed=12), dict(
+        num_swap_rounds=2, min_pair_transport_affinity=0.5)),
+}
+
+
+def make_swap(manifest: dict):
+    """``FCPASMLocalCoordinateSwapRouter.refine`` (proposed/fc_pasm_swap_routing.py:616)
+    on ``workloads.swap_case`` inputs, plus the transport operators its
+    objective used (``_transport_matrix`` :116)."""
+    from interaction_accel.methods.proposed import fc_pasm_swap_routing as fr
+
+    for name, (case_kw, cfg_kw) in SWAP_CASES.items():
+        w = workloads.swap_case(**case_kw)
+        router = fr.FCPASMLocalCoordinateSwapRouter(fr.FCPASMSwapRoutingConfig(**cfg_kw))
+        sel, rec = router.refine(
+            score=w.score, pooled_value=w.pooled_value, selected=w.selected.clone(), counts=w.counts,
+            local=w.local, memory_blocks=w.memory_blocks, spatial_shape=w.spatial_shape,
+            exact_current_frames=w.exact_frames, temporal_group_size=w.temporal_group_size,
+            current_boundary=w.current_boundary, transport=w.transport, layer_index=22)
+        keys, ops = [], []
+        if w.transport is not None:
+            frames = w.exact_frames
+            for left, right in zip(frames, frames[1:]):
+                if (left < w.current_boundary) != (right < w.current_boundary):
+                    continue
+                for t in range(left + 1, right):
+                    a = float(t - left) / float(right - left)
+                    for x in (a, -(1.0 - a)):
+                        m, _ = fr.FCPASMLocalCoordinateSwapRouter._transport_matrix(
+                            w.transport, (left, right), spatial_shape=w.spatial_shape,
+                            device=torch.device("cpu"), exponent=x)
+                        keys.append((left, right, x))
+                        ops.append(m.numpy())
+        sp = w.spatial_shape[0] * w.spatial_shape[1]
+        for tag, t in (("score", w.score), ("value", w.pooled_value), ("selected", w.selected),
+                       ("counts", w.counts)):
+            manifest["inputs"][f"swap_{name}_{tag}"] = sha(t.numpy())
+        np.savez_compressed(
+            os.path.join(HERE, f"swap_{name}.npz"),
+            selected_after=sel.numpy().astype(np.int64),
+            swap_count=np.int64(rec["swap_count"]),
+            objective_before=np.float64(float(rec["objective_before"])),
+            objective_after=np.float64(float(rec["objective_after"])),
+            status=np.array(rec["status"]),
+            op_keys=np.array(keys, dtype=np.float64).reshape(-1, 3),
+            ops=np.array(ops, dtype=np.float32).reshape(-1, sp, sp),
+        )
+        print(name, rec["status"], rec["swap_count"], float(rec["objective_before"]),
+              float(rec["objective_after"]))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the CAST src/ directory")
-    ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "compact", "par"),
+    ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "compact", "par", "swap"),
                     help="regenerate these fixtures only; other manifest entries are kept")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
@@ -296,7 +362,7 @@ def main():
     if args.only and os.path.exists(mpath):
         with open(mpath) as fh:
             manifest = json.load(fh)
-    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par"))
+    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par", "swap"))
     if "cfg1" in todo:
         make_cfg1({}, manifest)
     if "cfg2" in todo:
@@ -307,6 +373,8 @@ def main():
         make_compact(manifest)
     if "par" in todo:
         make_par(manifest)
+    if "swap" in todo:
+        make_swap(manifest)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             with open(os.path.join(HERE, f), "rb") as fh:

@@ -1,0 +1,162 @@
+"""FC-PASM swap router on the B200: the CUDA path (``cast_swap_route``)
+against the reference's own ``refine`` outputs (golden fixtures) and against
+the CPU oracle at a layer-sized case."""
+
+import numpy as np
+import pytest
+import torch
+
+from cast_b200 import _lib, workloads
+from cast_b200 import swap_router as sr
+from oracle import swap_router as osr
+
+from test_swap_router import CASES, _fixture, oracle_refine
+
+pytestmark = pytest.mark.gpu
+
+
+def _to(w, dev):
+    for name in ("score", "pooled_value", "selected", "counts", "local"):
+        setattr(w, name, getattr(w, name).to(dev))
+    if w.transport is not None:
+        for e in w.transport["pairs"].values():
+            e["theta"], e["affinity"] = e["theta"].to(dev), e["affinity"].to(dev)
+    return w
+
+
+def _refine(router, w):
+    return router.refine(score=w.score, pooled_value=w.pooled_value, selected=w.selected.clone(),
+                         counts=w.counts, local=w.local, memory_blocks=w.memory_blocks,
+                         spatial_shape=w.spatial_shape, exact_current_frames=w.exact_frames,
+                         temporal_group_size=w.temporal_group_size, current_boundary=w.current_boundary,
+                         transport=w.transport, layer_index=22)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_refine_matches_reference(name):
+    case_kw, cfg_kw = CASES[name]
+    w = _to(workloads.swap_case(**case_kw), "cuda")
+    fx = _fixture(name)
+    router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig(**cfg_kw))
+    sel, rec = _refine(router, w)
+    assert rec["status"] == str(fx["status"])
+    np.testing.assert_array_equal(sel.cpu().numpy(), fx["selected_after"])
+    assert rec["swap_count"] == int(fx["swap_count"])
+    # objectives: fp32 terms summed in another order (fp64 on the device)
+    assert float(rec["objective_before"]) == pytest.approx(float(fx["objective_before"]), rel=1e-4)
+    assert float(rec["objective_after"]) == pytest.approx(float(fx["objective_after"]), rel=1e-4)
+    assert _lib.load().cast_device_error(None) == 0
+
+
+def _layer_case(seed=21):
+    # a 24-head layer: 32 memory blocks, 4 current cells of 2x4 blocks, D=128
+    return workloads.swap_case(heads=24, memory_blocks=32, cells=4, spatial_shape=(2, 4), dim=128,
+                               width=16, exact_frames=(0, 3), transport=True, seed=seed)
+
+
+@pytest.mark.parametrize("rounds,eps", [(1, 0.0), (2, 1e-6)])
+def test_layer_case_matches_oracle(rounds, eps):
+    w = _layer_case()
+    ops = {}
+
+    def op(pair, x):
+        key = (pair, round(float(x), 12))
+        if key not in ops:
+            ops[key] = sr.transport_operator(w.transport, pair, spatial_shape=w.spatial_shape,
+                                             exponent=x, device="cpu")[0].numpy()
+        return ops[key]
+
+    cfg = dict(num_swap_rounds=rounds, swap_eps=eps)
+    sel_o, st = osr.refine(score=w.score.numpy(), pooled_value=w.pooled_value.numpy(),
+                           selected=w.selected.numpy(), counts=w.counts.numpy(), local=w.local.numpy(),
+                           memory_blocks=w.memory_blocks, spatial=8, exact_frames=w.exact_frames,
+                           group=1, boundary=4, config=osr.SwapConfig(**cfg), operator=op)
+    wd = _to(_layer_case(), "cuda")
+    router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig(**cfg))
+    sel, rec = _refine(router, wd)
+    assert st["swap_count"] >= 1
+    assert rec["swap_count"] == st["swap_count"]
+    np.testing.assert_array_equal(sel.cpu().numpy(), sel_o)
+    assert float(rec["objective_before"]) == pytest.approx(st["objective_before"], rel=1e-4)
+    assert float(rec["objective_after"]) == pytest.approx(st["objective_after"], rel=1e-4)
+
+
+def test_oracle_fixture_helper_on_device_inputs():
+    """The oracle path the GPU tests lean on agrees with the fixture too."""
+    case_kw, cfg_kw = CASES["fc_two_rounds"]
+    w = workloads.swap_case(**case_kw)
+    sel, st = oracle_refine(w, cfg_kw, _fixture("fc_two_rounds"))
+    np.testing.assert_array_equal(sel, _fixture("fc_two_rounds")["selected_after"])
+
+
+def test_c_abi_rejects_bad_arguments():
+    lib = _lib.load()
+    dev = "cuda"
+    w = _to(workloads.swap_case(), dev)
+    stats = torch.empty(4, dtype=torch.float64, device=dev)
+    coef = torch.zeros(32, device=dev)
+    hess = torch.zeros(32, 32, device=dev)
+    sel = w.selected.clone()
+    B, H, Q, K = w.score.shape
+    nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, 64, 10, 6, 2, 0, 16)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+    def call(**over):
+        a = dict(G=16, rounds=1, M=6, ws=ws.numel(), mult=2)
+        a.update(over)
+        return lib.cast_swap_route(w.score.data_ptr(), w.pooled_value.data_ptr(), sel.data_ptr(),
+                                   w.counts.data_ptr(), w.local.to(torch.uint8).data_ptr(), None,
+                                   coef.data_ptr(), hess.data_ptr(), B, H, Q, K, 64, 10, a["M"], a["mult"],
+                                   a["rounds"], 0.0, a["G"], 0, 0, 0, stats.data_ptr(), ws.data_ptr(),
+                                   a["ws"], None)
+
+    assert call(G=3) != 0          # odd sketch groups
+    assert call(G=24) != 0         # D not divisible
+    assert call(rounds=3) != 0
+    assert call(M=Q) != 0          # no current rows
+    assert call(mult=0) != 0
+    assert call(ws=16) != 0        # workspace too small
+    torch.cuda.synchronize()
+    assert torch.equal(sel, w.selected)
+
+
+def test_swap_route_graph_rate():
+    """One layer-sized call (proxy + one round + close) replayed from a CUDA
+    graph: reports the per-call device time."""
+    w = _to(_layer_case(), "cuda")
+    lib = _lib.load()
+    B, H, Q, K = w.score.shape
+    D, S, M = w.pooled_value.shape[-1], w.selected.shape[-1], w.memory_blocks
+    coef, hess, _ = sr.quadratic_terms(temporal_cells=4, spatial=8, exact_frames=(0, 3),
+                                       temporal_group_size=1, current_boundary=4, transport=w.transport,
+                                       lambda_anchor=1.0, lambda_reconstruction=1.0, device="cuda")
+    nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, D, S, M, 2, 0, 16)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    stats = torch.empty(4, dtype=torch.float64, device="cuda")
+    local = w.local.to(torch.uint8)
+    sel = w.selected.clone()
+    s = torch.cuda.Stream()
+
+    def launch():
+        _lib.call("cast_swap_route", w.score.data_ptr(), w.pooled_value.data_ptr(), sel.data_ptr(),
+                  w.counts.data_ptr(), local.data_ptr(), None, coef.data_ptr(), hess.data_ptr(), B, H, Q,
+                  K, D, S, M, 2, 1, 0.1, 16, 1, 0, 1, stats.data_ptr(), ws.data_ptr(), nbytes,
+                  s.cuda_stream)
+
+    with torch.cuda.stream(s):
+        launch()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(20):
+            launch()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / 20
+    print(f"swap route, 24 heads x 32 current rows, 64 keys, D=128: {us:.1f} us per call")
+    assert us < 1000.0
