@@ -114,6 +114,8 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   }
   const long long cnt = __ldg(counts + (size_t)bh * p.Q + q);
   for (int j = tid; j < p.S; j += blockDim.x) seli[j] = (int)__ldg(selected + ((size_t)bh * p.Q + q) * p.S + j);
+  // a NaN score leaves ranks unfilled: they name block 0 instead of garbage
+  for (int l = tid; l < p.Lc; l += blockDim.x) cand[l] = 0;
   __syncthreads();
 
   for (int d = tid; d < p.D; d += blockDim.x) {
