@@ -250,6 +250,69 @@ def compact_measure(dev, peaks, steps):
     }
 
 
+def swap_measure(dev, steps, cpu_leg=True):
+    """The FC-PASM swap router's device call (``cast_swap_route``: proxies,
+    one swap round, the closing objective pass) on a 24-head layer of pooled
+    blocks: 32 memory blocks plus 4 current cells of 2x4 blocks, 64 keys,
+    D=128, 16 selected per row, the factory's knobs (one round, one swap,
+    same-bank).  Graph replay of the raw C-ABI call (the Python ``refine``
+    adds its host gates and one stats read); beside it the CPU oracle on the
+    same call, one core."""
+    import time
+
+    import torch
+
+    from cast_b200 import _lib, swap_router, workloads
+
+    w = workloads.swap_case(heads=24, memory_blocks=32, cells=4, spatial_shape=(2, 4), dim=128,
+                            width=16, exact_frames=(0, 3), transport=True, seed=21)
+    B, H, Q, K = w.score.shape
+    D, S, M = w.pooled_value.shape[-1], w.selected.shape[-1], w.memory_blocks
+    coef, hess, _ = swap_router.quadratic_terms(
+        temporal_cells=4, spatial=8, exact_frames=(0, 3), temporal_group_size=1, current_boundary=4,
+        transport=w.transport, lambda_anchor=1.0, lambda_reconstruction=1.0, device=dev)
+    lib = _lib.load()
+    nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, D, S, M, 2, 0, 16)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    stats = torch.empty(4, dtype=torch.float64, device=dev)
+    sc, pv, cn = w.score.to(dev), w.pooled_value.to(dev), w.counts.to(dev)
+    lo, sel = w.local.to(torch.uint8).to(dev), w.selected.to(dev)
+
+    def call():
+        _lib.call("cast_swap_route", sc.data_ptr(), pv.data_ptr(), sel.data_ptr(), cn.data_ptr(),
+                  lo.data_ptr(), None, coef.data_ptr(), hess.data_ptr(), B, H, Q, K, D, S, M, 2, 1, 0.1,
+                  16, 1, 0, 1, stats.data_ptr(), ws.data_ptr(), nbytes,
+                  torch.cuda.current_stream(dev).cuda_stream)
+
+    us = _graph_us(call, max(10, steps), dev)
+    line = {"us_per_call": us, "launches_per_call": 3,
+            "workload": "24 heads, 32 memory + 32 current pooled blocks, D=128, 16 selected, "
+                        "FC transport, 1 round / 1 swap / same-bank",
+            "note": "latency-bound (a few hundred KB touched); CUDA graph replay, device time"}
+    if cpu_leg:
+        from oracle import swap_router as osr
+        ops = {}
+
+        def op(pair, x):
+            key = (pair, round(float(x), 12))
+            if key not in ops:
+                ops[key] = swap_router.transport_operator(w.transport, pair, spatial_shape=(2, 4),
+                                                          exponent=x, device="cpu")[0].numpy()
+            return ops[key]
+
+        args = dict(score=w.score.numpy(), pooled_value=w.pooled_value.numpy(),
+                    selected=w.selected.numpy(), counts=w.counts.numpy(), local=w.local.numpy(),
+                    memory_blocks=M, spatial=8, exact_frames=(0, 3), group=1, boundary=4,
+                    config=osr.SwapConfig(num_swap_rounds=1, swap_eps=0.1, max_swaps_per_call=1,
+                                          same_bank_only=True), operator=op)
+        osr.refine(**args)
+        t0 = time.perf_counter()
+        osr.refine(**args)
+        line["cpu_oracle_us"] = (time.perf_counter() - t0) * 1e6
+        line["cpu_oracle"] = "numpy restatement (oracle/swap_router.py), same call, host cores"
+    return line
+
+
 def par_measure(dev, peaks, peak_src, steps):
     """PAR (FC-PASM) on BASELINE config 4: bf16 residual [1, 1+4, 880, 3072]
     (one memory frame), anchors = current frames 0 and 3, targets 1 and 2.
@@ -434,6 +497,7 @@ def main():
     clocks = sampler.stop()
     par_line = par_measure(dev, peaks, peak_src, args.steps) if rank == 0 else None
     compact_line = compact_measure(dev, peaks, args.steps) if rank == 0 else None
+    swap_line = swap_measure(dev, args.steps, not args.no_cpu_baseline) if rank == 0 else None
 
     # ---- max over ranks
     vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms], dtype=torch.float64, device=dev)
@@ -515,6 +579,7 @@ def main():
         },
         "par": par_line,
         "compact_and_lift": compact_line,
+        "swap_router": swap_line,
         "gpu_launches": KERNELS_PER_CALL[args.policy] * args.steps,
         "clocks": clocks,
     }

@@ -27,7 +27,7 @@ from __future__ import annotations
 
 import importlib
 
-from . import barycentric, rcsa
+from . import barycentric, rcsa, swap_router
 from .par import FCPASMCorrector
 from .select import TABASelector
 
@@ -106,6 +106,29 @@ def attach(weave) -> None:
 
     ref.correct = correct
     ref._cast_b200_original_correct = original
+    attach_router(weave)
+
+
+def attach_router(weave) -> None:
+    """Runs a reference weave's FC-PASM swap routing (its
+    ``fc_pasm_swap_router``, built at proposed/matrix_curvature_phase_frame_
+    weave.py:585-604 and called at :6040) through ``cast_swap_route`` for
+    CUDA tensors; the router keeps the reference's config object."""
+    ref = getattr(weave, "fc_pasm_swap_router", None)
+    if ref is None or getattr(ref, "_cast_b200", False):
+        return
+    fast = swap_router.FCPASMLocalCoordinateSwapRouter(ref.config)
+    original = ref.refine
+
+    def refine(**kwargs):
+        if not kwargs["score"].is_cuda:
+            return original(**kwargs)
+        selected, record = fast.refine(**kwargs)
+        ref._records.append(record)
+        return selected, record
+
+    ref.refine = refine
+    ref._cast_b200 = True
 
 
 def make_cast_components():
@@ -118,6 +141,6 @@ def make_cast_components():
 
 
 __all__ = [
-    "make_cast_components", "install_kernels", "uninstall_kernels", "attach",
+    "make_cast_components", "install_kernels", "uninstall_kernels", "attach", "attach_router",
     "corrector_from_reference", "TABASelector",
 ]
