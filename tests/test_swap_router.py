@@ -175,3 +175,32 @@ def test_unsorted_anchor_frames_rejected():
     router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig())
     with pytest.raises(ValueError, match="unique and chronological"):
         _refine(router, w, exact_current_frames=(3, 0))
+
+
+def test_attach_router_keeps_original_for_host_tensors():
+    """``attach_router`` replaces a weave's router ``refine`` in place; host
+    tensors still reach the reference's own method, and attaching twice is a
+    no-op."""
+    from cast_b200 import components
+
+    calls = []
+
+    class FakeRouter:
+        config = sr.FCPASMSwapRoutingConfig(num_swap_rounds=2)
+        _records = []
+
+        def refine(self, **kw):
+            calls.append(kw["layer_index"])
+            return kw["selected"], {"status": "reference"}
+
+    class Weave:
+        fc_pasm_swap_router = FakeRouter()
+
+    weave = Weave()
+    components.attach_router(weave)
+    first = weave.fc_pasm_swap_router.refine
+    components.attach_router(weave)
+    assert weave.fc_pasm_swap_router.refine is first
+    w = workloads.swap_case()
+    _, rec = _refine(weave.fc_pasm_swap_router, w)
+    assert rec["status"] == "reference" and calls == [22]
