@@ -757,8 +757,8 @@ static SwapLayout swap_layout(const castk::SwapShape &p) {
   l.err = l.proxy + align_up(rows * p.Lc * p.G * sizeof(float), 256);
   l.limit = l.err + align_up(rows * p.G * sizeof(float), 256);
   l.best = l.limit + align_up(rows * sizeof(int), 256);
-  l.obj = l.best + align_up(bh * sizeof(castk::SwapBest), 256);
-  l.ctl = l.obj + align_up(2 * bh * sizeof(double), 256);
+  l.obj = l.best + align_up(rows * sizeof(castk::SwapBest), 256);
+  l.ctl = l.obj + align_up(2 * rows * sizeof(double), 256);
   l.total = l.ctl + 256;
   return l;
 }
@@ -797,7 +797,8 @@ extern "C" int cast_swap_route(const float *score, const float *pooled_value, lo
   if (!(swap_eps >= 0.f) || std::isinf(swap_eps))
     return fail(CAST_ERR_INVALID_ARGUMENT, "swap_eps must be finite and non-negative");
   const size_t sm1 = (size_t)(2 * K + D + 32) * sizeof(float) + (size_t)(2 * p.Lc + S) * sizeof(int);
-  const size_t sm2 = (size_t)2 * p.R * p.G * sizeof(float);
+  const size_t sm2 = (size_t)(p.R * p.G + p.Lc * p.G + S * p.G + p.G) * sizeof(float) +
+                     (size_t)(2 * p.Lc + 2 * S) * sizeof(int);
   if (sm1 > 48 * 1024 || sm2 > 48 * 1024)
     return fail(CAST_ERR_UNSUPPORTED, "too large for one CTA (K=%d S=%d rows=%d sketch_groups=%d)", K,
                 S, p.R, p.G);
@@ -816,25 +817,25 @@ extern "C" int cast_swap_route(const float *score, const float *pooled_value, lo
   double *obj = reinterpret_cast<double *>(ws + lay.obj);
   auto *ctl = reinterpret_cast<castk::SwapCtl *>(ws + lay.ctl);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int rows = B * H * p.R, bh = B * H;
+  const int rows = B * H * p.R;
   castk::swap_proxy_kernel<<<rows, castk::kSwapProxyThreads, sm1, s>>>(
       score, pooled_value, selected, counts, local, p, 1e-6f, cand, proxy, err, limit, ctl);
   CAST_CUDA_TRY(cudaGetLastError());
   // rounds: the first also records the objective before any swap; a last
   // pass records the objective after and writes the stats
   if (num_swap_rounds == 0) {
-    castk::swap_round_kernel<<<bh, castk::kSwapRoundThreads, sm2, s>>>(
+    castk::swap_round_kernel<<<rows, castk::kSwapRoundThreads, sm2, s>>>(
         selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
         ctl, stats, 0, 0, 0, swap_eps, max_swaps_per_call);
     CAST_CUDA_TRY(cudaGetLastError());
   }
   for (int r = 0; r < num_swap_rounds; ++r) {
-    castk::swap_round_kernel<<<bh, castk::kSwapRoundThreads, sm2, s>>>(
+    castk::swap_round_kernel<<<rows, castk::kSwapRoundThreads, sm2, s>>>(
         selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
         ctl, stats, 1, r == 0 ? 0 : -1, 0, swap_eps, max_swaps_per_call);
     CAST_CUDA_TRY(cudaGetLastError());
   }
-  castk::swap_round_kernel<<<bh, castk::kSwapRoundThreads, sm2, s>>>(
+  castk::swap_round_kernel<<<rows, castk::kSwapRoundThreads, sm2, s>>>(
       selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
       ctl, stats, 0, 1, 1, swap_eps, max_swaps_per_call);
   CAST_CUDA_TRY(cudaGetLastError());

@@ -11,9 +11,9 @@
 // a_r = c_r + H_rr and b_r = (H e)_r - H_rr e_r per row.
 //
 // Work is tiny and latency-bound (a few thousand pooled rows): one CTA per
-// (batch, head, current row) for the proxies, one CTA per (batch, head) per
-// round, and the last CTA of a round (atomic ticket) reduces the per-head
-// bests in (batch, head, row) order and applies the swap, so a whole call is
+// (batch, head, current row) for the proxies and again for each round, and
+// the last CTA of a round (atomic ticket) reduces the per-row bests in
+// (batch, head, row) order and applies the swap, so a whole call is
 // 2 + rounds launches with no host synchronisation.
 #pragma once
 
@@ -22,7 +22,7 @@
 namespace castk {
 
 constexpr int kSwapProxyThreads = 128;
-constexpr int kSwapRoundThreads = 256;
+constexpr int kSwapRoundThreads = 128;
 
 struct SwapShape {
   int B, H, Q, K, D, S, M, R, Lc, G, cand_blocks, mult, historical, same_bank;
@@ -35,7 +35,7 @@ struct SwapCtl {
   double improvement;
 };
 
-// Per (batch, head) best pair of a round.
+// Per-row best pair of a round.
 struct SwapBest {
   float value;
   int row, s, l;
@@ -120,6 +120,7 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
 
   for (int d = tid; d < p.D; d += blockDim.x) {
     float acc = 0.f;
+#pragma unroll 8
     for (int k = 0; k < p.K; ++k) acc = fmaf(prob[k], __ldg(V + (size_t)k * p.D + d), acc);
     outv[d] = acc;
   }
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
     const float scale = __fdiv_rn(pc, __fadd_rn(__fsub_rn(1.f, pc), eps));
     const float *vc = V + (size_t)c * p.D + g * width;
     float acc = 0.f;
+#pragma unroll 4
     for (int t = 0; t < width; ++t)
       acc = __fadd_rn(acc, __fmul_rn(scale, __fsub_rn(outv[g * width + t], __ldg(vc + t))));
     prow[i] = __fdiv_rn(acc, (float)width);
@@ -167,167 +169,206 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   }
 }
 
-// One CTA per (b, h).  Builds H e for the head's current-row errors, adds
-// the head's objective to obj_part[obj_slot] (when obj_slot >= 0) and, when
-// `search`, finds the head's best admissible (remove slot, add candidate)
-// pair.  The last CTA to finish takes the first minimum over (b, h, row) and,
-// if it beats -swap_eps and the swap cap allows, writes the added key into
-// the selection and moves the row's error by (removed proxy - added proxy).
-// With `finish` the last CTA writes the call's stats.
+// One CTA per current row (b, h, r).  Builds (H e)_r from the head's
+// current-row errors, stores the row's objective term in obj_part[obj_slot]
+// (when obj_slot >= 0) and, when `search`, the row's best admissible
+// (remove slot, add candidate) pair, from per-row tables in shared memory.
+// The last CTA to finish takes the first minimum over (b, h, row) with all
+// its threads and, if it beats -swap_eps and the swap cap allows, writes the
+// added key into the selection and moves the row's error by (removed proxy -
+// added proxy).  With `finish` the last CTA writes the call's stats.
 __global__ void __launch_bounds__(kSwapRoundThreads)
     swap_round_kernel(long long *__restrict__ selected, const long long *__restrict__ counts,
                       const uint8_t *__restrict__ local, const uint8_t *__restrict__ row_gate,
                       const float *__restrict__ coef, const float *__restrict__ hess, SwapShape p,
                       const int *__restrict__ cand_all, const float *__restrict__ proxy_all,
-                      float *__restrict__ err_all, const int *__restrict__ limit_all, SwapBest *best_bh,
+                      float *__restrict__ err_all, const int *__restrict__ limit_all, SwapBest *best_row,
                       double *__restrict__ obj_part, SwapCtl *ctl, double *__restrict__ stats,
                       int search, int obj_slot, int finish, float swap_eps, int max_swaps) {
   extern __shared__ float sm[];
-  const int RG = p.R * p.G;
-  float *e = sm;            // R*G
-  float *he = e + RG;       // R*G
+  float *e = sm;                        // R*G: the head's current-row errors
+  float *prx = e + p.R * p.G;           // Lc*G: this row's proxies
+  float *rem = prx + p.Lc * p.G;        // S*G: proxy of each selected slot's key
+  float *he = rem + p.S * p.G;          // G
+  int *cand = reinterpret_cast<int *>(he + p.G);  // Lc
+  int *addok = cand + p.Lc;             // Lc
+  int *remok = addok + p.Lc;            // S
+  int *key = remok + p.S;               // S
   __shared__ double dred[kSwapRoundThreads / 32];
-  __shared__ SwapBest wbest[kSwapRoundThreads / 32];
+  __shared__ float vred[kSwapRoundThreads / 32];
+  __shared__ long long kred[kSwapRoundThreads / 32];
   __shared__ bool last;
-  const int bh = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nwarps = blockDim.x >> 5;
-  float *eg = err_all + (size_t)bh * RG;
+  const int row = blockIdx.x, bh = row / p.R, r = row % p.R, q = p.M + r;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int RG = p.R * p.G;
+  const float *eg = err_all + (size_t)bh * RG;
   for (int i = tid; i < RG; i += blockDim.x) e[i] = eg[i];
   __syncthreads();
+  const float hrr = __ldg(hess + (size_t)r * p.R + r);
   double part = 0.0;
-  for (int i = tid; i < RG; i += blockDim.x) {
-    const int r = i / p.G, g = i % p.G;
+  for (int g = tid; g < p.G; g += blockDim.x) {
     float acc = 0.f;
     for (int t = 0; t < p.R; ++t) acc = fmaf(__ldg(hess + (size_t)r * p.R + t), e[t * p.G + g], acc);
-    he[i] = acc;
-    part += (double)__ldg(coef + r) * e[i] * e[i] + (double)e[i] * acc;
+    he[g] = acc;
+    const float er = e[r * p.G + g];
+    part += (double)__ldg(coef + r) * er * er + (double)er * acc;
   }
   for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   if (lane == 0) dred[warp] = part;
-  __syncthreads();
-  if (tid == 0 && obj_slot >= 0) {
-    double t = 0.0;
-    for (int w = 0; w < nwarps; ++w) t += dred[w];
-    obj_part[(size_t)obj_slot * p.B * p.H + bh] = t;
-  }
 
-  if (search) {
-    SwapBest mine{INFINITY, 0, 0, 0};
-    long long mkey = LLONG_MAX;
-    for (int r = warp; r < p.R; r += nwarps) {
-      if (row_gate && !row_gate[r]) continue;
-      const int q = p.M + r;
-      const size_t qrow = (size_t)bh * p.Q + q;
-      const int *cand = cand_all + ((size_t)bh * p.R + r) * p.Lc;
-      const float *prx = proxy_all + ((size_t)bh * p.R + r) * p.Lc * p.G;
-      const long long cnt = __ldg(counts + qrow);
-      const int limit = limit_all[(size_t)bh * p.R + r];
-      const float hrr = __ldg(hess + (size_t)r * p.R + r);
-      const float a = __ldg(coef + r) + hrr;
-      for (int pi = lane; pi < p.S * p.Lc; pi += 32) {
-        const int sl = pi / p.Lc, l = pi % p.Lc;
-        const int key = (int)selected[qrow * p.S + sl];
-        const int add = cand[l];
-        if (sl < cnt && (key < 0 || key >= p.K)) {  // a selected key outside the score
-          atomicExch(&g_cast_device_error, (int)CAST_ERR_INVALID_ARGUMENT);
-          continue;
-        }
-        bool ok = sl < cnt && l < limit && !local[(size_t)q * p.K + key];
-        if (p.historical) ok = ok && key < p.M;
-        if (p.same_bank) ok = ok && ((key < p.M) == (add < p.M));
-        if (!ok) continue;
-        // addable: the candidate is not among the valid selected keys
-        bool kept = false;
-        for (int j = 0; j < cnt && j < p.S; ++j) kept |= (int)selected[qrow * p.S + j] == add;
-        if (kept) continue;
-        int lr = -1;  // the removed key's candidate slot (its proxy), if any
-        for (int t = 0; t < p.Lc; ++t)
-          if (cand[t] == key) { lr = t; break; }
-        float v = 0.f;
-        for (int g = 0; g < p.G; ++g) {
-          const float eo = e[r * p.G + g];
-          const float b = he[r * p.G + g] - hrr * eo;
-          const float d = (lr >= 0 ? prx[lr * p.G + g] : 0.f) - prx[l * p.G + g];
-          v += a * (2.f * eo * d + d * d) + 2.f * b * d;
-        }
-        const long long k2 = (long long)r * p.S * p.Lc + pi;
-        if (swap_better(v, k2, mine.value, mkey)) {
-          mine = SwapBest{v, r, sl, l};
-          mkey = k2;
-        }
+  float best = INFINITY;
+  long long bkey = LLONG_MAX;
+  const bool gated = row_gate && !row_gate[r];
+  if (search && !gated) {
+    const size_t qrow = (size_t)bh * p.Q + q;
+    const long long cnt = __ldg(counts + qrow);
+    const int limit = limit_all[row];
+    const int *cg = cand_all + (size_t)row * p.Lc;
+    const float *pg = proxy_all + (size_t)row * p.Lc * p.G;
+    for (int i = tid; i < p.Lc * p.G; i += blockDim.x) prx[i] = pg[i];
+    for (int l = tid; l < p.Lc; l += blockDim.x) cand[l] = cg[l];
+    for (int j = tid; j < p.S; j += blockDim.x) key[j] = (int)selected[qrow * p.S + j];
+    __syncthreads();
+    for (int l = tid; l < p.Lc; l += blockDim.x) {
+      bool kept = false;
+      for (int j = 0; j < cnt && j < p.S; ++j) kept |= key[j] == cand[l];
+      addok[l] = l < limit && !kept;
+    }
+    for (int j = tid; j < p.S; j += blockDim.x) {
+      const int k = key[j];
+      bool ok = j < cnt;
+      if (ok && (k < 0 || k >= p.K)) {  // a selected key outside the score
+        atomicExch(&g_cast_device_error, (int)CAST_ERR_INVALID_ARGUMENT);
+        ok = false;
+      }
+      ok = ok && !local[(size_t)q * p.K + k];
+      if (p.historical) ok = ok && k < p.M;
+      remok[j] = ok;
+      int lr = -1;  // the removed key's candidate slot (its proxy), if any
+      for (int t = 0; t < p.Lc; ++t)
+        if (cand[t] == k) { lr = t; break; }
+      for (int g = 0; g < p.G; ++g) rem[j * p.G + g] = lr >= 0 ? prx[lr * p.G + g] : 0.f;
+    }
+    __syncthreads();
+    const float a = __ldg(coef + r) + hrr;
+    for (int pi = tid; pi < p.S * p.Lc; pi += blockDim.x) {
+      const int sl = pi / p.Lc, l = pi % p.Lc;
+      if (!remok[sl] || !addok[l]) continue;
+      if (p.same_bank && ((key[sl] < p.M) != (cand[l] < p.M))) continue;
+      float v = 0.f;
+      for (int g = 0; g < p.G; ++g) {
+        const float eo = e[r * p.G + g];
+        const float b = he[g] - hrr * eo;
+        const float d = rem[sl * p.G + g] - prx[l * p.G + g];
+        v += a * (2.f * eo * d + d * d) + 2.f * b * d;
+      }
+      if (swap_better(v, pi, best, bkey)) {
+        best = v;
+        bkey = pi;
       }
     }
     for (int o = 16; o; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, mine.value, o);
-      const long long ok2 = __shfl_xor_sync(0xffffffffu, mkey, o);
-      const int orow = __shfl_xor_sync(0xffffffffu, mine.row, o);
-      const int os = __shfl_xor_sync(0xffffffffu, mine.s, o);
-      const int ol = __shfl_xor_sync(0xffffffffu, mine.l, o);
-      if (swap_better(ov, ok2, mine.value, mkey)) {
-        mine = SwapBest{ov, orow, os, ol};
-        mkey = ok2;
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const long long ok2 = __shfl_xor_sync(0xffffffffu, bkey, o);
+      if (swap_better(ov, ok2, best, bkey)) {
+        best = ov;
+        bkey = ok2;
       }
     }
-    if (lane == 0) wbest[warp] = mine;
-    __syncthreads();
-    if (tid == 0) {
-      SwapBest b = wbest[0];
-      for (int w = 1; w < nwarps; ++w) {
-        const SwapBest c = wbest[w];
-        const long long kc = ((long long)c.row * p.S + c.s) * p.Lc + c.l;
-        const long long kb = ((long long)b.row * p.S + b.s) * p.Lc + b.l;
-        if (swap_better(c.value, kc, b.value, kb)) b = c;
-      }
-      best_bh[bh] = b;
+    if (lane == 0) {
+      vred[warp] = best;
+      kred[warp] = bkey;
     }
   }
+  __syncthreads();
   if (tid == 0) {
+    if (obj_slot >= 0) {
+      double t = 0.0;
+      for (int w = 0; w < nwarps; ++w) t += dred[w];
+      obj_part[(size_t)obj_slot * gridDim.x + row] = t;
+    }
+    if (search) {
+      SwapBest b{INFINITY, r, 0, 0};
+      if (!gated) {
+        float bv = vred[0];
+        long long bk = kred[0];
+        for (int w = 1; w < nwarps; ++w)
+          if (swap_better(vred[w], kred[w], bv, bk)) bv = vred[w], bk = kred[w];
+        if (bk != LLONG_MAX) b = SwapBest{bv, r, (int)(bk / p.Lc), (int)(bk % p.Lc)};
+      }
+      best_row[row] = b;
+    }
     __threadfence();
     last = atomicAdd(&ctl->ticket, 1u) == (unsigned)(gridDim.x - 1);
   }
   __syncthreads();
-  if (!last || tid != 0) return;
+  if (!last) return;
   __threadfence();
-  ctl->ticket = 0u;
+  const int n = gridDim.x;
   if (search) {
-    int bb = -1;
-    SwapBest b{INFINITY, 0, 0, 0};
-    for (int i = 0; i < (int)gridDim.x; ++i) {
-      const SwapBest c = best_bh[i];
-      if (c.value < b.value) {  // first minimum in (b, h, row) order
-        b = c;
-        bb = i;
-      }
+    // first minimum over (b, h, row): value, then row index
+    float bv = INFINITY;
+    long long bi = LLONG_MAX;
+    for (int i = tid; i < n; i += blockDim.x) {
+      const float v = best_row[i].value;
+      if (swap_better(v, i, bv, bi)) bv = v, bi = i;
     }
-    const bool capped = max_swaps > 0 && ctl->swaps >= max_swaps;
-    if (bb >= 0 && b.value < -swap_eps && !capped) {
-      const size_t qrow = (size_t)bb * p.Q + p.M + b.row;
-      const int *cand = cand_all + ((size_t)bb * p.R + b.row) * p.Lc;
-      const float *prx = proxy_all + ((size_t)bb * p.R + b.row) * p.Lc * p.G;
-      const int key = (int)selected[qrow * p.S + b.s];
-      int lr = -1;
-      for (int t = 0; t < p.Lc; ++t)
-        if (cand[t] == key) { lr = t; break; }
-      float *er = err_all + ((size_t)bb * p.R + b.row) * p.G;
-      for (int g = 0; g < p.G; ++g)
-        er[g] += (lr >= 0 ? prx[lr * p.G + g] : 0.f) - prx[b.l * p.G + g];
-      selected[qrow * p.S + b.s] = cand[b.l];
-      ctl->swaps += 1;
-      ctl->improvement += -(double)b.value;
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const long long oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (swap_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    if (lane == 0) vred[warp] = bv, kred[warp] = bi;
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < nwarps; ++w)
+        if (swap_better(vred[w], kred[w], bv, bi)) bv = vred[w], bi = kred[w];
+      const bool capped = max_swaps > 0 && ctl->swaps >= max_swaps;
+      if (bi != LLONG_MAX && bv < -swap_eps && !capped) {
+        const SwapBest b = best_row[bi];
+        const int bb = (int)bi / p.R;
+        const size_t qrow = (size_t)bb * p.Q + p.M + b.row;
+        const int *cg = cand_all + (size_t)bi * p.Lc;
+        const float *pg = proxy_all + (size_t)bi * p.Lc * p.G;
+        const int k = (int)selected[qrow * p.S + b.s];
+        int lr = -1;
+        for (int t = 0; t < p.Lc; ++t)
+          if (cg[t] == k) { lr = t; break; }
+        float *er = err_all + (size_t)bi * p.G;
+        for (int g = 0; g < p.G; ++g) er[g] += (lr >= 0 ? pg[lr * p.G + g] : 0.f) - pg[b.l * p.G + g];
+        selected[qrow * p.S + b.s] = cg[b.l];
+        ctl->swaps += 1;
+        ctl->improvement += -(double)bv;
+      }
     }
   }
   if (finish) {
-    const int BH = p.B * p.H;
     double before = 0.0, after = 0.0;
-    for (int i = 0; i < BH; ++i) {
-      before += obj_part[i];
-      after += obj_part[BH + i];
+    for (int i = tid; i < n; i += blockDim.x) before += obj_part[i], after += obj_part[n + i];
+    for (int o = 16; o; o >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+      after += __shfl_xor_sync(0xffffffffu, after, o);
     }
-    stats[0] = (double)ctl->swaps;
-    stats[1] = before;
-    stats[2] = after;
-    stats[3] = ctl->improvement;
+    __syncthreads();
+    if (lane == 0) dred[warp] = before;
+    __syncthreads();
+    if (tid == 0) {
+      double t = 0.0;
+      for (int w = 0; w < nwarps; ++w) t += dred[w];
+      stats[1] = t;
+    }
+    __syncthreads();
+    if (lane == 0) dred[warp] = after;
+    __syncthreads();
+    if (tid == 0) {
+      double t = 0.0;
+      for (int w = 0; w < nwarps; ++w) t += dred[w];
+      stats[0] = (double)ctl->swaps;
+      stats[2] = t;
+      stats[3] = ctl->improvement;
+    }
   }
+  if (tid == 0) ctl->ticket = 0u;
 }
 
 }  // namespace castk
