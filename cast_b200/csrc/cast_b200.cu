@@ -796,8 +796,9 @@ extern "C" int cast_swap_route(const float *score, const float *pooled_value, lo
   if (max_swaps_per_call < 0) return fail(CAST_ERR_INVALID_ARGUMENT, "negative max_swaps_per_call");
   if (!(swap_eps >= 0.f) || std::isinf(swap_eps))
     return fail(CAST_ERR_INVALID_ARGUMENT, "swap_eps must be finite and non-negative");
-  const size_t sm1 = (size_t)(2 * K + D + 32) * sizeof(float) + (size_t)(2 * p.Lc + S) * sizeof(int);
-  const size_t sm2 = (size_t)(p.R * p.G + p.Lc * p.G + S * p.G + p.G) * sizeof(float) +
+  const size_t sm1 = (size_t)(2 * K + D + 32 + p.Lc * p.G) * sizeof(float) +
+                     (size_t)(2 * p.Lc + S) * sizeof(int);
+  const size_t sm2 = (size_t)(p.R * p.G + p.Lc * p.G + S * p.G + p.G + p.R) * sizeof(float) +
                      (size_t)(2 * p.Lc + 2 * S) * sizeof(int);
   if (sm1 > 48 * 1024 || sm2 > 48 * 1024)
     return fail(CAST_ERR_UNSUPPORTED, "too large for one CTA (K=%d S=%d rows=%d sketch_groups=%d)", K,

@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   int *cand = reinterpret_cast<int *>(red + 32);  // Lc
   int *kept = cand + p.Lc;          // Lc
   int *seli = kept + p.Lc;          // S
+  float *pxs = reinterpret_cast<float *>(seli + p.S);  // Lc*G
   const int row = blockIdx.x;
   const int bh = row / p.R, r = row % p.R, q = p.M + r;
   const int tid = threadIdx.x;
@@ -156,7 +157,9 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
 #pragma unroll 4
     for (int t = 0; t < width; ++t)
       acc = __fadd_rn(acc, __fmul_rn(scale, __fsub_rn(outv[g * width + t], __ldg(vc + t))));
-    prow[i] = __fdiv_rn(acc, (float)width);
+    const float v = __fdiv_rn(acc, (float)width);
+    pxs[i] = v;
+    prow[i] = v;
   }
   for (int l = tid; l < p.Lc; l += blockDim.x) cand_out[(size_t)row * p.Lc + l] = cand[l];
   if (tid == 0) limit_out[row] = limit;
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   for (int g = tid; g < p.G; g += blockDim.x) {
     float e = 0.f;
     for (int l = 0; l < limit; ++l)
-      if (!kept[l]) e += prow[l * p.G + g];
+      if (!kept[l]) e += pxs[l * p.G + g];
     err_out[(size_t)row * p.G + g] = e;
   }
 }
@@ -194,6 +197,7 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
   int *addok = cand + p.Lc;             // Lc
   int *remok = addok + p.Lc;            // S
   int *key = remok + p.S;               // S
+  float *hrow = reinterpret_cast<float *>(key + p.S);  // R: this row of H
   __shared__ double dred[kSwapRoundThreads / 32];
   __shared__ float vred[kSwapRoundThreads / 32];
   __shared__ long long kred[kSwapRoundThreads / 32];
@@ -203,12 +207,13 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
   const int RG = p.R * p.G;
   const float *eg = err_all + (size_t)bh * RG;
   for (int i = tid; i < RG; i += blockDim.x) e[i] = eg[i];
+  for (int t = tid; t < p.R; t += blockDim.x) hrow[t] = __ldg(hess + (size_t)r * p.R + t);
   __syncthreads();
-  const float hrr = __ldg(hess + (size_t)r * p.R + r);
+  const float hrr = hrow[r];
   double part = 0.0;
   for (int g = tid; g < p.G; g += blockDim.x) {
     float acc = 0.f;
-    for (int t = 0; t < p.R; ++t) acc = fmaf(__ldg(hess + (size_t)r * p.R + t), e[t * p.G + g], acc);
+    for (int t = 0; t < p.R; ++t) acc = fmaf(hrow[t], e[t * p.G + g], acc);
     he[g] = acc;
     const float er = e[r * p.G + g];
     part += (double)__ldg(coef + r) * er * er + (double)er * acc;
@@ -320,25 +325,35 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
     }
     if (lane == 0) vred[warp] = bv, kred[warp] = bi;
     __syncthreads();
-    if (tid == 0) {
+    if (warp == 0) {  // the whole warp applies the swap: parallel scans, no serial loads
       for (int w = 1; w < nwarps; ++w)
         if (swap_better(vred[w], kred[w], bv, bi)) bv = vred[w], bi = kred[w];
       const bool capped = max_swaps > 0 && ctl->swaps >= max_swaps;
       if (bi != LLONG_MAX && bv < -swap_eps && !capped) {
         const SwapBest b = best_row[bi];
-        const int bb = (int)bi / p.R;
+        const int bb = (int)(bi / p.R);
         const size_t qrow = (size_t)bb * p.Q + p.M + b.row;
         const int *cg = cand_all + (size_t)bi * p.Lc;
         const float *pg = proxy_all + (size_t)bi * p.Lc * p.G;
         const int k = (int)selected[qrow * p.S + b.s];
-        int lr = -1;
-        for (int t = 0; t < p.Lc; ++t)
-          if (cg[t] == k) { lr = t; break; }
+        int lr = p.Lc;  // first candidate slot holding the removed key
+        for (int t0 = 0; t0 < p.Lc; t0 += 32) {
+          const int t = t0 + lane;
+          const unsigned m = __ballot_sync(0xffffffffu, t < p.Lc && cg[t] == k);
+          if (m) {
+            lr = t0 + __ffs(m) - 1;
+            break;
+          }
+        }
         float *er = err_all + (size_t)bi * p.G;
-        for (int g = 0; g < p.G; ++g) er[g] += (lr >= 0 ? pg[lr * p.G + g] : 0.f) - pg[b.l * p.G + g];
-        selected[qrow * p.S + b.s] = cg[b.l];
-        ctl->swaps += 1;
-        ctl->improvement += -(double)bv;
+        for (int g = lane; g < p.G; g += 32)
+          er[g] += (lr < p.Lc ? pg[lr * p.G + g] : 0.f) - pg[b.l * p.G + g];
+        __syncwarp();
+        if (lane == 0) {
+          selected[qrow * p.S + b.s] = cg[b.l];
+          ctl->swaps += 1;
+          ctl->improvement += -(double)bv;
+        }
       }
     }
   }
