@@ -746,6 +746,7 @@ static bool swap_shape(int B, int H, int Q, int K, int D, int S, int M, int mult
   p->cand_blocks = historical ? M : K;
   p->Lc = (int)std::min<long long>(p->cand_blocks, (long long)mult * S);
   p->mult = mult, p->historical = historical ? 1 : 0, p->same_bank = same_bank ? 1 : 0;
+  p->stage_v = 0;
   return p->cand_blocks > 0;
 }
 
@@ -796,8 +797,11 @@ extern "C" int cast_swap_route(const float *score, const float *pooled_value, lo
   if (max_swaps_per_call < 0) return fail(CAST_ERR_INVALID_ARGUMENT, "negative max_swaps_per_call");
   if (!(swap_eps >= 0.f) || std::isinf(swap_eps))
     return fail(CAST_ERR_INVALID_ARGUMENT, "swap_eps must be finite and non-negative");
-  const size_t sm1 = (size_t)(2 * K + D + 32 + p.Lc * p.G) * sizeof(float) +
-                     (size_t)(2 * p.Lc + S) * sizeof(int);
+  size_t sm1 = (size_t)(2 * K + D + 32 + p.Lc * p.G) * sizeof(float) +
+               (size_t)(2 * p.Lc + S) * sizeof(int);
+  const size_t vbytes = (size_t)K * D * sizeof(float);
+  p.stage_v = aligned16(pooled_value) && (K * D) % 4 == 0 && sm1 + vbytes <= 48 * 1024;
+  if (p.stage_v) sm1 += vbytes;
   const size_t sm2 = (size_t)(p.R * p.G + p.Lc * p.G + S * p.G + p.G + p.R) * sizeof(float) +
                      (size_t)(2 * p.Lc + 2 * S) * sizeof(int);
   if (sm1 > 48 * 1024 || sm2 > 48 * 1024)

@@ -26,6 +26,7 @@ constexpr int kSwapRoundThreads = 128;
 
 struct SwapShape {
   int B, H, Q, K, D, S, M, R, Lc, G, cand_blocks, mult, historical, same_bank;
+  int stage_v;  // the head's pooled values fit in shared memory (16-byte loads)
 };
 
 // Call-wide state in the workspace; zeroed by the proxy launch.
@@ -79,7 +80,8 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
                       int *__restrict__ cand_out, float *__restrict__ proxy_out,
                       float *__restrict__ err_out, int *__restrict__ limit_out, SwapCtl *ctl) {
   extern __shared__ float sm[];
-  float *prob = sm;                 // K
+  float *vsm = sm;                  // K*D when staged, first so it is 16-byte aligned
+  float *prob = sm + (p.stage_v ? p.K * p.D : 0);  // K
   float *rk = prob + p.K;           // K
   float *outv = rk + p.K;           // D
   float *red = outv + p.D;          // 32
@@ -96,8 +98,12 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
     ctl->improvement = 0.0;
   }
   const float *srow = score + ((size_t)bh * p.Q + q) * p.K;
-  const float *V = value + (size_t)bh * p.K * p.D;
+  const float *Vg = value + (size_t)bh * p.K * p.D;
   const uint8_t *lrow = local + (size_t)q * p.K;
+  if (p.stage_v)
+    for (int i = tid; i < p.K * p.D / 4; i += blockDim.x)
+      reinterpret_cast<float4 *>(vsm)[i] = __ldg(reinterpret_cast<const float4 *>(Vg) + i);
+  const float *V = p.stage_v ? vsm : Vg;  // staged copy (visible after the next barrier)
 
   float m = -INFINITY;
   for (int k = tid; k < p.K; k += blockDim.x) m = fmaxf(m, __ldg(srow + k));
@@ -122,7 +128,7 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   for (int d = tid; d < p.D; d += blockDim.x) {
     float acc = 0.f;
 #pragma unroll 8
-    for (int k = 0; k < p.K; ++k) acc = fmaf(prob[k], __ldg(V + (size_t)k * p.D + d), acc);
+    for (int k = 0; k < p.K; ++k) acc = fmaf(prob[k], V[(size_t)k * p.D + d], acc);
     outv[d] = acc;
   }
   // rank of every candidate block by (ranking desc, index asc)
@@ -156,7 +162,7 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
     float acc = 0.f;
 #pragma unroll 4
     for (int t = 0; t < width; ++t)
-      acc = __fadd_rn(acc, __fmul_rn(scale, __fsub_rn(outv[g * width + t], __ldg(vc + t))));
+      acc = __fadd_rn(acc, __fmul_rn(scale, __fsub_rn(outv[g * width + t], vc[t])));
     const float v = __fdiv_rn(acc, (float)width);
     pxs[i] = v;
     prow[i] = v;
