@@ -274,7 +274,7 @@ def swap_measure(dev, steps, cpu_leg=True):
     lib = _lib.load()
     nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, D, S, M, 2, 0, 16)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    stats = torch.empty(4, dtype=torch.float64, device=dev)
+    stats = torch.empty(5, dtype=torch.float64, device=dev)
     sc, pv, cn = w.score.to(dev), w.pooled_value.to(dev), w.counts.to(dev)
     lo, sel = w.local.to(torch.uint8).to(dev), w.selected.to(dev)
 

@@ -823,6 +823,7 @@ extern "C" int cast_swap_route(const float *score, const float *pooled_value, lo
   auto *ctl = reinterpret_cast<castk::SwapCtl *>(ws + lay.ctl);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int rows = B * H * p.R;
+  CAST_CUDA_TRY(cudaMemsetAsync(ctl, 0, sizeof(castk::SwapCtl), s));
   castk::swap_proxy_kernel<<<rows, castk::kSwapProxyThreads, sm1, s>>>(
       score, pooled_value, selected, counts, local, p, 1e-6f, cand, proxy, err, limit, ctl);
   CAST_CUDA_TRY(cudaGetLastError());

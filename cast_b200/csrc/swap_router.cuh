@@ -29,12 +29,22 @@ struct SwapShape {
   int stage_v;  // the head's pooled values fit in shared memory (16-byte loads)
 };
 
-// Call-wide state in the workspace; zeroed by the proxy launch.
+// Call-wide state in the workspace; zeroed by the host before the proxy
+// launch.  max_swappable is the largest swappable count over every row
+// (memory rows included), which sets the reference's candidate width
+// maximum_l = min(cand_blocks, mult * max_swappable).
 struct SwapCtl {
   unsigned int ticket;
   int swaps;
   double improvement;
+  int max_swappable;
 };
+
+// The reference's maximum_l: candidate slots at or beyond it hold no proxy
+// (its candidate list is only that wide).
+__device__ __forceinline__ int swap_width(const SwapShape &p, const SwapCtl *ctl) {
+  return min(p.Lc, min(p.cand_blocks, p.mult * *(volatile const int *)&ctl->max_swappable));
+}
 
 // Per-row best pair of a round.
 struct SwapBest {
@@ -92,10 +102,15 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   const int row = blockIdx.x;
   const int bh = row / p.R, r = row % p.R, q = p.M + r;
   const int tid = threadIdx.x;
-  if (row == 0 && tid == 0) {
-    ctl->ticket = 0u;
-    ctl->swaps = 0;
-    ctl->improvement = 0.0;
+  // memory rows take no search but their swappable counts widen the
+  // candidate list: the grid strides over them, one thread per row
+  for (int mr = blockIdx.x * blockDim.x + tid; mr < p.B * p.H * p.M; mr += gridDim.x * blockDim.x) {
+    const size_t qrow = (size_t)(mr / p.M) * p.Q + mr % p.M;
+    const long long c = __ldg(counts + qrow);
+    int sw = 0;
+    for (int j = 0; j < p.S && j < c; ++j)
+      sw += !p.historical || __ldg(selected + qrow * p.S + j) < p.M;
+    if (sw) atomicMax(&ctl->max_swappable, sw);
   }
   const float *srow = score + ((size_t)bh * p.Q + q) * p.K;
   const float *Vg = value + (size_t)bh * p.K * p.D;
@@ -146,6 +161,7 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   for (int j = 0; j < p.S; ++j)
     swappable += (j < cnt) && (!p.historical || seli[j] < p.M);
   const int limit = min(swappable * p.mult, p.cand_blocks);
+  if (tid == 0 && swappable) atomicMax(&ctl->max_swappable, swappable);
   for (int l = tid; l < p.Lc; l += blockDim.x) {
     int hit = 0;
     for (int j = 0; j < p.S; ++j) hit |= (j < cnt) && (seli[j] == cand[l]);
@@ -234,6 +250,7 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
     const size_t qrow = (size_t)bh * p.Q + q;
     const long long cnt = __ldg(counts + qrow);
     const int limit = limit_all[row];
+    const int width = swap_width(p, ctl);
     const int *cg = cand_all + (size_t)row * p.Lc;
     const float *pg = proxy_all + (size_t)row * p.Lc * p.G;
     for (int i = tid; i < p.Lc * p.G; i += blockDim.x) prx[i] = pg[i];
@@ -256,7 +273,7 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
       if (p.historical) ok = ok && k < p.M;
       remok[j] = ok;
       int lr = -1;  // the removed key's candidate slot (its proxy), if any
-      for (int t = 0; t < p.Lc; ++t)
+      for (int t = 0; t < width; ++t)
         if (cand[t] == k) { lr = t; break; }
       for (int g = 0; g < p.G; ++g) rem[j * p.G + g] = lr >= 0 ? prx[lr * p.G + g] : 0.f;
     }
@@ -342,10 +359,11 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
         const int *cg = cand_all + (size_t)bi * p.Lc;
         const float *pg = proxy_all + (size_t)bi * p.Lc * p.G;
         const int k = (int)selected[qrow * p.S + b.s];
-        int lr = p.Lc;  // first candidate slot holding the removed key
-        for (int t0 = 0; t0 < p.Lc; t0 += 32) {
+        const int width = swap_width(p, ctl);
+        int lr = width;  // first candidate slot holding the removed key
+        for (int t0 = 0; t0 < width; t0 += 32) {
           const int t = t0 + lane;
-          const unsigned m = __ballot_sync(0xffffffffu, t < p.Lc && cg[t] == k);
+          const unsigned m = __ballot_sync(0xffffffffu, t < width && cg[t] == k);
           if (m) {
             lr = t0 + __ffs(m) - 1;
             break;
@@ -353,7 +371,7 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
         }
         float *er = err_all + (size_t)bi * p.G;
         for (int g = lane; g < p.G; g += 32)
-          er[g] += (lr < p.Lc ? pg[lr * p.G + g] : 0.f) - pg[b.l * p.G + g];
+          er[g] += (lr < width ? pg[lr * p.G + g] : 0.f) - pg[b.l * p.G + g];
         __syncwarp();
         if (lane == 0) {
           selected[qrow * p.S + b.s] = cg[b.l];
@@ -387,6 +405,7 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
       stats[0] = (double)ctl->swaps;
       stats[2] = t;
       stats[3] = ctl->improvement;
+      stats[4] = (double)ctl->max_swappable;
     }
   }
   if (tid == 0) ctl->ticket = 0u;

@@ -281,9 +281,6 @@ class FCPASMLocalCoordinateSwapRouter:
         valid = slot[None, None, None] < counts[..., None]
         hist_sel = valid & (selected < memory_blocks)
         hist_counts = hist_sel.sum(-1)
-        swappable = (hist_sel if cfg.historical_only else valid).sum(-1)
-        if int(swappable.max().item()) == 0:
-            return self._fallback(layer_index, "no_swappable_kv_selected", baseline)
         coef, hess, cache_used = quadratic_terms(
             temporal_cells=cells, spatial=spatial, exact_frames=frames,
             temporal_group_size=int(temporal_group_size), current_boundary=int(current_boundary),
@@ -300,7 +297,7 @@ class FCPASMLocalCoordinateSwapRouter:
                                                      cfg.candidate_multiplier, int(cfg.historical_only),
                                                      cfg.sketch_groups)
         ws = self._workspace(nbytes, dev)
-        stats = torch.empty(4, dtype=torch.float64, device=dev)
+        stats = torch.empty(5, dtype=torch.float64, device=dev)
         sc = score.float().contiguous()
         pv = pooled_value.float().contiguous()
         cn = counts.to(torch.int64).contiguous()
@@ -313,8 +310,10 @@ class FCPASMLocalCoordinateSwapRouter:
                   torch.cuda.current_stream(dev).cuda_stream)
         if sel.data_ptr() != selected.data_ptr():
             selected.copy_(sel)
-        swaps, before, after, gained = (float(v) for v in stats.cpu())
-        swaps = int(swaps)
+        swaps, before, after, gained, max_swappable = (float(v) for v in stats.cpu())
+        swaps, max_swappable = int(swaps), int(max_swappable)
+        if max_swappable == 0:  # nothing was swappable: the kernels changed nothing
+            return self._fallback(layer_index, "no_swappable_kv_selected", baseline)
         final_hist = ((selected < memory_blocks) & valid).sum(-1)
         nonhist = lambda t: torch.where(valid & (t >= memory_blocks), t, K).sort(dim=-1).values  # noqa: E731
         unchanged = bool(torch.equal(nonhist(selected), nonhist(baseline)))
@@ -332,7 +331,7 @@ class FCPASMLocalCoordinateSwapRouter:
             "layer_index": int(layer_index), "status": "refined",
             "candidate_multiplier": cfg.candidate_multiplier,
             "candidate_max": min(memory_blocks if cfg.historical_only else K,
-                                 cfg.candidate_multiplier * int(swappable.max().item())),
+                                 cfg.candidate_multiplier * max_swappable),
             "swap_rounds": cfg.num_swap_rounds, "max_swaps_per_call": cfg.max_swaps_per_call,
             "swap_count": swaps, "objective_before": f64(before), "objective_after": f64(after),
             "objective_improvement": f64(before - after),

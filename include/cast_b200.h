@@ -118,7 +118,10 @@ CAST_API size_t cast_rcsa_select_quant_workspace_bytes(int B, int H, int Lq, int
  * Allocation-free variant of cast_rcsa_select_quant (no counterpart in the
  * reference).  Same arguments, outputs and results, minus the workspace: the
  * scratch lives in one static device array of CAST_NOALLOC_SCRATCH_BYTES per
- * device, inside this library.  The call makes no cudaMalloc / cudaFree or
+ * device, inside this library.  Loading the library reserves those 8 MiB on
+ * every device where its module loads, for every process that loads it, even
+ * one that never calls this entry point; they stay reserved until the process
+ * exits.  The call makes no cudaMalloc / cudaFree or
  * other allocating call; its first call on a device looks up that array's
  * address (cudaGetSymbolAddress) with the device current.
  *
@@ -280,15 +283,20 @@ CAST_API int cast_barycentric_pair_write(const float *active_residual, const flo
  *                J(e) = sum_r coefficient[r] |e_r|^2 + e^T hessian e over the
  *                current rows' sketched errors (anchor term and transport
  *                reconstruction terms, _objective_terms :414-548)
- *   stats        fp64 [4] device: swaps made, objective before, objective
- *                after, summed improvement
+ *   stats        fp64 [5] device: swaps made, objective before, objective
+ *                after, summed improvement, and the largest swappable count
+ *                over all rows (0: nothing to swap, the selection is unchanged)
  * Candidates are the top min(cand_blocks, multiplier*S) blocks of
  * score + 1e6*local (cand_blocks = memory_blocks if historical_only else K),
- * which holds every row's valid candidates of the reference's top-k.  Each
+ * which holds every row's valid candidates of the reference's top-k; a
+ * removed key's proxy is looked up only among the first
+ * min(cand_blocks, multiplier*max swappable count) slots, the reference's
+ * candidate width (:820-826), and is 0 beyond it.  Each
  * round accepts at most one swap over the whole call (the first minimum in
  * (b, h, row, slot, candidate) order) when it beats -swap_eps and the cap
  * allows.  A selected key outside [0,K) is skipped and reported by
- * cast_device_error().  Launches: 2 + num_swap_rounds (3 when 0 rounds).
+ * cast_device_error().  Launches: a memset of the call state, then
+ * 2 + num_swap_rounds kernels (3 when 0 rounds).
  */
 CAST_API int cast_swap_route(const float *score, const float *pooled_value, long long *selected,
                     const long long *counts, const uint8_t *local, const uint8_t *row_gate,

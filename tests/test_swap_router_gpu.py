@@ -93,7 +93,7 @@ def test_c_abi_rejects_bad_arguments():
     lib = _lib.load()
     dev = "cuda"
     w = _to(workloads.swap_case(), dev)
-    stats = torch.empty(4, dtype=torch.float64, device=dev)
+    stats = torch.empty(5, dtype=torch.float64, device=dev)
     coef = torch.zeros(32, device=dev)
     hess = torch.zeros(32, 32, device=dev)
     sel = w.selected.clone()
@@ -132,7 +132,7 @@ def test_swap_route_graph_rate():
                                        lambda_anchor=1.0, lambda_reconstruction=1.0, device="cuda")
     nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, D, S, M, 2, 0, 16)
     ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-    stats = torch.empty(4, dtype=torch.float64, device="cuda")
+    stats = torch.empty(5, dtype=torch.float64, device="cuda")
     local = w.local.to(torch.uint8)
     sel = w.selected.clone()
     s = torch.cuda.Stream()
@@ -160,3 +160,65 @@ def test_swap_route_graph_rate():
     us = e0.elapsed_time(e1) * 1e3 / 20
     print(f"swap route, 24 heads x 32 current rows, 64 keys, D=128: {us:.1f} us per call")
     assert us < 1000.0
+
+
+def _oracle_op(w):
+    ops = {}
+
+    def op(pair, x):
+        key = (pair, round(float(x), 12))
+        if key not in ops:
+            ops[key] = sr.transport_operator(w.transport, pair, spatial_shape=w.spatial_shape,
+                                             exponent=x, device="cpu")[0].numpy()
+        return ops[key]
+    return op
+
+
+def _short_rows_case(historical_only: bool, seed: int = 5):
+    """A layer case whose rows are all shorter than the selection width, so the
+    reference's candidate width min(cand_blocks, 2 * max swappable count) is
+    below the device's 2 * S slots.  Historical-only: each current row's
+    non-local keys are random memory blocks, so selected keys rank past that
+    width in the candidate order (their proxies must then count as zero)."""
+    w = _layer_case(seed=seed)
+    g = torch.Generator().manual_seed(seed)
+    B, H, Q, K = w.score.shape
+    S, M = w.selected.shape[-1], w.memory_blocks
+    sel = w.selected.clone()
+    counts = w.counts.clone()
+    if historical_only:
+        for h in range(H):
+            for q in range(M, Q):
+                n_local = int(w.local[q].sum())
+                pick = torch.randperm(M, generator=g)[: S - n_local]
+                sel[0, h, q, n_local:] = pick
+        counts[:] = S - 3 - torch.randint(0, 3, counts.shape, generator=g)
+    else:
+        counts[:] = S - 4 - torch.randint(0, 3, counts.shape, generator=g)
+    slot = torch.arange(S)[None, None, None]
+    pad = torch.gather(sel, -1, (counts - 1)[..., None])
+    w.selected = torch.where(slot < counts[..., None], sel, pad)
+    w.counts = counts
+    return w
+
+
+@pytest.mark.parametrize("historical_only", [False, True])
+def test_short_rows_match_oracle(historical_only):
+    """Rows shorter than the selection width: the removed key's proxy is looked
+    up only within the reference's candidate width (fc_pasm_swap_routing.py:
+    820-826); beyond it the proxy is zero, on the device as in the oracle."""
+    w = _short_rows_case(historical_only)
+    cfg = dict(num_swap_rounds=2, swap_eps=0.0, historical_only=historical_only)
+    sel_o, st = osr.refine(score=w.score.numpy(), pooled_value=w.pooled_value.numpy(),
+                           selected=w.selected.numpy(), counts=w.counts.numpy(), local=w.local.numpy(),
+                           memory_blocks=w.memory_blocks, spatial=8, exact_frames=w.exact_frames,
+                           group=1, boundary=4, config=osr.SwapConfig(**cfg), operator=_oracle_op(w))
+    wd = _to(_short_rows_case(historical_only), "cuda")
+    router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig(**cfg))
+    sel, rec = _refine(router, wd)
+    assert rec["status"] == "refined"
+    assert rec["swap_count"] == st["swap_count"]
+    np.testing.assert_array_equal(sel.cpu().numpy(), sel_o)
+    assert float(rec["objective_before"]) == pytest.approx(st["objective_before"], rel=1e-4)
+    assert float(rec["objective_after"]) == pytest.approx(st["objective_after"], rel=1e-4)
+    assert rec["candidate_max"] == st["candidate_max"] < 2 * w.selected.shape[-1]
