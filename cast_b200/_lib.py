@@ -25,6 +25,7 @@ SIGNATURES = {
     "cast_last_error_message": (ctypes.c_char_p, []),
     "cast_version": (c_int, []),
     "cast_device_error": (c_int, [c_void_p]),
+    "cast_selftest_bounded_wait": (c_int, [c_int, c_int, c_void_p]),
     "cast_rcsa_select_quant": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
@@ -117,6 +118,14 @@ def check(status: int, name: str) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
+
+
+def check_device(stream: int | None, where: str) -> None:
+    """Raises :class:`CastError` when a kernel reported a device-side error
+    (a bounded wait that gave up, an index out of range) since the last
+    check.  Synchronises ``stream``: call it where the caller synchronises
+    anyway."""
+    check(load().cast_device_error(stream), where)
 
 
 def ptr(t) -> int | None:

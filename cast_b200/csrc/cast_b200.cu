@@ -133,6 +133,32 @@ extern "C" int cast_device_error(cast_stream_t stream) {
   return CAST_OK;
 }
 
+// One CTA: an mbarrier expecting one arrival, which thread 0 makes only when
+// `arrive`; every thread then waits on it through the library's bounded wait
+// with the given limit.  Without the arrival the wait gives up, sets the
+// device error word and the kernel returns normally.
+__global__ void selftest_bounded_wait_kernel(int arrive, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    castdev::mbar_init(&bar, 1);
+    castdev::fence_barrier_init();
+  }
+  __syncthreads();
+  if (arrive && threadIdx.x == 0) castdev::mbar_arrive(&bar);
+  castdev::mbar_wait(&bar, 0, &g_cast_device_error, limit_ns);
+}
+
+extern "C" int cast_selftest_bounded_wait(int arrive, int limit_us, cast_stream_t stream) {
+  if (limit_us <= 0 || limit_us > 1000000)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "limit_us %d (1..1000000)", limit_us);
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  selftest_bounded_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      arrive, (unsigned long long)limit_us * 1000ull);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
 // ===========================================================================
 // RCSA selection + quantisation
 // ===========================================================================

@@ -105,14 +105,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete.  Returns false (and
 // records a device timeout) if it does not complete within kWaitLimitNs, or
 // as soon as another wait anywhere on the device has already given up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err_flag,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t spin = 0;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 255u) == 255u) {
       if (*reinterpret_cast<volatile int *>(err_flag) != 0) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         atomicExch(err_flag, (int)CAST_ERR_DEVICE_TIMEOUT);
         return false;
       }

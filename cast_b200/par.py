@@ -19,10 +19,52 @@ from . import _lib
 
 TILES = 18
 FREQS = 66
+MAX_PAIRS = 16                        # castk::kParMaxPairs
+STATS_PER_PAIR = TILES * (2 * FREQS + 5)  # theta, confidence, g, displacement, base, ramp
+
+
+def bracket_targets(anchors: list[int], current_length: int, boundary: int):
+    """Skipped current frames with their anchor pair, as the segment-local
+    bracket rule of ``_correct_frequency_confidence_pasm_reference`` walks
+    them (``:2981-3060``, ``:3225-3232``): chronological targets, each between
+    the nearest anchors on either side within its own segment (frames below
+    ``boundary`` and frames at or above it never pair).  Returns
+    ``(targets, pair_of_target, pairs)`` with ``pairs`` the distinct
+    ``(left, right)`` anchor frames in order of first use -- the order in
+    which ``cast_par_fcpasm`` lays out its per-pair statistics."""
+    targets, pair_of_target, pairs = [], [], []
+    anchor_set = set(anchors)
+    for t in range(current_length):
+        if t in anchor_set:
+            continue
+        same = t < boundary
+        seg = [f for f in anchors if (f < boundary) == same]
+        left = [f for f in seg if f < t]
+        right = [f for f in seg if f > t]
+        if not left or not right:
+            continue
+        pair = (left[-1], right[0])
+        if pair not in pairs:
+            pairs.append(pair)
+        targets.append(t)
+        pair_of_target.append(pairs.index(pair))
+    return targets, pair_of_target, pairs
 
 
 class FCPASMCorrector:
-    """FC-PASM corrector with the frozen factory knobs (``cast_matrix.py:74-96``)."""
+    """FC-PASM corrector with the frozen factory knobs (``cast_matrix.py:74-96``).
+
+    Besides the reconstruction it keeps the reference corrector's routing
+    state: after a corrected layer whose successor runs the swap router it
+    publishes the detached endpoint transport sketch (per target: the
+    anchor pair's per-frequency phase ``theta`` and affinity ``g``, both
+    ``[18, 11, 6]``) in the format of ``_publish_fc_routing_transport``
+    (``proposed/matrix_world_spectral_residual.py:577-658``), read back by
+    :meth:`fc_pasm_routing_transport`, and it updates
+    ``_fc_previous_mean_affinity`` (``:3667-3669``).  Both come from the
+    statistics the PAR kernels already compute, so publishing costs no
+    extra kernel work.
+    """
 
     mode = "frequency_confidence_phase_aligned_spectral_mixing"
 
@@ -55,12 +97,59 @@ class FCPASMCorrector:
         self._records: list[dict] = []
         self._workspace: dict = {}
         self.last_stats: torch.Tensor | None = None
+        # routing state (:492, :530, :541): the published sketches by
+        # (step, layer), the layers whose successor routes (None: all), and
+        # the mean affinity of the last corrected layer
+        self._fc_routing_transport: dict = {}
+        self._fc_routing_publish_layers: frozenset | None = None
+        self._fc_previous_mean_affinity: torch.Tensor | None = None
 
     def begin_model_call(self, *, geometry=None, chunk_index: int, step_index: int, device=None) -> None:
         """``WorldAlignedSpectralResidualCorrector.begin_model_call`` (``:544-556``)."""
         del geometry, device
         self._chunk = int(chunk_index)
         self._step = int(step_index)
+        self._fc_routing_transport.clear()
+
+    def should_publish_fc_routing_transport(self, layer_index: int) -> bool:
+        """Whether a router at ``layer_index + 1`` can read this layer's sketch (:532-542)."""
+        layers = self._fc_routing_publish_layers
+        return layers is None or int(layer_index) in layers
+
+    def fc_pasm_routing_transport(self, *, layer_index: int):
+        """The previous layer's sketch in this model call, or None (:660-668)."""
+        source = int(layer_index) - 1
+        if source < 0:
+            return None
+        return self._fc_routing_transport.get((int(self._step), source))
+
+    def _publish(self, layer_index, anchors, pair_of_target, pairs, stats, h, w):
+        theta, affinity = stats_views(stats, len(pairs))
+        if len(pairs) == 1:
+            mean = affinity[0].mean()
+        else:  # every target's copy of its pair's affinity, as the reference stacks them
+            mean = torch.stack([affinity[i] for i in pair_of_target]).mean()
+        self._fc_previous_mean_affinity = mean.detach()
+        if not self.should_publish_fc_routing_transport(layer_index):
+            return
+        published = {}
+        for i, key in enumerate(pairs):
+            aff = affinity[i]
+            published[key] = {
+                "theta": theta[i], "affinity": aff, "mean_affinity": aff.mean(),
+                "mean_affinity_reduction": "all_tile_frequencies",
+                "affinity_support_count": torch.full((), aff.numel(), dtype=torch.long,
+                                                     device=aff.device),
+                "affinity_total_count": int(aff.numel()),
+            }
+        self._fc_routing_transport[(int(self._step), int(layer_index))] = {
+            "source_layer": int(layer_index), "source_step": int(self._step),
+            "exact_frames": tuple(int(f) for f in anchors), "tile_grid": (3, 6),
+            "output_shape": (int(h), int(w)), "transport_shape": (11, 10),
+            "window_shape": (11, 10), "stride": (8, 8), "padding": (4, 5), "pairs": published,
+            "detached": True, "endpoint_only": True,
+            "transport_formula": "per_frequency_exp(i*g*theta)",
+        }
 
     def _ws(self, device, nbytes: int) -> torch.Tensor:
         buf = self._workspace.get(device)
@@ -109,13 +198,16 @@ class FCPASMCorrector:
         t_total, hw, c = full_residual.shape[1:]
         if hw != spatial_height * spatial_width:
             raise RuntimeError("residual token count differs from the latent grid")
+        anchors = [f - int(memory_length) for f in frames if f >= memory_length]
+        targets, pair_of_target, pairs = bracket_targets(
+            anchors, t_total - int(memory_length), self.current_anchor_boundary)
         lib = _lib.load()
         nbytes = lib.cast_par_fcpasm_workspace_bytes(t_total, spatial_height, spatial_width, c)
         ws = self._ws(full_residual.device, nbytes)
         frames_arr = (_lib.ctypes.c_int32 * len(frames))(*frames)
         stats = None
-        if self.record_stats:
-            stats = torch.empty(16 * TILES * (2 * FREQS + 5), dtype=torch.float32,
+        if self.record_stats or targets:
+            stats = torch.empty(MAX_PAIRS * STATS_PER_PAIR, dtype=torch.float32,
                                 device=full_residual.device)
         if tile_confidence is not None:
             tile_confidence = tile_confidence.to(device=full_residual.device,
@@ -129,13 +221,28 @@ class FCPASMCorrector:
             ws.numel(), torch.cuda.current_stream(full_residual.device).cuda_stream,
         )
         self.last_stats = stats
-        self._records.append({"layer_index": int(layer_index), "status": "corrected"})
+        if targets:
+            self._publish(layer_index, anchors, pair_of_target, pairs, stats, spatial_height,
+                          spatial_width)
+        self._records.append({"layer_index": int(layer_index), "status": "corrected",
+                              "target_frames": targets,
+                              "target_anchor_pairs": [list(pairs[i]) for i in pair_of_target]})
         return full_residual
 
 
+def stats_views(stats: torch.Tensor, n_pairs: int):
+    """``theta`` and affinity ``g`` of every anchor pair, ``[n_pairs, 18, 11, 6]``
+    views into the statistics block (no copy, no synchronisation)."""
+    blk = stats[: n_pairs * STATS_PER_PAIR].view(n_pairs, STATS_PER_PAIR)
+    theta = blk[:, : TILES * FREQS].view(n_pairs, TILES, 11, 6)
+    g0 = TILES * FREQS + TILES
+    affinity = blk[:, g0: g0 + TILES * FREQS].view(n_pairs, TILES, 11, 6)
+    return theta, affinity
+
+
 def unpack_stats(stats: torch.Tensor, n_pairs: int) -> list[dict]:
-    """Splits the per-pair statistics block written when ``record_stats`` is on."""
-    per = TILES * (2 * FREQS + 5)
+    """Splits the per-pair statistics block (written whenever a call has targets)."""
+    per = STATS_PER_PAIR
     out = []
     for i in range(n_pairs):
         s = stats[i * per:(i + 1) * per]

@@ -402,6 +402,13 @@ class RCSAPlan:
         return Selection(self.indices, self.counts, self.q_codes, self.q_scales, self.k_codes,
                          self.k_scales, None, None, self.qk_mode, None)
 
+    def check(self) -> None:
+        """Waits for the plan's stream and raises :class:`cast_b200._lib.CastError`
+        if a kernel reported a device-side error (a bounded wait that gave up,
+        an index out of range) since the last check; the outputs of such a
+        call are not valid."""
+        _lib.check_device(_stream(self.device), "RCSAPlan")
+
     def capture(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, parts: str = "all",
                 out: torch.Tensor | None = None):
         """CUDA graph of one call on these input buffers (``parts``: all,
@@ -460,9 +467,14 @@ class RCSAHostPlan:
         self.device = dev
 
     def __call__(self, hq: torch.Tensor, hk: torch.Tensor, hv: torch.Tensor,
-                 hout: torch.Tensor) -> torch.Tensor:
+                 hout: torch.Tensor, check: bool = True) -> torch.Tensor:
         """``hq``/``hk``/``hv``/``hout``: pinned host bf16 tensors of the plan's
-        shapes; the attention output lands in ``hout``."""
+        shapes; the attention output lands in ``hout``.  With ``check`` (the
+        default) the call waits for the output copy, so ``hout`` is ready on
+        return, and raises :class:`cast_b200._lib.CastError` if a kernel
+        reported a device-side error; without it the call only enqueues, and
+        the output copy is ordered before anything the caller enqueues next on
+        its stream."""
         B, H, Lq, Lk, D = self.shape
         for name, t, L in (("q", hq, Lq), ("k", hk, Lk), ("v", hv, Lk), ("out", hout, Lq)):
             if t.is_cuda or t.dtype != torch.bfloat16 or tuple(t.shape) != (B, H, L, D):
@@ -492,4 +504,6 @@ class RCSAHostPlan:
             with torch.cuda.stream(self.d2h):
                 hout[:, h0:h1].copy_(self.out[:, h0:h1], non_blocking=True)
         cur.wait_stream(self.d2h)
+        if check:
+            _lib.check_device(cur.cuda_stream, "RCSAHostPlan")
         return hout

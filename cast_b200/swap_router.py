@@ -311,6 +311,7 @@ class FCPASMLocalCoordinateSwapRouter:
         if sel.data_ptr() != selected.data_ptr():
             selected.copy_(sel)
         swaps, before, after, gained, max_swappable = (float(v) for v in stats.cpu())
+        _lib.check_device(torch.cuda.current_stream(dev).cuda_stream, "cast_swap_route")
         swaps, max_swappable = int(swaps), int(max_swappable)
         if max_swappable == 0:  # nothing was swappable: the kernels changed nothing
             return self._fallback(layer_index, "no_swappable_kv_selected", baseline)

@@ -49,6 +49,14 @@ CAST_API int cast_version(void);
 /* Test/debug helper: synchronises `stream`, then reads and clears the device
  * error word that bounded device-side waits set when they give up. */
 CAST_API int cast_device_error(cast_stream_t stream);
+/* Self-test of the bounded device-side wait (no counterpart in the reference):
+ * one CTA waits on an mbarrier through the same bounded wait the kernels use,
+ * with a limit of `limit_us` microseconds (1..1000000).  With `arrive` != 0 the
+ * awaited arrival is made and the wait completes; with 0 nothing arrives, the
+ * wait gives up, the kernel sets the device error word and returns normally,
+ * and the next cast_device_error() reports CAST_ERR_DEVICE_TIMEOUT.  No trap,
+ * no fault: the context stays usable. */
+CAST_API int cast_selftest_bounded_wait(int arrive, int limit_us, cast_stream_t stream);
 
 /* Selection rule for cast_rcsa_select_quant. */
 enum cast_select_rule {

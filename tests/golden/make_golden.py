@@ -44,6 +44,11 @@ Files:
   per-pair affinity gate): the selection after, swap count, objective before
   and after, and the transport operators (``_transport_matrix`` :116-268) the
   objective used.
+* ``transport_*.npz``    -- the FC routing transport the reference corrector
+  publishes after PAR at layer 21 (per anchor pair: theta, affinity, mean
+  affinity; the layer's mean affinity; the corrected frames), and the
+  reference router's ``refine`` at layer 22 on that sketch under the
+  factory's production knobs and with two rounds.
 * ``MANIFEST.json``      -- SHA-256 of every fixture and of every regenerated
   input (mirrors the hash manifest idea of ``scripts/check_release.py:19-26``).
 """
@@ -347,10 +352,100 @@ def make_swap(manifest: dict):
               float(rec["objective_after"]))
 
 
+TRANSPORT_ROUTER = {
+    # router configurations run on the published sketch (FCPASMSwapRoutingConfig kwargs)
+    "production": dict(num_swap_rounds=1, swap_eps=0.10, max_swaps_per_call=1, same_bank_only=True,
+                       require_fc_transport=True, min_transport_affinity=0.5,
+                       active_layers=(22, 26)),
+    "two_rounds": dict(num_swap_rounds=2, require_fc_transport=True, min_transport_affinity=0.5),
+}
+
+
+def _smooth_motion(seed: int, frames: int, active: list[int], shift: tuple[float, float]):
+    """Residual frames that are shifted crops of one smooth pattern (bilinear
+    2x upsampling of N(0, 0.02) noise), moving ``shift`` latent pixels per
+    frame, so the anchor pairs see coherent phase (mean affinity well above
+    the router's 0.5 gate, not saturated)."""
+    g = torch.Generator().manual_seed(seed)
+    base = torch.randn(1, 64, 25, 34, generator=g) * 0.02
+    base = torch.nn.functional.interpolate(base, scale_factor=2, mode="bilinear", align_corners=False)
+    out = []
+    for t in range(frames):
+        dy, dx = int(round(t * shift[0])), int(round(t * shift[1]))
+        crop = base[:, :, 4 + dy:4 + dy + 22, 4 + dx:4 + dx + 40]
+        out.append(crop.permute(0, 2, 3, 1).reshape(1, 880, 64))
+    return workloads.PARWorkload("smooth_motion", torch.stack(out, 1).to(torch.bfloat16), active, 1, 22, 40)
+
+
+def transport_cases():
+    """(name, PAR workload, router swap_case kwargs) for the layer-21 -> 22 chain."""
+    return [
+        ("one_pair", _smooth_motion(5, 5, [0, 1, 4], (0.34, 0.67)),
+         dict(heads=3, memory_blocks=6, cells=4, exact_frames=(0, 3), seed=31)),
+        ("two_pairs", _smooth_motion(6, 9, [0, 1, 4, 5, 8], (0.34, 0.67)),
+         dict(heads=3, memory_blocks=6, cells=8, exact_frames=(0, 3, 4, 7), seed=32)),
+    ]
+
+
+def make_transport(manifest: dict):
+    """The FC routing transport the reference corrector publishes after a
+    corrected layer (``_publish_fc_routing_transport``,
+    proposed/matrix_world_spectral_residual.py:577-658, called at :3652-3669)
+    and what the reference router does with it one layer later: PAR at layer
+    21 with publishing on for that layer (as the factory's weave sets up for
+    a router at layer 22, proposed/matrix_curvature_phase_frame_weave.py:
+    675-683), then ``refine`` at layer 22 on ``workloads.swap_case`` scores
+    with the sketch (plus the attention grid the weave adds, :6025-6028)."""
+    from interaction_accel.methods.proposed import fc_pasm_swap_routing as fr
+
+    for name, wl, case_kw in transport_cases():
+        c = par_corrector()
+        c._fc_routing_publish_layers = frozenset({21})
+        full = wl.full_residual.clone()
+        c.correct(layer_index=21, full_input=full, full_residual=full,
+                  active_residual=wl.active_residual, active_frames=torch.tensor(wl.active_frames),
+                  memory_length=wl.memory_length, spatial_height=22, spatial_width=40,
+                  active_frame_values=tuple(wl.active_frames))
+        tr = c.fc_pasm_routing_transport(layer_index=22)
+        assert tr is not None and c.fc_pasm_routing_transport(layer_index=23) is None
+        out = {"pairs": np.array(sorted(tr["pairs"]), dtype=np.int64),
+               "exact_frames": np.array(tr["exact_frames"], dtype=np.int64),
+               "previous_mean_affinity": np.float64(float(c._fc_previous_mean_affinity)),
+               # every 11th value of the current frames (targets reconstructed, anchors copied)
+               "current_sample": full[0, wl.memory_length:].float().flatten()[::11].numpy()}
+        for (left, right) in sorted(tr["pairs"]):
+            e = tr["pairs"][(left, right)]
+            out[f"theta_{left}_{right}"] = e["theta"].numpy()
+            out[f"affinity_{left}_{right}"] = e["affinity"].numpy()
+            out[f"mean_affinity_{left}_{right}"] = np.float64(float(e["mean_affinity"]))
+        w = workloads.swap_case(**case_kw)
+        transport = dict(tr)
+        transport["attention_spatial_h"], transport["attention_spatial_w"] = w.spatial_shape
+        for tag, cfg_kw in TRANSPORT_ROUTER.items():
+            router = fr.FCPASMLocalCoordinateSwapRouter(fr.FCPASMSwapRoutingConfig(**cfg_kw))
+            sel, rec = router.refine(
+                score=w.score, pooled_value=w.pooled_value, selected=w.selected.clone(),
+                counts=w.counts, local=w.local, memory_blocks=w.memory_blocks,
+                spatial_shape=w.spatial_shape, exact_current_frames=w.exact_frames,
+                temporal_group_size=w.temporal_group_size, current_boundary=w.current_boundary,
+                transport=transport, layer_index=22)
+            out[f"{tag}_status"] = np.array(rec["status"])
+            out[f"{tag}_selected_after"] = sel.numpy().astype(np.int64)
+            out[f"{tag}_swap_count"] = np.int64(rec["swap_count"])
+            if rec["status"] == "refined":
+                out[f"{tag}_objective_before"] = np.float64(float(rec["objective_before"]))
+                out[f"{tag}_objective_after"] = np.float64(float(rec["objective_after"]))
+            print(name, tag, rec["status"], rec.get("fallback_reason"), rec["swap_count"],
+                  {k: float(out[f"mean_affinity_{k[0]}_{k[1]}"]) for k in tr["pairs"]})
+        manifest["inputs"][f"transport_{name}_full_residual"] = sha(wl.full_residual)
+        np.savez_compressed(os.path.join(HERE, f"transport_{name}.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the CAST src/ directory")
-    ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "compact", "par", "swap"),
+    ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "compact", "par", "swap",
+                                                   "transport"),
                     help="regenerate these fixtures only; other manifest entries are kept")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
@@ -362,7 +457,7 @@ def main():
     if args.only and os.path.exists(mpath):
         with open(mpath) as fh:
             manifest = json.load(fh)
-    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par", "swap"))
+    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par", "swap", "transport"))
     if "cfg1" in todo:
         make_cfg1({}, manifest)
     if "cfg2" in todo:
@@ -375,6 +470,8 @@ def main():
         make_par(manifest)
     if "swap" in todo:
         make_swap(manifest)
+    if "transport" in todo:
+        make_transport(manifest)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             with open(os.path.join(HERE, f), "rb") as fh:
