@@ -1,21 +1,24 @@
 """RCSA benchmark on B200: one Matrix-shaped DiT attention layer (config 2).
 
-A step is one RCSA layer call per local rollout: pooled-QK block selection +
-per-block int8 quantisation (one fused pass over Q/K) and the tcgen05
-block-sparse attention, on H=24 heads x d128, 3520 queries (4 frames of 880
-tokens), 32 history + 4 current key frames, budget 8 blocks, block-causal.
+A step is one RCSA layer call: pooled-QK block selection + per-block int8
+quantisation (one fused pass over Q/K) and the tcgen05 block-sparse
+attention, on H=24 heads x d128, 3520 queries (4 frames of 880 tokens), 32
+history + 4 current key frames, budget 8 blocks, block-causal.
 
 Usage::
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--policy auto|int8|bf16] [--shard rollout|head]
+                    [--policy auto|int8|bf16] [--shard head|rollout]
 
-Multi-GPU (torchrun, one process per GPU): ``--shard rollout`` (default) runs
-one independent rollout per GPU with no collective (weak scaling);
-``--shard head`` splits the 24 heads of one call across the GPUs and
-all-gathers the head outputs over NCCL (strong scaling).  ``value`` is
-microseconds per RCSA layer call for the whole job (time of the slowest rank
-divided by the layer calls all ranks completed).
+Multi-GPU (torchrun, one process per GPU): ``--shard head`` (default) splits
+the 24 heads of every call across the GPUs (24/12/6/3 per GPU at 1/2/4/8) and
+all-gathers the bf16 head outputs over NCCL inside the timed step (strong
+scaling: ``value`` is microseconds per layer call of the whole job, the
+slowest rank's time); the same run also reports rollout sharding (every GPU
+runs its own full call, no collective) under ``rollout``.  ``--shard
+rollout`` makes that the headline instead.  ``--impl reference`` times the
+reference's PyTorch path (a CPU port, ``oracle/cpu_reference.py``) on all
+host cores, all 24 heads per step, on rank 0.
 """
 
 from __future__ import annotations
@@ -39,10 +42,9 @@ BLOCK, BUDGET, HEADS, D = 880, 8, 24, 128
 # under the auto policy the code pass for the blocks int8 query blocks read
 KERNELS_PER_CALL = {"auto": 4, "int8": 3, "bf16": 3}
 HIST, CUR = 32, 4
-# DRAM bytes (read + write) of one attention launch on the full config-2
-# workload (auto policy), from the single-pass ncu capture in
-# profiles/rcsa_attention_config2_traffic.md; other policies have no capture.
-ATTN_TRAFFIC_BYTES = {"auto": 712.4e6}
+# Algorithmic work of one config-2 attention call (every score pair of the
+# budget-8 block-causal selection, 24 heads): int8 QK^T ops and bf16 P.V FLOP.
+ALG_OPS_INT8 = ALG_OPS_BF16 = 199.83e9
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -123,8 +125,34 @@ def attention_ops(counts, qk_mode, block):
     return float((qk * m).sum()), float((qk * (1 - m)).sum() + pv.sum())
 
 
+CONFIG2_WORKLOAD = ("config2: RCSA layer (select+int8 quant+block-sparse attention), H=24 d128, "
+                    "Lq=3520 (4x880), 32+4 key frames, budget 8, block-causal")
+
+
+def layer_config(world: int, shard: str) -> dict:
+    """The ``config`` of both arms' lines (identical for the same N and shard)."""
+    return {"workload": CONFIG2_WORKLOAD, "parallelism": f"{shard}-sharded x{world}",
+            "l2": "inputs larger than L2 (Q+K 216 MB read per call by the selection pass)"}
+
+
+def _cpu_layer_us(w, threads: int, repeats: int) -> float:
+    """Median wall time of the reference's CPU path over all 24 heads."""
+    import torch
+
+    from oracle import cpu_reference
+
+    torch.set_num_threads(threads)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        cpu_reference.rcsa_layer(w.q, w.k, w.v, BLOCK, BUDGET)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6
+
+
 def run_reference(args, world, rank):
-    """CPU reference arm: the reference's PyTorch path on the host cores."""
+    """CPU reference arm: the reference's PyTorch path (selection + explicit
+    softmax attention, all 24 heads per step) on all host cores, rank 0."""
     import torch
 
     from cast_b200 import workloads
@@ -135,49 +163,76 @@ def run_reference(args, world, rank):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     w = workloads.config2()
-    sample_heads = 2
-    heads_list = [list(range(i, i + sample_heads)) for i in range(0, HEADS, sample_heads)]
-    for i in range(args.warmup):
-        cpu_reference.rcsa_layer(w.q, w.k, w.v, BLOCK, BUDGET, heads=heads_list[i % len(heads_list)])
-    times = []
-    for i in range(args.steps):
-        t0 = time.perf_counter()
-        cpu_reference.rcsa_layer(w.q, w.k, w.v, BLOCK, BUDGET, heads=heads_list[i % len(heads_list)])
-        times.append(time.perf_counter() - t0)
-    per_call_us = statistics.mean(times) * HEADS / sample_heads * 1e6
+    for _ in range(args.warmup):
+        cpu_reference.rcsa_layer(w.q, w.k, w.v, BLOCK, BUDGET)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference.rcsa_layer(w.q, w.k, w.v, BLOCK, BUDGET)
+    per_call_us = (time.perf_counter() - t0) / args.steps * 1e6
     line = {
         "impl": "reference", "metric": METRIC, "value": per_call_us, "unit": "us/call",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per_call_us / 1000.0, "higher_is_better": False, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config 2)",
-        "config": {"workload": "config2: RCSA layer, H=24 d128, Lq=3520 (4x880), 32+4 key frames, budget 8",
-                   "sample": f"{sample_heads} of {HEADS} heads per step, scaled x{HEADS // sample_heads}"},
+        "ms_per_step": per_call_us / 1000.0, "higher_is_better": False,
+        "scaling": "strong" if args.shard == "head" else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config 2: N(0,1)*U(0.5,2) per head)",
+        "config": layer_config(world, args.shard),
         "cpu_baseline": {"value": per_call_us, "unit": "us/call", "cores": threads, "kind": "port",
-                         "sample": f"{sample_heads} heads per step (selection + attention), scaled to 24"},
+                         "sample": f"the whole config-2 call (all 24 heads), {args.steps} timed steps"},
         "e2e": {"value": per_call_us, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "timing": "host wall clock over the timed steps (the reference path runs on the CPU)",
     }
     print(json.dumps(line))
     return 0
 
 
 def cpu_baseline_sample():
+    """The reference's CPU path on this host: the whole config-2 call on all
+    cores (median of 3) and on one core (one run), and the config-4 PAR
+    correction restated in numpy (``oracle/par.py``) on all cores."""
     import torch
 
     from cast_b200 import workloads
-    from oracle import cpu_reference
+    from oracle import par as opar
 
     threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
     w = workloads.config2()
-    cpu_reference.rcsa_layer(w.q, w.k, w.v, BLOCK, BUDGET, heads=[0])
-    times = []
-    for i in range(3):
-        t0 = time.perf_counter()
-        cpu_reference.rcsa_layer(w.q, w.k, w.v, BLOCK, BUDGET, heads=[2 * i + 1, 2 * i + 2])
-        times.append(time.perf_counter() - t0)
-    per_call = statistics.median(times) * HEADS / 2
-    return {"value": per_call * 1e6, "unit": "us/call", "cores": threads, "kind": "port",
-            "sample": "2 of 24 heads (selection + explicit-softmax attention), median of 3, x12"}
+    _cpu_layer_us(w, threads, 1)  # warm-up
+    all_cores = _cpu_layer_us(w, threads, 3)
+    one_core = _cpu_layer_us(w, 1, 1)
+    torch.set_num_threads(threads)
+    p4 = workloads.config4()
+    full = p4.full_residual.float().numpy()
+    act = p4.active_residual.float().numpy()
+    opar.correct(full, act, p4.active_frames, p4.memory_length, 22, 40)
+    t0 = time.perf_counter()
+    opar.correct(full, act, p4.active_frames, p4.memory_length, 22, 40)
+    par_us = (time.perf_counter() - t0) * 1e6
+    return {"value": all_cores, "unit": "us/call", "cores": threads, "kind": "port",
+            "sample": "the whole config-2 call (all 24 heads: selection + explicit-softmax attention), "
+                      "median of 3",
+            "one_core_us": one_core, "one_core_sample": "the same call on 1 thread, one run",
+            "par_config4_us": par_us,
+            "par_config4_sample": "config-4 FC-PASM correct() restated in numpy, one run, all cores"}
+
+
+def attention_traffic(policy: str, heads: int, config: int):
+    """DRAM bytes per attention launch from the committed ncu capture of the
+    same workload, if that capture was taken of the current kernel source."""
+    import hashlib
+
+    path = os.path.join(ROOT, "profiles", "attention_traffic.json")
+    key = f"config{config}_{policy}_{heads}heads"
+    if not os.path.exists(path):
+        return None, "no capture"
+    with open(path) as fh:
+        rec = json.load(fh).get(key)
+    if rec is None:
+        return None, f"no capture of {key}"
+    with open(os.path.join(ROOT, "cast_b200", "csrc", "attention.cuh"), "rb") as fh:
+        sha = hashlib.sha256(fh.read()).hexdigest()
+    if sha != rec.get("attention_cuh_sha256"):
+        return None, f"capture of {key} predates the current kernel source"
+    return float(rec["dram_bytes_per_launch"]), f"ncu capture of {key}: {rec['command']}"
 
 
 def _graph_us(fn, n, dev):
@@ -251,65 +306,73 @@ def compact_measure(dev, peaks, steps):
 
 
 def swap_measure(dev, steps, cpu_leg=True):
-    """The FC-PASM swap router's device call (``cast_swap_route``: proxies,
-    one swap round, the closing objective pass) on a 24-head layer of pooled
+    """The FC-PASM swap router's whole ``refine`` on a 24-head layer of pooled
     blocks: 32 memory blocks plus 4 current cells of 2x4 blocks, 64 keys,
-    D=128, 16 selected per row, the factory's knobs (one round, one swap,
-    same-bank).  Graph replay of the raw C-ABI call (the Python ``refine``
-    adds its host gates and one stats read); beside it the CPU oracle on the
-    same call, one core."""
+    D=128, 16 selected per row, a published FC sketch, the factory's knobs
+    (one round, one swap, same-bank, transport gate 0.5).  ``device_us``: the
+    call's kernels (objective + gates: 2 launches; proxies, one round, the
+    closing pass: 3) replayed from a CUDA graph; ``refine_us``: the Python
+    call end to end (host gates, the launches, its one stats read, the
+    record), wall clock.  Beside it the CPU oracle on the same call."""
     import time
 
     import torch
 
-    from cast_b200 import _lib, swap_router, workloads
+    from cast_b200 import swap_router, workloads
 
     w = workloads.swap_case(heads=24, memory_blocks=32, cells=4, spatial_shape=(2, 4), dim=128,
                             width=16, exact_frames=(0, 3), transport=True, seed=21)
-    B, H, Q, K = w.score.shape
-    D, S, M = w.pooled_value.shape[-1], w.selected.shape[-1], w.memory_blocks
-    coef, hess, _ = swap_router.quadratic_terms(
-        temporal_cells=4, spatial=8, exact_frames=(0, 3), temporal_group_size=1, current_boundary=4,
-        transport=w.transport, lambda_anchor=1.0, lambda_reconstruction=1.0, device=dev)
-    lib = _lib.load()
-    nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, D, S, M, 2, 0, 16)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    stats = torch.empty(5, dtype=torch.float64, device=dev)
-    sc, pv, cn = w.score.to(dev), w.pooled_value.to(dev), w.counts.to(dev)
-    lo, sel = w.local.to(torch.uint8).to(dev), w.selected.to(dev)
-
-    def call():
-        _lib.call("cast_swap_route", sc.data_ptr(), pv.data_ptr(), sel.data_ptr(), cn.data_ptr(),
-                  lo.data_ptr(), None, coef.data_ptr(), hess.data_ptr(), B, H, Q, K, D, S, M, 2, 1, 0.1,
-                  16, 1, 0, 1, stats.data_ptr(), ws.data_ptr(), nbytes,
-                  torch.cuda.current_stream(dev).cuda_stream)
-
-    us = _graph_us(call, max(10, steps), dev)
-    line = {"us_per_call": us, "launches_per_call": 3,
+    M = w.memory_blocks
+    for e in w.transport["pairs"].values():
+        e["theta"], e["affinity"] = e["theta"].to(dev), e["affinity"].to(dev)
+        e["mean_affinity"] = e["mean_affinity"].to(dev)
+    router = swap_router.FCPASMLocalCoordinateSwapRouter(swap_router.FCPASMSwapRoutingConfig(
+        num_swap_rounds=1, swap_eps=0.10, max_swaps_per_call=1, same_bank_only=True,
+        require_fc_transport=True, min_transport_affinity=0.5, active_layers=(22, 26)))
+    sel = w.selected.to(dev)
+    kw = dict(score=w.score.to(dev), pooled_value=w.pooled_value.to(dev), selected=sel,
+              counts=w.counts.to(dev), local=w.local.to(dev), memory_blocks=M, spatial_shape=(2, 4),
+              exact_current_frames=(0, 3), temporal_group_size=1, current_boundary=4,
+              transport=w.transport, layer_index=22)
+    _, rec = router.refine(**kw)
+    us = _graph_us(lambda: router.enqueue(**kw), max(10, steps), dev)
+    n = max(10, steps)
+    router.refine(**kw)
+    t0 = time.perf_counter()
+    for _ in range(n):
+        router.refine(**kw)
+    refine_us = (time.perf_counter() - t0) / n * 1e6
+    line = {"device_us": us, "refine_us": refine_us, "launches_per_call": 5,
+            "status": rec["status"], "swaps": rec["swap_count"],
             "workload": "24 heads, 32 memory + 32 current pooled blocks, D=128, 16 selected, "
                         "FC transport, 1 round / 1 swap / same-bank",
-            "note": "latency-bound (a few hundred KB touched); CUDA graph replay, device time"}
+            "note": "device_us: CUDA graph replay of the call's 5 kernels; refine_us: the whole Python "
+                    "refine, wall clock, one host synchronisation per call"}
     if cpu_leg:
         from oracle import swap_router as osr
+        tr_cpu = workloads.swap_case(heads=24, memory_blocks=32, cells=4, spatial_shape=(2, 4), dim=128,
+                                     width=16, exact_frames=(0, 3), transport=True, seed=21)
         ops = {}
 
         def op(pair, x):
             key = (pair, round(float(x), 12))
             if key not in ops:
-                ops[key] = swap_router.transport_operator(w.transport, pair, spatial_shape=(2, 4),
+                ops[key] = swap_router.transport_operator(tr_cpu.transport, pair, spatial_shape=(2, 4),
                                                           exponent=x, device="cpu")[0].numpy()
             return ops[key]
 
-        args = dict(score=w.score.numpy(), pooled_value=w.pooled_value.numpy(),
-                    selected=w.selected.numpy(), counts=w.counts.numpy(), local=w.local.numpy(),
-                    memory_blocks=M, spatial=8, exact_frames=(0, 3), group=1, boundary=4,
-                    config=osr.SwapConfig(num_swap_rounds=1, swap_eps=0.1, max_swaps_per_call=1,
-                                          same_bank_only=True), operator=op)
+        args = dict(score=tr_cpu.score.numpy(), pooled_value=tr_cpu.pooled_value.numpy(),
+                    selected=tr_cpu.selected.numpy(), counts=tr_cpu.counts.numpy(),
+                    local=tr_cpu.local.numpy(), memory_blocks=M, spatial=8, exact_frames=(0, 3), group=1,
+                    boundary=4, config=osr.SwapConfig(num_swap_rounds=1, swap_eps=0.1, max_swaps_per_call=1,
+                                                      same_bank_only=True), operator=op)
         osr.refine(**args)
+        ops.clear()
         t0 = time.perf_counter()
         osr.refine(**args)
         line["cpu_oracle_us"] = (time.perf_counter() - t0) * 1e6
-        line["cpu_oracle"] = "numpy restatement (oracle/swap_router.py), same call, host cores"
+        line["cpu_oracle"] = ("numpy restatement (oracle/swap_router.py) with the torch transport operators, "
+                              "same call, host cores")
     return line
 
 
@@ -371,9 +434,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--policy", default="auto", choices=["auto", "int8", "bf16"])
-    ap.add_argument("--shard", default="rollout", choices=["rollout", "head"])
+    ap.add_argument("--shard", default="head", choices=["head", "rollout"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the PAR / compact / swap-router lines (profiling runs)")
     ap.add_argument("--heads", type=int, default=HEADS,
                     help="heads of the config-2 layer (smaller values only for profiling captures)")
     ap.add_argument("--config", type=int, default=2, choices=[2, 3],
@@ -405,47 +470,12 @@ def main():
     if args.sweep:
         return run_sweep(args, world, rank, local, dev, peaks, peak_src)
 
-    head_lo, head_hi = 0, args.heads
-    if args.shard == "head" and world > 1:
-        head_lo, head_hi = cdist.head_range(args.heads, world, rank)
     if args.config == 3:
         w = workloads.config3(heads=args.heads)
     else:
-        w = workloads.config2(heads=args.heads, seed=1 + (rank if args.shard == "rollout" else 0))
+        w = workloads.config2(heads=args.heads, seed=1)
     budget = w.budget
-    q_h = w.q[:, head_lo:head_hi].contiguous()
-    k_h = w.k[:, head_lo:head_hi].contiguous()
-    v_h = w.v[:, head_lo:head_hi].contiguous()
-    q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
-    gathered = None
-    if args.shard == "head" and world > 1:
-        gathered = torch.empty(world * q.shape[0], *q.shape[1:], dtype=q.dtype, device=dev)
-
     stream = torch.cuda.current_stream(dev)
-    b_, h_, lq_, d_ = q.shape
-    plan = rcsa.RCSAPlan(b_, h_, lq_, k.shape[2], d_, block_size=BLOCK, budget=budget,
-                         policy=args.policy, device=dev)
-
-    # eager warm-up through the plan (no allocation per call)
-    for _ in range(args.warmup):
-        plan(q, k, v)
-    torch.cuda.synchronize()
-    # host cost of an eager call (diagnostic: the timed loop replays a graph)
-    h0 = time.perf_counter()
-    for _ in range(5):
-        plan(q, k, v)
-    host_us = (time.perf_counter() - h0) / 5 * 1e6
-    torch.cuda.synchronize()
-
-    # One RCSA layer call = 3 kernels (pool+quant, select, attention), captured
-    # once into a CUDA graph and replayed; the graph recomputes everything from
-    # the input buffers on every replay.
-    g_all = plan.capture(q, k, v, "all")
-    g_att = plan.capture(q, k, v, "attend")
-    g_sel = plan.capture(q, k, v, "select")
-    for _ in range(3):
-        g_all.replay()
-    torch.cuda.synchronize()
 
     def timed(fn, n):
         if world > 1:
@@ -462,28 +492,82 @@ def main():
             dist.barrier()
         return a.elapsed_time(b)
 
-    def full_step():
+    def setup(lo, hi):
+        q_h, k_h, v_h = (t[:, lo:hi].contiguous() for t in (w.q, w.k, w.v))
+        q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
+        b_, h_, lq_, d_ = q.shape
+        plan = rcsa.RCSAPlan(b_, h_, lq_, k.shape[2], d_, block_size=BLOCK, budget=budget,
+                             policy=args.policy, device=dev)
+        for _ in range(args.warmup):  # eager warm-up (the plan allocates nothing per call)
+            plan(q, k, v)
+        torch.cuda.synchronize()
+        return (q_h, k_h, v_h), (q, k, v), plan
+
+    # ---- the headline: this rank's share of one call (all heads, or H/N heads
+    # plus the all-gather of the head outputs)
+    head = args.shard == "head"
+    lo, hi = cdist.head_range(args.heads, world, rank) if head else (0, args.heads)
+    host_in, (q, k, v), plan = setup(lo, hi)
+    h0 = time.perf_counter()
+    for _ in range(5):
+        plan(q, k, v)
+    host_us = (time.perf_counter() - h0) / 5 * 1e6
+    torch.cuda.synchronize()
+    # one call = the plan's kernels captured once in a CUDA graph and replayed;
+    # every replay recomputes everything from the input buffers
+    g_all = plan.capture(q, k, v, "all")
+    g_att = plan.capture(q, k, v, "attend")
+    g_sel = plan.capture(q, k, v, "select")
+    gathered = None
+    if head and world > 1:
+        gathered = torch.empty((world * q.shape[0], *q.shape[1:]), dtype=q.dtype, device=dev)
+
+    def step():
         g_all.replay()
         if gathered is not None:
-            cdist.gather_heads(plan.out, world, gathered=gathered)
+            dist.all_gather_into_tensor(gathered, plan.out)
 
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if gathered is not None:  # the gathered heads are the single-call output, in head order
+        g_all.replay()
+        dist.all_gather_into_tensor(gathered, plan.out)
+        torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    total_ms = timed(full_step, args.steps)
+    total_ms = timed(step, args.steps)
+    clocks = sampler.stop()
     att_ms = timed(g_att.replay, args.steps) / args.steps
     sel_ms = timed(g_sel.replay, args.steps) / args.steps
+    gather_ms = 0.0
+    if gathered is not None:
+        gather_ms = timed(lambda: dist.all_gather_into_tensor(gathered, plan.out), args.steps) / args.steps
     sel = plan.selection()
+    counts_cpu = sel.counts.cpu()
+    mode_cpu = sel.qk_mode.cpu() if sel.qk_mode is not None else None
+
+    # ---- rollout sharding at the same N: every GPU runs its own full call
+    rollout_ms = None
+    if world > 1 and head:
+        _, (rq, rk, rv), rplan = setup(0, args.heads)
+        g_roll = rplan.capture(rq, rk, rv, "all")
+        for _ in range(3):
+            g_roll.replay()
+        rollout_ms = timed(g_roll.replay, args.steps) / args.steps
+        del g_roll, rplan, rq, rk, rv
 
     # ---- end to end through the public API with host buffers: pinned host
-    # inputs copied in, the plan call, the output copied back, every step.
+    # inputs copied in, the plan call, the output copied back and checked,
+    # every step
     e2e = None
     if not args.no_e2e:
-        hq, hk, hv = (t.pin_memory() for t in (q_h, k_h, v_h))
-        hout = torch.empty(q_h.shape, dtype=q_h.dtype).pin_memory()
-        # the host-input plan: head groups whose copies overlap the compute
+        hq, hk, hv = (t.pin_memory() for t in host_in)
+        hout = torch.empty(hq.shape, dtype=hq.dtype).pin_memory()
+        b_, h_, lq_, d_ = q.shape
         host_plan = rcsa.RCSAHostPlan(b_, h_, lq_, k.shape[2], d_, block_size=BLOCK, budget=budget,
-                                      policy=args.policy, groups=4, device=dev)
+                                      policy=args.policy, groups=min(4, h_), device=dev)
         e_steps = max(3, min(10, args.steps))
 
         def e2e_step():
@@ -492,44 +576,49 @@ def main():
         for _ in range(2):
             e2e_step()
         e2e_ms = timed(e2e_step, e_steps) / e_steps
-        e2e = {"ms": e2e_ms, "h2d": sum(t.numel() * t.element_size() for t in (hq, hk, hv)),
-               "d2h": hout.numel() * hout.element_size()}
-    clocks = sampler.stop()
-    par_line = par_measure(dev, peaks, peak_src, args.steps) if rank == 0 else None
-    compact_line = compact_measure(dev, peaks, args.steps) if rank == 0 else None
-    swap_line = swap_measure(dev, args.steps, not args.no_cpu_baseline) if rank == 0 else None
+        # bytes of the whole job: every rank copies its heads in and out
+        e2e = {"ms": e2e_ms, "h2d": world * sum(t.numel() * t.element_size() for t in (hq, hk, hv)),
+               "d2h": world * hout.numel() * hout.element_size()}
+    extras = rank == 0 and world == 1 and not args.no_extras
+    par_line = par_measure(dev, peaks, peak_src, args.steps) if extras else None
+    compact_line = compact_measure(dev, peaks, args.steps) if extras else None
+    swap_line = swap_measure(dev, args.steps, not args.no_cpu_baseline) if extras else None
 
     # ---- max over ranks
-    vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms], dtype=torch.float64, device=dev)
+    vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms, gather_ms,
+                         rollout_ms or 0.0], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, att_ms, e2e_ms, sel_ms = (float(x) for x in vals.tolist())
+    total_ms, att_ms, e2e_ms, sel_ms, gather_ms, rollout_ms = (float(x) for x in vals.tolist())
     ms_per_step = total_ms / args.steps
-    calls_per_step = world if (args.shard == "rollout" and world > 1) else 1
-    value_us = ms_per_step * 1000.0 / calls_per_step
+    value_us = ms_per_step * 1000.0
 
-    i8_ops, bf_ops = attention_ops(sel.counts.cpu(), sel.qk_mode.cpu() if sel.qk_mode is not None else None, BLOCK)
+    # ---- roofline of the attention kernel on this rank's heads
+    i8_ops, bf_ops = attention_ops(counts_cpu, mode_cpu, BLOCK)
     p_bf16 = peaks["bf16_tflops"] * 1e12
     p_i8 = 2.0 * p_bf16
-    t_roof = i8_ops / p_i8 + bf_ops / p_bf16
-    achieved = (i8_ops + bf_ops) / (att_ms * 1e-3) / 1e12
-    peak_eff = (i8_ops + bf_ops) / t_roof / 1e12
-    int8_frac = float(sel.qk_mode.float().mean()) if sel.qk_mode is not None else 0.0
+    share = (hi - lo) / HEADS
+    alg_i8, alg_bf = ALG_OPS_INT8 * share, ALG_OPS_BF16 * share
+    t_alg = alg_i8 / p_i8 + alg_bf / p_bf16          # the fixed algorithmic roofline
+    t_ww = i8_ops / p_i8 + bf_ops / p_bf16           # the work this launch chose
+    att_s = att_ms * 1e-3
+    traffic, traffic_src = attention_traffic(args.policy, hi - lo, args.config)
+    int8_frac = float(mode_cpu.float().mean()) if mode_cpu is not None else 0.0
     sq_read = (q.numel() + k.numel()) * 2
     if args.policy == "auto" and sel.qk_mode is not None:
         # codes only for the blocks the int8 query blocks read, which the code
         # pass reads again (bf16) and writes (int8)
-        mode, idx, cnt = sel.qk_mode.cpu(), sel.indices.cpu(), sel.counts.cpu()
+        idx = sel.indices.cpu()
         coded = 0
-        for b in range(mode.shape[0]):
-            for h in range(mode.shape[1]):
+        for b in range(mode_cpu.shape[0]):
+            for h in range(mode_cpu.shape[1]):
                 kset = set()
-                for i in range(mode.shape[2]):
-                    if mode[b, h, i]:
+                for i in range(mode_cpu.shape[2]):
+                    if mode_cpu[b, h, i]:
                         coded += 1
-                        kset.update(int(x) for x in idx[b, h, i, :cnt[b, h, i]])
+                        kset.update(int(x) for x in idx[b, h, i, :counts_cpu[b, h, i]])
                 coded += len(kset)
-        sq_bytes = sq_read + coded * BLOCK * d_ * 3
+        sq_bytes = sq_read + coded * BLOCK * q.shape[-1] * 3
     else:
         sq_bytes = sq_read + (q.numel() + k.numel())  # bf16 read + int8 codes written
 
@@ -540,22 +629,14 @@ def main():
     line = {
         "metric": METRIC, "value": value_us, "unit": "us/call", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": False,
-        "scaling": "weak" if args.shard == "rollout" else "strong",
+        "higher_is_better": False, "scaling": "strong" if head else "weak",
         "vs_baseline": None, "dtype": "int8+bf16" if args.policy != "bf16" else "bf16",
         "data": ("synthetic (seeded config 2: N(0,1)*U(0.5,2) per head)" if args.config == 2 else
                  "synthetic (seeded config 3: N(0,1)*U(0.5,2) per head, linear drift over history frames)"),
-        "config": {
-            "workload": ("config2: RCSA layer (select+int8 quant+block-sparse attention), "
-                         "H=24 d128, Lq=3520 (4x880), 32+4 key frames, budget 8, block-causal"
-                         if args.config == 2 else
-                         "config3: RCSA layer, H=24 d128, 128 history frames + 2 anchors, "
-                         "anchor-only queries Lq=1760 (2x880), budget 16, block-causal"),
-            "parallelism": f"{args.shard}-sharded x{world}",
-            "policy": args.policy, "int8_row_fraction": int8_frac,
-            "heads_per_gpu": head_hi - head_lo,
-            "l2": f"inputs larger than L2 (Q+K {sq_read / 1e6:.0f} MB read per step by the selection pass)",
-        },
+        "config": (layer_config(world, args.shard) if args.config == 2 and args.heads == HEADS else
+                   {"workload": f"config{args.config}, {args.heads} heads",
+                    "parallelism": f"{args.shard}-sharded x{world}"}),
+        "details": {"policy": args.policy, "int8_row_fraction": int8_frac, "heads_per_gpu": hi - lo},
         "attention_us": att_ms * 1000.0,
         "select_quant_us": sel_ms * 1000.0,
         "select_quant_roofline": {
@@ -566,16 +647,20 @@ def main():
                      "again); pooled/RMS/scales ignored"),
         },
         "host_enqueue_us_eager": host_us,
-        "timing": (f"CUDA graph replay of the {KERNELS_PER_CALL[args.policy]}-kernel layer call; "
-                   "events on the replay stream"),
+        "timing": (f"CUDA graph replay of the {KERNELS_PER_CALL[args.policy]}-kernel layer call"
+                   + (" + NCCL all-gather of the head outputs" if gathered is not None else "")
+                   + "; CUDA events on the launching stream, max over ranks"),
         "roofline": {
-            "bound": "tensor", "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
-            "frac": achieved / peak_eff,
-            "traffic": ATTN_TRAFFIC_BYTES.get(args.policy) if (args.heads == HEADS and args.config == 2) else None,
-            "note": (f"attention kernel; peak = work-weighted harmonic of bf16 {peaks['bf16_tflops']} "
-                     f"TFLOP/s ({peak_src} cuBLAS burst) and int8 = 2x bf16 (no measured int8 peak); "
-                     "traffic = ncu DRAM bytes per launch; "
-                     f"ops/launch int8 {i8_ops:.4g} bf16 {bf_ops:.4g}"),
+            "bound": "tensor", "achieved": (alg_i8 + alg_bf) / att_s / 1e12,
+            "peak": (alg_i8 + alg_bf) / t_alg / 1e12, "unit": "TFLOP/s", "frac": t_alg / att_s,
+            "traffic": traffic,
+            "note": (f"attention kernel, this GPU's {hi - lo} heads; algorithmic work of the call "
+                     f"({alg_i8:.4g} int8 QK^T ops + {alg_bf:.4g} bf16 P.V FLOP, all score pairs of the "
+                     f"selection) at int8 = 2x bf16 and bf16 {peaks['bf16_tflops']} TFLOP/s ({peak_src} "
+                     f"cuBLAS burst; no measured int8 peak); traffic: {traffic_src}"),
+            "work_weighted": {"frac": t_ww / att_s, "ops_int8": i8_ops, "ops_bf16": bf_ops,
+                              "note": "the same kernel against the work it chose (int8 QK^T only for "
+                                      "the auto policy's int8 query blocks)"},
         },
         "par": par_line,
         "compact_and_lift": compact_line,
@@ -583,10 +668,18 @@ def main():
         "gpu_launches": KERNELS_PER_CALL[args.policy] * args.steps,
         "clocks": clocks,
     }
+    if gathered is not None:
+        line["all_gather_us"] = gather_ms * 1000.0
+        line["rollout"] = {"value": rollout_ms * 1000.0 / world, "unit": "us/call",
+                           "note": f"rollout sharding: each of {world} GPUs runs its own full call, no "
+                                   "collective; value = slowest GPU's call time / N"}
     if e2e:
-        line["e2e"] = {"value": e2e_ms * 1000.0 / calls_per_step, "unit": "us/call",
-                       "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]}
-    if not args.no_cpu_baseline and world == 1 and args.config == 2:
+        line["e2e"] = {"value": e2e_ms * 1000.0, "unit": "us/call",
+                       "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                       "path": "RCSAHostPlan: pinned host q/k/v in, head-group copies overlapped with the "
+                               "compute, output copied back and the device error word checked"
+                               + (" (each rank its own heads, in parallel)" if world > 1 else "")}
+    if not args.no_cpu_baseline and world == 1 and args.config == 2 and args.heads == HEADS:
         line["cpu_baseline"] = cpu_baseline_sample()
     print(json.dumps(line))
     return 0

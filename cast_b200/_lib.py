@@ -65,8 +65,15 @@ SIGNATURES = {
     ),
     "cast_swap_route": (
         c_int,
-        [c_void_p] * 8 + [c_int] * 9 + [c_float, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+        [c_void_p] * 9 + [c_int] * 9 + [c_float, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                          c_size_t, c_void_p],
+    ),
+    "cast_swap_objective": (
+        c_int,
+        [c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_int, c_float, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p],
     ),
     "cast_swap_route_workspace_bytes": (c_size_t, [c_int] * 10),
     "cast_par_fcpasm": (

@@ -800,9 +800,89 @@ extern "C" size_t cast_swap_route_workspace_bytes(int B, int H, int Q, int K, in
   return swap_layout(p).total;
 }
 
+extern "C" int cast_swap_objective(int n, int tiles, int bins, const float *u_re, const float *u_im,
+                                   const float *v_re, const float *v_im, int cells,
+                                   const float *cell_anchor_count, int n_targets,
+                                   const float *const *target_theta,
+                                   const float *const *target_affinity, const double *target_alpha,
+                                   const int32_t *target_cells, int n_pairs,
+                                   const float *const *pair_mean, const float *pair_mean_value,
+                                   const int32_t *pair_cells, const int32_t *pair_matching,
+                                   int require_fc_transport, float min_transport_affinity,
+                                   float min_pair_transport_affinity, float lambda_anchor,
+                                   float lambda_reconstruction, float *coefficient, float *hessian,
+                                   uint8_t *row_gate, int32_t *gate, double *stats, float *operators,
+                                   cast_stream_t stream) {
+  using castk::kSwapObjMaxBins;
+  using castk::kSwapObjMaxCells;
+  using castk::kSwapObjMaxPairs;
+  using castk::kSwapObjMaxTargets;
+  if (!cell_anchor_count || !coefficient || !hessian || !gate || !stats || !operators)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "cell counts, coefficient, hessian, gate, stats and "
+                                           "operators are required");
+  if (n <= 0 || cells <= 0 || cells > kSwapObjMaxCells || n_targets <= 0 ||
+      n_targets > kSwapObjMaxTargets || n_pairs < 0 || n_pairs > kSwapObjMaxPairs)
+    return fail(CAST_ERR_UNSUPPORTED, "objective sizes (n=%d cells=%d targets=%d pairs=%d; at most "
+                                      "%d cells, %d targets, %d pairs)", n, cells, n_targets, n_pairs,
+                kSwapObjMaxCells, kSwapObjMaxTargets, kSwapObjMaxPairs);
+  if ((long long)cells * n > 4096) return fail(CAST_ERR_UNSUPPORTED, "more than 4096 current rows");
+  if (n_targets && (!target_theta || !target_affinity || !target_alpha || !target_cells))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "target tables are required");
+  if (n_pairs && (!pair_mean || !pair_mean_value || !pair_cells || !pair_matching))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "pair tables are required");
+  if (min_pair_transport_affinity > 0.f && !row_gate)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "the pair gate needs row_gate");
+  castk::SwapObjParams p;
+  memset(&p, 0, sizeof(p));
+  bool sketched = false;
+  for (int t = 0; t < n_targets; ++t) {
+    const int lc = target_cells[2 * t], rc = target_cells[2 * t + 1];
+    if (lc < 0 || lc >= cells || rc < 0 || rc >= cells)
+      return fail(CAST_ERR_INVALID_ARGUMENT, "target %d cells (%d, %d) outside [0,%d)", t, lc, rc, cells);
+    if ((target_theta[t] == nullptr) != (target_affinity[t] == nullptr))
+      return fail(CAST_ERR_INVALID_ARGUMENT, "target %d: theta and affinity go together", t);
+    const double a = target_alpha[t];
+    p.t[t] = castk::SwapObjTarget{target_theta[t], target_affinity[t], (float)a, (float)(-(1.0 - a)),
+                                  (float)(1.0 - a), (float)a, lc, rc};
+    sketched |= target_theta[t] != nullptr;
+  }
+  if (sketched) {
+    if (!u_re || !u_im || !v_re || !v_im || tiles <= 0 || bins <= 0 || tiles * bins > kSwapObjMaxBins)
+      return fail(CAST_ERR_INVALID_ARGUMENT, "sketched targets need the transport basis "
+                                             "(tiles x bins <= %d)", kSwapObjMaxBins);
+  }
+  for (int i = 0; i < n_pairs; ++i) {
+    const int lo = pair_cells[2 * i], hi = pair_cells[2 * i + 1];
+    if (lo < 0 || hi < lo || hi >= cells)
+      return fail(CAST_ERR_INVALID_ARGUMENT, "pair %d cells [%d, %d] outside [0,%d)", i, lo, hi, cells);
+    p.pr[i] = castk::SwapObjPair{pair_mean[i], pair_mean_value[i], lo, hi, pair_matching[i] ? 1 : 0};
+  }
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  p.n = n, p.tiles = tiles, p.bins = bins, p.cells = cells, p.R = cells * n, p.T = n_targets;
+  p.n_pairs = n_pairs;
+  p.u_re = u_re, p.u_im = u_im, p.v_re = v_re, p.v_im = v_im;
+  p.lam_a = lambda_anchor, p.lam_r = lambda_reconstruction;
+  p.min_match = min_transport_affinity, p.min_pair = min_pair_transport_affinity;
+  p.require_fc = require_fc_transport ? 1 : 0;
+  p.pair_gate = min_pair_transport_affinity > 0.f ? 1 : 0;
+  for (int c = 0; c < cells; ++c) p.cell_count[c] = cell_anchor_count[c];
+  p.ops = operators, p.coef = coefficient, p.hess = hessian, p.row_gate = row_gate;
+  p.gate = gate, p.stats = stats;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 g1(2 * n_targets, ceil_div(n * n, castk::kSwapObjThreads));
+  castk::swap_operator_kernel<<<g1, castk::kSwapObjThreads, 0, s>>>(p);
+  CAST_CUDA_TRY(cudaGetLastError());
+  const int g2 = std::max(1, std::min(1024, ceil_div(p.R * p.R + p.R, castk::kSwapObjThreads)));
+  castk::swap_hessian_kernel<<<g2, castk::kSwapObjThreads, 0, s>>>(p);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
 extern "C" int cast_swap_route(const float *score, const float *pooled_value, long long *selected,
                                const long long *counts, const uint8_t *local, const uint8_t *row_gate,
-                               const float *coefficient, const float *hessian, int B, int H, int Q,
+                               const int32_t *gate, const float *coefficient, const float *hessian,
+                               int B, int H, int Q,
                                int K, int D, int S, int memory_blocks, int candidate_multiplier,
                                int num_swap_rounds, float swap_eps, int sketch_groups,
                                int max_swaps_per_call, int historical_only, int same_bank_only,
@@ -851,25 +931,25 @@ extern "C" int cast_swap_route(const float *score, const float *pooled_value, lo
   const int rows = B * H * p.R;
   CAST_CUDA_TRY(cudaMemsetAsync(ctl, 0, sizeof(castk::SwapCtl), s));
   castk::swap_proxy_kernel<<<rows, castk::kSwapProxyThreads, sm1, s>>>(
-      score, pooled_value, selected, counts, local, p, 1e-6f, cand, proxy, err, limit, ctl);
+      score, pooled_value, selected, counts, local, p, 1e-6f, cand, proxy, err, limit, ctl, gate);
   CAST_CUDA_TRY(cudaGetLastError());
   // rounds: the first also records the objective before any swap; a last
   // pass records the objective after and writes the stats
   if (num_swap_rounds == 0) {
     castk::swap_round_kernel<<<rows, castk::kSwapRoundThreads, sm2, s>>>(
         selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
-        ctl, stats, 0, 0, 0, swap_eps, max_swaps_per_call);
+        ctl, stats, 0, 0, 0, swap_eps, max_swaps_per_call, gate);
     CAST_CUDA_TRY(cudaGetLastError());
   }
   for (int r = 0; r < num_swap_rounds; ++r) {
     castk::swap_round_kernel<<<rows, castk::kSwapRoundThreads, sm2, s>>>(
         selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
-        ctl, stats, 1, r == 0 ? 0 : -1, 0, swap_eps, max_swaps_per_call);
+        ctl, stats, 1, r == 0 ? 0 : -1, 0, swap_eps, max_swaps_per_call, gate);
     CAST_CUDA_TRY(cudaGetLastError());
   }
   castk::swap_round_kernel<<<rows, castk::kSwapRoundThreads, sm2, s>>>(
       selected, counts, local, row_gate, coefficient, hessian, p, cand, proxy, err, limit, best, obj,
-      ctl, stats, 0, 1, 1, swap_eps, max_swaps_per_call);
+      ctl, stats, 0, 1, 1, swap_eps, max_swaps_per_call, gate);
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;
 }

@@ -38,6 +38,10 @@ struct SwapCtl {
   int swaps;
   double improvement;
   int max_swappable;
+  int min_count_flip;        // INT_MAX - the smallest count over every row (0: no row yet)
+  int max_count;             // the largest count over every row
+  int current_changed;       // a swap removed or added a current-chunk key
+  unsigned long long count_sum, hist_before;
 };
 
 // The reference's maximum_l: candidate slots at or beyond it hold no proxy
@@ -88,7 +92,8 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
                       const long long *__restrict__ selected, const long long *__restrict__ counts,
                       const uint8_t *__restrict__ local, SwapShape p, float eps,
                       int *__restrict__ cand_out, float *__restrict__ proxy_out,
-                      float *__restrict__ err_out, int *__restrict__ limit_out, SwapCtl *ctl) {
+                      float *__restrict__ err_out, int *__restrict__ limit_out, SwapCtl *ctl,
+                      const int *__restrict__ gate) {
   extern __shared__ float sm[];
   float *vsm = sm;                  // K*D when staged, first so it is 16-byte aligned
   float *prob = sm + (p.stage_v ? p.K * p.D : 0);  // K
@@ -102,15 +107,24 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   const int row = blockIdx.x;
   const int bh = row / p.R, r = row % p.R, q = p.M + r;
   const int tid = threadIdx.x;
-  // memory rows take no search but their swappable counts widen the
-  // candidate list: the grid strides over them, one thread per row
-  for (int mr = blockIdx.x * blockDim.x + tid; mr < p.B * p.H * p.M; mr += gridDim.x * blockDim.x) {
-    const size_t qrow = (size_t)(mr / p.M) * p.Q + mr % p.M;
-    const long long c = __ldg(counts + qrow);
-    int sw = 0;
-    for (int j = 0; j < p.S && j < c; ++j)
-      sw += !p.historical || __ldg(selected + qrow * p.S + j) < p.M;
+  if (gate && *gate) return;  // a transport gate failed: the call leaves the selection as it is
+  // every row's count statistics (memory rows take no search, but their
+  // swappable counts widen the candidate list): the grid strides over the
+  // B*H*Q rows, one thread per row
+  for (int qr = blockIdx.x * blockDim.x + tid; qr < p.B * p.H * p.Q; qr += gridDim.x * blockDim.x) {
+    const long long c = __ldg(counts + qr);
+    int sw = 0, hist = 0;
+    for (int j = 0; j < p.S && j < c; ++j) {
+      const bool h = __ldg(selected + (size_t)qr * p.S + j) < p.M;
+      hist += h;
+      sw += !p.historical || h;
+    }
     if (sw) atomicMax(&ctl->max_swappable, sw);
+    const int ci = (int)min(max(c, 0ll), (long long)INT_MAX);
+    atomicMax(&ctl->min_count_flip, INT_MAX - ci);
+    atomicMax(&ctl->max_count, ci);
+    atomicAdd(&ctl->count_sum, (unsigned long long)max(c, 0ll));
+    if (hist) atomicAdd(&ctl->hist_before, (unsigned long long)hist);
   }
   const float *srow = score + ((size_t)bh * p.Q + q) * p.K;
   const float *Vg = value + (size_t)bh * p.K * p.D;
@@ -161,7 +175,6 @@ __global__ void __launch_bounds__(kSwapProxyThreads)
   for (int j = 0; j < p.S; ++j)
     swappable += (j < cnt) && (!p.historical || seli[j] < p.M);
   const int limit = min(swappable * p.mult, p.cand_blocks);
-  if (tid == 0 && swappable) atomicMax(&ctl->max_swappable, swappable);
   for (int l = tid; l < p.Lc; l += blockDim.x) {
     int hit = 0;
     for (int j = 0; j < p.S; ++j) hit |= (j < cnt) && (seli[j] == cand[l]);
@@ -209,7 +222,8 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
                       const int *__restrict__ cand_all, const float *__restrict__ proxy_all,
                       float *__restrict__ err_all, const int *__restrict__ limit_all, SwapBest *best_row,
                       double *__restrict__ obj_part, SwapCtl *ctl, double *__restrict__ stats,
-                      int search, int obj_slot, int finish, float swap_eps, int max_swaps) {
+                      int search, int obj_slot, int finish, float swap_eps, int max_swaps,
+                      const int *__restrict__ gate) {
   extern __shared__ float sm[];
   float *e = sm;                        // R*G: the head's current-row errors
   float *prx = e + p.R * p.G;           // Lc*G: this row's proxies
@@ -227,6 +241,23 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
   const int row = blockIdx.x, bh = row / p.R, r = row % p.R, q = p.M + r;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int RG = p.R * p.G;
+  if (gate && *gate) {  // a transport gate failed: no work; the last CTA writes zero stats
+    search = 0;
+    obj_slot = -1;
+    if (tid == 0) {
+      __threadfence();
+      last = atomicAdd(&ctl->ticket, 1u) == (unsigned)(gridDim.x - 1);
+    }
+    __syncthreads();
+    if (last && tid == 0) {
+      if (finish)
+        for (int i = 0; i < 5; ++i) stats[i] = 0.0;
+      if (finish)
+        for (int i = 8; i < 14; ++i) stats[i] = 0.0;
+      ctl->ticket = 0u;
+    }
+    return;
+  }
   const float *eg = err_all + (size_t)bh * RG;
   for (int i = tid; i < RG; i += blockDim.x) e[i] = eg[i];
   for (int t = tid; t < p.R; t += blockDim.x) hrow[t] = __ldg(hess + (size_t)r * p.R + t);
@@ -377,6 +408,7 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
           selected[qrow * p.S + b.s] = cg[b.l];
           ctl->swaps += 1;
           ctl->improvement += -(double)bv;
+          ctl->current_changed |= (k >= p.M) || (cg[b.l] >= p.M);
         }
       }
     }
@@ -406,9 +438,173 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
       stats[2] = t;
       stats[3] = ctl->improvement;
       stats[4] = (double)ctl->max_swappable;
+      stats[8] = (double)(INT_MAX - ctl->min_count_flip);
+      stats[9] = (double)ctl->max_count;
+      stats[10] = (double)ctl->count_sum;
+      stats[11] = (double)ctl->hist_before;
+      stats[13] = (double)ctl->current_changed;
+    }
+    // the historical budget after the swaps, over every valid slot
+    unsigned long long hist = 0;
+    for (int i = tid; i < p.B * p.H * p.Q * p.S; i += blockDim.x) {
+      const int qr = i / p.S, j = i % p.S;
+      hist += (j < counts[qr]) && selected[i] < p.M;
+    }
+    for (int o = 16; o; o >>= 1) hist += __shfl_xor_sync(0xffffffffu, hist, o);
+    __syncthreads();
+    if (lane == 0) dred[warp] = (double)hist;
+    __syncthreads();
+    if (tid == 0) {
+      double t = 0.0;
+      for (int w = 0; w < nwarps; ++w) t += dred[w];
+      stats[12] = t;
     }
   }
   if (tid == 0) ctl->ticket = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// The routing objective on the device: transport operators, coefficient
+// vector and Hessian over the current rows, and the transport gates.
+// ---------------------------------------------------------------------------
+constexpr int kSwapObjThreads = 256;
+constexpr int kSwapObjMaxTargets = 32, kSwapObjMaxPairs = 16, kSwapObjMaxCells = 64;
+constexpr int kSwapObjMaxBins = 2048;  // tiles x bins of one sketch (18 x 66 = 1188)
+
+struct SwapObjTarget {
+  const float *theta, *aff;  // the pair's sketch [tiles][bins], or NULL: identity operator
+  float x_l, x_r;            // exponents of the left and right operators: a and -(1-a)
+  float s_l, s_r;            // their weights: 1-a and a
+  int lc, rc;                // left and right anchor cells
+};
+
+struct SwapObjPair {          // a same-segment anchor pair with skipped frames
+  const float *mean;          // its sketch's mean affinity on the device, or NULL: mean_val
+  float mean_val;
+  int c_lo, c_hi;             // the cells of its skipped frames, inclusive
+  int matching;               // it has a sketch (counts for the transport gate)
+};
+
+struct SwapObjParams {
+  int n, tiles, bins, cells, R, T, n_pairs;
+  const float *u_re, *u_im;   // [tiles][bins][n]
+  const float *v_re, *v_im;   // [tiles][n][bins]
+  float lam_a, lam_r, min_match, min_pair;
+  int require_fc, pair_gate;
+  float cell_count[kSwapObjMaxCells];
+  SwapObjTarget t[kSwapObjMaxTargets];
+  SwapObjPair pr[kSwapObjMaxPairs];
+  float *ops;                 // [2T][n][n] (out, in), weighted
+  float *coef, *hess;         // [R], [R][R]
+  uint8_t *row_gate;          // [R] (pair gate) or NULL
+  int *gate;                  // 0 ok, 1 weak transport, 2 no strong pair cells
+  double *stats;              // [5]: gate, [6]: matching affinity, [7]: gated cells
+};
+
+// grid (2T, ceil(n*n / threads)): op k = 2t + side is
+//   s * (I + sum_p V_p ((exp(i x g_p theta_p) - 1) * U_p))
+// (side 0: x = a, s = 1-a; side 1: x = -(1-a), s = a).  CTA (0, 0) also
+// evaluates the transport gates.
+__global__ void __launch_bounds__(kSwapObjThreads) swap_operator_kernel(const __grid_constant__ SwapObjParams p) {
+  __shared__ float rc_[kSwapObjMaxBins], rs_[kSwapObjMaxBins];
+  const int k = blockIdx.x, t = k >> 1, side = k & 1;
+  const SwapObjTarget &tg = p.t[t];
+  const float x = side ? tg.x_r : tg.x_l, sc = side ? tg.s_r : tg.s_l;
+  const int nb = p.tiles * p.bins;
+  if (tg.theta)
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+      const float ang = __fmul_rn(__fmul_rn(x, tg.aff[i]), tg.theta[i]);
+      float sn, cs;
+      sincosf(ang, &sn, &cs);
+      rc_[i] = cs - 1.0f;
+      rs_[i] = sn;
+    }
+  __syncthreads();
+  const int idx = blockIdx.y * blockDim.x + threadIdx.x;
+  if (idx < p.n * p.n) {
+    const int o = idx / p.n, j = idx % p.n;
+    float acc = 0.f;
+    if (tg.theta)
+      for (int tp = 0; tp < p.tiles; ++tp) {
+        const float *ur = p.u_re + (size_t)tp * p.bins * p.n + j, *ui = p.u_im + (size_t)tp * p.bins * p.n + j;
+        const float *vr = p.v_re + ((size_t)tp * p.n + o) * p.bins, *vi = p.v_im + ((size_t)tp * p.n + o) * p.bins;
+        const float *c = rc_ + tp * p.bins, *s = rs_ + tp * p.bins;
+        for (int f = 0; f < p.bins; ++f) {
+          const float a = __ldg(ur + (size_t)f * p.n), b = __ldg(ui + (size_t)f * p.n);
+          const float wr = c[f] * a - s[f] * b, wi = c[f] * b + s[f] * a;
+          acc = fmaf(__ldg(vr + f), wr, fmaf(__ldg(vi + f), wi, acc));
+        }
+      }
+    p.ops[(size_t)k * p.n * p.n + idx] = sc * ((o == j ? 1.f : 0.f) + acc);
+  }
+  if (k == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    int status = 0;
+    float match = 0.f;
+    bool any = false;
+    for (int i = 0; i < p.n_pairs; ++i)
+      if (p.pr[i].matching) {
+        const float m = p.pr[i].mean ? *p.pr[i].mean : p.pr[i].mean_val;
+        match = any ? fmaxf(match, m) : m;
+        any = true;
+      }
+    if (p.require_fc && !(any && match >= p.min_match)) status = 1;
+    int gated = 0;
+    if (status == 0 && p.pair_gate) {
+      bool cell[kSwapObjMaxCells] = {};
+      for (int i = 0; i < p.n_pairs; ++i) {
+        const float m = p.pr[i].mean ? *p.pr[i].mean : p.pr[i].mean_val;
+        if (!(m >= p.min_pair)) continue;
+        for (int c = p.pr[i].c_lo; c <= p.pr[i].c_hi; ++c) {
+          gated += !cell[c];
+          cell[c] = true;
+        }
+      }
+      for (int r = 0; r < p.R; ++r) p.row_gate[r] = cell[r / p.n] ? 1 : 0;
+      if (!gated) status = 2;
+    }
+    *p.gate = status;
+    p.stats[5] = status;
+    p.stats[6] = match;
+    p.stats[7] = gated;
+  }
+}
+
+// grid-stride over R*R + R: the Hessian, every entry summed over the
+// targets in order (no atomics), then the anchor coefficients
+//   hess[(ci,a),(cj,b)] = lam_r * sum_t sum_k X_t[k][a] Y_t[k][b]
+// with X, Y the target's operator on the side of cell ci, cj (A + B when
+// both anchors share a cell), and coef[(c,a)] = lam_a * anchors in cell c.
+__global__ void __launch_bounds__(kSwapObjThreads) swap_hessian_kernel(const __grid_constant__ SwapObjParams p) {
+  const int n = p.n, nn = n * n;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.R * p.R + p.R; i += gridDim.x * blockDim.x) {
+    if (i >= p.R * p.R) {
+      const int r = i - p.R * p.R;
+      p.coef[r] = p.lam_a * p.cell_count[r / n];
+      continue;
+    }
+    const int row = i / p.R, col = i % p.R;
+    const int ci = row / n, a = row % n, cj = col / n, b = col % n;
+    float acc = 0.f;
+    for (int t = 0; t < p.T; ++t) {
+      const SwapObjTarget &tg = p.t[t];
+      const float *A = p.ops + (size_t)(2 * t) * nn, *B = A + nn;
+      if (tg.lc == tg.rc) {
+        if (ci != tg.lc || cj != tg.lc) continue;
+        float s = 0.f;
+        for (int kk = 0; kk < n; ++kk)
+          s = fmaf(A[kk * n + a] + B[kk * n + a], A[kk * n + b] + B[kk * n + b], s);
+        acc += s;
+      } else {
+        const float *X = ci == tg.lc ? A : (ci == tg.rc ? B : nullptr);
+        const float *Y = cj == tg.lc ? A : (cj == tg.rc ? B : nullptr);
+        if (!X || !Y) continue;
+        float s = 0.f;
+        for (int kk = 0; kk < n; ++kk) s = fmaf(X[kk * n + a], Y[kk * n + b], s);
+        acc += s;
+      }
+    }
+    p.hess[i] = p.lam_r * acc;
+  }
 }
 
 }  // namespace castk

@@ -276,6 +276,50 @@ CAST_API int cast_barycentric_pair_write(const float *active_residual, const flo
                                 int arithmetic_mode, cast_stream_t stream);
 
 /*
+ * The swap router's objective and transport gates on the device: the
+ * transport operators, coefficient vector and Hessian of
+ * FCPASMLocalCoordinateSwapRouter._objective_terms (proposed/
+ * fc_pasm_swap_routing.py:414-548, operators _transport_matrix :116-268) and
+ * the gates of refine on the published sketch's mean affinities (:733-820).
+ *   n              cells of the attention grid (nh*nw); R = cells * n rows
+ *   u_re, u_im     fp32 [tiles][bins][n]: the operator's analysis of the grid's
+ *                  basis maps (lift, reflect pad, windowed tiles, rfft2)
+ *   v_re, v_im     fp32 [tiles][n][bins]: its synthesis of one tile's bin
+ *                  (irfft2, windowed overlap-add, crop, pooling), for the real
+ *                  and the imaginary unit -- both built once per geometry
+ *   cell_anchor_count host fp32 [cells]: Exact anchors per temporal cell
+ *   target_*       host tables of the skipped targets t (left anchor l, right
+ *                  anchor r of one segment): the pair's theta and affinity
+ *                  (device fp32 [tiles*bins], NULL: identity operator), alpha
+ *                  = (t-l)/(r-l), and the (left, right) anchor cells
+ *   pair_*         host tables of the same-segment anchor pairs with skipped
+ *                  frames: the mean affinity (a device fp32 scalar, or NULL and
+ *                  the host value), the first and last cell of the skipped
+ *                  frames, whether the pair has a sketch
+ * Writes coefficient [R] = lambda_anchor * anchors of the row's cell,
+ * hessian [R,R] = lambda_reconstruction * sum_t [A_t B_t]^T [A_t B_t] on the
+ * (left, right) cells with A_t = (1-a) M(a), B_t = a M(-(1-a)),
+ * M(x) = I + sum_p V_p ((exp(i x g_p theta_p) - 1) U_p), operators [2T][n][n]
+ * (scratch), the gate (0 ok, 1 the matching sketches' mean affinity is below
+ * min_transport_affinity under require_fc_transport, 2 no cell passes the
+ * pair gate) into gate[0] and stats[5], the matching affinity into stats[6],
+ * the gated cells into stats[7], and, with min_pair_transport_affinity > 0,
+ * row_gate [R].  Launches: 2.  No host synchronisation.
+ */
+CAST_API int cast_swap_objective(int n, int tiles, int bins, const float *u_re, const float *u_im,
+                        const float *v_re, const float *v_im, int cells,
+                        const float *cell_anchor_count, int n_targets,
+                        const float *const *target_theta, const float *const *target_affinity,
+                        const double *target_alpha, const int32_t *target_cells, int n_pairs,
+                        const float *const *pair_mean, const float *pair_mean_value,
+                        const int32_t *pair_cells, const int32_t *pair_matching,
+                        int require_fc_transport, float min_transport_affinity,
+                        float min_pair_transport_affinity, float lambda_anchor,
+                        float lambda_reconstruction, float *coefficient, float *hessian,
+                        uint8_t *row_gate, int32_t *gate, double *stats, float *operators,
+                        cast_stream_t stream);
+
+/*
  * FC-PASM fixed-budget swap router: the numeric body of
  * FCPASMLocalCoordinateSwapRouter.refine (proposed/fc_pasm_swap_routing.py:
  * 616-1077, called at proposed/matrix_curvature_phase_frame_weave.py:6040)
@@ -287,13 +331,20 @@ CAST_API int cast_barycentric_pair_write(const float *active_residual, const flo
  *                counts int64 [B,H,Q] (valid slots per row); local uint8 [Q,K]
  *   row_gate     uint8 [R] or NULL: rows a swap may touch (the per-pair
  *                transport-affinity gate, :785-820)
+ *   gate         int32 [1] device or NULL: the transport gate written by
+ *                cast_swap_objective; nonzero leaves the selection as it is
+ *                (the kernels skip their work)
  *   coefficient  fp32 [R], hessian fp32 [R,R]: the objective
  *                J(e) = sum_r coefficient[r] |e_r|^2 + e^T hessian e over the
  *                current rows' sketched errors (anchor term and transport
  *                reconstruction terms, _objective_terms :414-548)
- *   stats        fp64 [5] device: swaps made, objective before, objective
- *                after, summed improvement, and the largest swappable count
- *                over all rows (0: nothing to swap, the selection is unchanged)
+ *   stats        fp64 [14] device: [0] swaps made, [1] objective before,
+ *                [2] objective after, [3] summed improvement, [4] the largest
+ *                swappable count over all rows (0: nothing to swap, the
+ *                selection is unchanged), [8] smallest, [9] largest and
+ *                [10] summed row count, [11] historical slots before and
+ *                [12] after, [13] 1 if a swap removed or added a current key;
+ *                [5..7] belong to cast_swap_objective
  * Candidates are the top min(cand_blocks, multiplier*S) blocks of
  * score + 1e6*local (cand_blocks = memory_blocks if historical_only else K),
  * which holds every row's valid candidates of the reference's top-k; a
@@ -308,7 +359,8 @@ CAST_API int cast_barycentric_pair_write(const float *active_residual, const flo
  */
 CAST_API int cast_swap_route(const float *score, const float *pooled_value, long long *selected,
                     const long long *counts, const uint8_t *local, const uint8_t *row_gate,
-                    const float *coefficient, const float *hessian, int B, int H, int Q, int K,
+                    const int32_t *gate, const float *coefficient, const float *hessian, int B, int H,
+                    int Q, int K,
                     int D, int S, int memory_blocks, int candidate_multiplier, int num_swap_rounds,
                     float swap_eps, int sketch_groups, int max_swaps_per_call, int historical_only,
                     int same_bank_only, double *stats, void *workspace, size_t workspace_bytes,

@@ -327,6 +327,7 @@ def block_sparse_attention(
     k_codes: np.ndarray | None = None,
     k_scales: np.ndarray | None = None,
     heads: list[int] | None = None,
+    rows: np.ndarray | None = None,
 ) -> np.ndarray:
     """Explicit softmax over the allowed, valid keys of each query block.
 
@@ -337,7 +338,8 @@ def block_sparse_attention(
     logits are instead the exact int8 simulation
     ``(qc . kc) * s_q[qblock] * s_k[kblock] * sm_scale``.
     Query rows whose key set is empty produce zeros.  Returns float64
-    ``[B,H,Lq,D]`` (only ``heads`` filled when given).
+    ``[B,H,Lq,D]`` (only ``heads`` filled when given; with ``rows``, only
+    those row offsets within every query block, the others left zero).
     """
     b, h, lq, d = q.shape
     lk = k.shape[-2]
@@ -351,6 +353,7 @@ def block_sparse_attention(
         for hi in hs:
             for qb in range(nqb):
                 r0, r1 = qb * query_block, min(lq, (qb + 1) * query_block)
+                rsel = np.arange(r0, r1) if rows is None else r0 + rows[rows < r1 - r0]
                 n = int(counts[bi, hi, qb])
                 blocks = [int(x) for x in indices[bi, hi, qb, :n]]
                 keys = []
@@ -369,19 +372,19 @@ def block_sparse_attention(
                 if len(toks) == 0:
                     continue
                 if int8:
-                    qc = q_codes[bi, hi, r0:r1].astype(np.float64)
+                    qc = q_codes[bi, hi, rsel].astype(np.float64)
                     kc = k_codes[bi, hi, toks].astype(np.float64)
                     logits = (qc @ kc.T) * (
                         float(q_scales[bi, hi, qb]) * np.concatenate(kscale)[None, :]
                     ) * sm_scale
                 else:
-                    qf = q[bi, hi, r0:r1].astype(np.float64)
+                    qf = q[bi, hi, rsel].astype(np.float64)
                     kf = k[bi, hi, toks].astype(np.float64)
                     logits = (qf @ kf.T) * sm_scale
                 logits = logits - logits.max(axis=1, keepdims=True)
                 w = np.exp(logits)
                 w = w / w.sum(axis=1, keepdims=True)
-                out[bi, hi, r0:r1] = w @ v[bi, hi, toks].astype(np.float64)
+                out[bi, hi, rsel] = w @ v[bi, hi, toks].astype(np.float64)
     return out
 
 

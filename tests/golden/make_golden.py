@@ -26,6 +26,8 @@ Files:
 * ``cfg3_select_h2.npz`` -- config 3 (anchor queries over 128 history
   frames, budget 16) generated with 2 heads: reference-primitive scores and
   the budget rule's selection.
+* ``cfg2_select_h24.npz``, ``cfg3_select_h24.npz`` -- the same for all 24
+  heads of config 2 and of config 3 generated with 24 heads.
 * ``compact_pack.npz`` -- the compact path's RoPE phase
   (``MatrixCurvaturePhaseFrameWeave._cached_compact_rope_phase``), rotation
   (``_apply_compact_rope_phase``), packing and output scatter (the lines of
@@ -149,6 +151,13 @@ def make_cfg2(manifest: dict):
     sel, cnt = budget_rule(scores, 4, 8)
     np.savez_compressed(os.path.join(HERE, "cfg2_select_h2.npz"),
                         scores_f32=scores, selected=sel, counts=cnt)
+    # all 24 heads: the full-size call's selection
+    qn = ref_pooled(_tile_visual_tensor, w.q, 4, (22, 40), (1, 22, 40))
+    kn = ref_pooled(_tile_visual_tensor, w.k, 36, (22, 40), (1, 22, 40))
+    scores = torch.matmul(qn, kn.transpose(-2, -1)).numpy()
+    sel, cnt = budget_rule(scores, 4, 8)
+    np.savez_compressed(os.path.join(HERE, "cfg2_select_h24.npz"),
+                        scores_f32=scores, selected=sel, counts=cnt)
 
 
 def make_cfg3(manifest: dict):
@@ -163,6 +172,15 @@ def make_cfg3(manifest: dict):
     scores = torch.matmul(qn, kn.transpose(-2, -1)).numpy()
     sel, cnt = budget_rule(scores, nq, w.budget)
     np.savez_compressed(os.path.join(HERE, "cfg3_select_h2.npz"),
+                        scores_f32=scores, selected=sel, counts=cnt)
+    # config 3 as BASELINE states it: 24 heads
+    w = workloads.config3(heads=24)
+    manifest["inputs"]["config3_h24"] = {"q": sha(w.q), "k": sha(w.k), "v": sha(w.v)}
+    qn = ref_pooled(_tile_visual_tensor, w.q, nq, (22, 40), (1, 22, 40))
+    kn = ref_pooled(_tile_visual_tensor, w.k, nk, (22, 40), (1, 22, 40))
+    scores = torch.matmul(qn, kn.transpose(-2, -1)).numpy()
+    sel, cnt = budget_rule(scores, nq, w.budget)
+    np.savez_compressed(os.path.join(HERE, "cfg3_select_h24.npz"),
                         scores_f32=scores, selected=sel, counts=cnt)
 
 

@@ -155,3 +155,15 @@ def test_fast_quantiser_matches_ieee_division_exhaustively(tmp_path):
     res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "mismatches 0" in res.stdout and "out of range 0" in res.stdout
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg3"])
+def test_budget_rule_matches_reference_primitives_all_heads(name):
+    """All 24 heads of config 2, and config 3 generated with 24 heads: the
+    oracle's selection equals the one built from the reference's own pooling
+    primitives (``cfg*_select_h24.npz``)."""
+    w = workloads.config2() if name == "cfg2" else workloads.config3(heads=24)
+    sel, cnt, _, _, _ = orc.rcsa_select(w.q.float().numpy(), w.k.float().numpy(), 880, w.budget)
+    g = np.load(os.path.join(GOLDEN, f"{name}_select_h24.npz"))
+    np.testing.assert_array_equal(sel, g["selected"])
+    np.testing.assert_array_equal(cnt, g["counts"])

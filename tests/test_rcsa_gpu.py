@@ -447,3 +447,62 @@ def test_host_plan_matches_device_plan(cuda):
         assert torch.equal(plan.qk_mode, dp.qk_mode[:, h0:h1])
     d = (hout.float() - ref.float().cpu()).abs()
     assert float(d.max()) < MAX_ABS and float(d.mean()) < MEAN_ABS
+
+
+ROW_SAMPLE = np.array([0, 1, 2, 63, 64, 127, 128, 255, 256, 383, 384, 511, 512, 639, 640, 767, 768, 800,
+                       860, 879])
+
+
+def _full_size(w, gold_name):
+    """Every head at full size: selection, counts, int8 codes and scales
+    bit-exact against the oracle (and the selection against the reference-
+    derived golden), attention on 20 sampled rows of every query block of
+    every head against the oracle's bf16 path (bf16 and auto policies) and
+    its exact int8 simulation (int8 policy)."""
+    qd, kd, vd = w.q.cuda(), w.k.cuda(), w.v.cuda()
+    results = {}
+    for policy in ("bf16", "auto", "int8"):
+        out, sel = rcsa.rcsa_attention(qd, kd, vd, block_size=880, budget=w.budget, policy=policy)
+        torch.cuda.synchronize()
+        results[policy] = (out.cpu(), sel)
+    del qd, kd, vd
+    sel = results["int8"][1]
+    q, k, v = _np(w.q), _np(w.k), _np(w.v)
+    o_sel, o_cnt, _, _, _ = orc.rcsa_select(q, k, 880, w.budget)
+    np.testing.assert_array_equal(sel.indices.cpu().numpy(), o_sel)
+    np.testing.assert_array_equal(sel.counts.cpu().numpy(), o_cnt)
+    gold = np.load(os.path.join(GOLDEN, gold_name))
+    np.testing.assert_array_equal(o_sel, gold["selected"])
+    for policy in ("bf16", "auto"):  # every policy selects the same blocks
+        np.testing.assert_array_equal(results[policy][1].indices.cpu().numpy(), o_sel)
+    qc, qs = orc.quantize_blocks(q, 880)
+    kc, ks = orc.quantize_blocks(k, 880)
+    np.testing.assert_array_equal(sel.q_scales.cpu().numpy(), qs)
+    np.testing.assert_array_equal(sel.k_scales.cpu().numpy(), ks)
+    np.testing.assert_array_equal(sel.q_codes.cpu().numpy(), qc)
+    np.testing.assert_array_equal(sel.k_codes.cpu().numpy(), kc)
+    ref_b = orc.block_sparse_attention(q, k, v, o_sel, o_cnt, 880, 880, rows=ROW_SAMPLE)
+    ref_i = orc.block_sparse_attention(q, k, v, o_sel, o_cnt, 880, 880, q_codes=qc, q_scales=qs,
+                                       k_codes=kc, k_scales=ks, rows=ROW_SAMPLE)
+    nqb = q.shape[2] // 880
+    rows = (np.arange(nqb)[:, None] * 880 + ROW_SAMPLE[None]).reshape(-1)
+    errs = {}
+    for policy, ref in (("bf16", ref_b), ("auto", ref_b), ("int8", ref_i)):
+        got = results[policy][0].float().numpy()[:, :, rows].astype(np.float64)
+        d = np.abs(got - ref[:, :, rows])
+        errs[policy] = (float(d.max()), float(d.mean()))
+        assert d.max() < MAX_ABS and d.mean() < MEAN_ABS, (policy, errs[policy])
+    # the pure int8 policy against the bf16 path: measured, reported
+    got = results["int8"][0].float().numpy()[:, :, rows].astype(np.float64)
+    d = np.abs(got - ref_b[:, :, rows])
+    print(f"{gold_name}: errors {errs}; int8 policy vs bf16 path max {d.max():.3e} mean {d.mean():.3e}; "
+          f"auto int8 fraction {float(results['auto'][1].qk_mode.float().mean()):.3f}")
+    return d
+
+
+def test_rcsa_config2_all_heads_bitexact(cuda):
+    _full_size(workloads.config2(), "cfg2_select_h24.npz")
+
+
+def test_rcsa_config3_all_heads_bitexact(cuda):
+    _full_size(workloads.config3(heads=24), "cfg3_select_h24.npz")

@@ -155,12 +155,11 @@ def _refine(router, w, **over):
     ({}, dict(exact_current_frames=(0, 1, 2)), "no_skipped_frames"),
     ({}, dict(memory_blocks=7), "no_rectangular_current_rows"),
     (dict(require_fc_transport=True), dict(transport=None), "missing_previous_layer_fc_transport"),
-    (dict(require_fc_transport=True, min_transport_affinity=1.0), {}, "weak_previous_layer_fc_transport"),
-    (dict(min_pair_transport_affinity=1.0), {}, "no_strong_transport_pair_cells"),
 ])
 def test_fallback_records(cfg, over, reason):
-    """The gates run before any device work, on the host, as in the
-    reference (proposed/fc_pasm_swap_routing.py:636-820)."""
+    """The host-only gates run before any device work, as in the reference
+    (proposed/fc_pasm_swap_routing.py:636-760); the two gates on the
+    sketches' mean affinities run on the device (tests/test_swap_router_gpu.py)."""
     w = workloads.swap_case(transport=True)
     router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig(**cfg))
     sel, rec = _refine(router, w, **over)

@@ -93,7 +93,7 @@ def test_c_abi_rejects_bad_arguments():
     lib = _lib.load()
     dev = "cuda"
     w = _to(workloads.swap_case(), dev)
-    stats = torch.empty(5, dtype=torch.float64, device=dev)
+    stats = torch.empty(14, dtype=torch.float64, device=dev)
     coef = torch.zeros(32, device=dev)
     hess = torch.zeros(32, 32, device=dev)
     sel = w.selected.clone()
@@ -106,7 +106,7 @@ def test_c_abi_rejects_bad_arguments():
         a.update(over)
         return lib.cast_swap_route(w.score.data_ptr(), w.pooled_value.data_ptr(), sel.data_ptr(),
                                    w.counts.data_ptr(), w.local.to(torch.uint8).data_ptr(), None,
-                                   coef.data_ptr(), hess.data_ptr(), B, H, Q, K, 64, 10, a["M"], a["mult"],
+                                   None, coef.data_ptr(), hess.data_ptr(), B, H, Q, K, 64, 10, a["M"], a["mult"],
                                    a["rounds"], 0.0, a["G"], 0, 0, 0, stats.data_ptr(), ws.data_ptr(),
                                    a["ws"], None)
 
@@ -132,14 +132,14 @@ def test_swap_route_graph_rate():
                                        lambda_anchor=1.0, lambda_reconstruction=1.0, device="cuda")
     nbytes = lib.cast_swap_route_workspace_bytes(B, H, Q, K, D, S, M, 2, 0, 16)
     ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-    stats = torch.empty(5, dtype=torch.float64, device="cuda")
+    stats = torch.empty(14, dtype=torch.float64, device="cuda")
     local = w.local.to(torch.uint8)
     sel = w.selected.clone()
     s = torch.cuda.Stream()
 
     def launch():
         _lib.call("cast_swap_route", w.score.data_ptr(), w.pooled_value.data_ptr(), sel.data_ptr(),
-                  w.counts.data_ptr(), local.data_ptr(), None, coef.data_ptr(), hess.data_ptr(), B, H, Q,
+                  w.counts.data_ptr(), local.data_ptr(), None, None, coef.data_ptr(), hess.data_ptr(), B, H, Q,
                   K, D, S, M, 2, 1, 0.1, 16, 1, 0, 1, stats.data_ptr(), ws.data_ptr(), nbytes,
                   s.cuda_stream)
 
@@ -222,3 +222,59 @@ def test_short_rows_match_oracle(historical_only):
     assert float(rec["objective_before"]) == pytest.approx(st["objective_before"], rel=1e-4)
     assert float(rec["objective_after"]) == pytest.approx(st["objective_after"], rel=1e-4)
     assert rec["candidate_max"] == st["candidate_max"] < 2 * w.selected.shape[-1]
+
+
+@pytest.mark.parametrize("frames,group,cells", [((0, 3), 1, 4), ((0, 3, 4, 7), 1, 8), ((0, 2, 5), 2, 3)])
+def test_device_objective_matches_host_restatement(cuda, frames, group, cells):
+    """cast_swap_objective's coefficient vector and Hessian against the torch
+    restatement of the reference's per-call construction (transport
+    operators from the sketch, then the quadratic terms), with the sketch
+    published for some pairs and missing (identity operator) for others."""
+    w = workloads.swap_case(transport=True, exact_frames=frames, cells=cells, temporal_group_size=group,
+                            width=12, seed=8)
+    pairs = w.transport["pairs"]
+    if len(pairs) > 1:  # one pair without a sketch: identity operators
+        pairs.pop(sorted(pairs)[-1])
+    coef_ref, hess_ref, _ = sr.quadratic_terms(
+        temporal_cells=cells, spatial=8, exact_frames=frames, temporal_group_size=group,
+        current_boundary=4, transport=w.transport, lambda_anchor=1.0, lambda_reconstruction=0.7,
+        device="cpu")
+    for e in pairs.values():
+        for name in ("theta", "affinity", "mean_affinity"):
+            e[name] = e[name].cuda()
+    router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig(lambda_reconstruction=0.7))
+    stats = torch.zeros(14, dtype=torch.float64, device="cuda")
+    same_seg = [(a, b) for a, b in zip(frames, frames[1:]) if (a < 4) == (b < 4)]
+    obj = router._objective(cells=cells, spatial=8, spatial_shape=(2, 4), frames=frames, same_seg=same_seg,
+                            pairs=pairs, transport=w.transport, group=group, boundary=4, stats=stats,
+                            device=torch.device("cuda"), stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(obj["coef"].cpu().numpy(), coef_ref.numpy(), rtol=1e-6)
+    scale = float(hess_ref.abs().max())
+    assert float((obj["hess"].cpu() - hess_ref).abs().max()) < 1e-5 * scale
+    assert int(stats[5]) == 0 and obj["sketched"] == bool(pairs)
+
+
+def test_device_gates(cuda):
+    """The transport gates on the device: a sketch below the matching gate,
+    and a pair gate that no pair passes, give the reference's fallbacks and
+    leave the selection as it is."""
+    w = _to(workloads.swap_case(transport=True), "cuda")
+    for e in w.transport["pairs"].values():
+        e["mean_affinity"] = torch.tensor(0.3, device="cuda")
+    for cfg, reason in ((dict(require_fc_transport=True, min_transport_affinity=0.5),
+                         "weak_previous_layer_fc_transport"),
+                        (dict(min_pair_transport_affinity=0.5), "no_strong_transport_pair_cells")):
+        router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig(num_swap_rounds=2, **cfg))
+        sel, rec = _refine(router, w)
+        assert rec["status"] == "independent_topk_fallback" and rec["fallback_reason"] == reason
+        assert rec["matching_transport_affinity"] == pytest.approx(0.3)
+        assert torch.equal(sel, w.selected)
+    # the same sketch above both gates refines
+    for e in w.transport["pairs"].values():
+        e["mean_affinity"] = torch.tensor(0.8, device="cuda")
+    router = sr.FCPASMLocalCoordinateSwapRouter(sr.FCPASMSwapRoutingConfig(
+        num_swap_rounds=2, require_fc_transport=True, min_transport_affinity=0.5,
+        min_pair_transport_affinity=0.5))
+    _, rec = _refine(router, w)
+    assert rec["status"] == "refined" and rec["pair_gate_cells"] >= 1
