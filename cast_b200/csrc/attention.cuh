@@ -301,11 +301,21 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
+// acc + the low (high) bf16 half of a packed pair, widened exactly to fp32:
+// one mixed-precision add (sm_100) instead of an unpack and an add.
+__device__ __forceinline__ float add_bf16_lo(uint32_t pk, float acc) {
+  float r;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.rn.f32.bf16 %0, lo, %2;\n\t}"
+      : "=f"(r) : "r"(pk), "f"(acc));
+  return r;
 }
+__device__ __forceinline__ float add_bf16_hi(uint32_t pk, float acc) {
+  float r;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.rn.f32.bf16 %0, hi, %2;\n\t}"
+      : "=f"(r) : "r"(pk), "f"(acc));
+  return r;
+}
+
 // The fast path accepts a step whose probabilities (against a running max
 // that may be stale) sum to at most 2^kFastSumLog2: each is then at most
 // 2^16, far from overflow in bf16 and in the fp32 sums and accumulators, and
@@ -314,8 +324,8 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 constexpr float kFastSumLimit = 65536.0f;
 
 // Probabilities exp2(S*c2 - base) of a 64-key step in one pass: packed FFMA
-// for the exponent, MUFU exp2, packed row sums, bf16 pairs written in place
-// into v[0..31].  Returns their sum.  For s32 scores the int->float
+// for the exponent, MUFU exp2, bf16 pairs written in place into v[0..31],
+// packed row sums of those bf16 values.  Returns their sum.  For s32 scores the int->float
 // conversion is folded into the FFMA: float(S) = as_float(S + 0x4B400000) -
 // 1.5*2^23, exact for |S| < 2^22.
 template <bool kInt8, bool kMasked>
@@ -324,7 +334,7 @@ __device__ __forceinline__ float step_probs(uint32_t (&v)[64], const uint32_t (&
   const float bias = kInt8 ? fmaf(12582912.0f, c2, base) : base;
   const uint64_t c2x2 = f2_pack(c2, c2);
   const uint64_t nbx2 = f2_pack(-bias, -bias);
-  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
     const uint32_t a = kInt8 ? v[2 * c] + 0x4B400000u : v[2 * c];
@@ -338,15 +348,16 @@ __device__ __forceinline__ float step_probs(uint32_t (&v)[64], const uint32_t (&
       e0 = ((w >> ((2 * c) % 32)) & 1u) ? e0 : 0.0f;
       e1 = ((w >> ((2 * c + 1) % 32)) & 1u) ? e1 : 0.0f;
     }
-    acc[c & 3] = f2_add(acc[c & 3], f2_pack(e0, e1));
-    v[c] = pack_bf16x2(e0, e1);
+    // the row sum adds the bf16-rounded probabilities the P.V MMA reads, so
+    // the normalised weights sum to one: a row dominated by a few keys then
+    // reproduces their values instead of carrying the rounding of their
+    // weights (up to 2^-9 relative) into the output
+    const uint32_t pk = pack_bf16x2(e0, e1);
+    acc[2 * (c & 3)] = add_bf16_lo(pk, acc[2 * (c & 3)]);
+    acc[2 * (c & 3) + 1] = add_bf16_hi(pk, acc[2 * (c & 3) + 1]);
+    v[c] = pk;
   }
-  float s0, s1, s2, s3, s4, s5, s6, s7;
-  f2_unpack(acc[0], s0, s1);
-  f2_unpack(acc[1], s2, s3);
-  f2_unpack(acc[2], s4, s5);
-  f2_unpack(acc[3], s6, s7);
-  return ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
+  return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
 }
 
 template <bool kInt8>

@@ -870,7 +870,7 @@ extern "C" int cast_swap_objective(int n, int tiles, int bins, const float *u_re
   p.ops = operators, p.coef = coefficient, p.hess = hessian, p.row_gate = row_gate;
   p.gate = gate, p.stats = stats;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const dim3 g1(2 * n_targets, ceil_div(n * n, castk::kSwapObjThreads));
+  const dim3 g1(2 * n_targets, ceil_div(n * n, castk::kSwapObjThreads / 32));
   castk::swap_operator_kernel<<<g1, castk::kSwapObjThreads, 0, s>>>(p);
   CAST_CUDA_TRY(cudaGetLastError());
   const int g2 = std::max(1, std::min(1024, ceil_div(p.R * p.R + p.R, castk::kSwapObjThreads)));

@@ -1284,7 +1284,39 @@ __global__ void __launch_bounds__(kParStatThreads, 1)
 
 // ---------------------------------------------------------------------------
 // grid (HW, n_targets); each thread handles 4 channels.
+// The routing transport's mean affinities (stats tail): each used pair's
+// mean over its 18 x 66 affinities, and the mean over the targets of their
+// pair's affinities, summed in double in a fixed order by one CTA.
+__device__ void par_mean_affinity(const ParParams &p) {
+  __shared__ double red[256 / 32];
+  __shared__ double pair_sum[kParMaxPairs];
+  constexpr int per = kParTiles * (2 * kParFreq + 5), g0 = kParTiles * (kParFreq + 1);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int pr = 0; pr < p.n_pairs; ++pr) {
+    const float *g = p.stats + (size_t)pr * per + g0;
+    double s = 0.0;
+    for (int i = threadIdx.x; i < kParTiles * kParFreq; i += blockDim.x) s += (double)g[i];
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+      pair_sum[pr] = t;
+      p.stats[(size_t)kParMaxPairs * per + pr] = (float)(t / (kParTiles * kParFreq));
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0 && p.n_targets > 0) {
+    double t = 0.0;
+    for (int tg = 0; tg < p.n_targets; ++tg) t += pair_sum[p.target_pair[tg]];
+    p.stats[(size_t)kParMaxPairs * per + kParMaxPairs] =
+        (float)(t / ((double)p.n_targets * kParTiles * kParFreq));
+  }
+}
+
 __global__ void __launch_bounds__(256) par_ola_kernel(const ParParams p) {
+  if (p.stats && blockIdx.x == 0 && blockIdx.y == 0) par_mean_affinity(p);
   const int pix = blockIdx.x, tg = blockIdx.y;
   const int y = pix / kParW, x = pix % kParW;
   int tiles[4], offs[4], n = 0;

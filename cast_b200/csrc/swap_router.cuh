@@ -41,6 +41,7 @@ struct SwapCtl {
   int min_count_flip;        // INT_MAX - the smallest count over every row (0: no row yet)
   int max_count;             // the largest count over every row
   int current_changed;       // a swap removed or added a current-chunk key
+  int hist_delta;            // historical slots added minus removed by the swaps
   unsigned long long count_sum, hist_before;
 };
 
@@ -409,6 +410,7 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
           ctl->swaps += 1;
           ctl->improvement += -(double)bv;
           ctl->current_changed |= (k >= p.M) || (cg[b.l] >= p.M);
+          ctl->hist_delta += (cg[b.l] < p.M ? 1 : 0) - (k < p.M ? 1 : 0);
         }
       }
     }
@@ -442,22 +444,8 @@ __global__ void __launch_bounds__(kSwapRoundThreads)
       stats[9] = (double)ctl->max_count;
       stats[10] = (double)ctl->count_sum;
       stats[11] = (double)ctl->hist_before;
+      stats[12] = (double)ctl->hist_before + (double)ctl->hist_delta;
       stats[13] = (double)ctl->current_changed;
-    }
-    // the historical budget after the swaps, over every valid slot
-    unsigned long long hist = 0;
-    for (int i = tid; i < p.B * p.H * p.Q * p.S; i += blockDim.x) {
-      const int qr = i / p.S, j = i % p.S;
-      hist += (j < counts[qr]) && selected[i] < p.M;
-    }
-    for (int o = 16; o; o >>= 1) hist += __shfl_xor_sync(0xffffffffu, hist, o);
-    __syncthreads();
-    if (lane == 0) dred[warp] = (double)hist;
-    __syncthreads();
-    if (tid == 0) {
-      double t = 0.0;
-      for (int w = 0; w < nwarps; ++w) t += dred[w];
-      stats[12] = t;
     }
   }
   if (tid == 0) ctl->ticket = 0u;
@@ -501,10 +489,11 @@ struct SwapObjParams {
   double *stats;              // [5]: gate, [6]: matching affinity, [7]: gated cells
 };
 
-// grid (2T, ceil(n*n / threads)): op k = 2t + side is
+// grid (2T, ceil(n*n / 8)), 8 warps: op k = 2t + side is
 //   s * (I + sum_p V_p ((exp(i x g_p theta_p) - 1) * U_p))
-// (side 0: x = a, s = 1-a; side 1: x = -(1-a), s = a).  CTA (0, 0) also
-// evaluates the transport gates.
+// (side 0: x = a, s = 1-a; side 1: x = -(1-a), s = a).  Each warp computes
+// one output entry (o, j), its lanes splitting the tiles x bins terms, then a
+// shuffle reduction.  CTA (0, 0) also evaluates the transport gates.
 __global__ void __launch_bounds__(kSwapObjThreads) swap_operator_kernel(const __grid_constant__ SwapObjParams p) {
   __shared__ float rc_[kSwapObjMaxBins], rs_[kSwapObjMaxBins];
   const int k = blockIdx.x, t = k >> 1, side = k & 1;
@@ -520,22 +509,32 @@ __global__ void __launch_bounds__(kSwapObjThreads) swap_operator_kernel(const __
       rs_[i] = sn;
     }
   __syncthreads();
-  const int idx = blockIdx.y * blockDim.x + threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int idx = blockIdx.y * (kSwapObjThreads / 32) + warp;
   if (idx < p.n * p.n) {
     const int o = idx / p.n, j = idx % p.n;
-    float acc = 0.f;
+    float acc0 = 0.f, acc1 = 0.f;
     if (tg.theta)
-      for (int tp = 0; tp < p.tiles; ++tp) {
-        const float *ur = p.u_re + (size_t)tp * p.bins * p.n + j, *ui = p.u_im + (size_t)tp * p.bins * p.n + j;
-        const float *vr = p.v_re + ((size_t)tp * p.n + o) * p.bins, *vi = p.v_im + ((size_t)tp * p.n + o) * p.bins;
-        const float *c = rc_ + tp * p.bins, *s = rs_ + tp * p.bins;
-        for (int f = 0; f < p.bins; ++f) {
-          const float a = __ldg(ur + (size_t)f * p.n), b = __ldg(ui + (size_t)f * p.n);
-          const float wr = c[f] * a - s[f] * b, wi = c[f] * b + s[f] * a;
-          acc = fmaf(__ldg(vr + f), wr, fmaf(__ldg(vi + f), wi, acc));
+      for (int i = lane; i < nb; i += 64) {
+#pragma unroll
+        for (int u2 = 0; u2 < 2; ++u2) {
+          const int ii = i + 32 * u2;
+          if (ii >= nb) break;
+          const int tp = ii / p.bins, f = ii - tp * p.bins;
+          const float a = __ldg(p.u_re + (size_t)ii * p.n + j), b = __ldg(p.u_im + (size_t)ii * p.n + j);
+          const float vr = __ldg(p.v_re + ((size_t)tp * p.n + o) * p.bins + f);
+          const float vi = __ldg(p.v_im + ((size_t)tp * p.n + o) * p.bins + f);
+          const float c = rc_[ii], s = rs_[ii];
+          const float wr = c * a - s * b, wi = c * b + s * a;
+          if (u2 == 0)
+            acc0 = fmaf(vr, wr, fmaf(vi, wi, acc0));
+          else
+            acc1 = fmaf(vr, wr, fmaf(vi, wi, acc1));
         }
       }
-    p.ops[(size_t)k * p.n * p.n + idx] = sc * ((o == j ? 1.f : 0.f) + acc);
+    float acc = acc0 + acc1;
+    for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) p.ops[(size_t)k * p.n * p.n + idx] = sc * ((o == j ? 1.f : 0.f) + acc);
   }
   if (k == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
     int status = 0;

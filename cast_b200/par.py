@@ -21,6 +21,9 @@ TILES = 18
 FREQS = 66
 MAX_PAIRS = 16                        # castk::kParMaxPairs
 STATS_PER_PAIR = TILES * (2 * FREQS + 5)  # theta, confidence, g, displacement, base, ramp
+MEANS_AT = MAX_PAIRS * STATS_PER_PAIR    # per-pair mean affinities, then the layer's
+STATS_FLOATS = MEANS_AT + MAX_PAIRS + 1
+_COUNT_CACHE: dict = {}  # device -> the constant affinity support count (18 * 66)
 
 
 def bracket_targets(anchors: list[int], current_length: int, boundary: int):
@@ -123,24 +126,23 @@ class FCPASMCorrector:
             return None
         return self._fc_routing_transport.get((int(self._step), source))
 
-    def _publish(self, layer_index, anchors, pair_of_target, pairs, stats, h, w):
+    def _publish(self, layer_index, anchors, pairs, stats, h, w):
+        # every value below is a view into the statistics the kernels wrote:
+        # publishing launches nothing
         theta, affinity = stats_views(stats, len(pairs))
-        if len(pairs) == 1:
-            mean = affinity[0].mean()
-        else:  # every target's copy of its pair's affinity, as the reference stacks them
-            mean = torch.stack([affinity[i] for i in pair_of_target]).mean()
-        self._fc_previous_mean_affinity = mean.detach()
+        self._fc_previous_mean_affinity = stats[MEANS_AT + MAX_PAIRS]
         if not self.should_publish_fc_routing_transport(layer_index):
             return
+        count = _COUNT_CACHE.get(stats.device)
+        if count is None:
+            count = torch.full((), TILES * FREQS, dtype=torch.long, device=stats.device)
+            _COUNT_CACHE[stats.device] = count
         published = {}
         for i, key in enumerate(pairs):
-            aff = affinity[i]
             published[key] = {
-                "theta": theta[i], "affinity": aff, "mean_affinity": aff.mean(),
+                "theta": theta[i], "affinity": affinity[i], "mean_affinity": stats[MEANS_AT + i],
                 "mean_affinity_reduction": "all_tile_frequencies",
-                "affinity_support_count": torch.full((), aff.numel(), dtype=torch.long,
-                                                     device=aff.device),
-                "affinity_total_count": int(aff.numel()),
+                "affinity_support_count": count, "affinity_total_count": TILES * FREQS,
             }
         self._fc_routing_transport[(int(self._step), int(layer_index))] = {
             "source_layer": int(layer_index), "source_step": int(self._step),
@@ -207,8 +209,7 @@ class FCPASMCorrector:
         frames_arr = (_lib.ctypes.c_int32 * len(frames))(*frames)
         stats = None
         if self.record_stats or targets:
-            stats = torch.empty(MAX_PAIRS * STATS_PER_PAIR, dtype=torch.float32,
-                                device=full_residual.device)
+            stats = torch.empty(STATS_FLOATS, dtype=torch.float32, device=full_residual.device)
         if tile_confidence is not None:
             tile_confidence = tile_confidence.to(device=full_residual.device,
                                                  dtype=torch.float32).contiguous()
@@ -222,8 +223,7 @@ class FCPASMCorrector:
         )
         self.last_stats = stats
         if targets:
-            self._publish(layer_index, anchors, pair_of_target, pairs, stats, spatial_height,
-                          spatial_width)
+            self._publish(layer_index, anchors, pairs, stats, spatial_height, spatial_width)
         self._records.append({"layer_index": int(layer_index), "status": "corrected",
                               "target_frames": targets,
                               "target_anchor_pairs": [list(pairs[i]) for i in pair_of_target]})

@@ -383,9 +383,17 @@ CAST_API size_t cast_swap_route_workspace_bytes(int B, int H, int Q, int K, int 
  *   tile_confidence float [n_pairs,P] or NULL: per-tile confidence replacing
  *                   base*ramp (the reference's precomputed_tile_confidence),
  *                   pairs in chronological order of the used anchor pairs.
- *   stats_out       float or NULL: per used pair [P,11,6] theta, [P] conf,
- *                   [P,11,6] affinity, [P,2] displacement (see par.cu).
- * Supported: H=22, W=40 (3x6 tiles of 11x10), C multiple of 32.
+ *   stats_out       float [16*(18*137) + 17] or NULL: for each of up to 16
+ *                   used anchor pairs (chronological order of first use) a
+ *                   block of 18*137 floats: theta [18,11,6], confidence [18],
+ *                   affinity g [18,11,6], displacement [18,2], base confidence
+ *                   [18], ramp confidence [18]; then, at offset 16*18*137, the
+ *                   mean affinity of each pair [16] and the mean of every
+ *                   target's pair affinity [1] -- the FC routing transport's
+ *                   mean_affinity and the corrector's _fc_previous_mean_affinity
+ *                   (:577-658, :3667-3669), reduced on the device in a fixed
+ *                   order.  Written only when the call has targets.
+ * Supported: H=22, W=40 (3x6 tiles of 11x10), C a multiple of 4.
  */
 CAST_API int cast_par_fcpasm(void *full_residual, const void *active_residual, const int32_t *active_frames,
                     int n_active, int T, int memory_length, int H, int W, int C, float tau_low,

@@ -491,6 +491,9 @@ def _full_size(w, gold_name):
         got = results[policy][0].float().numpy()[:, :, rows].astype(np.float64)
         d = np.abs(got - ref[:, :, rows])
         errs[policy] = (float(d.max()), float(d.mean()))
+        at = np.unravel_index(int(d.argmax()), d.shape)
+        print(f"{gold_name} {policy}: max {d.max():.4e} at (b,h,row,d)={tuple(int(x) for x in at)} "
+              f"got {got[at]:.5f} ref {ref[:, :, rows][at]:.5f}; |ref| max {np.abs(ref[:, :, rows]).max():.3f}")
         assert d.max() < MAX_ABS and d.mean() < MEAN_ABS, (policy, errs[policy])
     # the pure int8 policy against the bf16 path: measured, reported
     got = results["int8"][0].float().numpy()[:, :, rows].astype(np.float64)
