@@ -39,6 +39,13 @@ SIGNATURES = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_int, c_float, c_void_p, c_void_p],
     ),
+    "cast_compact_select": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float,
+         c_void_p, c_void_p, c_size_t, c_void_p],
+    ),
+    "cast_compact_select_workspace_bytes": (c_size_t, [c_int] * 5),
     "cast_taba_select": (
         c_int,
         [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,

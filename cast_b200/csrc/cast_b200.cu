@@ -310,6 +310,114 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
 }
 
 // ===========================================================================
+// Compact-path selection
+// ===========================================================================
+extern "C" size_t cast_compact_select_workspace_bytes(int B, int H, int n_blocks, int block_size,
+                                                      int D) {
+  if (B <= 0 || H <= 0 || n_blocks <= 0 || block_size <= 0 || D <= 0) return 0;
+  const int L = n_blocks * block_size;
+  return cast_rcsa_select_quant_workspace_bytes(B, H, L, L, D, block_size);
+}
+
+extern "C" int cast_compact_select(const void *q, const void *k, const uint8_t *valid, int B, int H,
+                                   int n_blocks, int block_size, int D, int nh, int nw,
+                                   const int32_t *row_degrees, int max_degree, int32_t *sel_idx,
+                                   int32_t *sel_cnt, int8_t *q_codes, float *q_scales,
+                                   int8_t *k_codes, float *k_scales, uint8_t *qk_mode, int policy,
+                                   float int8_tolerance, double *pooled, void *workspace,
+                                   size_t workspace_bytes, cast_stream_t stream) {
+  if (!q || !k || !valid || !row_degrees || !sel_idx || !sel_cnt)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "q, k, valid, row_degrees, sel_idx and sel_cnt are required");
+  if (B <= 0 || H <= 0 || n_blocks <= 0 || block_size <= 0 || nh <= 0 || nw <= 0 ||
+      max_degree <= 0 || max_degree > n_blocks || n_blocks % (nh * nw))
+    return fail(CAST_ERR_INVALID_ARGUMENT,
+                "bad sizes (B=%d H=%d blocks=%d block=%d grid %dx%d max_degree=%d)", B, H, n_blocks,
+                block_size, nh, nw, max_degree);
+  if (policy < CAST_POLICY_BF16 || policy > CAST_POLICY_AUTO)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "unknown precision policy %d", policy);
+  if (D != 64 && D != 128) return fail(CAST_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", D);
+  if (!aligned16(q) || !aligned16(k)) return fail(CAST_ERR_ALIGNMENT, "q/k must be 16-byte aligned");
+  if ((q_codes && !aligned16(q_codes)) || (k_codes && !aligned16(k_codes)))
+    return fail(CAST_ERR_ALIGNMENT, "code buffers must be 16-byte aligned");
+  if (qk_mode && policy != CAST_POLICY_BF16 && (!q_codes || !k_codes || !q_scales || !k_scales))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "int8 policies need q/k codes and scales");
+  const int nb = n_blocks, L = nb * block_size;
+  const size_t need = cast_compact_select_workspace_bytes(B, H, nb, block_size, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(CAST_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  double *pooled_ws = reinterpret_cast<double *>(ws);
+  ws += sq_pooled_bytes(B, H, nb, nb, D);
+  float *rms = reinterpret_cast<float *>(ws);
+  ws += sq_rms_bytes(B, H, nb, nb);
+  float *qs = q_scales ? q_scales : reinterpret_cast<float *>(ws);
+  ws += align_up((size_t)B * H * 2 * nb * sizeof(float), 256);
+  float *ks = k_scales ? k_scales : reinterpret_cast<float *>(ws);
+  ws += align_up((size_t)B * H * 2 * nb * sizeof(float), 256);
+  uint8_t *need_flags = ws;
+  double *pooled_out = pooled ? pooled : pooled_ws;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __nv_bfloat16 *qb = static_cast<const __nv_bfloat16 *>(q);
+  const __nv_bfloat16 *kb = static_cast<const __nv_bfloat16 *>(k);
+  // pooled (masked) means, block RMS and scales; codes in the same pass for
+  // the int8 policy, after the selection for the auto policy
+  const bool lazy = policy == CAST_POLICY_AUTO && qk_mode;
+  const bool codes_now = policy == CAST_POLICY_INT8 && qk_mode;
+  int8_t *qc1 = codes_now ? q_codes : nullptr, *kc1 = codes_now ? k_codes : nullptr;
+  uint8_t *nf = lazy ? need_flags : nullptr;
+  dim3 grid(2 * nb, B * H);
+  if (D == 128)
+    castk::pool_quant_kernel<128, true><<<grid, 256, 0, s>>>(qb, kb, nullptr, valid, valid, L, L, block_size,
+                                                             nb, nb, qc1, qs, kc1, ks, nullptr, nullptr,
+                                                             pooled_out, rms, nf);
+  else
+    castk::pool_quant_kernel<64, true><<<grid, 128, 0, s>>>(qb, kb, nullptr, valid, valid, L, L, block_size,
+                                                            nb, nb, qc1, qs, kc1, ks, nullptr, nullptr,
+                                                            pooled_out, rms, nf);
+  CAST_CUDA_TRY(cudaGetLastError());
+  int pw = 1;
+  while (pw < nb) pw <<= 1;
+  const size_t dsm_base = (sizeof(double) + sizeof(int32_t)) * pw + 2 * sizeof(float) * nb + 16;
+  const size_t stage_bytes = (size_t)nb * D * sizeof(double);
+  const bool stage_k = stage_bytes <= 160 * 1024;
+  const size_t dsm = dsm_base + (stage_k ? stage_bytes : 0);
+  if (dsm > 200 * 1024) return fail(CAST_ERR_UNSUPPORTED, "too many compact blocks (%d)", nb);
+  static std::once_flag csel_once;
+  static cudaError_t csel_err = cudaSuccess;
+  std::call_once(csel_once, [] {
+    csel_err = cudaFuncSetAttribute(castk::compact_select_kernel<128>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (csel_err == cudaSuccess)
+      csel_err = cudaFuncSetAttribute(castk::compact_select_kernel<64>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  CAST_CUDA_TRY(csel_err);
+  dim3 g2(nb, B * H);
+  if (D == 128)
+    castk::compact_select_kernel<128><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nb, nh, nw, row_degrees,
+                                                           max_degree, sel_idx, sel_cnt, qk_mode, policy,
+                                                           int8_tolerance, stage_k, nf);
+  else
+    castk::compact_select_kernel<64><<<g2, 256, dsm, s>>>(pooled_out, rms, qs, ks, nb, nh, nw, row_degrees,
+                                                          max_degree, sel_idx, sel_cnt, qk_mode, policy,
+                                                          int8_tolerance, stage_k, nf);
+  CAST_CUDA_TRY(cudaGetLastError());
+  if (lazy) {
+    const int g3 = B * H * 2 * nb;
+    if (D == 128)
+      castk::quant_needed_kernel<128, true><<<g3, 256, 0, s>>>(qb, kb, valid, valid, L, L, block_size, nb,
+                                                               nb, B * H, need_flags, q_codes, qs, k_codes, ks);
+    else
+      castk::quant_needed_kernel<64, true><<<g3, 128, 0, s>>>(qb, kb, valid, valid, L, L, block_size, nb,
+                                                              nb, B * H, need_flags, q_codes, qs, k_codes, ks);
+    CAST_CUDA_TRY(cudaGetLastError());
+  }
+  return CAST_OK;
+}
+
+// ===========================================================================
 // TABA selection
 // ===========================================================================
 extern "C" size_t cast_taba_select_workspace_bytes(int B, int H, int T, int Hl, int Wl, int D,

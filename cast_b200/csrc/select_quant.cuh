@@ -576,6 +576,96 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
+// Compact-path selection (proposed/matrix_curvature_phase_frame_weave.py:
+// 5687-5831): every compact block ranks every block by its pooled cosine plus
+// 1e6 on the Manhattan-<=1 stencil of the (cell, nh, nw) grid (added to the
+// float32 score, as the reference adds it), keeps the first maxdeg in
+// (rank descending, index ascending) order, and counts row_degrees[i] of
+// them; then the int8/bf16 QK^T policy over those counted blocks.
+// grid = (nb, B*H), 256 threads.  Pooled layout [BH][2*nb][D] (queries then
+// keys), as pool_quant_kernel writes it with nqb = nkb = nb.
+// Dynamic smem: the key blocks' pooled vectors (when stage_k), the sort keys
+// [P] and indices [P], the key blocks' RMS and scales [nb] each.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256)
+    compact_select_kernel(const double *__restrict__ pooled, const float *__restrict__ block_rms,
+                          const float *__restrict__ q_scales, const float *__restrict__ k_scales,
+                          int nb, int nh, int nw, const int32_t *__restrict__ row_degrees,
+                          int maxdeg, int32_t *sel_idx, int32_t *sel_cnt, uint8_t *qk_mode,
+                          int policy, float tol, bool stage_k, uint8_t *need_flags) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  int P = 1;
+  while (P < nb) P <<= 1;
+  double *kst = reinterpret_cast<double *>(dsm);                   // [nb][D] or none
+  double *score = kst + (stage_k ? (size_t)nb * D : 0);            // [P]
+  int32_t *sidx = reinterpret_cast<int32_t *>(score + P);          // [P]
+  float *k_rms = reinterpret_cast<float *>(sidx + P);              // [nb]
+  float *k_sc = k_rms + nb;                                        // [nb]
+  __shared__ double qn[D];
+  const int qi = blockIdx.x, bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n_warps = blockDim.x >> 5;
+  const double *prow = pooled + (size_t)bh * 2 * nb * D;
+  if (stage_k) {
+    const double *src = prow + (size_t)nb * D;
+    for (int e = threadIdx.x * 2; e < nb * D; e += blockDim.x * 2) cp_async16(kst + e, src + e);
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = prow[(size_t)qi * D + d];
+  const bool auto_policy = qk_mode && policy == CAST_POLICY_AUTO;
+  if (auto_policy)
+    for (int kb = threadIdx.x; kb < nb; kb += blockDim.x) {
+      k_rms[kb] = block_rms[(size_t)bh * 2 * nb + nb + kb];
+      k_sc[kb] = k_scales[(size_t)bh * nb + kb];
+    }
+  if (stage_k) cp_async_wait_all();
+  __syncthreads();
+  const int spatial = nh * nw;
+  const int ti = qi / spatial, hi = (qi % spatial) / nw, wi = qi % nw;
+  for (int kb = warp; kb < nb; kb += n_warps) {
+    const double *b = stage_k ? kst + (size_t)kb * D : prow + (size_t)(nb + kb) * D;
+    const double s = warp_dot<D>(qn, b, lane);
+    if (lane == 0) {
+      const int tj = kb / spatial, hj = (kb % spatial) / nw, wj = kb % nw;
+      const bool local = abs(ti - tj) + abs(hi - hj) + abs(wi - wj) <= 1;
+      const float s32 = (float)s;
+      score[kb] = (double)(local ? __fadd_rn(s32, 1.0e6f) : s32);
+      sidx[kb] = kb;
+    }
+  }
+  __syncthreads();
+  cta_sort_better(score, sidx, nb, P);
+  const int cnt = min(max(row_degrees[qi], 0), maxdeg);
+  int32_t *out = sel_idx + ((size_t)bh * nb + qi) * maxdeg;
+  for (int j = threadIdx.x; j < maxdeg; j += blockDim.x) out[j] = j < nb ? sidx[j] : -1;
+  if (threadIdx.x == 0) sel_cnt[(size_t)bh * nb + qi] = cnt;
+  if (qk_mode && warp == 0) {
+    uint8_t mode = policy == CAST_POLICY_INT8 ? 1 : 0;
+    if (auto_policy) {
+      // the same predicted logit error as the budget rule's policy, over the
+      // counted blocks of this row
+      const float rq = block_rms[(size_t)bh * 2 * nb + qi];
+      const float sq = q_scales[(size_t)bh * nb + qi];
+      float worst = 0.0f;
+      for (int j = lane; j < cnt; j += 32) {
+        const int kb = sidx[j];
+        const float rk = k_rms[kb], sk = k_sc[kb];
+        const float err = sqrtf((sq * sq * rk * rk + sk * sk * rq * rq) * (1.0f / 12.0f));
+        worst = fmaxf(worst, err * rq * rk);
+      }
+#pragma unroll
+      for (int s2 = 16; s2 >= 1; s2 >>= 1) worst = fmaxf(worst, __shfl_xor_sync(0xffffffffu, worst, s2));
+      mode = worst <= tol ? 1 : 0;
+    }
+    if (lane == 0) qk_mode[(size_t)bh * nb + qi] = mode;
+    if (need_flags && mode) {
+      uint8_t *nf = need_flags + (size_t)bh * 2 * nb;
+      if (lane == 0) nf[qi] = 1;
+      for (int j = lane; j < cnt; j += 32) nf[nb + sidx[j]] = 1;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // TABA: pooled means over (tt,th,tw) tiles of the visual grid (zero padding
 // counts in the mean, as _tile_visual_tensor does), then ranking.
 // grid = (nblocks, B*H).

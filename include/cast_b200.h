@@ -159,6 +159,38 @@ CAST_API int cast_rcsa_select_quant_noalloc(const void *q, const void *k, const 
                                    float int8_tolerance, double *pooled, cast_stream_t stream);
 
 /*
+ * Compact-path selection: the pooled-Q/K ranking of
+ * MatrixCurvaturePhaseFrameWeave._compact_cwca_attention (proposed/
+ * matrix_curvature_phase_frame_weave.py:5687-5701 pooling, :5718-5725
+ * stencil, :5828-5832 ranking and top-k) on the packed compact blocks, and
+ * the per-block int8 quantisation the attention reads.
+ *   q, k          bf16 [B,H,n_blocks*block_size,D], packed (padding rows may
+ *                 hold anything: they are excluded by `valid`)
+ *   valid         uint8 [n_blocks*block_size]: 1 for a real token
+ *   nh, nw        the spatial block grid; blocks are (cell, nh, nw) row-major
+ *   row_degrees   int32 [n_blocks] device: each row's degree (host-computed
+ *                 budget, :5726-5817); max_degree = its maximum
+ *   sel_idx       int32 [B,H,n_blocks,max_degree]: every block ranked by its
+ *                 pooled (masked mean, L2-normalised) cosine + 1e6 on the
+ *                 Manhattan-<=1 stencil, first max_degree in (rank desc,
+ *                 index asc) order; sel_cnt int32 [B,H,n_blocks] = degrees
+ *   q/k_codes, q/k_scales, qk_mode, policy, int8_tolerance: as
+ *                 cast_rcsa_select_quant (auto: int8 QK^T only where the
+ *                 predicted logit error over the row's counted blocks is below
+ *                 the tolerance, codes written only for the blocks it reads)
+ *   pooled        double [B,H,2*n_blocks,D] or NULL
+ * Launches: 2 (3 under the auto policy).
+ */
+CAST_API int cast_compact_select(const void *q, const void *k, const uint8_t *valid, int B, int H,
+                        int n_blocks, int block_size, int D, int nh, int nw,
+                        const int32_t *row_degrees, int max_degree, int32_t *sel_idx,
+                        int32_t *sel_cnt, int8_t *q_codes, float *q_scales, int8_t *k_codes,
+                        float *k_scales, uint8_t *qk_mode, int policy, float int8_tolerance,
+                        double *pooled, void *workspace, size_t workspace_bytes,
+                        cast_stream_t stream);
+CAST_API size_t cast_compact_select_workspace_bytes(int B, int H, int n_blocks, int block_size, int D);
+
+/*
  * TABA full-layer selection: pooled-QK cosine on the (tt,th,tw) block grid of
  * a [T,Hl,Wl] latent, +1e6 Manhattan-<=1 stencil (added in float32 as the
  * reference does), stable descending order truncated to max(row_degrees).
