@@ -27,7 +27,7 @@ from .select import TABASelector  # noqa: F401
 __version__ = "0.1.0"
 
 
-def make_cast_components():
+def make_cast_components(**kwargs):
     from .components import make_cast_components as _mk
 
-    return _mk()
+    return _mk(**kwargs)

@@ -24,7 +24,14 @@ code, and :func:`patched_seams` lists what is installed):
   own FC knobs; it publishes the FC routing transport into the reference
   corrector's own cache, so the weave's swap router reads it;
 * the weave's ``fc_pasm_swap_router.refine`` ->
-  :class:`cast_b200.swap_router.FCPASMLocalCoordinateSwapRouter`.
+  :class:`cast_b200.swap_router.FCPASMLocalCoordinateSwapRouter`;
+* ``MatrixCurvaturePhaseFrameWeave._compact_cwca_attention`` (the compact
+  layers' packing, pooled-Q/K ranking, block-sparse attention and scatter) ->
+  :func:`cast_b200.compact_attention.compact_cwca_attention`, with the QK^T
+  precision policy given to :func:`make_cast_components` (``"auto"``: int8
+  QK^T where its predicted logit error stays below the tolerance); on the
+  router's layers the reference's method keeps the ranking and hands it to
+  the B200 router and attention.
 
 The reference package itself (its orchestration, CAFS, degree budgets, the
 memory compiler) is not part of this repository; it is imported from the
@@ -38,11 +45,13 @@ import math
 
 import torch
 
-from . import _lib, barycentric, rcsa, swap_router
+from . import _lib, barycentric, compact_attention, rcsa, swap_router
 from .par import FCPASMCorrector
 from .select import TABASelector
 
 _PATCHED: dict = {}
+# QK^T precision of the compact layers' attention (make_cast_components)
+_SETTINGS = {"precision": "auto", "int8_tolerance": rcsa.DEFAULT_INT8_TOLERANCE}
 
 # FC knobs of the reference corrector that change its arithmetic, with the
 # value the B200 path implements (the factory's, cast_matrix.py:74-96).  A
@@ -132,9 +141,18 @@ def _taba_select(self, q, k, *, geometry_indices, geometry_counts, latent_hw, bl
     return selected, counts, report
 
 
+def _compact_cwca(self, module, q, k, v, layout):
+    """``MatrixCurvaturePhaseFrameWeave._compact_cwca_attention`` on the B200."""
+    original = _PATCHED["compact_cwca"].__get__(self, type(self))
+    return compact_attention.compact_cwca_attention(
+        self, module, q, k, v, layout, original=original, policy=_SETTINGS["precision"],
+        int8_tolerance=_SETTINGS["int8_tolerance"])
+
+
 def install_kernels() -> None:
     """Replaces the reference's static seams: the attention launches, the
-    TABA selection and the pair writer (idempotent)."""
+    TABA selection, the compact CWCA attention and the pair writer
+    (idempotent)."""
     jit = _ref("matrix_jit_spatial_acceleration")
     weave = _ref("matrix_curvature_phase_frame_weave")
     qk = _ref("qk_uncertainty_tangent_attention")
@@ -152,6 +170,9 @@ def install_kernels() -> None:
         cls = qk.MatrixTrajectoryAdaptiveBudgetAttentionCompiler
         _PATCHED["taba_select"] = cls.select
         cls.select = _taba_select
+    if "compact_cwca" not in _PATCHED:
+        _PATCHED["compact_cwca"] = weave.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention
+        weave.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention = _compact_cwca
 
 
 def uninstall_kernels() -> None:
@@ -169,6 +190,9 @@ def uninstall_kernels() -> None:
     if "taba_select" in _PATCHED:
         qk = _ref("qk_uncertainty_tangent_attention")
         qk.MatrixTrajectoryAdaptiveBudgetAttentionCompiler.select = _PATCHED.pop("taba_select")
+    if "compact_cwca" in _PATCHED:
+        weave = _ref("matrix_curvature_phase_frame_weave")
+        weave.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention = _PATCHED.pop("compact_cwca")
 
 
 def unsupported_fc_knob(ref_corrector) -> str | None:
@@ -274,6 +298,7 @@ def patched_seams(weave=None) -> dict:
         "longcat_asymmetric": wv.MatrixCausalFrameLayerRelay._longcat_asymmetric is rcsa.longcat_asymmetric,
         "pair_write": wv.direct_control_barycentric_pair_write is barycentric.direct_control_barycentric_pair_write,
         "taba_select": qk.MatrixTrajectoryAdaptiveBudgetAttentionCompiler.select is _taba_select,
+        "compact_cwca": wv.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention is _compact_cwca,
     }
     if weave is not None:
         out["correct"] = bool(getattr(getattr(weave, "world_spectral_corrector", None), "_cast_b200", False))
@@ -281,8 +306,17 @@ def patched_seams(weave=None) -> dict:
     return out
 
 
-def make_cast_components():
-    """``make_cast_components()`` with the B200 hot path installed."""
+def make_cast_components(*, precision: str = "auto",
+                         int8_tolerance: float = rcsa.DEFAULT_INT8_TOLERANCE):
+    """``make_cast_components()`` with the B200 hot path installed.
+
+    ``precision`` is the compact layers' QK^T policy: ``"auto"`` (int8 where
+    the predicted logit error of the int8 product stays below
+    ``int8_tolerance``, bf16 elsewhere), ``"bf16"`` (the reference's numerics)
+    or ``"int8"``."""
+    if precision not in rcsa.POLICIES:
+        raise ValueError(f"precision must be one of {sorted(rcsa.POLICIES)}")
+    _SETTINGS.update(precision=precision, int8_tolerance=float(int8_tolerance))
     factory = importlib.import_module("interaction_accel.cast_matrix")
     install_kernels()
     memory, attention, weave = factory.make_cast_components()

@@ -307,6 +307,32 @@ def taba_select(
     return sel, cnt, sc
 
 
+def compact_pack(x: np.ndarray, block_indices: np.ndarray) -> np.ndarray:
+    """Token-order ``[B, L, H, D]`` -> packed ``[B, H, P, D]``: slot ``p`` holds
+    token ``block_indices[p]``, zeros where it is -1
+    (``proposed/matrix_curvature_phase_frame_weave.py:5677-5684``)."""
+    flat = block_indices.reshape(-1)
+    out = np.zeros((x.shape[0], x.shape[2], flat.size, x.shape[3]), dtype=x.dtype)
+    ok = flat >= 0
+    out[:, :, ok] = np.transpose(x[:, flat[ok]], (0, 2, 1, 3))
+    return out
+
+
+def compact_select(q_packed: np.ndarray, k_packed: np.ndarray, valid: np.ndarray, block_size: int,
+                   grid: tuple[int, int, int], row_degrees: np.ndarray):
+    """The compact path's ranking (``proposed/matrix_curvature_phase_frame_weave.py``
+    :5687-5701 masked pooled means, :5718-5725 the stencil on the
+    (cell, nh, nw) grid, :5828-5832 ``topk`` of score + 1e6 * stencil): the
+    first ``max(row_degrees)`` blocks of every row in (rank descending, index
+    ascending) order, counts ``row_degrees``.  ``valid``: bool ``[P]``."""
+    index = contiguous_block_index(q_packed.shape[-2], block_size)
+    qs, qc = block_sums(q_packed, index, valid)
+    ks, kc = block_sums(k_packed, index, valid)
+    sc = pooled_scores(pooled_normalized(qs, qc), pooled_normalized(ks, kc))
+    sel, cnt = taba_select_from_scores(sc, block_grid_local(*grid), row_degrees)
+    return sel, cnt, sc
+
+
 # ---------------------------------------------------------------------------
 # block-sparse attention
 # ---------------------------------------------------------------------------

@@ -51,6 +51,10 @@ Files:
   affinity; the layer's mean affinity; the corrected frames), and the
   reference router's ``refine`` at layer 22 on that sketch under the
   factory's production knobs and with two rounds.
+* ``compact_select_*.npz`` -- the compact path's selection: the layout the
+  reference's ``_layout`` builds, and the indices / counts its
+  ``_compact_cwca_attention`` hands to the attention launch, with the
+  curvature branch of its degree split (uniform and two curved profiles).
 * ``MANIFEST.json``      -- SHA-256 of every fixture and of every regenerated
   input (mirrors the hash manifest idea of ``scripts/check_release.py:19-26``).
 """
@@ -370,6 +374,72 @@ def make_swap(manifest: dict):
               float(rec["objective_after"]))
 
 
+COMPACT_SELECT_CASES = {
+    # name: (frames T, memory frames, active frames, block shape, heads, curvature or None, seed)
+    "uniform": (8, 3, (0, 1, 2, 3, 5, 6, 7), (1, 11, 8), 4, None, 41),
+    "curved": (9, 2, (0, 1, 2, 4, 5, 7, 8), (1, 11, 10), 3, (0.01, 0.02, 9.0, 0.03, 6.0, 0.05, 0.04), 42),
+    "tt2": (10, 4, (0, 1, 2, 3, 4, 6, 7, 9), (2, 11, 20), 2, (0.02, 0.03, 7.0, 0.01, 0.04, 5.0), 43),
+}
+
+
+def compact_select_case(name):
+    """Seeded token-order q/k/v ``[1, L, H, 128]`` (bf16) of a compact layer."""
+    frames, mem, active, shape, heads, curvature, seed = COMPACT_SELECT_CASES[name]
+    g = torch.Generator().manual_seed(seed)
+    n = len(active) * 22 * 40
+    q, k, v = ((torch.randn(1, n, heads, 128, generator=g) * (0.5 + i)).bfloat16() for i in range(3))
+    return q, k, v
+
+
+def make_compact_select(manifest: dict):
+    """The compact path's ranking through the reference's own
+    ``_compact_cwca_attention`` (proposed/matrix_curvature_phase_frame_weave.py:
+    5643-6125) on CPU: the factory's weave, its ``_layout`` of the active
+    frames, a plain (non-closed-loop) budget provider so the curvature branch
+    of the degrees runs with a fixed profile, and the attention launch
+    replaced by a recorder of the selection it receives."""
+    import types
+
+    from interaction_accel.cast_matrix import make_cast_components
+    from interaction_accel.methods.proposed import matrix_jit_spatial_acceleration as jit
+
+    _, _, weave = make_cast_components()
+    weave.geometry_provider = types.SimpleNamespace(mode="open_loop")
+    seen = {}
+
+    def recorder(q, k, v, indices, counts, valid, block_size):
+        seen.update(indices=indices.clone(), counts=counts.clone(), valid=valid.clone())
+        return torch.zeros_like(q)
+
+    saved = jit.MatrixJiTSpatialAcceleration._longcat_active
+    jit.MatrixJiTSpatialAcceleration._longcat_active = staticmethod(recorder)
+    try:
+        for name, (frames, mem, active, shape, heads, curvature, seed) in COMPACT_SELECT_CASES.items():
+            weave._current_curvature = (lambda n, c=curvature: None if c is None
+                                        else torch.tensor(c, dtype=torch.float32)[:n])
+            weave._layout_cache.clear()
+            layout = weave._layout(
+                x=torch.zeros(1, frames * 880, 8), grid_sizes=torch.tensor([[frames, 22, 40]]),
+                memory_length=mem, active_frames=torch.tensor(active),
+                orbit_sparse_layout=types.SimpleNamespace(block_shape=shape))
+            q, k, v = compact_select_case(name)
+            module = types.SimpleNamespace(block_idx=5, o=lambda t: t)
+            weave._compact_cwca_attention(module, q, k, v, layout)
+            rec = weave._last_compact_attention
+            manifest["inputs"][f"compact_select_{name}"] = {"q": sha(q), "k": sha(k), "v": sha(v)}
+            np.savez_compressed(
+                os.path.join(HERE, f"compact_select_{name}.npz"),
+                block_indices=layout.compact_block_indices.numpy(),
+                token_to_packed=layout.compact_token_to_packed.numpy(),
+                valid=seen["valid"].numpy(), selected=seen["indices"].numpy(),
+                counts=seen["counts"].numpy(), edge_budget=np.int64(rec["edge_budget"]),
+                maximum_degree=np.int64(rec["maximum_degree"]))
+            print(name, tuple(seen["indices"].shape), rec["edge_budget"], rec["maximum_degree"],
+                  sorted(set(seen["counts"][0, 0].tolist())))
+    finally:
+        jit.MatrixJiTSpatialAcceleration._longcat_active = saved
+
+
 TRANSPORT_ROUTER = {
     # router configurations run on the published sketch (FCPASMSwapRoutingConfig kwargs)
     "production": dict(num_swap_rounds=1, swap_eps=0.10, max_swaps_per_call=1, same_bank_only=True,
@@ -463,7 +533,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the CAST src/ directory")
     ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "compact", "par", "swap",
-                                                   "transport"),
+                                                   "transport", "compact_select"),
                     help="regenerate these fixtures only; other manifest entries are kept")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
@@ -475,7 +545,8 @@ def main():
     if args.only and os.path.exists(mpath):
         with open(mpath) as fh:
             manifest = json.load(fh)
-    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par", "swap", "transport"))
+    todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par", "swap", "transport",
+                             "compact_select"))
     if "cfg1" in todo:
         make_cfg1({}, manifest)
     if "cfg2" in todo:
@@ -490,6 +561,8 @@ def main():
         make_swap(manifest)
     if "transport" in todo:
         make_transport(manifest)
+    if "compact_select" in todo:
+        make_compact_select(manifest)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             with open(os.path.join(HERE, f), "rb") as fh:

@@ -41,7 +41,7 @@ def test_every_claimed_seam_is_patched(factory):
     seams = components.patched_seams(weave)
     assert seams == {k: True for k in seams}, seams
     assert set(seams) == {"longcat_active", "longcat_asymmetric", "pair_write", "taba_select",
-                          "correct", "refine"}
+                          "compact_cwca", "correct", "refine"}
     # the attention compiler reaches the patched TABA select through super()
     qk = importlib.import_module("interaction_accel.methods.proposed.qk_uncertainty_tangent_attention")
     assert isinstance(attention, qk.MatrixTrajectoryAdaptiveBudgetAttentionCompiler)
@@ -177,3 +177,79 @@ def test_transport_goldens_are_self_consistent():
         assert list(g["exact_frames"]) == anchors
         for tag in ("production", "two_rounds"):
             assert str(g[f"{tag}_status"]) == "refined" and int(g[f"{tag}_swap_count"]) >= 1
+
+
+def _golden_module():
+    import importlib.util
+    here = os.path.join(os.path.dirname(__file__), "golden")
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(here, "make_golden.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.mark.parametrize("name", ["uniform", "curved", "tt2"])
+def test_compact_degrees_match_reference(factory, name):
+    """The host-side degree split of the B200 compact path equals the counts
+    the reference's ``_compact_cwca_attention`` handed to its attention launch
+    (tests/golden/compact_select_*.npz), on the reference's own weave and
+    layout."""
+    import types
+
+    from cast_b200 import compact_attention as ca
+
+    mg = _golden_module()
+    frames, mem, active, shape, heads, curvature, _ = mg.COMPACT_SELECT_CASES[name]
+    _, _, weave = components.make_cast_components()
+    weave.geometry_provider = types.SimpleNamespace(mode="open_loop")
+    weave._current_curvature = (lambda n, c=curvature: None if c is None
+                                else torch.tensor(c, dtype=torch.float32)[:n])
+    layout = weave._layout(x=torch.zeros(1, frames * 880, 8), grid_sizes=torch.tensor([[frames, 22, 40]]),
+                           memory_length=mem, active_frames=torch.tensor(active),
+                           orbit_sparse_layout=types.SimpleNamespace(block_shape=shape))
+    tt, th, tw = shape
+    nh, nw = -(-22 // th), -(-40 // tw)
+    blocks = layout.compact_block_indices.shape[0]
+    cells = blocks // (nh * nw)
+    memory_frames = sum(1 for f in active if f < mem)
+    deg, _, meta = ca.compact_degrees(weave, layout, layer_index=5, blocks=blocks,
+                                      local_max=ca.stencil_max(cells, nh, nw), spatial=nh * nw, tt=tt,
+                                      compact_frames=len(active), memory_frames=memory_frames,
+                                      provider=None, device=torch.device("cpu"))
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", f"compact_select_{name}.npz"))
+    np.testing.assert_array_equal(deg.numpy(), g["counts"][0, 0])
+    assert meta is None
+    # the stencil maximum the reference computes with a [blocks, blocks] mask
+    ids = torch.arange(blocks)
+    bt, rem = ids // (nh * nw), ids % (nh * nw)
+    local = ((bt[:, None] - bt[None]).abs() + (rem // nw)[:, None].sub((rem // nw)[None]).abs()
+             + (rem % nw)[:, None].sub((rem % nw)[None]).abs()) <= 1
+    assert ca.stencil_max(cells, nh, nw) == int(local.sum(-1).max())
+
+
+def test_compact_degrees_closed_loop_provider_is_consulted():
+    """With a closed-loop provider the current rows' degrees are the
+    provider's, as the reference takes them (:5754-5772)."""
+    import types
+
+    from cast_b200 import compact_attention as ca
+
+    calls = {}
+
+    class Provider:
+        mode = "closed_loop"
+
+        def compact_closed_loop_degrees(self, **kw):
+            calls.update(kw)
+            n = kw["total_blocks"] - kw["memory_blocks"]
+            return torch.arange(n) % 3 + kw["base_degree"], {"source": "fake", "previous_layer": 4}
+
+    layout = types.SimpleNamespace(active_frames=torch.tensor([0, 2, 3]), memory_temporal=1,
+                                   total_temporal=4)
+    weave = types.SimpleNamespace(sparse_density=0.5)
+    deg, mean, meta = ca.compact_degrees(weave, layout, layer_index=7, blocks=12, local_max=4, spatial=4,
+                                         tt=1, compact_frames=3, memory_frames=1, provider=Provider(),
+                                         device=torch.device("cpu"))
+    assert mean == 6 and meta["source"] == "fake" and calls["layer_index"] == 7
+    assert calls["base_degree"] == 5 and calls["memory_blocks"] == 4
+    assert int(deg.sum()) == 12 * 6 and int(deg.max()) <= 12
