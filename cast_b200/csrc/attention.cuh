@@ -640,9 +640,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           kmask[w] = lo >= 32 ? 0xffffffffu : (lo <= 0 ? 0u : ((1u << lo) - 1u));
         }
         if (p.key_valid && valid_cols > 0) {
-          // 16-byte loads for whole chunks inside the step's valid keys, byte
-          // loads for a ragged last chunk; nothing past key valid_cols - 1.
+          // 16-byte loads for whole chunks inside the step's valid keys when
+          // the step's first key is 16-byte aligned in key_valid (key blocks
+          // of any size start anywhere), byte loads otherwise and for a
+          // ragged last chunk; nothing past key valid_cols - 1.
           const uint8_t *kv = p.key_valid + krow;
+          const bool kv16 = (reinterpret_cast<uintptr_t>(kv) & 15u) == 0;
 #pragma unroll
           for (int w = 0; w < 2; ++w) {
             uint32_t bits = 0;
@@ -650,11 +653,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             for (int q2 = 0; q2 < 2; ++q2) {
               const int c0 = 32 * w + 16 * q2;
               uint32_t words[4] = {0u, 0u, 0u, 0u};
-              if (c0 + 16 <= valid_cols) {
+              if (kv16 && c0 + 16 <= valid_cols) {
                 const uint4 b = *reinterpret_cast<const uint4 *>(kv + c0);
                 words[0] = b.x, words[1] = b.y, words[2] = b.z, words[3] = b.w;
               } else if (c0 < valid_cols) {
-                for (int c = c0; c < valid_cols; ++c)
+                for (int c = c0; c < min(valid_cols, c0 + 16); ++c)
                   words[(c - c0) >> 2] |= (uint32_t)kv[c] << (8 * ((c - c0) & 3));
               }
 #pragma unroll

@@ -2,6 +2,7 @@
 // declared in include/cast_b200.h and the host-side launch logic.
 #include <algorithm>
 #include <cstdarg>
+#include <cstdlib>
 #include <cmath>
 #include <functional>
 #include <map>
@@ -658,8 +659,6 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   int st = attention_dims_ok(B, H, Lq, Lk, q_block, k_block, max_degree);
   if (st) return st;
   if (D != 128) return fail(CAST_ERR_UNSUPPORTED, "attention head_dim %d (supported: 128)", D);
-  if (q_block % 16 || k_block % 16)
-    return fail(CAST_ERR_UNSUPPORTED, "block sizes must be multiples of 16 (q %d, k %d)", q_block, k_block);
   if (max_degree > castk::kMaxBlockList)
     return fail(CAST_ERR_UNSUPPORTED, "max_degree %d > %d key blocks per query block",
                 max_degree, castk::kMaxBlockList);

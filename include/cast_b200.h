@@ -239,7 +239,8 @@ CAST_API size_t cast_taba_select_workspace_bytes(int B, int H, int T, int Hl, in
  *   tiles into parts whose partial results (fp32) are merged on the device;
  *   with NULL every item runs whole.  Calls that share a workspace must not
  *   overlap on the GPU.
- * Supported: D == 128, q_block and k_block multiples of 16.
+ * Supported: D == 128, any q_block and k_block (compact blocks of 88 or 110
+ * tokens included).
  */
 CAST_API int cast_rcsa_attention(const void *q, const void *k, const void *v, const int8_t *q_codes,
                         const float *q_scales, const int8_t *k_codes, const float *k_scales,

@@ -1,0 +1,77 @@
+"""Head-sharded RCSA over NCCL on two B200s: the gathered output of
+``HeadShardedRCSA`` (each rank its half of the heads, then the all-gather)
+against the single-GPU ``RCSAPlan`` on the same inputs.  Selection and
+codes are per (batch, head), so each rank's selection equals its slice of
+the single-GPU one exactly; the attention may be planned into other work
+splits at fewer heads per launch (fp32 partial merges in another order), so
+the outputs agree within the attention bar.  Skips with fewer than two GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(heads=4, nq=2, nh=6, block=880, seed=5):
+    g = torch.Generator().manual_seed(seed)
+    scale = 0.5 + 1.5 * torch.rand(1, heads, 1, 1, generator=g)
+    q = (torch.randn(1, heads, nq * block, 128, generator=g) * scale).bfloat16()
+    k = (torch.randn(1, heads, (nq + nh) * block, 128, generator=g) * scale).bfloat16()
+    v = (torch.randn(1, heads, (nq + nh) * block, 128, generator=g) * scale).bfloat16()
+    return q, k, v
+
+
+def _worker(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    from cast_b200 import distributed as cd
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        q, k, v = _inputs()
+        layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, block_size=880, budget=3,
+                                   policy="auto", device=dev)
+        out = layer(*(layer.local_heads(t).to(dev) for t in (q, k, v)))
+        torch.cuda.synchronize()
+        torch.save(layer.plan.indices.cpu(), os.path.join(out_dir, f"sel{rank}.pt"))
+        if rank == 0:
+            torch.save(out.cpu(), os.path.join(out_dir, "gathered.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_sharded_equals_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from cast_b200 import rcsa
+
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    q, k, v = _inputs()
+    plan = rcsa.RCSAPlan(1, q.shape[1], q.shape[2], k.shape[2], 128, block_size=880, budget=3,
+                         policy="auto", device=torch.device("cuda", 0))
+    single = plan(q.cuda(), k.cuda(), v.cuda()).cpu()
+    gathered = torch.load(os.path.join(tmp_path, "gathered.pt"))
+    assert gathered.shape == single.shape
+    half = q.shape[1] // world
+    for r in range(world):
+        sel = torch.load(os.path.join(tmp_path, f"sel{r}.pt"))
+        assert torch.equal(sel, plan.indices.cpu()[:, r * half:(r + 1) * half])
+    d = (gathered.float() - single.float()).abs()
+    assert float(d.max()) < 2e-2 and float(d.mean()) < 2e-3

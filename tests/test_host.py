@@ -49,9 +49,9 @@ def test_attention_rejects_null_and_unsupported(lib):
     st = lib.cast_rcsa_attention(fake, fake, fake, None, None, None, None, None, fake, fake, 1, None,
                                  1, 1, 128, 128, 64, 128, 128, 0.1, fake, None, None, None, 0, None)
     assert st == 2 and b"head_dim" in lib.cast_last_error_message()
-    st = lib.cast_rcsa_attention(fake, fake, fake, None, None, None, None, None, fake, fake, 1, None,
-                                 1, 1, 128, 128, 128, 100, 128, 0.1, fake, None, None, None, 0, None)
-    assert st == 2 and b"multiples of 16" in lib.cast_last_error_message()
+    st = lib.cast_rcsa_attention(fake, fake, fake, None, None, None, None, None, fake, fake, 300, None,
+                                 1, 1, 128, 128, 128, 110, 110, 0.1, fake, None, None, None, 0, None)
+    assert st == 2 and b"max_degree 300" in lib.cast_last_error_message()
     odd = ctypes.c_void_p(4097)
     st = lib.cast_rcsa_attention(odd, fake, fake, None, None, None, None, None, fake, fake, 1, None,
                                  1, 1, 128, 128, 128, 128, 128, 0.1, fake, None, None, None, 0, None)

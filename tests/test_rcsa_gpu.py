@@ -509,3 +509,39 @@ def test_rcsa_config2_all_heads_bitexact(cuda):
 
 def test_rcsa_config3_all_heads_bitexact(cuda):
     _full_size(workloads.config3(heads=24), "cfg3_select_h24.npz")
+
+
+@pytest.mark.parametrize("block", [110, 88, 440])
+def test_attention_any_block_size(cuda, block):
+    """Blocks that are not multiples of 16 (the compact path's 1x11x10 = 110,
+    1x11x8 = 88 and 2x11x20 = 440): key blocks start anywhere in the key
+    validity mask (byte loads where the 16-byte ones would be misaligned),
+    both precisions, with and without a mask, against the oracle."""
+    nq, nh, budget = 2, 5, 2
+    q, k, v = _rand_problem(2, nq, nh, block, seed=block)
+    g = torch.Generator().manual_seed(block)
+    valid = (torch.rand(k.shape[2], generator=g) > 0.15)
+    for kv in (None, valid):
+        kvd = None if kv is None else kv.to(torch.uint8).cuda()
+        sel = rcsa.select_quant(q.cuda(), k.cuda(), block_size=block, budget=budget, policy="int8",
+                                k_valid=kvd)
+        torch.cuda.synchronize()
+        kvn = None if kv is None else kv.numpy()
+        o_sel, o_cnt, _, _, _ = orc.rcsa_select(_np(q), _np(k), block, budget, k_valid=kvn)
+        assert np.array_equal(sel.indices.cpu().numpy(), o_sel)
+        qc, qs = orc.quantize_blocks(_np(q), block)
+        kc, ks = orc.quantize_blocks(_np(k), block, kvn)
+        ref_b = orc.block_sparse_attention(_np(q), _np(k), _np(v), o_sel, o_cnt, block, block, key_valid=kvn)
+        ref_i = orc.block_sparse_attention(_np(q), _np(k), _np(v), o_sel, o_cnt, block, block, key_valid=kvn,
+                                           q_codes=qc, q_scales=qs, k_codes=kc, k_scales=ks)
+        qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+        out_b = rcsa.block_sparse_attention(qd, kd, vd, sel.indices, sel.counts, q_block=block,
+                                            k_block=block, key_valid=kvd)
+        out_i = rcsa.block_sparse_attention(qd, kd, vd, sel.indices, sel.counts, q_block=block,
+                                            k_block=block, key_valid=kvd, q_codes=sel.q_codes,
+                                            q_scales=sel.q_scales, k_codes=sel.k_codes,
+                                            k_scales=sel.k_scales)
+        torch.cuda.synchronize()
+        for out, ref in ((out_b, ref_b), (out_i, ref_i)):
+            m, a = _errs(out, ref)
+            assert m < MAX_ABS and a < MEAN_ABS, (block, kv is not None, m, a)
