@@ -42,6 +42,9 @@
 
 namespace castk {
 
+#ifndef CAST_ATTN_HEAD_GROUP
+#define CAST_ATTN_HEAD_GROUP (1 << 20)
+#endif
 constexpr int kAttnThreads = 384;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -108,6 +111,28 @@ struct AttnParams {
   uint16_t part_first[kMaxSplitItems + 1];
   uint16_t part_tiles[kMaxSplitItems];
 };
+
+// Work items are ordered in groups of kHeadGroup heads: within a group,
+// query blocks heaviest first (the last query block selects the most key
+// blocks), then head, then tile pair.  A group's CTAs run close together, so
+// the key/value blocks its heads selected are read from DRAM once and shared
+// through L2, while the order inside a group keeps the heavy items early.
+constexpr int kHeadGroup = CAST_ATTN_HEAD_GROUP;
+
+// (bh, query block, pair) of item y (pairs: per = full_pairs; single tiles:
+// per = 1) in the grouped order above.
+__host__ __device__ __forceinline__ void item_coords(int y, int BH, int nqb, int per, int &bh,
+                                                     int &qb, int &pair) {
+  const int G = kHeadGroup < BH ? kHeadGroup : BH;
+  const int group_items = G * nqb * per;
+  const int g = y / group_items;
+  const int gh = min(G, BH - g * G);
+  const int r = y - g * group_items;
+  pair = r % per;
+  const int rest = r / per;
+  bh = g * G + rest % gh;
+  qb = nqb - 1 - rest / gh;
+}
 
 // First key tile of part j of n over T planned tiles.
 __device__ __forceinline__ int part_lo(int j, int T, int n) {
@@ -427,15 +452,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   int bh, qb, pair;
   {
     if (x < p.n_full_items) {
-      pair = x % p.full_pairs;
-      const int rest = x / p.full_pairs;
-      bh = rest % p.BH;
-      qb = p.nqb - 1 - rest / p.BH;
+      item_coords(x, p.BH, p.nqb, p.full_pairs, bh, qb, pair);
     } else {
-      x -= p.n_full_items;
+      int unused;
+      item_coords(x - p.n_full_items, p.BH, p.nqb, 1, bh, qb, unused);
       pair = p.full_pairs;
-      bh = x % p.BH;
-      qb = p.nqb - 1 - x / p.BH;
     }
   }
   const int t0 = 2 * pair + max(conv_tile, 0);

@@ -508,17 +508,12 @@ static AttnSplitPlan plan_attention_split(int BH, int nqb, int q_tiles, int k_ti
   std::vector<int> T(n_items);
   std::vector<double> cost(n_items);
   for (int x = 0; x < n_items; ++x) {
-    int bh, qb;
+    int bh, qb, unused;
     bool pair_item = x < n_full;
-    if (pair_item) {
-      const int rest = x / full_pairs;
-      bh = rest % BH;
-      qb = nqb - 1 - rest / BH;
-    } else {
-      const int y = x - n_full;
-      bh = y % BH;
-      qb = nqb - 1 - y / BH;
-    }
+    if (pair_item)
+      castk::item_coords(x, BH, nqb, full_pairs, bh, qb, unused);
+    else
+      castk::item_coords(x - n_full, BH, nqb, 1, bh, qb, unused);
     const int c = count_hint ? std::min(std::max(count_hint[(size_t)bh * nqb + qb], 0), deg) : deg;
     T[x] = c * k_tiles;
     // a single tile splits its key tiles over both softmax warpgroups
