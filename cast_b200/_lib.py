@@ -70,6 +70,12 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_longlong, c_int,
          c_void_p],
     ),
+    "cast_barycentric_weights": (
+        c_int,
+        [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int,
+         c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_float, c_float, c_void_p,
+         c_void_p],
+    ),
     "cast_swap_route": (
         c_int,
         [c_void_p] * 9 + [c_int] * 9 + [c_float, c_int, c_int, c_int, c_int, c_void_p, c_void_p,

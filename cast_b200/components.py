@@ -19,6 +19,10 @@ code, and :func:`patched_seams` lists what is installed):
 * the frame weave's ``direct_control_barycentric_pair_write`` (the
   control-barycentric lift's two-anchor writer) ->
   :func:`cast_b200.barycentric.direct_control_barycentric_pair_write`;
+* ``MatrixCurvaturePhaseFrameWeave._control_barycentric_residual_lift`` (the
+  whole lift: camera / action state, every target's weights, the rows) ->
+  :func:`cast_b200.barycentric.control_barycentric_residual_lift` for batch-1
+  fp32 residuals;
 * the weave's ``world_spectral_corrector.correct`` (FC-PASM reference
   numerics) -> :class:`cast_b200.par.FCPASMCorrector` with the corrector's
   own FC knobs; it publishes the FC routing transport into the reference
@@ -149,10 +153,27 @@ def _compact_cwca(self, module, q, k, v, layout):
         int8_tolerance=_SETTINGS["int8_tolerance"])
 
 
+def _lift(cls, active_residual, active_frames, total_temporal, memory_temporal, current_segment_boundary,
+          full_plucker, *args, **kwargs):
+    """``MatrixCurvaturePhaseFrameWeave._control_barycentric_residual_lift``
+    on the B200 for batch-1 fp32 CUDA residuals; other inputs keep the
+    reference's method."""
+    if (isinstance(active_residual, torch.Tensor) and active_residual.is_cuda
+            and active_residual.dtype == torch.float32 and active_residual.ndim == 4
+            and active_residual.shape[0] == 1 and isinstance(full_plucker, torch.Tensor)
+            and full_plucker.device == active_residual.device):
+        return barycentric.control_barycentric_residual_lift(
+            active_residual, active_frames, total_temporal, memory_temporal, current_segment_boundary,
+            full_plucker, *args, **kwargs)
+    return _PATCHED["lift"](
+        cls, active_residual, active_frames, total_temporal, memory_temporal, current_segment_boundary,
+        full_plucker, *args, **kwargs)
+
+
 def install_kernels() -> None:
     """Replaces the reference's static seams: the attention launches, the
-    TABA selection, the compact CWCA attention and the pair writer
-    (idempotent)."""
+    TABA selection, the compact CWCA attention, the pair writer and the
+    control-barycentric lift (idempotent)."""
     jit = _ref("matrix_jit_spatial_acceleration")
     weave = _ref("matrix_curvature_phase_frame_weave")
     qk = _ref("qk_uncertainty_tangent_attention")
@@ -173,6 +194,11 @@ def install_kernels() -> None:
     if "compact_cwca" not in _PATCHED:
         _PATCHED["compact_cwca"] = weave.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention
         weave.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention = _compact_cwca
+    if "lift" not in _PATCHED:
+        cls = weave.MatrixCurvaturePhaseFrameWeave
+        # the undecorated function of the classmethod, rebound per call
+        _PATCHED["lift"] = cls.__dict__["_control_barycentric_residual_lift"].__func__
+        cls._control_barycentric_residual_lift = classmethod(_lift)
 
 
 def uninstall_kernels() -> None:
@@ -193,6 +219,10 @@ def uninstall_kernels() -> None:
     if "compact_cwca" in _PATCHED:
         weave = _ref("matrix_curvature_phase_frame_weave")
         weave.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention = _PATCHED.pop("compact_cwca")
+    if "lift" in _PATCHED:
+        weave = _ref("matrix_curvature_phase_frame_weave")
+        weave.MatrixCurvaturePhaseFrameWeave._control_barycentric_residual_lift = classmethod(
+            _PATCHED.pop("lift"))
 
 
 def unsupported_fc_knob(ref_corrector) -> str | None:
@@ -299,6 +329,8 @@ def patched_seams(weave=None) -> dict:
         "pair_write": wv.direct_control_barycentric_pair_write is barycentric.direct_control_barycentric_pair_write,
         "taba_select": qk.MatrixTrajectoryAdaptiveBudgetAttentionCompiler.select is _taba_select,
         "compact_cwca": wv.MatrixCurvaturePhaseFrameWeave._compact_cwca_attention is _compact_cwca,
+        "lift": wv.MatrixCurvaturePhaseFrameWeave.__dict__["_control_barycentric_residual_lift"].__func__
+        is _lift,
     }
     if weave is not None:
         out["correct"] = bool(getattr(getattr(weave, "world_spectral_corrector", None), "_cast_b200", False))

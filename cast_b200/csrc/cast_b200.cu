@@ -858,6 +858,58 @@ extern "C" int cast_barycentric_pair_write(const float *active_residual, const f
   return CAST_OK;
 }
 
+extern "C" int cast_barycentric_weights(const void *plucker, int plucker_bf16, int B, int rows, int P,
+                                        int S, int T, int M, const float *mouse, int mouse_len,
+                                        int mouse_ch, const float *keyboard, int keyboard_len,
+                                        int keyboard_ch, const float *mouse_memory,
+                                        int mouse_memory_len, const float *keyboard_memory,
+                                        int keyboard_memory_len, int n_targets,
+                                        const int32_t *targets, const float *prior, float lambda_p,
+                                        float lambda_a, float *weights, cast_stream_t stream) {
+  using castk::kLiftMaxAct;
+  using castk::kLiftMaxFeat;
+  using castk::kLiftMaxTargets;
+  if (!plucker || !targets || !prior || !weights)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "plucker, targets, prior and weights are required");
+  if (B <= 0 || P <= 0 || P > kLiftMaxFeat || S <= 0 || T <= 0 || M < 0 || M >= T ||
+      rows < T * S || n_targets <= 0 || n_targets > kLiftMaxTargets)
+    return fail(CAST_ERR_INVALID_ARGUMENT,
+                "bad sizes (B=%d rows=%d P=%d S=%d T=%d memory=%d targets=%d; P <= %d, targets <= %d)",
+                B, rows, P, S, T, M, n_targets, kLiftMaxFeat, kLiftMaxTargets);
+  const int cm = mouse ? mouse_ch : 0, ck = keyboard ? keyboard_ch : 0;
+  if (cm + ck > kLiftMaxAct) return fail(CAST_ERR_UNSUPPORTED, "more than %d control channels", kLiftMaxAct);
+  if ((mouse && mouse_len <= 0) || (keyboard && keyboard_len <= 0) ||
+      (mouse_memory && (!mouse || mouse_memory_len <= 0)) ||
+      (keyboard_memory && (!keyboard || keyboard_memory_len <= 0)))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "control sequences must be non-empty and memory controls "
+                                           "need their current counterpart");
+  castk::LiftParams p;
+  memset(&p, 0, sizeof(p));
+  for (int n = 0; n < n_targets; ++n) {
+    for (int j = 0; j < 3; ++j) {
+      const int f = targets[3 * n + j];
+      if (f < 0 || f >= T) return fail(CAST_ERR_INVALID_ARGUMENT, "target %d frame %d outside [0,%d)", n, f, T);
+      p.targets[n][j] = f;
+    }
+    p.prior[n][0] = prior[2 * n];
+    p.prior[n][1] = prior[2 * n + 1];
+  }
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  p.plucker = plucker, p.plucker_bf16 = plucker_bf16 ? 1 : 0, p.P = P, p.S = S, p.T = T, p.M = M;
+  p.rows = rows;
+  p.cur[0] = castk::LiftCond{mouse, mouse_len, mouse_ch};
+  p.cur[1] = castk::LiftCond{keyboard, keyboard_len, keyboard_ch};
+  p.mem[0] = castk::LiftCond{mouse_memory, mouse_memory_len, mouse_ch};
+  p.mem[1] = castk::LiftCond{keyboard_memory, keyboard_memory_len, keyboard_ch};
+  p.action = (mouse || keyboard) ? 1 : 0;
+  p.lp = lambda_p, p.la = lambda_a, p.weights = weights, p.N = n_targets;
+  castk::barycentric_weights_kernel<<<dim3(n_targets, B), castk::kLiftThreads, 0,
+                                       reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
 // ===========================================================================
 // FC-PASM swap router
 // ===========================================================================

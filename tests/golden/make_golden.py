@@ -55,6 +55,9 @@ Files:
   reference's ``_layout`` builds, and the indices / counts its
   ``_compact_cwca_attention`` hands to the attention launch, with the
   curvature branch of its degree split (uniform and two curved profiles).
+* ``lift_*.npz``         -- the control-barycentric lift
+  (``_control_barycentric_residual_lift``) on seeded residuals, camera
+  features and controls: the reconstructed target rows.
 * ``MANIFEST.json``      -- SHA-256 of every fixture and of every regenerated
   input (mirrors the hash manifest idea of ``scripts/check_release.py:19-26``).
 """
@@ -440,6 +443,57 @@ def make_compact_select(manifest: dict):
         jit.MatrixJiTSpatialAcceleration._longcat_active = saved
 
 
+LIFT_CASES = {
+    # name: (T, memory frames, active frames, boundary, plucker dtype, controls, lambdas, seed)
+    "current_only": (8, 0, (0, 3, 5, 7), None, "f32", "current", (1.0, 1.0, 1.0), 51),
+    "memory_boundary": (10, 2, (0, 1, 2, 5, 6, 9), 4, "f32", "both", (1.0, 0.7, 1.3), 52),
+    "no_controls": (6, 1, (0, 1, 3, 5), None, "bf16", "none", (1.0, 1.0, 1.0), 53),
+}
+
+
+def lift_case(name):
+    """Seeded inputs of the control-barycentric lift: fp32 active residual
+    ``[1, A, 880, 16]``, Plucker camera features ``[1, T*880, 6]`` whose frame
+    means turn from frame to frame, frame-rate mouse / keyboard controls."""
+    frames, mem, active, _, dtype, controls, _, seed = LIFT_CASES[name]
+    g = torch.Generator().manual_seed(seed)
+    act = torch.randn(1, len(active), 880, 16, generator=g)
+    direction = torch.randn(frames, 1, 6, generator=g)
+    plucker = (direction + 0.3 * torch.randn(frames, 880, 6, generator=g)).reshape(1, frames * 880, 6)
+    if dtype == "bf16":
+        plucker = plucker.bfloat16()
+    cur_len, mem_len = 4 * (frames - mem) - 3, max(4 * mem - 3, 1)
+    mouse = keyboard = mouse_m = keyboard_m = None
+    if controls in ("current", "both"):
+        mouse = torch.randn(1, cur_len, 2, generator=g)
+        keyboard = (torch.rand(1, cur_len, 4, generator=g) > 0.5).float()
+    if controls == "both":
+        mouse_m = torch.randn(1, mem_len, 2, generator=g)
+        keyboard_m = (torch.rand(1, mem_len, 4, generator=g) > 0.5).float()
+    return act, torch.tensor(active), plucker, mouse, keyboard, mouse_m, keyboard_m
+
+
+def make_lift(manifest: dict):
+    """The reference's ``_control_barycentric_residual_lift``
+    (proposed/matrix_curvature_phase_frame_weave.py:3810-4374) on CPU, its
+    contraction path: the reconstructed target rows and the record."""
+    from interaction_accel.methods.proposed.matrix_curvature_phase_frame_weave import (
+        MatrixCurvaturePhaseFrameWeave as Weave,
+    )
+
+    for name, (frames, mem, active, boundary, _, _, lambdas, _) in LIFT_CASES.items():
+        act, af, plucker, mouse, keyboard, mouse_m, keyboard_m = lift_case(name)
+        full, rec = Weave._control_barycentric_residual_lift(
+            act, af, frames, mem, boundary, plucker, mouse, keyboard, mouse_m, keyboard_m, lambdas,
+            True)
+        targets = [t for t in range(frames) if t not in active]
+        manifest["inputs"][f"lift_{name}"] = {"active": sha(act), "plucker": sha(plucker.float())}
+        np.savez_compressed(os.path.join(HERE, f"lift_{name}.npz"), targets=np.array(targets),
+                            target_rows=full[0, targets].numpy(), n_targets=np.int64(rec["targets"]),
+                            action_available=np.bool_(rec["action_available"]))
+        print(name, rec["targets"], rec["action_available"])
+
+
 TRANSPORT_ROUTER = {
     # router configurations run on the published sketch (FCPASMSwapRoutingConfig kwargs)
     "production": dict(num_swap_rounds=1, swap_eps=0.10, max_swaps_per_call=1, same_bank_only=True,
@@ -533,7 +587,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the CAST src/ directory")
     ap.add_argument("--only", nargs="+", choices=("cfg1", "cfg2", "cfg3", "compact", "par", "swap",
-                                                   "transport", "compact_select"),
+                                                   "transport", "compact_select", "lift"),
                     help="regenerate these fixtures only; other manifest entries are kept")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
@@ -546,7 +600,7 @@ def main():
         with open(mpath) as fh:
             manifest = json.load(fh)
     todo = set(args.only or ("cfg1", "cfg2", "cfg3", "compact", "par", "swap", "transport",
-                             "compact_select"))
+                             "compact_select", "lift"))
     if "cfg1" in todo:
         make_cfg1({}, manifest)
     if "cfg2" in todo:
@@ -563,6 +617,8 @@ def main():
         make_transport(manifest)
     if "compact_select" in todo:
         make_compact_select(manifest)
+    if "lift" in todo:
+        make_lift(manifest)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             with open(os.path.join(HERE, f), "rb") as fh:

@@ -6,6 +6,7 @@ the rounding modes against the reference's own einsum contraction
 from fractions import Fraction
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import barycentric as ob
@@ -49,3 +50,20 @@ def test_modes_agree_with_reference_einsum():
     for mode in (1, 2, 3):
         got = ob.mix(mode, l, wl, r, wr)
         assert np.allclose(got, ref, rtol=2e-6, atol=1e-7)
+
+
+def test_lift_targets_follow_reference_segments():
+    """The lift's targets: per segment (memory, then the current frames split
+    at the boundary), each non-anchor frame between its nearest anchors of
+    that segment; a segment without an anchor, an unbracketed frame or a
+    boundary outside the current frames is refused like the reference."""
+    from cast_b200.barycentric import lift_targets
+    got = lift_targets([0, 1, 2, 5, 6, 9], 10, 2, 4)
+    assert [t[:3] for t in got] == [(3, 2, 5), (4, 2, 5), (7, 6, 9), (8, 6, 9)]
+    assert got[0][3:5] == (2, 3) and abs(got[1][5] - 2 / 3) < 1e-12
+    with pytest.raises(RuntimeError, match="no exact anchor"):
+        lift_targets([0, 1, 5, 7], 8, 2, 2)
+    with pytest.raises(RuntimeError, match="not bracketed"):
+        lift_targets([0, 2, 5], 7, 0, None)
+    with pytest.raises(RuntimeError, match="Current boundary"):
+        lift_targets([0, 3], 4, 0, 4)

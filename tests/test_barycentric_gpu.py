@@ -86,3 +86,58 @@ def test_pair_write_config4_scale_rate(cuda):
     # algorithmic: the two shared anchor frames read once, two targets written
     nbytes = 4 * 880 * 3072 * 4
     print(f"barycentric pair write (2 targets, 880x3072 fp32): {us:.1f} us, {nbytes / us / 1e3:.0f} GB/s")
+
+
+def _lift_golden(name):
+    import importlib.util
+    import os
+    here = os.path.join(os.path.dirname(__file__), "golden")
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(here, "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    return mg, np.load(os.path.join(here, f"lift_{name}.npz"))
+
+
+@pytest.mark.parametrize("name", ["current_only", "memory_boundary", "no_controls"])
+def test_lift_matches_reference(cuda, name):
+    """The whole control-barycentric lift on the device (weights kernel, then
+    the pair writer): the weights within fp32 rounding of the oracle's
+    float64 ones, the target rows within 1e-5 of the reference's, the
+    anchors copied exactly, the record's counts the reference's."""
+    mg, g = _lift_golden(name)
+    frames, mem, active, boundary, _, _, lambdas, _ = mg.LIFT_CASES[name]
+    act, af, plucker, mouse, keyboard, mm, km = mg.lift_case(name)
+    dev = lambda x: None if x is None else x.to(cuda)  # noqa: E731
+    full, rec = barycentric.control_barycentric_residual_lift(
+        act.to(cuda), af.to(cuda), frames, mem, boundary, plucker.to(cuda), dev(mouse), dev(keyboard),
+        dev(mm), dev(km), lambdas, True)
+    torch.cuda.synchronize()
+    assert rec["targets"] == int(g["n_targets"]) and rec["action_available"] == bool(g["action_available"])
+    full = full[0].cpu().numpy()
+    np.testing.assert_allclose(full[g["targets"]], g["target_rows"], rtol=0, atol=1e-5)
+    assert np.array_equal(full[list(active)], act[0].numpy())
+    # the weights kernel alone against the oracle
+    npy = lambda x: None if x is None else x[0].float().numpy()  # noqa: E731
+    _, w_ref, targets = ob.lift(npy(act), list(active), frames, mem, boundary, npy(plucker), npy(mouse),
+                                npy(keyboard), npy(mm), npy(km), lambdas)
+    tg = barycentric.lift_targets(list(active), frames, mem, boundary)
+    assert [t[:3] for t in tg] == [tuple(t) for t in targets]
+    w, _ = barycentric.lift_weights(tg, plucker.to(cuda), dev(mouse), dev(keyboard), dev(mm), dev(km),
+                                    total_temporal=frames, memory_temporal=mem, spatial=880,
+                                    lambdas=lambdas)
+    np.testing.assert_allclose(w[0].cpu().numpy(), w_ref, rtol=0, atol=2e-6)
+
+
+def test_lift_anchor_only_and_batch_check(cuda):
+    """Every frame an anchor: no launch, the residual is the output; batches
+    other than 1 are refused."""
+    act = torch.randn(1, 4, 880, 16, device=cuda)
+    plucker = torch.randn(1, 4 * 880, 6, device=cuda)
+    full, rec = barycentric.control_barycentric_residual_lift(
+        act, torch.arange(4, device=cuda), 4, 0, None, plucker, None, None, None, None, (1, 1, 1))
+    assert rec["targets"] == 0 and rec["direct_pair_kernel_calls"] == 0
+    assert torch.equal(full, act)
+    with pytest.raises(ValueError, match="batch-1"):
+        barycentric.control_barycentric_residual_lift(
+            act.expand(2, -1, -1, -1).contiguous(), torch.arange(4, device=cuda), 4, 0, None,
+            plucker.expand(2, -1, -1).contiguous(), None, None, None, None, (1, 1, 1))

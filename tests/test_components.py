@@ -9,6 +9,7 @@ is absent (the GPU box) they skip.
 """
 
 import importlib
+import importlib.util
 import os
 import sys
 
@@ -41,7 +42,7 @@ def test_every_claimed_seam_is_patched(factory):
     seams = components.patched_seams(weave)
     assert seams == {k: True for k in seams}, seams
     assert set(seams) == {"longcat_active", "longcat_asymmetric", "pair_write", "taba_select",
-                          "compact_cwca", "correct", "refine"}
+                          "compact_cwca", "lift", "correct", "refine"}
     # the attention compiler reaches the patched TABA select through super()
     qk = importlib.import_module("interaction_accel.methods.proposed.qk_uncertainty_tangent_attention")
     assert isinstance(attention, qk.MatrixTrajectoryAdaptiveBudgetAttentionCompiler)
@@ -62,6 +63,24 @@ def test_uninstall_restores_reference_seams(factory):
     assert not any(seams.values()), seams
     components.install_kernels()
     assert all(components.patched_seams().values())
+
+
+def test_host_tensors_keep_reference_lift(factory):
+    """CPU residuals run the reference's own control-barycentric lift through
+    the patched classmethod: the same rows as the golden."""
+    components.make_cast_components()
+    weave_mod = importlib.import_module("interaction_accel.methods.proposed.matrix_curvature_phase_frame_weave")
+    spec = importlib.util.spec_from_file_location(
+        "make_golden", os.path.join(os.path.dirname(__file__), "golden", "make_golden.py"))
+    gold = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gold)
+    act, af, plucker, mouse, keyboard, mm, km = gold.lift_case("memory_boundary")
+    frames, mem, _, boundary, _, _, lambdas, _ = gold.LIFT_CASES["memory_boundary"]
+    full, rec = weave_mod.MatrixCurvaturePhaseFrameWeave._control_barycentric_residual_lift(
+        act, af, frames, mem, boundary, plucker, mouse, keyboard, mm, km, lambdas, True)
+    assert "backend" not in rec
+    ref = np.load(os.path.join(os.path.dirname(gold.__file__), "lift_memory_boundary.npz"))
+    assert np.array_equal(full[0, ref["targets"]].numpy(), ref["target_rows"])
 
 
 def test_host_tensors_keep_reference_correct(factory):

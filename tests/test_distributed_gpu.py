@@ -73,5 +73,10 @@ def test_head_sharded_equals_single_gpu(tmp_path):
     for r in range(world):
         sel = torch.load(os.path.join(tmp_path, f"sel{r}.pt"))
         assert torch.equal(sel, plan.indices.cpu()[:, r * half:(r + 1) * half])
-    d = (gathered.float() - single.float()).abs()
-    assert float(d.max()) < 2e-2 and float(d.mean()) < 2e-3
+    # Both outputs are bf16 roundings of fp32 results that differ only in the
+    # order of the partial merges: they agree to one bf16 unit in the last place.
+    g, s = gathered.float(), single.float()
+    d = (g - s).abs()
+    ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(g.abs(), s.abs()).clamp_min(2.0 ** -126))) - 7)
+    assert bool((d <= ulp).all()), float((d / ulp).max())
+    assert float(d.mean()) < 2e-3

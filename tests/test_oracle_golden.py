@@ -210,3 +210,30 @@ def assert_same_rows(sel, ref, cnt):
     ours = np.sort(np.where(in_count, sel, -1), axis=-1)
     theirs = np.sort(np.where(in_count, ref, -1), axis=-1)
     np.testing.assert_array_equal(ours, theirs)
+
+
+def _make_golden():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(GOLDEN, "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    return mg
+
+
+@pytest.mark.parametrize("name", ["current_only", "memory_boundary", "no_controls"])
+def test_lift_matches_reference(name):
+    """The control-barycentric lift restated in the oracle (camera and action
+    state, clamped cosines, softmax with the temporal prior, the two-anchor
+    contraction) reproduces the reference's target rows."""
+    from oracle import barycentric as obary
+    mg = _make_golden()
+    frames, mem, active, boundary, _, _, lambdas, _ = mg.LIFT_CASES[name]
+    act, af, plucker, mouse, keyboard, mm, km = mg.lift_case(name)
+    npy = lambda x: None if x is None else x[0].float().numpy()  # noqa: E731
+    full, w, targets = obary.lift(npy(act), list(active), frames, mem, boundary, npy(plucker), npy(mouse),
+                                  npy(keyboard), npy(mm), npy(km), lambdas)
+    g = np.load(os.path.join(GOLDEN, f"lift_{name}.npz"))
+    assert [t[0] for t in targets] == list(g["targets"])
+    assert int(g["n_targets"]) == len(targets)
+    np.testing.assert_allclose(full[g["targets"]], g["target_rows"], rtol=0, atol=2e-6)
+    np.testing.assert_allclose(w.sum(-1), 1.0, atol=1e-6)
