@@ -73,8 +73,8 @@ SIGNATURES = {
     "cast_barycentric_weights": (
         c_int,
         [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int,
-         c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_float, c_float, c_void_p,
-         c_void_p],
+         c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_float,
+         c_void_p, c_void_p],
     ),
     "cast_swap_route": (
         c_int,

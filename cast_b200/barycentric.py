@@ -136,17 +136,18 @@ def lift_weights(targets, full_plucker, mouse_cond, keyboard_cond, mouse_cond_me
             raise RuntimeError("control condition must have shape [B,T,C]")
         return x.detach().to(device=dev, dtype=torch.float32).contiguous()
 
-    mouse, keyboard, mouse_m, keyboard_m = (cond(x) for x in (mouse_cond, keyboard_cond,
-                                                               mouse_cond_memory, keyboard_cond_memory))
-    current = [c for c in (mouse, keyboard) if c is not None]
-    memory = [c for c in (mouse_m, keyboard_m) if c is not None]
-    if memory_temporal and current and memory:
-        if sum(c.shape[-1] for c in memory) != sum(c.shape[-1] for c in current):
-            raise RuntimeError("Memory/Current action dimensions disagree")
-    if mouse_m is not None and mouse is None or keyboard_m is not None and keyboard is None:
+    # the reference pools a sequence only for a non-empty segment (:3570)
+    current = [cond(x) for x in (mouse_cond, keyboard_cond) if isinstance(x, torch.Tensor)]
+    memory = [cond(x) for x in (mouse_cond_memory, keyboard_cond_memory)
+              if memory_temporal and isinstance(x, torch.Tensor)]
+    if current and memory and sum(c.shape[-1] for c in memory) != sum(c.shape[-1] for c in current):
         raise RuntimeError("Memory/Current action dimensions disagree")
-    if not (memory_temporal and current):
-        mouse_m = keyboard_m = None
+    if not current:
+        memory = []
+    # the kernel concatenates slot 0 and slot 1 along channels like the
+    # reference's torch.cat of the given sequences
+    mouse, keyboard = (current + [None, None])[:2]
+    mouse_m, keyboard_m = (memory + [None, None])[:2]
     tgt = (ctypes.c_int32 * (3 * n))(*[v for t in targets for v in t[:3]])
     prior = (ctypes.c_float * (2 * n))(*[v for t in targets
                                          for v in (math.log1p(-t[5]), math.log(t[5]))])
@@ -156,7 +157,8 @@ def lift_weights(targets, full_plucker, mouse_cond, keyboard_cond, mouse_cond_me
     _lib.call("cast_barycentric_weights", P(plucker), int(plucker.dtype == torch.bfloat16), b,
               int(plucker.shape[1]), int(plucker.shape[2]), int(spatial), int(total_temporal),
               int(memory_temporal), P(mouse), ln(mouse), ch(mouse), P(keyboard), ln(keyboard),
-              ch(keyboard), P(mouse_m), ln(mouse_m), P(keyboard_m), ln(keyboard_m), n,
+              ch(keyboard), P(mouse_m), ln(mouse_m), ch(mouse_m), P(keyboard_m), ln(keyboard_m),
+              ch(keyboard_m), n,
               ctypes.cast(tgt, ctypes.c_void_p), ctypes.cast(prior, ctypes.c_void_p),
               float(lambdas[1]), float(lambdas[2]), P(out), _stream(dev))
     return out, bool(current)

@@ -109,7 +109,7 @@ struct LiftCond {              // one control sequence [B, L, C] fp32, or null
 struct LiftParams {
   const void *plucker;          // [B, rows >= T*S, P], fp32 or bf16
   int plucker_bf16, P, S, T, M, rows;
-  LiftCond cur[2], mem[2];      // mouse, keyboard
+  LiftCond cur[2], mem[2];      // the given sequences in order (mouse, keyboard)
   int action;                   // any current control given
   float lp, la;
   float *weights;               // [B, N, 2]
@@ -169,7 +169,8 @@ __global__ void __launch_bounds__(kLiftThreads) barycentric_weights_kernel(const
     }
     __syncthreads();
   }
-  // action: pooled controls of each frame, mouse then keyboard, normalised
+  // action: each frame's pooled controls, the given sequences concatenated
+  // along channels in order (slot 0 then slot 1), normalised
   int A = 0;
   if (p.action) {
     A = (p.cur[0].x ? p.cur[0].C : 0) + (p.cur[1].x ? p.cur[1].C : 0);
@@ -177,13 +178,13 @@ __global__ void __launch_bounds__(kLiftThreads) barycentric_weights_kernel(const
       const int j = i / A, ch = i % A;
       const bool memory = fr[j] < p.M;
       const int cell = memory ? fr[j] : fr[j] - p.M, cells = memory ? p.M : p.T - p.M;
-      const LiftCond &m = memory ? p.mem[0] : p.cur[0], &k = memory ? p.mem[1] : p.cur[1];
-      const int cm = p.cur[0].x ? p.cur[0].C : 0;
+      const LiftCond &s0 = memory ? p.mem[0] : p.cur[0], &s1 = memory ? p.mem[1] : p.cur[1];
+      const int split = s0.x ? s0.C : 0;
       float v = 0.f;  // missing memory controls count as zeros
-      if (ch < cm) {
-        if (m.x) v = lift_pool(m, b, cell, cells, ch);
-      } else if (k.x) {
-        v = lift_pool(k, b, cell, cells, ch - cm);
+      if (ch < split) {
+        v = lift_pool(s0, b, cell, cells, ch);
+      } else if (s1.x) {
+        v = lift_pool(s1, b, cell, cells, ch - split);
       }
       act[j][ch] = v;
     }

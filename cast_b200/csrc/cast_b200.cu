@@ -862,8 +862,9 @@ extern "C" int cast_barycentric_weights(const void *plucker, int plucker_bf16, i
                                         int S, int T, int M, const float *mouse, int mouse_len,
                                         int mouse_ch, const float *keyboard, int keyboard_len,
                                         int keyboard_ch, const float *mouse_memory,
-                                        int mouse_memory_len, const float *keyboard_memory,
-                                        int keyboard_memory_len, int n_targets,
+                                        int mouse_memory_len, int mouse_memory_ch,
+                                        const float *keyboard_memory, int keyboard_memory_len,
+                                        int keyboard_memory_ch, int n_targets,
                                         const int32_t *targets, const float *prior, float lambda_p,
                                         float lambda_a, float *weights, cast_stream_t stream) {
   using castk::kLiftMaxAct;
@@ -877,12 +878,16 @@ extern "C" int cast_barycentric_weights(const void *plucker, int plucker_bf16, i
                 "bad sizes (B=%d rows=%d P=%d S=%d T=%d memory=%d targets=%d; P <= %d, targets <= %d)",
                 B, rows, P, S, T, M, n_targets, kLiftMaxFeat, kLiftMaxTargets);
   const int cm = mouse ? mouse_ch : 0, ck = keyboard ? keyboard_ch : 0;
+  const int mm = mouse_memory ? mouse_memory_ch : 0, km = keyboard_memory ? keyboard_memory_ch : 0;
   if (cm + ck > kLiftMaxAct) return fail(CAST_ERR_UNSUPPORTED, "more than %d control channels", kLiftMaxAct);
-  if ((mouse && mouse_len <= 0) || (keyboard && keyboard_len <= 0) ||
-      (mouse_memory && (!mouse || mouse_memory_len <= 0)) ||
-      (keyboard_memory && (!keyboard || keyboard_memory_len <= 0)))
-    return fail(CAST_ERR_INVALID_ARGUMENT, "control sequences must be non-empty and memory controls "
-                                           "need their current counterpart");
+  if ((mouse && (mouse_len <= 0 || mouse_ch <= 0)) || (keyboard && (keyboard_len <= 0 || keyboard_ch <= 0)) ||
+      (mouse_memory && (mouse_memory_len <= 0 || mouse_memory_ch <= 0)) ||
+      (keyboard_memory && (keyboard_memory_len <= 0 || keyboard_memory_ch <= 0)))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "control sequences must be non-empty");
+  if ((mouse_memory || keyboard_memory) && (!(mouse || keyboard) || M == 0 || mm + km != cm + ck))
+    return fail(CAST_ERR_INVALID_ARGUMENT,
+                "Memory/Current action dimensions disagree (memory %d, current %d channels, memory frames %d)",
+                mm + km, cm + ck, M);
   castk::LiftParams p;
   memset(&p, 0, sizeof(p));
   for (int n = 0; n < n_targets; ++n) {
@@ -900,8 +905,8 @@ extern "C" int cast_barycentric_weights(const void *plucker, int plucker_bf16, i
   p.rows = rows;
   p.cur[0] = castk::LiftCond{mouse, mouse_len, mouse_ch};
   p.cur[1] = castk::LiftCond{keyboard, keyboard_len, keyboard_ch};
-  p.mem[0] = castk::LiftCond{mouse_memory, mouse_memory_len, mouse_ch};
-  p.mem[1] = castk::LiftCond{keyboard_memory, keyboard_memory_len, keyboard_ch};
+  p.mem[0] = castk::LiftCond{mouse_memory, mouse_memory_len, mm};
+  p.mem[1] = castk::LiftCond{keyboard_memory, keyboard_memory_len, km};
   p.action = (mouse || keyboard) ? 1 : 0;
   p.lp = lambda_p, p.la = lambda_a, p.weights = weights, p.N = n_targets;
   castk::barycentric_weights_kernel<<<dim3(n_targets, B), castk::kLiftThreads, 0,

@@ -317,18 +317,22 @@ CAST_API int cast_barycentric_pair_write(const float *active_residual, const flo
  * softmax(prior[n] - lambda_p * (1 - cos camera) - lambda_a * (1 - cos action))
  * over its two anchors, where the camera state of a frame is the L2-normalised
  * mean of its S rows of plucker ([B, rows >= T*S, P], fp32 or bf16) and the
- * action state the L2-normalised mouse | keyboard controls ([B, len, ch] fp32,
- * frame rate) area-pooled to the T - M current latent cells (the memory
- * frames' own sequences to M cells; missing memory controls count as zeros;
- * no controls at all: equal action distances, which cancel).  Cosines are
+ * action state the L2-normalised controls ([B, len, ch] fp32, frame rate)
+ * area-pooled to the T - M current latent cells and concatenated along
+ * channels, the "mouse" slot first, then the "keyboard" slot (the memory
+ * frames use their own two slots, pooled to M cells and concatenated the same
+ * way, their channels summing to the current ones; missing memory controls
+ * count as zeros; no controls at all: equal action distances, which cancel).  A slot may be null; the host fills the
+ * slots in the reference's order of the given sequences.  Cosines are
  * clamped to [-1, 1].  weights fp32 [B, n_targets, 2].  n_targets <= 64,
- * P <= 16, mouse + keyboard channels <= 64.
+ * P <= 16, channels of the two slots <= 64.
  */
 CAST_API int cast_barycentric_weights(const void *plucker, int plucker_bf16, int B, int rows, int P,
                              int S, int T, int M, const float *mouse, int mouse_len, int mouse_ch,
                              const float *keyboard, int keyboard_len, int keyboard_ch,
-                             const float *mouse_memory, int mouse_memory_len,
-                             const float *keyboard_memory, int keyboard_memory_len, int n_targets,
+                             const float *mouse_memory, int mouse_memory_len, int mouse_memory_ch,
+                             const float *keyboard_memory, int keyboard_memory_len,
+                             int keyboard_memory_ch, int n_targets,
                              const int32_t *targets, const float *prior, float lambda_p,
                              float lambda_a, float *weights, cast_stream_t stream);
 

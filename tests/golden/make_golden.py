@@ -448,6 +448,9 @@ LIFT_CASES = {
     "current_only": (8, 0, (0, 3, 5, 7), None, "f32", "current", (1.0, 1.0, 1.0), 51),
     "memory_boundary": (10, 2, (0, 1, 2, 5, 6, 9), 4, "f32", "both", (1.0, 0.7, 1.3), 52),
     "no_controls": (6, 1, (0, 1, 3, 5), None, "bf16", "none", (1.0, 1.0, 1.0), 53),
+    # keyboard only in the current frames, two memory sequences whose
+    # channels add up to the keyboard's: the concatenation is positional
+    "memory_split": (9, 3, (0, 2, 3, 6, 8), None, "f32", "split", (1.0, 0.5, 2.0), 54),
 }
 
 
@@ -470,6 +473,10 @@ def lift_case(name):
     if controls == "both":
         mouse_m = torch.randn(1, mem_len, 2, generator=g)
         keyboard_m = (torch.rand(1, mem_len, 4, generator=g) > 0.5).float()
+    if controls == "split":
+        keyboard = (torch.rand(1, cur_len, 4, generator=g) > 0.5).float()
+        mouse_m = torch.randn(1, mem_len, 1, generator=g)
+        keyboard_m = torch.randn(1, mem_len + 2, 3, generator=g)
     return act, torch.tensor(active), plucker, mouse, keyboard, mouse_m, keyboard_m
 
 

@@ -98,7 +98,7 @@ def _lift_golden(name):
     return mg, np.load(os.path.join(here, f"lift_{name}.npz"))
 
 
-@pytest.mark.parametrize("name", ["current_only", "memory_boundary", "no_controls"])
+@pytest.mark.parametrize("name", ["current_only", "memory_boundary", "no_controls", "memory_split"])
 def test_lift_matches_reference(cuda, name):
     """The whole control-barycentric lift on the device (weights kernel, then
     the pair writer): the weights within fp32 rounding of the oracle's

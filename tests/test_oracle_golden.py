@@ -220,7 +220,7 @@ def _make_golden():
     return mg
 
 
-@pytest.mark.parametrize("name", ["current_only", "memory_boundary", "no_controls"])
+@pytest.mark.parametrize("name", ["current_only", "memory_boundary", "no_controls", "memory_split"])
 def test_lift_matches_reference(name):
     """The control-barycentric lift restated in the oracle (camera and action
     state, clamped cosines, softmax with the temporal prior, the two-anchor
