@@ -290,8 +290,10 @@ def compact_measure(dev, peaks, steps):
     us_pair = _graph_us(lambda: barycentric.direct_control_barycentric_pair_write(
         act, wts, prs, tgs, full, arithmetic_mode="left_then_right_fma"), n, dev)
     pair_bytes = 4 * 880 * 3072 * 4  # two shared anchor frames read, two targets written
+    lift = lift_measure(dev, n)
     del np
     return {
+        "lift": lift,
         "compact_pack": {"us_per_call": us_pack, "algorithmic_bytes": pack_bytes,
                          "achieved_gbs": pack_bytes / us_pack / 1e3,
                          "frac": pack_bytes / us_pack / 1e3 / peaks["hbm_gbs"],
@@ -303,6 +305,44 @@ def compact_measure(dev, peaks, steps):
                                    "graph of one call (L2 holds the 43 MB, an upper bound)"},
         "note": "HBM peak measured; CUDA graph replay, device time",
     }
+
+
+def lift_measure(dev, n):
+    """The whole control-barycentric lift (``control_barycentric_residual_lift``:
+    targets on the host, the weights kernel, the pair writer, the anchors
+    copied in) on an 8-frame residual of 880 x 3072 fp32 rows, anchors 0, 3,
+    5, 7, mouse and keyboard controls: wall clock per call including its host
+    work and small index copies, synchronised every call."""
+    import time
+
+    import torch
+
+    from cast_b200 import barycentric
+
+    g = torch.Generator().manual_seed(12)
+    frames, active = 8, (0, 3, 5, 7)
+    act = torch.randn(1, len(active), 880, 3072, generator=g).to(dev)
+    af = torch.tensor(active, device=dev)
+    plucker = torch.randn(1, frames * 880, 6, generator=g).to(dev)
+    mouse = torch.randn(1, 4 * frames - 3, 2, generator=g).to(dev)
+    keyboard = (torch.rand(1, 4 * frames - 3, 4, generator=g) > 0.5).float().to(dev)
+
+    def call():
+        return barycentric.control_barycentric_residual_lift(
+            act, af, frames, 0, None, plucker, mouse, keyboard, None, None, (1.0, 1.0, 1.0), True)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for _ in range(n):
+        call()
+        torch.cuda.synchronize(dev)
+    us = (time.perf_counter() - t0) / n * 1e6
+    return {"us_per_call_wall": us, "targets": 4, "launches_per_call": 3,
+            "workload": "8 frames x 880 x 3072 fp32, anchors 0, 3, 5, 7, mouse + keyboard controls",
+            "note": "wall clock, synchronised per call: host targets, weights kernel, pair writer, "
+                    "anchor copy"}
 
 
 def swap_measure(dev, steps, cpu_leg=True):
@@ -576,9 +616,15 @@ def main():
         for _ in range(2):
             e2e_step()
         e2e_ms = timed(e2e_step, e_steps) / e_steps
-        # bytes of the whole job: every rank copies its heads in and out
-        e2e = {"ms": e2e_ms, "h2d": world * sum(t.numel() * t.element_size() for t in (hq, hk, hv)),
-               "d2h": world * hout.numel() * hout.element_size()}
+        # bytes of the whole job: every rank copies its heads' Q, K and
+        # selected value blocks in and its output out (the same selection
+        # every step, so the last call's counts hold for each)
+        moved = torch.tensor([host_plan.last_h2d_bytes, host_plan.last_d2h_bytes], dtype=torch.float64,
+                             device=dev)
+        if world > 1:
+            dist.all_reduce(moved)
+        e2e = {"ms": e2e_ms, "h2d": int(moved[0]), "d2h": int(moved[1]),
+               "h2d_all_values": world * sum(t.numel() * t.element_size() for t in (hq, hk, hv))}
     extras = rank == 0 and world == 1 and not args.no_extras
     par_line = par_measure(dev, peaks, peak_src, args.steps) if extras else None
     compact_line = compact_measure(dev, peaks, args.steps) if extras else None
@@ -676,7 +722,9 @@ def main():
     if e2e:
         line["e2e"] = {"value": e2e_ms * 1000.0, "unit": "us/call",
                        "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                       "path": "RCSAHostPlan: pinned host q/k/v in, head-group copies overlapped with the "
+                       "h2d_bytes_all_values": e2e["h2d_all_values"],
+                       "path": "RCSAHostPlan: pinned host q and k in, each head group's selection read back "
+                               "and only its selected value blocks copied in, copies overlapped with the "
                                "compute, output copied back and the device error word checked"
                                + (" (each rank its own heads, in parallel)" if world > 1 else "")}
     if not args.no_cpu_baseline and world == 1 and args.config == 2 and args.heads == HEADS:

@@ -88,6 +88,7 @@ struct AttnParams {
   float *lse;
   int max_degree;
   int BH, Lq, Lk, q_block, k_block, nqb, nkb;
+  int nkb_full;          // key blocks read through the block-structured value map (0: none)
   int q_tiles, k_tiles;  // 128-row tiles per query block / per key block
   int full_pairs;        // q_tiles / 2
   int n_full_items;      // BH * nqb * full_pairs
@@ -397,7 +398,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                           const __grid_constant__ CUtensorMap tm_k8,
                           const __grid_constant__ CUtensorMap tm_q16,
                           const __grid_constant__ CUtensorMap tm_k16,
-                          const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+                          const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ CUtensorMap tm_vb, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -415,7 +417,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + AttnSmem::tmem_slot);
   volatile uint32_t *part_flag = tmem_slot + 1;  // this CTA merges its cut item
   int32_t *blist = reinterpret_cast<int32_t *>(smem + AttnSmem::blist);
-  int *err = &g_cast_device_error;
+  // set when one of this CTA's waits gives up, so the others stop too
+  int *err = reinterpret_cast<int *>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -502,6 +505,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == kProducerWarp && lane == 0) {
     // The producer thread initialises the barriers and starts the Q load
     // before the CTA-wide sync, so the load overlaps the rest of the set-up.
+    *err = 0;
     for (int i = 0; i < AttnSmem::n_bars; ++i) castdev::mbar_init(&bar[i], 1);
     for (int i = 0; i < 4; ++i) castdev::mbar_init(&p_full[i], 4);
     castdev::mbar_init(merge_bar, 4);
@@ -513,6 +517,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     castdev::tma_prefetch_desc(mode ? &tm_q8 : &tm_q16);
     castdev::tma_prefetch_desc(mode ? &tm_k8 : &tm_k16);
     castdev::tma_prefetch_desc(&tm_v);
+    if (p.nkb_full > 0) castdev::tma_prefetch_desc(&tm_vb);
     if (n_kv > 0) {
       const int qrow0 = qb * p.q_block + t0 * 128;
       castdev::mbar_arrive_expect_tx(q_full, nq * q_bytes);
@@ -574,14 +579,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int kt = kt_lo + ring0.key_tile(j);
           const int blk = blist[kt / p.k_tiles];
           const int tin = kt % p.k_tiles;
-          const int krow = (blk >= 0 && blk < p.nkb) ? blk * p.k_block + tin * 128 : 0;
+          const bool blk_ok = blk >= 0 && blk < p.nkb;
+          const int krow = blk_ok ? blk * p.k_block + tin * 128 : 0;
           const int vs = j % kVStages;
           if (j >= kVStages && !castdev::mbar_wait(&v_empty[vs], ((j / kVStages) - 1) & 1, err))
             break;
           uint8_t *vd = smem + v_off + vs * 32768;
           castdev::mbar_arrive_expect_tx(&v_full[vs], 32768);
-          castdev::tma_load_3d(vd, &tm_v, &v_full[vs], 0, krow, bh);
-          castdev::tma_load_3d(vd + 16384, &tm_v, &v_full[vs], 64, krow, bh);
+          if (p.nkb_full > 0 && (!blk_ok || blk < p.nkb_full)) {
+            // whole block (rows past its end are zeros), or an entry the
+            // attention skips: a tile wholly outside the map, all zeros
+            const int r = blk_ok ? tin * 128 : p.k_block;
+            const int b = blk_ok ? blk : 0;
+            castdev::tma_load_4d(vd, &tm_vb, &v_full[vs], 0, r, b, bh);
+            castdev::tma_load_4d(vd + 16384, &tm_vb, &v_full[vs], 64, r, b, bh);
+          } else {
+            castdev::tma_load_3d(vd, &tm_v, &v_full[vs], 0, krow, bh);
+            castdev::tma_load_3d(vd + 16384, &tm_v, &v_full[vs], 64, krow, bh);
+          }
           issued = j + 1;
         }
         for (int j = max(0, issued - kVStages); j < issued; ++j)

@@ -82,6 +82,24 @@ int make_map_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, i
 }
 
 // 4-D tiled map over a dense [d3][d2][d1][d0] tensor, box (box0, box1, box2, 1).
+// A 4-D map with explicit byte strides of dims 1..3 (multiples of 16).
+int make_map_4d_strided(CUtensorMap *map, const void *base, CUtensorMapDataType dtype,
+                        const uint64_t (&dims)[4], const uint64_t (&strides)[3], uint32_t box0,
+                        uint32_t box1, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc;
+  int st = get_encode_tiled(&enc);
+  if (st) return st;
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t str[3] = {strides[0], strides[1], strides[2]};
+  cuuint32_t box[4] = {box0, box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype, 4, const_cast<void *>(base), d, str, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CAST_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return CAST_OK;
+}
+
 int make_map_4d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes,
                 uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint32_t box0, uint32_t box1,
                 uint32_t box2, CUtensorMapSwizzle swizzle) {
@@ -140,13 +158,15 @@ extern "C" int cast_device_error(cast_stream_t stream) {
 // device error word and the kernel returns normally.
 __global__ void selftest_bounded_wait_kernel(int arrive, unsigned long long limit_ns) {
   __shared__ __align__(8) uint64_t bar;
+  __shared__ int cta_abort;
   if (threadIdx.x == 0) {
+    cta_abort = 0;
     castdev::mbar_init(&bar, 1);
     castdev::fence_barrier_init();
   }
   __syncthreads();
   if (arrive && threadIdx.x == 0) castdev::mbar_arrive(&bar);
-  castdev::mbar_wait(&bar, 0, &g_cast_device_error, limit_ns);
+  castdev::mbar_wait(&bar, 0, &cta_abort, limit_ns);
 }
 
 extern "C" int cast_selftest_bounded_wait(int arrive, int limit_us, cast_stream_t stream) {
@@ -675,9 +695,24 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   if (st) return st;
 
   const int BH = B * H;
-  CUtensorMap tm_q8, tm_k8, tm_q16, tm_k16, tm_v;
+  CUtensorMap tm_q8, tm_k8, tm_q16, tm_k16, tm_v, tm_vb;
   memset(&tm_q8, 0, sizeof(tm_q8));
   memset(&tm_k8, 0, sizeof(tm_k8));
+  // Values of whole key blocks through a block-structured map [BH][block][row]
+  // [D]: the rows a block's last 128-row tile reads past the block's end are
+  // outside the map and arrive as zeros, so whatever the next block holds
+  // (it may be unselected, even non-finite) never meets the zero
+  // probabilities of those masked rows.  The ragged last block (Lk not a
+  // multiple of the block) and blocks shorter than a tile use the plain map,
+  // whose rows past Lk are zeros too.
+  const int nkb_full = k_block >= 128 ? Lk / k_block : 0;
+  if (nkb_full > 0) {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)k_block, (uint64_t)nkb_full, (uint64_t)BH};
+    const uint64_t strides[3] = {(uint64_t)D * 2, (uint64_t)k_block * D * 2, (uint64_t)Lk * D * 2};
+    if ((st = make_map_4d_strided(&tm_vb, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, 64, 128,
+                                  CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  }
   if ((st = make_map_3d(&tm_q16, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, Lq, BH, 64, 128,
                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
@@ -687,6 +722,7 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   if ((st = make_map_3d(&tm_v, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, Lk, BH, 64, 128,
                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
+  if (nkb_full == 0) tm_vb = tm_v;  // never read
   if (have_codes) {
     if ((st = make_map_3d(&tm_q8, q_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, Lq, BH, 128, 128,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -716,6 +752,7 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   p.k_block = k_block;
   p.nqb = ceil_div(Lq, q_block);
   p.nkb = ceil_div(Lk, k_block);
+  p.nkb_full = nkb_full;
   p.q_tiles = ceil_div(q_block, 128);
   p.k_tiles = ceil_div(k_block, 128);
   p.full_pairs = p.q_tiles / 2;
@@ -761,7 +798,7 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   CAST_CUDA_TRY(attr_err);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   castk::rcsa_attention_kernel<<<grid, castk::kAttnThreads, castk::AttnSmem::alloc, s>>>(
-      tm_q8, tm_k8, tm_q16, tm_k16, tm_v, p);
+      tm_q8, tm_k8, tm_q16, tm_k16, tm_v, tm_vb, p);
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;
 }

@@ -102,19 +102,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete.  Returns false (and
-// records a device timeout) if it does not complete within kWaitLimitNs, or
-// as soon as another wait anywhere on the device has already given up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err_flag,
+// Waits for the phase with the given parity to complete.  Returns false if
+// it does not complete within limit_ns -- the device error word then records
+// a timeout for the host and `cta_abort` (a flag in the calling CTA's shared
+// memory) tells the CTA's other waits to give up too -- or as soon as
+// another wait of this CTA has given up.  The device error word itself is
+// never consulted: a flag left by an earlier kernel (a timeout nobody read,
+// an index some kernel skipped and reported) must not stop this one.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *cta_abort,
                                           uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t spin = 0;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 255u) == 255u) {
-      if (*reinterpret_cast<volatile int *>(err_flag) != 0) return false;
+      if (*reinterpret_cast<volatile int *>(cta_abort) != 0) return false;
       if (global_timer_ns() - t0 > limit_ns) {
-        atomicExch(err_flag, (int)CAST_ERR_DEVICE_TIMEOUT);
+        atomicExch(&g_cast_device_error, (int)CAST_ERR_DEVICE_TIMEOUT);
+        *reinterpret_cast<volatile int *>(cta_abort) = 1;
         return false;
       }
     }
@@ -125,13 +130,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
 // `bar` before the CTA releases the memory it targets.  Bounded by time only:
 // it does not give up early when another wait has failed, because the work it
 // waits for was already issued.
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, int *err_flag) {
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, int *cta_abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t spin = 0;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
-      atomicExch(err_flag, (int)CAST_ERR_DEVICE_TIMEOUT);
+      atomicExch(&g_cast_device_error, (int)CAST_ERR_DEVICE_TIMEOUT);
+      *reinterpret_cast<volatile int *>(cta_abort) = 1;
       return false;
     }
   }

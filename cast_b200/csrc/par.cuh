@@ -728,7 +728,8 @@ __global__ void __launch_bounds__(kParPredThreads, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ParMmaSmem::bars);
   uint64_t *a_full = bars, *b_full = bars + 2, *mma_done = bars + 3, *tmem_free = bars + 5;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + ParMmaSmem::tmem_slot);
-  int *err = &g_cast_device_error;
+  // set when one of this CTA's waits gives up, so the others stop too
+  int *err = reinterpret_cast<int *>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = (p.C + 127) / 128;
   const int n_units = p.n_targets * kParTiles * nch;
@@ -737,6 +738,7 @@ __global__ void __launch_bounds__(kParPredThreads, 1)
   const int n = u1 - u0;
 
   if (threadIdx.x == 0) {
+    *err = 0;
     for (int i = 0; i < 2; ++i) {
       castdev::mbar_init(&a_full[i], 1);
       castdev::mbar_init(&mma_done[i], 1);
@@ -1062,7 +1064,8 @@ __global__ void __launch_bounds__(kParStatThreads, 1)
   uint64_t *a_full = bars, *mma_done = bars + 2, *tmem_free = bars + 4, *b_full = bars + 6;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + ParStatSmem::tmem_slot);
   float *wsum = reinterpret_cast<float *>(smem + ParStatSmem::wsum);
-  int *err = &g_cast_device_error;
+  // set when one of this CTA's waits gives up, so the others stop too
+  int *err = reinterpret_cast<int *>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = p.n_stat_chunks;
 
@@ -1082,6 +1085,7 @@ __global__ void __launch_bounds__(kParStatThreads, 1)
   };
 
   if (threadIdx.x == 0) {
+    *err = 0;
     for (int i = 0; i < 2; ++i) {
       castdev::mbar_init(&a_full[i], 1);
       castdev::mbar_init(&mma_done[i], 1);

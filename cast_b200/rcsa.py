@@ -29,7 +29,7 @@ import torch
 from . import _lib
 
 POLICIES = {"bf16": 0, "int8": 1, "auto": 2}
-DEFAULT_INT8_TOLERANCE = 0.025
+DEFAULT_INT8_TOLERANCE = 0.035
 RULE_BUDGET_CAUSAL = 0
 
 
@@ -436,18 +436,32 @@ class RCSAHostPlan:
     """An RCSA layer call whose inputs and output live in pinned host memory.
 
     The heads are split into ``groups`` contiguous groups, each with its own
-    :class:`RCSAPlan`.  Group g's host-to-device copy runs on one copy stream,
-    its selection + attention on the caller's stream once that copy is in,
-    and its device-to-host copy on a second copy stream once its attention is
-    done -- so the copies of one group overlap the compute of another, and
-    the two copy directions overlap each other.  The call returns with the
-    output copy ordered before anything the caller enqueues next on its
-    stream.  Batch size 1 (a head slice of ``[1,H,L,D]`` is contiguous).
+    :class:`RCSAPlan`.  Group g's Q and K cross to the device on one copy
+    stream, its selection runs on the caller's stream once they are in, and
+    its attention once its values are in; its device-to-host copy runs on a
+    second copy stream once its attention is done -- so the copies of one
+    group overlap the compute of another, and the two copy directions overlap
+    each other.
+
+    Values: with ``v_selected`` (the default) only the value blocks some
+    query block of the head selected cross the link (the attention reads no
+    others): the call reads each group's selection back as soon as it is
+    made and copies the union of its blocks, one copy per run of consecutive
+    blocks; the other blocks of the device buffer keep earlier contents,
+    which are finite (the buffer starts zeroed), so the masked rows a key
+    tile reads past its block's end contribute exact zeros.  Without it the
+    whole value tensor is copied before the selection.
+
+    The call returns with the output copy ordered before anything the caller
+    enqueues next on its stream; ``last_h2d_bytes`` / ``last_d2h_bytes`` are
+    the bytes it moved.  Batch size 1 (a head slice of ``[1,H,L,D]`` is
+    contiguous).
     """
 
     def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int,
                  budget: int, policy: str = "auto", groups: int = 4,
-                 int8_tolerance: float = DEFAULT_INT8_TOLERANCE, device=None):
+                 int8_tolerance: float = DEFAULT_INT8_TOLERANCE, device=None,
+                 v_selected: bool = True):
         if B != 1:
             raise ValueError("RCSAHostPlan takes batch size 1 (contiguous head slices)")
         dev = torch.device(device if device is not None else "cuda")
@@ -459,12 +473,41 @@ class RCSAHostPlan:
                       for h0, h1 in self.heads]
         self.q = torch.empty(B, H, Lq, D, dtype=torch.bfloat16, device=dev)
         self.k = torch.empty(B, H, Lk, D, dtype=torch.bfloat16, device=dev)
-        self.v = torch.empty(B, H, Lk, D, dtype=torch.bfloat16, device=dev)
+        self.v = torch.zeros(B, H, Lk, D, dtype=torch.bfloat16, device=dev)
         self.out = torch.empty(B, H, Lq, D, dtype=torch.bfloat16, device=dev)
         self.h2d = torch.cuda.Stream(dev)
         self.d2h = torch.cuda.Stream(dev)
         self.shape = (B, H, Lq, Lk, D)
+        self.block_size = block_size
         self.device = dev
+        self.v_selected = bool(v_selected)
+        # each group's selection, read back into pinned memory
+        self._sel_host = [(torch.empty(p.indices.shape, dtype=torch.int32).pin_memory(),
+                           torch.empty(p.counts.shape, dtype=torch.int32).pin_memory())
+                          for p in self.plans]
+        self.last_h2d_bytes = self.last_d2h_bytes = 0
+
+    def _value_runs(self, g: int):
+        """Runs ``(head, first key row, last key row + 1)`` of the value blocks
+        group g's selection reads, consecutive blocks merged."""
+        idx, cnt = (t.numpy() for t in self._sel_host[g])
+        h0 = self.heads[g][0]
+        Lk, bs = self.shape[3], self.block_size
+        nkb = -(-Lk // bs)
+        runs = []
+        for h in range(idx.shape[1]):
+            # the attention skips entries outside [0, nkb) the same way
+            blocks = sorted({int(b) for qb in range(idx.shape[2])
+                             for b in idx[0, h, qb, :max(0, int(cnt[0, h, qb]))] if 0 <= b < nkb})
+            start = prev = None
+            for b in blocks + [None]:
+                if b is not None and prev is not None and b == prev + 1:
+                    prev = b
+                    continue
+                if start is not None:
+                    runs.append((h0 + h, start * bs, min(Lk, (prev + 1) * bs)))
+                start = prev = b
+        return runs
 
     def __call__(self, hq: torch.Tensor, hk: torch.Tensor, hv: torch.Tensor,
                  hout: torch.Tensor, check: bool = True) -> torch.Tensor:
@@ -485,24 +528,49 @@ class RCSAHostPlan:
         # the previous call's compute and copies are done with the buffers
         self.h2d.wait_stream(cur)
         self.d2h.wait_stream(cur)
+        row_bytes = D * 2
+        h2d = 0
         ready = []
         with torch.cuda.stream(self.h2d):
             for h0, h1 in self.heads:
-                for dst, src in ((self.q, hq), (self.k, hk), (self.v, hv)):
+                pairs = ((self.q, hq), (self.k, hk)) + (() if self.v_selected else ((self.v, hv),))
+                for dst, src in pairs:
                     dst[:, h0:h1].copy_(src[:, h0:h1], non_blocking=True)
+                    h2d += dst[:, h0:h1].numel() * 2
                 ev = torch.cuda.Event()
                 ev.record(self.h2d)
                 ready.append(ev)
-        for (h0, h1), plan, ev in zip(self.heads, self.plans, ready):
+        picked = []
+        for g, (plan, ev) in enumerate(zip(self.plans, ready)):
+            h0, h1 = self.heads[g]
             cur.wait_event(ev)
-            q, k, v = self.q[:, h0:h1], self.k[:, h0:h1], self.v[:, h0:h1]
-            plan.select(q, k)
-            plan.attend(q, k, v, out=self.out[:, h0:h1])
+            plan.select(self.q[:, h0:h1], self.k[:, h0:h1])
+            if self.v_selected:
+                idx, cnt = self._sel_host[g]
+                idx.copy_(plan.indices, non_blocking=True)
+                cnt.copy_(plan.counts, non_blocking=True)
+                sel = torch.cuda.Event()
+                sel.record(cur)
+                picked.append(sel)
+        for g, plan in enumerate(self.plans):
+            h0, h1 = self.heads[g]
+            if self.v_selected:
+                picked[g].synchronize()
+                with torch.cuda.stream(self.h2d):
+                    for h, r0, r1 in self._value_runs(g):
+                        self.v[0, h, r0:r1].copy_(hv[0, h, r0:r1], non_blocking=True)
+                        h2d += (r1 - r0) * row_bytes
+                    vin = torch.cuda.Event()
+                    vin.record(self.h2d)
+                cur.wait_event(vin)
+            plan.attend(self.q[:, h0:h1], self.k[:, h0:h1], self.v[:, h0:h1], out=self.out[:, h0:h1])
             done = torch.cuda.Event()
             done.record(cur)
             self.d2h.wait_event(done)
             with torch.cuda.stream(self.d2h):
                 hout[:, h0:h1].copy_(self.out[:, h0:h1], non_blocking=True)
+        self.last_h2d_bytes = h2d
+        self.last_d2h_bytes = hout.numel() * 2
         cur.wait_stream(self.d2h)
         if check:
             _lib.check_device(cur.cuda_stream, "RCSAHostPlan")

@@ -447,6 +447,48 @@ def test_host_plan_matches_device_plan(cuda):
         assert torch.equal(plan.qk_mode, dp.qk_mode[:, h0:h1])
     d = (hout.float() - ref.float().cpu()).abs()
     assert float(d.max()) < MAX_ABS and float(d.mean()) < MEAN_ABS
+    # only the selected value blocks crossed the link; copying every value
+    # block gives the same bits
+    full_bytes = sum(t.numel() * 2 for t in (hq, hk, hv))
+    assert hp.last_h2d_bytes < full_bytes and hp.last_d2h_bytes == hout.numel() * 2
+    hv_all = rcsa.RCSAHostPlan(1, 4, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8,
+                               groups=3, device="cuda", v_selected=False)
+    hout2 = torch.empty_like(hout).pin_memory()
+    hv_all(hq, hk, hv, hout2)
+    assert hv_all.last_h2d_bytes == full_bytes
+    assert torch.equal(hout2, hout)
+
+
+def test_host_plan_copies_exactly_the_selected_values(cuda):
+    """The value blocks a selected-values call copies are the union of its
+    heads' selections: poisoning every other block of the host values with
+    NaN leaves the output finite and unchanged."""
+    w = workloads.config2(heads=2)
+    hq, hk, hv = (t.pin_memory() for t in (w.q, w.k, w.v))
+    hp = rcsa.RCSAHostPlan(1, 2, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8,
+                           groups=2, device="cuda")
+    hout = torch.empty(w.q.shape, dtype=torch.bfloat16).pin_memory()
+    hp(hq, hk, hv, hout)
+    first = hout.clone()
+    used = np.zeros((2, -(-w.k.shape[2] // 880)), dtype=bool)
+    for (h0, h1), plan in zip(hp.heads, hp.plans):
+        idx, cnt = plan.indices.cpu().numpy(), plan.counts.cpu().numpy()
+        for h in range(h1 - h0):
+            for qb in range(idx.shape[2]):
+                used[h0 + h, idx[0, h, qb, :cnt[0, h, qb]]] = True
+    assert not used.all()
+    poisoned = hv.clone().pin_memory()
+    for h in range(2):
+        for b in np.flatnonzero(~used[h]):
+            poisoned[0, h, b * 880:(b + 1) * 880] = float("nan")
+    hp2 = rcsa.RCSAHostPlan(1, 2, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8,
+                            groups=2, device="cuda")
+    hp2(hq, hk, poisoned, hout)
+    assert torch.equal(hout, first)
+    assert hp2.last_h2d_bytes == hp.last_h2d_bytes
+    rows = int(used.sum()) * 880 - sum(880 - (w.k.shape[2] - 880 * (used.shape[1] - 1))
+                                        for h in range(2) if used[h, -1])
+    assert hp.last_h2d_bytes == sum(t.numel() * 2 for t in (hq, hk)) + rows * 128 * 2
 
 
 ROW_SAMPLE = np.array([0, 1, 2, 63, 64, 127, 128, 255, 256, 383, 384, 511, 512, 639, 640, 767, 768, 800,
@@ -545,3 +587,48 @@ def test_attention_any_block_size(cuda, block):
         for out, ref in ((out_b, ref_b), (out_i, ref_i)):
             m, a = _errs(out, ref)
             assert m < MAX_ABS and a < MEAN_ABS, (block, kv is not None, m, a)
+
+
+def test_unselected_values_never_reach_the_output(cuda):
+    """A key block's last 128-row tile reaches 16 rows into the next block
+    (880 = 6 x 128 + 112); those rows are masked, and the block-structured
+    value map brings them in as zeros.  Non-finite values in every block no
+    query block of the head selected leave the output bit-identical."""
+    w = workloads.config2(heads=2)
+    plan = rcsa.RCSAPlan(1, 2, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8, device="cuda")
+    q, k, v = w.q.cuda(), w.k.cuda(), w.v.cuda()
+    clean = plan(q, k, v).clone()
+    idx, cnt = plan.indices.cpu().numpy(), plan.counts.cpu().numpy()
+    nkb = w.k.shape[2] // 880
+    used = np.zeros((2, nkb), dtype=bool)
+    for h in range(2):
+        for qb in range(idx.shape[2]):
+            used[h, idx[0, h, qb, :cnt[0, h, qb]]] = True
+    # some unselected block follows a selected one (its first rows are read)
+    assert any(used[h, b] and not used[h, b + 1] for h in range(2) for b in range(nkb - 1))
+    vp = v.clone()
+    for h in range(2):
+        for b in np.flatnonzero(~used[h]):
+            vp[0, h, b * 880:(b + 1) * 880] = float("nan") if b % 2 else float("inf")
+    dirty = plan(q, k, vp)
+    torch.cuda.synchronize()
+    assert torch.equal(dirty, clean)
+
+
+@pytest.mark.parametrize("config", [2, 3])
+@pytest.mark.parametrize("policy", ["int8", "auto", "bf16"])
+def test_every_output_row_is_written(cuda, config, policy):
+    """Every query row of the layer gets its output, whatever work split the
+    planner chose: an output buffer filled with NaN comes back finite."""
+    w = workloads.config2() if config == 2 else workloads.config3(heads=24)
+    q, k, v = w.q.cuda(), w.k.cuda(), w.v.cuda()
+    plan = rcsa.RCSAPlan(1, q.shape[1], q.shape[2], k.shape[2], 128, block_size=880, budget=w.budget,
+                         policy=policy, device=cuda)
+    plan.select(q, k)
+    out = torch.full_like(q, float("nan"))
+    plan.attend(q, k, v, out=out)
+    plan.check()
+    bad = ~torch.isfinite(out)
+    if bad.any():
+        h, r, _ = (int(x) for x in torch.nonzero(bad[0])[0])
+        pytest.fail(f"{int(bad.sum())} outputs not written, first at head {h} row {r}")
