@@ -475,6 +475,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--policy", default="auto", choices=["auto", "int8", "bf16"])
     ap.add_argument("--shard", default="head", choices=["head", "rollout"])
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="head sharding: the all-gather fused into the attention (peer) or NCCL after it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
@@ -497,6 +499,7 @@ def main():
     import torch
     import torch.distributed as dist
 
+    from cast_b200 import _lib
     from cast_b200 import distributed as cdist
     from cast_b200 import rcsa, workloads
 
@@ -562,15 +565,41 @@ def main():
     if head and world > 1:
         gathered = torch.empty((world * q.shape[0], *q.shape[1:]), dtype=q.dtype, device=dev)
 
-    def step():
+    def nccl_step():
         g_all.replay()
         if gathered is not None:
             dist.all_gather_into_tensor(gathered, plan.out)
 
+    # Head sharding with the gather fused into the attention (default): every
+    # rank's attention stores its rows into every rank's gathered buffer over
+    # NVLink, then waits for the peers' rows; one CUDA graph per gathered
+    # buffer, alternating.
+    peer = None
+    if gathered is not None and args.gather == "peer":
+        peer = cdist.PeerGather(q.shape[0], q.shape[1], q.shape[2], q.shape[3], device=dev)
+        peer_graphs = []
+        for par in (0, 1):
+            gph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side), torch.cuda.graph(gph, stream=side):
+                plan.select(q, k)
+                plan.attend(q, k, v, out=peer.slot(par), peers=peer.peers(par))
+                peer.wait()
+            stream.wait_stream(side)
+            peer_graphs.append(gph)
+        turn = [0]
+
+        def step():
+            peer_graphs[turn[0] & 1].replay()
+            turn[0] += 1
+    else:
+        step = nccl_step
+
     for _ in range(3):
         step()
     torch.cuda.synchronize()
-    if gathered is not None:  # the gathered heads are the single-call output, in head order
+    if gathered is not None and peer is None:  # the gathered heads are the single-call output
         g_all.replay()
         dist.all_gather_into_tensor(gathered, plan.out)
         torch.cuda.synchronize()
@@ -579,11 +608,19 @@ def main():
     time.sleep(0.3)
     total_ms = timed(step, args.steps)
     clocks = sampler.stop()
+    if peer is not None:
+        _lib.check_device(stream.cuda_stream, "fused gather")
     att_ms = timed(g_att.replay, args.steps) / args.steps
     sel_ms = timed(g_sel.replay, args.steps) / args.steps
-    gather_ms = 0.0
+    gather_ms = nccl_ms = 0.0
     if gathered is not None:
         gather_ms = timed(lambda: dist.all_gather_into_tensor(gathered, plan.out), args.steps) / args.steps
+        if peer is not None:  # the same call with the NCCL all-gather after it, for comparison
+            for _ in range(3):
+                nccl_step()
+            nccl_ms = timed(nccl_step, args.steps) / args.steps
+            del peer_graphs
+            peer.close()
     sel = plan.selection()
     counts_cpu = sel.counts.cpu()
     mode_cpu = sel.qk_mode.cpu() if sel.qk_mode is not None else None
@@ -632,10 +669,10 @@ def main():
 
     # ---- max over ranks
     vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms, gather_ms,
-                         rollout_ms or 0.0], dtype=torch.float64, device=dev)
+                         rollout_ms or 0.0, nccl_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, att_ms, e2e_ms, sel_ms, gather_ms, rollout_ms = (float(x) for x in vals.tolist())
+    total_ms, att_ms, e2e_ms, sel_ms, gather_ms, rollout_ms, nccl_ms = (float(x) for x in vals.tolist())
     ms_per_step = total_ms / args.steps
     value_us = ms_per_step * 1000.0
 
@@ -694,7 +731,10 @@ def main():
         },
         "host_enqueue_us_eager": host_us,
         "timing": (f"CUDA graph replay of the {KERNELS_PER_CALL[args.policy]}-kernel layer call"
-                   + (" + NCCL all-gather of the head outputs" if gathered is not None else "")
+                   + ("" if gathered is None else
+                      " with the head outputs' all-gather fused into the attention (peer stores over "
+                      "NVLink) and the wait for the peers' rows" if peer is not None else
+                      " + NCCL all-gather of the head outputs")
                    + "; CUDA events on the launching stream, max over ranks"),
         "roofline": {
             "bound": "tensor", "achieved": (alg_i8 + alg_bf) / att_s / 1e12,
@@ -711,11 +751,16 @@ def main():
         "par": par_line,
         "compact_and_lift": compact_line,
         "swap_router": swap_line,
-        "gpu_launches": KERNELS_PER_CALL[args.policy] * args.steps,
+        "gpu_launches": (KERNELS_PER_CALL[args.policy] + (1 if peer is not None else 0)) * args.steps,
         "clocks": clocks,
     }
     if gathered is not None:
         line["all_gather_us"] = gather_ms * 1000.0
+        line["gather"] = args.gather
+        if peer is not None:
+            line["nccl_gather_value"] = {
+                "value": nccl_ms * 1000.0, "unit": "us/call",
+                "note": "the same call with a separate NCCL all-gather after it, max over ranks"}
         line["rollout"] = {"value": rollout_ms * 1000.0 / world, "unit": "us/call",
                            "note": f"rollout sharding: each of {world} GPUs runs its own full call, no "
                                    "collective; value = slowest GPU's call time / N"}

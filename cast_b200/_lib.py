@@ -59,6 +59,18 @@ SIGNATURES = {
          c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     ),
     "cast_rcsa_attention_workspace_bytes": (c_size_t, [c_int] * 7 + [c_void_p]),
+    "cast_rcsa_attention_peers": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p],
+    ),
+    "cast_peer_alloc": (c_int, [c_size_t, c_void_p, c_void_p]),
+    "cast_peer_open": (c_int, [c_void_p, c_void_p]),
+    "cast_peer_close": (c_int, [c_void_p]),
+    "cast_peer_free": (c_int, [c_void_p]),
+    "cast_peer_wait": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "cast_compact_pack": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,

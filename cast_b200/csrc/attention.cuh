@@ -60,6 +60,7 @@ constexpr int kMaxItemParts = 64;    // parts of one cut item
 // [row], so a warp's 32 rows are contiguous), then per tile the running max
 // and the row sum of its 128 rows.
 constexpr int kPartSlotFloats = 2 * 128 * 128 + 2 * 2 * 128;
+constexpr int kMaxPeers = 7;  // other ranks a launch writes its outputs to
 
 // Shared memory (offsets from the 1024-byte aligned base).  The Q and K
 // areas depend on the QK^T precision of the CTA:
@@ -111,6 +112,18 @@ struct AttnParams {
   float *part_ws;
   uint16_t part_first[kMaxSplitItems + 1];
   uint16_t part_tiles[kMaxSplitItems];
+  // Head-sharded all-gather fused into the epilogue (n_peers > 0): every
+  // output row is also stored, over NVLink, at the same offset of each
+  // peer's gathered buffer (peer_out[r] is this rank's slot there).  Every
+  // CTA fences its stores at system scope and takes a ticket; the launch's
+  // last CTA then raises this rank's flag in every peer to this call's
+  // number (*calls + 1, a release store) and resets the ticket.  The call
+  // counter lives on the device, so a captured graph replays correctly.
+  int n_peers;
+  const uint32_t *calls;
+  uint32_t *done_ticket;
+  __nv_bfloat16 *peer_out[kMaxPeers];
+  uint32_t *peer_flag[kMaxPeers];
 };
 
 // Work items are ordered in groups of kHeadGroup heads: within a group,
@@ -393,6 +406,19 @@ __device__ __forceinline__ float step_probs_any(uint32_t (&v)[64], const uint32_
               : step_probs<kInt8, true>(v, kmask, c2, base);
 }
 
+// A CTA's exit with the fused all-gather: its ticket; the launch's last CTA
+// raises this rank's flag in every peer.  Every CTA fenced its own stores at
+// system scope before taking its ticket.
+__device__ __forceinline__ void peer_ticket(const AttnParams &p) {
+  const uint32_t t = atomicAdd(p.done_ticket, 1u);
+  if (t == gridDim.x - 1) {
+    __threadfence_system();
+    const uint32_t call = *reinterpret_cast<const volatile uint32_t *>(p.calls) + 1u;
+    for (int r = 0; r < p.n_peers; ++r) castdev::st_release_sys(p.peer_flag[r], call);
+    atomicExch(p.done_ticket, 0u);
+  }
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 1)
     rcsa_attention_kernel(const __grid_constant__ CUtensorMap tm_q8,
                           const __grid_constant__ CUtensorMap tm_k8,
@@ -477,12 +503,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     n_kv = min(hi, n_kv_item) - kt_lo;
     n_live = 0;
     for (int j = 0; j < n_parts; ++j) n_live += part_lo(j, planned, n_parts) < n_kv_item;
-    if (n_kv_item == 0) {
-      if (part > 0) return;  // part 0 writes the item's (zero) rows
-      n_live = 1;
-    } else if (n_kv == 0) {
+    if ((n_kv_item == 0 && part > 0) || (n_kv_item > 0 && n_kv == 0)) {
+      // no key tiles here (part 0 of an empty item writes its zero rows)
+      if (p.n_peers > 0 && threadIdx.x == 0) peer_ticket(p);
       return;
     }
+    if (n_kv_item == 0) n_live = 1;
   }
   // A single query tile (the last of an odd tile count) splits its key tiles
   // between the two warpgroups (split item), whose partial results are merged
@@ -845,9 +871,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint32_t *wp = reinterpret_cast<uint32_t *>(w);
 #pragma unroll
         for (int c = 0; c < 16; ++c) wp[c] = pack_bf16x2(o[2 * c] * inv_l, o[2 * c + 1] * inv_l);
-        uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)bh * p.Lq + qrow) * 128 + 32 * cc);
+        const size_t off = ((size_t)bh * p.Lq + qrow) * 128 + 32 * cc;
+        uint4 *dst = reinterpret_cast<uint4 *>(p.out + off);
 #pragma unroll
         for (int c = 0; c < 4; ++c) dst[c] = w[c];
+        for (int r = 0; r < p.n_peers; ++r) {
+          uint4 *pd = reinterpret_cast<uint4 *>(p.peer_out[r] + off);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) pd[c] = w[c];
+        }
       };
       if (n_live == 1) {
         // the whole item ran here: normalise and write
@@ -924,11 +956,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   }
 
+  // this thread's output stores (peer ones included) before the ticket
+  if (p.n_peers > 0) __threadfence_system();
   __syncthreads();
   if (warp == kMmaWarp) {
     castdev::tc_fence_after();
     castdev::tmem_dealloc(tmem, 512);
   }
+  if (p.n_peers > 0 && threadIdx.x == 0) peer_ticket(p);
 }
 
 }  // namespace castk

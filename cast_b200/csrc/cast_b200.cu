@@ -660,15 +660,22 @@ extern "C" size_t cast_rcsa_attention_workspace_bytes(int B, int H, int Lq, int 
       .ws_bytes;
 }
 
-extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
-                                   const int8_t *q_codes, const float *q_scales,
-                                   const int8_t *k_codes, const float *k_scales,
-                                   const uint8_t *qk_mode, const int32_t *indices,
-                                   const int32_t *counts, int max_degree,
-                                   const uint8_t *key_valid, int B, int H, int Lq, int Lk, int D,
-                                   int q_block, int k_block, float sm_scale, void *out,
-                                   float *lse, const int32_t *count_hint, void *workspace,
-                                   size_t workspace_bytes, cast_stream_t stream) {
+// The fused all-gather of a head-sharded call (cast_rcsa_attention_peers).
+struct PeerArgs {
+  int n_peers = 0;
+  const uint32_t *calls = nullptr;
+  uint32_t *done_ticket = nullptr;
+  void *const *peer_out = nullptr;
+  uint32_t *const *peer_flag = nullptr;
+};
+
+static int attention_impl(const void *q, const void *k, const void *v, const int8_t *q_codes,
+                          const float *q_scales, const int8_t *k_codes, const float *k_scales,
+                          const uint8_t *qk_mode, const int32_t *indices, const int32_t *counts,
+                          int max_degree, const uint8_t *key_valid, int B, int H, int Lq, int Lk,
+                          int D, int q_block, int k_block, float sm_scale, void *out, float *lse,
+                          const int32_t *count_hint, void *workspace, size_t workspace_bytes,
+                          const PeerArgs &peers, cast_stream_t stream) {
   if (!q || !k || !v || !indices || !counts || !out)
     return fail(CAST_ERR_INVALID_ARGUMENT, "q, k, v, indices, counts and out are required");
   int st = attention_dims_ok(B, H, Lq, Lk, q_block, k_block, max_degree);
@@ -767,6 +774,13 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   p.part_ws = nullptr;
   memset(p.part_first, 0, sizeof(p.part_first));
   memset(p.part_tiles, 0, sizeof(p.part_tiles));
+  p.n_peers = peers.n_peers;
+  p.calls = peers.calls;
+  p.done_ticket = peers.done_ticket;
+  for (int r = 0; r < castk::kMaxPeers; ++r) {
+    p.peer_out[r] = r < peers.n_peers ? static_cast<__nv_bfloat16 *>(peers.peer_out[r]) : nullptr;
+    p.peer_flag[r] = r < peers.n_peers ? peers.peer_flag[r] : nullptr;
+  }
   // Items are cut only with a workspace; converting tail pairs needs none.
   const AttnSplitPlan plan = attention_plan(BH, p.nqb, p.q_tiles, p.k_tiles, max_degree, count_hint,
                                             n_sms, workspace != nullptr);
@@ -799,6 +813,123 @@ extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   castk::rcsa_attention_kernel<<<grid, castk::kAttnThreads, castk::AttnSmem::alloc, s>>>(
       tm_q8, tm_k8, tm_q16, tm_k16, tm_v, tm_vb, p);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
+extern "C" int cast_rcsa_attention(const void *q, const void *k, const void *v,
+                                   const int8_t *q_codes, const float *q_scales,
+                                   const int8_t *k_codes, const float *k_scales,
+                                   const uint8_t *qk_mode, const int32_t *indices,
+                                   const int32_t *counts, int max_degree,
+                                   const uint8_t *key_valid, int B, int H, int Lq, int Lk, int D,
+                                   int q_block, int k_block, float sm_scale, void *out,
+                                   float *lse, const int32_t *count_hint, void *workspace,
+                                   size_t workspace_bytes, cast_stream_t stream) {
+  return attention_impl(q, k, v, q_codes, q_scales, k_codes, k_scales, qk_mode, indices, counts,
+                        max_degree, key_valid, B, H, Lq, Lk, D, q_block, k_block, sm_scale, out, lse,
+                        count_hint, workspace, workspace_bytes, PeerArgs{}, stream);
+}
+
+extern "C" int cast_rcsa_attention_peers(
+    const void *q, const void *k, const void *v, const int8_t *q_codes, const float *q_scales,
+    const int8_t *k_codes, const float *k_scales, const uint8_t *qk_mode, const int32_t *indices,
+    const int32_t *counts, int max_degree, const uint8_t *key_valid, int B, int H, int Lq, int Lk,
+    int D, int q_block, int k_block, float sm_scale, void *out, float *lse,
+    const int32_t *count_hint, void *workspace, size_t workspace_bytes, int n_peers,
+    void *const *peer_out, uint32_t *const *peer_flag, uint32_t *done_ticket,
+    const uint32_t *calls, cast_stream_t stream) {
+  if (n_peers < 0 || n_peers > castk::kMaxPeers)
+    return fail(CAST_ERR_UNSUPPORTED, "%d peers (at most %d)", n_peers, castk::kMaxPeers);
+  if (n_peers > 0) {
+    if (!peer_out || !peer_flag || !done_ticket || !calls)
+      return fail(CAST_ERR_INVALID_ARGUMENT, "peer_out, peer_flag, done_ticket and calls are required");
+    for (int r = 0; r < n_peers; ++r)
+      if (!peer_out[r] || !peer_flag[r] || !aligned16(peer_out[r]) || (reinterpret_cast<uintptr_t>(peer_flag[r]) & 3))
+        return fail(CAST_ERR_ALIGNMENT, "peer %d: output must be 16-byte and its flag 4-byte aligned", r);
+  }
+  PeerArgs peers;
+  peers.n_peers = n_peers;
+  peers.calls = calls;
+  peers.done_ticket = done_ticket;
+  peers.peer_out = peer_out;
+  peers.peer_flag = peer_flag;
+  return attention_impl(q, k, v, q_codes, q_scales, k_codes, k_scales, qk_mode, indices, counts,
+                        max_degree, key_valid, B, H, Lq, Lk, D, q_block, k_block, sm_scale, out, lse,
+                        count_hint, workspace, workspace_bytes, peers, stream);
+}
+
+// ===========================================================================
+// peer buffers (CUDA IPC, no multicast) and the gather's completion wait
+// ===========================================================================
+namespace castk {
+// One thread per source rank: until the rank's flag holds this call's number
+// (*calls + 1; acquire, system scope), bounded by kWaitLimitNs -- a wait that
+// gives up sets the device error word; then the call counter advances.
+__global__ void peer_wait_kernel(const uint32_t *flags, int n_src, int self_rank, uint32_t *calls) {
+  const int r = threadIdx.x;
+  const uint32_t call = *calls + 1u;
+  if (r < n_src && r != self_rank && castdev::ld_acquire_sys(flags + r) != call) {
+    const uint64_t t0 = castdev::global_timer_ns();
+    for (uint32_t spin = 0;; ++spin) {
+      if (castdev::ld_acquire_sys(flags + r) == call) break;
+      if ((spin & 255u) == 255u && castdev::global_timer_ns() - t0 > castdev::kWaitLimitNs) {
+        atomicExch(&g_cast_device_error, (int)CAST_ERR_DEVICE_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+  if (r == 0) *calls = call;
+}
+}  // namespace castk
+
+extern "C" int cast_peer_alloc(size_t bytes, void **ptr, void *ipc_handle) {
+  if (!ptr || !ipc_handle || bytes == 0) return fail(CAST_ERR_INVALID_ARGUMENT, "bytes, ptr and handle required");
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  void *p = nullptr;
+  CAST_CUDA_TRY(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(CAST_ERR_CUDA, "peer buffer: %s", cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return CAST_OK;
+}
+
+extern "C" int cast_peer_open(const void *ipc_handle, void **ptr) {
+  if (!ptr || !ipc_handle) return fail(CAST_ERR_INVALID_ARGUMENT, "handle and ptr required");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  CAST_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return CAST_OK;
+}
+
+extern "C" int cast_peer_close(void *ptr) {
+  if (!ptr) return fail(CAST_ERR_INVALID_ARGUMENT, "ptr required");
+  CAST_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return CAST_OK;
+}
+
+extern "C" int cast_peer_free(void *ptr) {
+  if (!ptr) return fail(CAST_ERR_INVALID_ARGUMENT, "ptr required");
+  CAST_CUDA_TRY(cudaFree(ptr));
+  return CAST_OK;
+}
+
+extern "C" int cast_peer_wait(const uint32_t *flags, int n_src, int self_rank, uint32_t *calls,
+                              cast_stream_t stream) {
+  if (!flags || !calls || n_src <= 0 || n_src > castk::kMaxPeers + 1 || self_rank < 0 ||
+      self_rank >= n_src)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "flags, calls, %d sources (1..%d), rank %d", n_src,
+                castk::kMaxPeers + 1, self_rank);
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  castk::peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, n_src, self_rank,
+                                                                                  calls);
   CAST_CUDA_TRY(cudaGetLastError());
   return CAST_OK;
 }

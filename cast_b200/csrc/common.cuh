@@ -143,6 +143,16 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, 
   }
 }
 
+// ---- system-scope flags between GPUs (plain peer loads and stores) ----
+__device__ __forceinline__ void st_release_sys(uint32_t *addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
 // ---- TMA (no multicast anywhere in this library) ----
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {

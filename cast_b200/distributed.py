@@ -16,9 +16,12 @@ B200 partitioning around its per-head arithmetic.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .rcsa import RCSAPlan
 
 
@@ -59,6 +62,111 @@ def gather_heads(out_local: torch.Tensor, world: int, group=None,
     return gathered.view(world, b, hl, length, d).permute(1, 0, 2, 3, 4).reshape(b, world * hl, length, d)
 
 
+class _DeviceArray:
+    """A borrowed device buffer seen by ``torch.as_tensor`` (no ownership)."""
+
+    def __init__(self, address: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (address, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGather:
+    """The gathered head buffers of a head-sharded layer, written directly by
+    every rank's attention (``cast_rcsa_attention_peers``): each rank owns one
+    device buffer, shared with the others through CUDA IPC (no multicast),
+    holding two gathered outputs ``[2][world*B][H/world][Lq][D]`` bf16 (the
+    calls alternate between them, so a peer never writes the output its
+    owner may still be reading), then the flag word each peer raises when its
+    rows have landed, the attention's CTA ticket and the call counter.
+
+    Every rank must make the same number of calls; :meth:`close` (collective)
+    releases the buffers before the process group goes away."""
+
+    def __init__(self, B: int, heads_local: int, Lq: int, D: int, *, device: torch.device, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= 8:
+            raise ValueError("the fused gather runs on 2 to 8 ranks")
+        self.device = torch.device(device)
+        self.shape = (B, heads_local, Lq, D)
+        slot = B * heads_local * Lq * D * 2
+        self.slot_bytes = slot
+        buf = 2 * self.world * slot
+        self.flag_off = (buf + 255) // 256 * 256
+        total = self.flag_off + 256
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        with torch.cuda.device(self.device):
+            _lib.call("cast_peer_alloc", total, ctypes.byref(own), ctypes.byref(handle))
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        bases = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+                p = ctypes.c_void_p()
+                _lib.call("cast_peer_open", ctypes.byref(hb), ctypes.byref(p))
+                self._opened.append(p.value)
+                bases.append(p.value)
+        others = [r for r in range(self.world) if r != self.rank]
+        self._peer_out = [(ctypes.c_void_p * len(others))(
+            *[bases[r] + (par * self.world + self.rank) * slot for r in others]) for par in (0, 1)]
+        self._peer_flag = (ctypes.c_void_p * len(others))(
+            *[bases[r] + self.flag_off + 4 * self.rank for r in others])
+        self.flags = self._own + self.flag_off  # uint32 [8]: the peers' call numbers
+        self.ticket = self.flags + 32
+        self.calls = self.flags + 36
+        self.gathered = torch.as_tensor(
+            _DeviceArray(self._own, (2, self.world * B, heads_local, Lq, D), "<i2"),
+            device=self.device).view(torch.bfloat16)
+        self.calls_made = 0
+
+    def slot(self, parity: int) -> torch.Tensor:
+        """This rank's ``[B, H/world, Lq, D]`` slot of gathered buffer ``parity``."""
+        B = self.shape[0]
+        return self.gathered[parity, self.rank * B:(self.rank + 1) * B]
+
+    def peers(self, parity: int):
+        """``cast_rcsa_attention_peers``'s gather arguments for buffer ``parity``."""
+        return (self.world - 1, ctypes.cast(self._peer_out[parity], ctypes.c_void_p),
+                ctypes.cast(self._peer_flag, ctypes.c_void_p), self.ticket, self.calls)
+
+    def wait(self) -> None:
+        """Orders the stream after every peer's rows of this call."""
+        _lib.call("cast_peer_wait", self.flags, self.world, self.rank, self.calls,
+                  torch.cuda.current_stream(self.device).cuda_stream)
+
+    def heads(self, parity: int) -> torch.Tensor:
+        """Gathered buffer ``parity`` as ``[B, H, Lq, D]`` in head order."""
+        B, hl, lq, d = self.shape
+        g = self.gathered[parity]
+        if B == 1:
+            return g.view(1, self.world * hl, lq, d)
+        return g.view(self.world, B, hl, lq, d).permute(1, 0, 2, 3, 4).reshape(B, self.world * hl, lq, d)
+
+    def close(self) -> None:
+        """Collective: every rank stops using the peers' buffers, then frees its own."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.call("cast_peer_close", ctypes.c_void_p(p))
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.gathered = None
+        with torch.cuda.device(self.device):
+            _lib.call("cast_peer_free", ctypes.c_void_p(self._own))
+        self._own = None
+
+
 class HeadShardedRCSA:
     """One RCSA layer call split by heads over the ranks of a process group.
 
@@ -67,21 +175,40 @@ class HeadShardedRCSA:
     """
 
     def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int, budget: int,
-                 policy: str = "auto", device: torch.device, group=None):
+                 policy: str = "auto", device: torch.device, group=None, gather: str = "nccl"):
+        if gather not in ("nccl", "peer"):
+            raise ValueError("gather must be 'nccl' or 'peer'")
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.group = group
         self.lo, self.hi = head_range(H, self.world, self.rank)
         self.plan = RCSAPlan(B, self.hi - self.lo, Lq, Lk, D, block_size=block_size,
                              budget=budget, policy=policy, device=device)
-        self.gathered = torch.empty((self.world * B, self.hi - self.lo, Lq, D),
-                                    dtype=torch.bfloat16, device=device)
+        self.peer = (PeerGather(B, self.hi - self.lo, Lq, D, device=device, group=group)
+                     if gather == "peer" and self.world > 1 else None)
+        self.gathered = None if self.peer else torch.empty(
+            (self.world * B, self.hi - self.lo, Lq, D), dtype=torch.bfloat16, device=device)
 
     def local_heads(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's head slice of a full ``[B, H, L, D]`` tensor."""
         return x[:, self.lo:self.hi].contiguous()
 
     def __call__(self, q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor):
-        """``q/k/v_local``: this rank's heads; returns all heads' outputs."""
-        out = self.plan(q_local, k_local, v_local)
-        return gather_heads(out, self.world, self.group, self.gathered)
+        """``q/k/v_local``: this rank's heads; returns all heads' outputs.
+        With the fused gather the result is a view of one of the two gathered
+        buffers, valid until the call after next."""
+        if self.peer is None:
+            out = self.plan(q_local, k_local, v_local)
+            return gather_heads(out, self.world, self.group, self.gathered)
+        par = self.peer.calls_made & 1
+        self.plan.select(q_local, k_local)
+        self.plan.attend(q_local, k_local, v_local, out=self.peer.slot(par), peers=self.peer.peers(par))
+        self.peer.wait()
+        self.peer.calls_made += 1
+        return self.peer.heads(par)
+
+    def close(self) -> None:
+        """Collective with the fused gather: releases the peer buffers."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None

@@ -371,9 +371,12 @@ class RCSAPlan:
         )
 
     def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, peers=None) -> torch.Tensor:
         """Attention with the last selection; into ``out`` (bf16 ``[B,H,Lq,D]``)
-        when given, else into the plan's own output buffer."""
+        when given, else into the plan's own output buffer.  ``peers``: the
+        fused all-gather's arguments ``(n_peers, peer_out, peer_flag,
+        done_ticket, calls)`` (see :class:`cast_b200.distributed.PeerGather`),
+        which store every output row into the peers' gathered buffers too."""
         B, H, Lq, Lk, D = self.shape
         _need_cuda("v", v, torch.bfloat16, 4)
         if out is None:
@@ -383,15 +386,16 @@ class RCSAPlan:
         else:
             _need_cuda("out", out, torch.bfloat16, 4)
         P = _lib.ptr
-        _lib.call(
-            "cast_rcsa_attention", P(q), P(k), P(v), P(self.q_codes), P(self.q_scales),
-            P(self.k_codes), P(self.k_scales), P(self.qk_mode), P(self.indices), P(self.counts),
-            int(self.indices.shape[-1]), None, B, H, Lq, Lk, D, self.block_size, self.block_size,
-            float(self.sm_scale), P(out), None, self.count_hint.ctypes.data,
-            P(self.attn_workspace),
-            0 if self.attn_workspace is None else self.attn_workspace.numel(),
-            _stream(self.device),
-        )
+        args = (P(q), P(k), P(v), P(self.q_codes), P(self.q_scales),
+                P(self.k_codes), P(self.k_scales), P(self.qk_mode), P(self.indices), P(self.counts),
+                int(self.indices.shape[-1]), None, B, H, Lq, Lk, D, self.block_size, self.block_size,
+                float(self.sm_scale), P(out), None, self.count_hint.ctypes.data,
+                P(self.attn_workspace),
+                0 if self.attn_workspace is None else self.attn_workspace.numel())
+        if peers is None:
+            _lib.call("cast_rcsa_attention", *args, _stream(self.device))
+        else:
+            _lib.call("cast_rcsa_attention_peers", *args, *peers, _stream(self.device))
         return out
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
@@ -447,7 +451,7 @@ class RCSAHostPlan:
     query block of the head selected cross the link (the attention reads no
     others): the call reads each group's selection back as soon as it is
     made and copies the union of its blocks, one copy per run of consecutive
-    blocks; the other blocks of the device buffer keep earlier contents,
+    blocks (runs ``value_gap`` or fewer blocks apart merged); the other blocks of the device buffer keep earlier contents,
     which are finite (the buffer starts zeroed), so the masked rows a key
     tile reads past its block's end contribute exact zeros.  Without it the
     whole value tensor is copied before the selection.
@@ -461,7 +465,7 @@ class RCSAHostPlan:
     def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int,
                  budget: int, policy: str = "auto", groups: int = 4,
                  int8_tolerance: float = DEFAULT_INT8_TOLERANCE, device=None,
-                 v_selected: bool = True):
+                 v_selected: bool = True, value_gap: int = 2):
         if B != 1:
             raise ValueError("RCSAHostPlan takes batch size 1 (contiguous head slices)")
         dev = torch.device(device if device is not None else "cuda")
@@ -481,6 +485,7 @@ class RCSAHostPlan:
         self.block_size = block_size
         self.device = dev
         self.v_selected = bool(v_selected)
+        self.value_gap = max(0, int(value_gap))
         # each group's selection, read back into pinned memory
         self._sel_host = [(torch.empty(p.indices.shape, dtype=torch.int32).pin_memory(),
                            torch.empty(p.counts.shape, dtype=torch.int32).pin_memory())
@@ -489,7 +494,9 @@ class RCSAHostPlan:
 
     def _value_runs(self, g: int):
         """Runs ``(head, first key row, last key row + 1)`` of the value blocks
-        group g's selection reads, consecutive blocks merged."""
+        group g's selection reads, consecutive blocks merged, and so are runs
+        at most ``value_gap`` unselected blocks apart (one larger copy costs
+        less than two small ones across a short gap)."""
         idx, cnt = (t.numpy() for t in self._sel_host[g])
         h0 = self.heads[g][0]
         Lk, bs = self.shape[3], self.block_size
@@ -501,7 +508,7 @@ class RCSAHostPlan:
                              for b in idx[0, h, qb, :max(0, int(cnt[0, h, qb]))] if 0 <= b < nkb})
             start = prev = None
             for b in blocks + [None]:
-                if b is not None and prev is not None and b == prev + 1:
+                if b is not None and prev is not None and b <= prev + 1 + self.value_gap:
                     prev = b
                     continue
                 if start is not None:

@@ -256,6 +256,58 @@ CAST_API size_t cast_rcsa_attention_workspace_bytes(int B, int H, int Lq, int Lk
                                                     const int32_t *count_hint);
 
 /*
+ * Head-sharded call with the all-gather of the head outputs fused into the
+ * attention (no reference counterpart: the reference runs on one device; the
+ * multi-GPU split is this library's, with the reference's per-head
+ * arithmetic).  As cast_rcsa_attention, and every output row is also stored,
+ * over NVLink, to the same offset of peer_out[r] (r < n_peers <= 7; host
+ * arrays of device pointers, opened with cast_peer_open): this rank's slot of
+ * each peer's gathered buffer (plain peer stores, no multicast).  Every CTA
+ * fences its stores at system scope and counts itself in *done_ticket
+ * (device memory, zero before the first call; the launch leaves it zero);
+ * the launch's last CTA then stores the call's number, *calls + 1 (calls:
+ * this rank's device call counter, which cast_peer_wait advances), to every
+ * *peer_flag[r] (this rank's flag word in peer r, a release store at system
+ * scope).  The counter lives on the device, so a CUDA graph of the call
+ * replays correctly.  `out` is this rank's slot of its own gathered buffer.
+ * A rank reads the gathered heads after cast_peer_wait on its stream.  Calls
+ * that share done_ticket must not overlap on the GPU; every rank makes the
+ * same number of calls; a peer must not write a gathered buffer its owner
+ * still reads (alternate two buffers).
+ */
+CAST_API int cast_rcsa_attention_peers(
+    const void *q, const void *k, const void *v, const int8_t *q_codes, const float *q_scales,
+    const int8_t *k_codes, const float *k_scales, const uint8_t *qk_mode, const int32_t *indices,
+    const int32_t *counts, int max_degree, const uint8_t *key_valid, int B, int H, int Lq, int Lk,
+    int D, int q_block, int k_block, float sm_scale, void *out, float *lse,
+    const int32_t *count_hint, void *workspace, size_t workspace_bytes, int n_peers,
+    void *const *peer_out, uint32_t *const *peer_flag, uint32_t *done_ticket,
+    const uint32_t *calls, cast_stream_t stream);
+
+/*
+ * Peer buffers for the fused gather (CUDA IPC, no multicast): cast_peer_alloc
+ * makes a zero-filled device buffer of `bytes` on the current device and
+ * writes its 64-byte IPC handle to ipc_handle; another process opens it with
+ * cast_peer_open (peer access enabled) and releases it with cast_peer_close;
+ * the owner frees it with cast_peer_free once no peer holds it open.
+ */
+CAST_API int cast_peer_alloc(size_t bytes, void **ptr, void *ipc_handle);
+CAST_API int cast_peer_open(const void *ipc_handle, void **ptr);
+CAST_API int cast_peer_close(void *ptr);
+CAST_API int cast_peer_free(void *ptr);
+
+/*
+ * On `stream`: waits until flags[r] == *calls + 1 (acquire, system scope) for
+ * every source rank r < n_src other than self_rank -- every peer's fused
+ * gather of this call has landed in this rank's buffer -- then advances
+ * *calls (device memory, this rank's call counter, zero at the start).
+ * Bounded (1 s per rank); a wait that gives up sets the device error word
+ * (CAST_ERR_DEVICE_TIMEOUT).  n_src <= 8.
+ */
+CAST_API int cast_peer_wait(const uint32_t *flags, int n_src, int self_rank, uint32_t *calls,
+                            cast_stream_t stream);
+
+/*
  * Compact-layout packing for the compact selection / attention path, with
  * the RoPE phase applied on the way.  Replaces, for one layer call, the
  * reference's RoPE rotation MatrixCurvaturePhaseFrameWeave.

@@ -80,3 +80,65 @@ def test_head_sharded_equals_single_gpu(tmp_path):
     ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(g.abs(), s.abs()).clamp_min(2.0 ** -126))) - 7)
     assert bool((d <= ulp).all()), float((d / ulp).max())
     assert float(d.mean()) < 2e-3
+
+
+def _peer_worker(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    from cast_b200 import _lib
+    from cast_b200 import distributed as cd
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    layer = None
+    try:
+        q, k, v = _inputs()
+        kw = dict(block_size=880, budget=3, policy="auto", device=dev)
+        ref_layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, **kw)
+        ql, kl, vl = (ref_layer.local_heads(t).to(dev) for t in (q, k, v))
+        ref = ref_layer(ql, kl, vl).clone()
+        layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, gather="peer", **kw)
+        outs = [layer(ql, kl, vl).clone() for _ in range(3)]  # both buffers, then the first again
+        torch.cuda.synchronize()
+        _lib.check_device(torch.cuda.current_stream(dev).cuda_stream, "peer gather")
+        for o in outs:
+            assert torch.equal(o, ref)
+        # a CUDA graph of the call replays with the device call counter
+        par = layer.peer.calls_made & 1
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+            layer.plan.select(ql, kl)
+            layer.plan.attend(ql, kl, vl, out=layer.peer.slot(par), peers=layer.peer.peers(par))
+            layer.peer.wait()
+        layer.peer.gathered[par].zero_()
+        dist.barrier()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        _lib.check_device(torch.cuda.current_stream(dev).cuda_stream, "peer gather graph")
+        assert torch.equal(layer.peer.heads(par), ref)
+        del g
+        if rank == 0:
+            torch.save(ref.cpu(), os.path.join(out_dir, "peer_ref.pt"))
+    finally:
+        if layer is not None:
+            layer.close()
+        dist.destroy_process_group()
+
+
+def test_fused_peer_gather_equals_nccl_gather(tmp_path):
+    """The attention storing every output row into the peers' gathered
+    buffers over NVLink (plain peer stores, IPC buffers) gives the NCCL
+    all-gather's result bit for bit, on three calls in a row (both buffers)
+    and on CUDA-graph replays."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    mp.start_processes(_peer_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    assert os.path.exists(os.path.join(tmp_path, "peer_ref.pt"))

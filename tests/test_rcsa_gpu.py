@@ -461,8 +461,9 @@ def test_host_plan_matches_device_plan(cuda):
 
 def test_host_plan_copies_exactly_the_selected_values(cuda):
     """The value blocks a selected-values call copies are the union of its
-    heads' selections: poisoning every other block of the host values with
-    NaN leaves the output finite and unchanged."""
+    heads' selections (with the default gap merging, plus short gaps between
+    them): poisoning every other block of the host values with NaN leaves the
+    output finite and unchanged."""
     w = workloads.config2(heads=2)
     hq, hk, hv = (t.pin_memory() for t in (w.q, w.k, w.v))
     hp = rcsa.RCSAHostPlan(1, 2, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8,
@@ -486,9 +487,12 @@ def test_host_plan_copies_exactly_the_selected_values(cuda):
     hp2(hq, hk, poisoned, hout)
     assert torch.equal(hout, first)
     assert hp2.last_h2d_bytes == hp.last_h2d_bytes
-    rows = int(used.sum()) * 880 - sum(880 - (w.k.shape[2] - 880 * (used.shape[1] - 1))
-                                        for h in range(2) if used[h, -1])
-    assert hp.last_h2d_bytes == sum(t.numel() * 2 for t in (hq, hk)) + rows * 128 * 2
+    # with no gap merging, exactly the selected blocks' rows cross
+    hp0 = rcsa.RCSAHostPlan(1, 2, w.q.shape[2], w.k.shape[2], 128, block_size=880, budget=8,
+                            groups=2, device="cuda", value_gap=0)
+    hp0(hq, hk, poisoned, hout)
+    assert torch.equal(hout, first)
+    assert hp0.last_h2d_bytes == sum(t.numel() * 2 for t in (hq, hk)) + int(used.sum()) * 880 * 128 * 2
 
 
 ROW_SAMPLE = np.array([0, 1, 2, 63, 64, 127, 128, 255, 256, 383, 384, 511, 512, 639, 640, 767, 768, 800,
