@@ -86,7 +86,7 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int,
          c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_float,
-         c_void_p, c_void_p],
+         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     ),
     "cast_swap_route": (
         c_int,

@@ -117,9 +117,11 @@ def lift_targets(anchor_values: list[int], total_temporal: int, memory_temporal:
 
 def lift_weights(targets, full_plucker, mouse_cond, keyboard_cond, mouse_cond_memory,
                  keyboard_cond_memory, *, total_temporal: int, memory_temporal: int, spatial: int,
-                 lambdas):
+                 lambdas, writer_inputs=None):
     """``cast_barycentric_weights``: the weights ``[B, N, 2]`` of the targets
-    from the camera and action state, on the plucker tensor's device."""
+    from the camera and action state, on the plucker tensor's device.  With
+    ``writer_inputs`` (int32 device tensors ``(pairs [N,2], frames [N])``) the
+    launch also fills the pair writer's anchor slots and target frames."""
     dev = full_plucker.device
     b = full_plucker.shape[0]
     n = len(targets)
@@ -151,6 +153,11 @@ def lift_weights(targets, full_plucker, mouse_cond, keyboard_cond, mouse_cond_me
     tgt = (ctypes.c_int32 * (3 * n))(*[v for t in targets for v in t[:3]])
     prior = (ctypes.c_float * (2 * n))(*[v for t in targets
                                          for v in (math.log1p(-t[5]), math.log(t[5]))])
+    slots = pairs_dev = frames_dev = None
+    if writer_inputs is not None:
+        slots = ctypes.cast((ctypes.c_int32 * (2 * n))(*[v for t in targets for v in t[3:5]]),
+                            ctypes.c_void_p)
+        pairs_dev, frames_dev = (_lib.ptr(x) for x in writer_inputs)
     P = _lib.ptr
     ln = lambda x: 0 if x is None else int(x.shape[1])  # noqa: E731
     ch = lambda x: 0 if x is None else int(x.shape[2])  # noqa: E731
@@ -160,7 +167,7 @@ def lift_weights(targets, full_plucker, mouse_cond, keyboard_cond, mouse_cond_me
               ch(keyboard), P(mouse_m), ln(mouse_m), ch(mouse_m), P(keyboard_m), ln(keyboard_m),
               ch(keyboard_m), n,
               ctypes.cast(tgt, ctypes.c_void_p), ctypes.cast(prior, ctypes.c_void_p),
-              float(lambdas[1]), float(lambdas[2]), P(out), _stream(dev))
+              float(lambdas[1]), float(lambdas[2]), P(out), slots, pairs_dev, frames_dev, _stream(dev))
     return out, bool(current)
 
 
@@ -176,8 +183,9 @@ def control_barycentric_residual_lift(active_residual, active_frames, total_temp
     """``MatrixCurvaturePhaseFrameWeave._control_barycentric_residual_lift``
     (``proposed/matrix_curvature_phase_frame_weave.py:3810-4374``) on the
     B200: the reference's checks and targets, every target's weights in one
-    launch (``cast_barycentric_weights``), every target row in one launch of
-    the pair writer (``left_then_right_fma`` rounding), the anchors copied in.
+    launch (``cast_barycentric_weights``, which also writes the writer's
+    anchor slots and target frames), every target row in one launch of the
+    pair writer (``left_then_right_fma`` rounding), the anchors copied in.
     The reference's control-state and weight caches are not kept: the
     weights are recomputed on the device every call.  Batch 1, fp32 residuals
     (the production Matrix path)."""
@@ -208,17 +216,18 @@ def control_barycentric_residual_lift(active_residual, active_frames, total_temp
     full = active_residual.new_empty(batch, total_temporal, spatial, channels)
     action_available = any(isinstance(x, torch.Tensor) for x in (mouse_cond, keyboard_cond))
     if targets:
+        dev = active_residual.device
+        # the weights launch also writes the writer's slots and frames: no copy
+        index = torch.empty(3 * len(targets), dtype=torch.int32, device=dev)
+        pairs, frames = index[:2 * len(targets)], index[2 * len(targets):]
         weights, action_available = lift_weights(
             targets, full_plucker, mouse_cond, keyboard_cond, mouse_cond_memory, keyboard_cond_memory,
             total_temporal=total_temporal, memory_temporal=memory_temporal, spatial=spatial,
-            lambdas=lambdas)
-        dev = active_residual.device
-        pairs = torch.tensor([[t[3], t[4]] for t in targets], dtype=torch.int32).to(dev)
-        frames = torch.tensor([t[0] for t in targets], dtype=torch.int32).to(dev)
+            lambdas=lambdas, writer_inputs=(pairs, frames))
         _lib.call("cast_barycentric_pair_write", _lib.ptr(active_residual.contiguous()), _lib.ptr(weights),
                   _lib.ptr(pairs), _lib.ptr(frames), _lib.ptr(full), active_count, total_temporal,
                   len(targets), spatial * channels, _MODES["left_then_right_fma"], _stream(dev))
-    full[:, active_frames] = active_residual
+    full.index_copy_(1, active_frames.to(device=full.device, dtype=torch.long), active_residual)
     return full, {
         "mode": "control_conditioned_local_two_anchor_residual",
         "control_lambdas": [lambdas[1], lambdas[2]],

@@ -115,6 +115,9 @@ struct LiftParams {
   float *weights;               // [B, N, 2]
   int N;
   int targets[kLiftMaxTargets][3];  // target, left, right frames
+  int slots[kLiftMaxTargets][2];    // left, right anchor slots (rows of the active residual)
+  int32_t *pairs_out;               // [N][2] slots for the pair writer, or null
+  int32_t *frames_out;              // [N] target frames for the pair writer, or null
   float prior[kLiftMaxTargets][2];  // log1p(-alpha), log(alpha)
 };
 
@@ -213,6 +216,11 @@ __global__ void __launch_bounds__(kLiftThreads) barycentric_weights_kernel(const
     const float sum = e0 + e1;
     p.weights[((size_t)b * p.N + n) * 2] = e0 / sum;
     p.weights[((size_t)b * p.N + n) * 2 + 1] = e1 / sum;
+    if (b == 0 && p.pairs_out) {
+      p.pairs_out[2 * n] = p.slots[n][0];
+      p.pairs_out[2 * n + 1] = p.slots[n][1];
+      p.frames_out[n] = p.targets[n][0];
+    }
   }
 }
 

@@ -1034,7 +1034,9 @@ extern "C" int cast_barycentric_weights(const void *plucker, int plucker_bf16, i
                                         const float *keyboard_memory, int keyboard_memory_len,
                                         int keyboard_memory_ch, int n_targets,
                                         const int32_t *targets, const float *prior, float lambda_p,
-                                        float lambda_a, float *weights, cast_stream_t stream) {
+                                        float lambda_a, float *weights, const int32_t *slots,
+                                        int32_t *source_pairs, int32_t *target_frames,
+                                        cast_stream_t stream) {
   using castk::kLiftMaxAct;
   using castk::kLiftMaxFeat;
   using castk::kLiftMaxTargets;
@@ -1066,7 +1068,15 @@ extern "C" int cast_barycentric_weights(const void *plucker, int plucker_bf16, i
     }
     p.prior[n][0] = prior[2 * n];
     p.prior[n][1] = prior[2 * n + 1];
+    if (slots) {
+      p.slots[n][0] = slots[2 * n];
+      p.slots[n][1] = slots[2 * n + 1];
+    }
   }
+  if ((slots != nullptr) != (source_pairs != nullptr) || (source_pairs != nullptr) != (target_frames != nullptr))
+    return fail(CAST_ERR_INVALID_ARGUMENT, "slots, source_pairs and target_frames go together");
+  p.pairs_out = source_pairs;
+  p.frames_out = target_frames;
   int st = current_device_sm100(nullptr);
   if (st) return st;
   p.plucker = plucker, p.plucker_bf16 = plucker_bf16 ? 1 : 0, p.P = P, p.S = S, p.T = T, p.M = M;

@@ -377,7 +377,11 @@ CAST_API int cast_barycentric_pair_write(const float *active_residual, const flo
  * count as zeros; no controls at all: equal action distances, which cancel).  A slot may be null; the host fills the
  * slots in the reference's order of the given sequences.  Cosines are
  * clamped to [-1, 1].  weights fp32 [B, n_targets, 2].  n_targets <= 64,
- * P <= 16, channels of the two slots <= 64.
+ * P <= 16, channels of the two slots <= 64.  With `slots` (HOST int32
+ * [n_targets][2]: the rows of the active residual holding each target's left
+ * and right anchor) the same launch also writes the pair writer's device
+ * inputs: source_pairs int32 [n_targets][2] and target_frames int32
+ * [n_targets] (all three given, or none), so a whole lift needs no copy.
  */
 CAST_API int cast_barycentric_weights(const void *plucker, int plucker_bf16, int B, int rows, int P,
                              int S, int T, int M, const float *mouse, int mouse_len, int mouse_ch,
@@ -386,7 +390,8 @@ CAST_API int cast_barycentric_weights(const void *plucker, int plucker_bf16, int
                              const float *keyboard_memory, int keyboard_memory_len,
                              int keyboard_memory_ch, int n_targets,
                              const int32_t *targets, const float *prior, float lambda_p,
-                             float lambda_a, float *weights, cast_stream_t stream);
+                             float lambda_a, float *weights, const int32_t *slots,
+                             int32_t *source_pairs, int32_t *target_frames, cast_stream_t stream);
 
 /*
  * The swap router's objective and transport gates on the device: the
