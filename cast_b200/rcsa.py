@@ -465,7 +465,7 @@ class RCSAHostPlan:
     def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int,
                  budget: int, policy: str = "auto", groups: int = 4,
                  int8_tolerance: float = DEFAULT_INT8_TOLERANCE, device=None,
-                 v_selected: bool = True, value_gap: int = 2):
+                 v_selected: bool = True, value_gap: int = 2, copy_streams: int = 1):
         if B != 1:
             raise ValueError("RCSAHostPlan takes batch size 1 (contiguous head slices)")
         dev = torch.device(device if device is not None else "cuda")
@@ -479,7 +479,10 @@ class RCSAHostPlan:
         self.k = torch.empty(B, H, Lk, D, dtype=torch.bfloat16, device=dev)
         self.v = torch.zeros(B, H, Lk, D, dtype=torch.bfloat16, device=dev)
         self.out = torch.empty(B, H, Lq, D, dtype=torch.bfloat16, device=dev)
-        self.h2d = torch.cuda.Stream(dev)
+        # host-to-device copy streams (more than one spreads the copies over
+        # the device's copy engines)
+        self.h2d_streams = [torch.cuda.Stream(dev) for _ in range(max(1, int(copy_streams)))]
+        self.h2d = self.h2d_streams[0]
         self.d2h = torch.cuda.Stream(dev)
         self.shape = (B, H, Lq, Lk, D)
         self.block_size = block_size
@@ -533,24 +536,30 @@ class RCSAHostPlan:
                 raise ValueError(f"{name} must be in pinned host memory")
         cur = torch.cuda.current_stream(self.device)
         # the previous call's compute and copies are done with the buffers
-        self.h2d.wait_stream(cur)
+        for st in self.h2d_streams:
+            st.wait_stream(cur)
         self.d2h.wait_stream(cur)
         row_bytes = D * 2
         h2d = 0
+        n_cs = len(self.h2d_streams)
         ready = []
-        with torch.cuda.stream(self.h2d):
-            for h0, h1 in self.heads:
-                pairs = ((self.q, hq), (self.k, hk)) + (() if self.v_selected else ((self.v, hv),))
-                for dst, src in pairs:
+        for g, (h0, h1) in enumerate(self.heads):
+            pairs = ((self.q, hq), (self.k, hk)) + (() if self.v_selected else ((self.v, hv),))
+            evs = []
+            for i, (dst, src) in enumerate(pairs):
+                st = self.h2d_streams[(g + i) % n_cs]
+                with torch.cuda.stream(st):
                     dst[:, h0:h1].copy_(src[:, h0:h1], non_blocking=True)
-                    h2d += dst[:, h0:h1].numel() * 2
-                ev = torch.cuda.Event()
-                ev.record(self.h2d)
-                ready.append(ev)
+                    ev = torch.cuda.Event()
+                    ev.record(st)
+                evs.append(ev)
+                h2d += dst[:, h0:h1].numel() * 2
+            ready.append(evs)
         picked = []
-        for g, (plan, ev) in enumerate(zip(self.plans, ready)):
+        for g, (plan, evs) in enumerate(zip(self.plans, ready)):
             h0, h1 = self.heads[g]
-            cur.wait_event(ev)
+            for ev in evs:
+                cur.wait_event(ev)
             plan.select(self.q[:, h0:h1], self.k[:, h0:h1])
             if self.v_selected:
                 idx, cnt = self._sel_host[g]
@@ -563,13 +572,14 @@ class RCSAHostPlan:
             h0, h1 = self.heads[g]
             if self.v_selected:
                 picked[g].synchronize()
-                with torch.cuda.stream(self.h2d):
-                    for h, r0, r1 in self._value_runs(g):
+                for i, (h, r0, r1) in enumerate(self._value_runs(g)):
+                    with torch.cuda.stream(self.h2d_streams[i % n_cs]):
                         self.v[0, h, r0:r1].copy_(hv[0, h, r0:r1], non_blocking=True)
-                        h2d += (r1 - r0) * row_bytes
+                    h2d += (r1 - r0) * row_bytes
+                for st in self.h2d_streams:
                     vin = torch.cuda.Event()
-                    vin.record(self.h2d)
-                cur.wait_event(vin)
+                    vin.record(st)
+                    cur.wait_event(vin)
             plan.attend(self.q[:, h0:h1], self.k[:, h0:h1], self.v[:, h0:h1], out=self.out[:, h0:h1])
             done = torch.cuda.Event()
             done.record(cur)

@@ -132,3 +132,32 @@ def test_compact_wrapper_refuses_cpu_tensors():
     x = torch.zeros(1, 8, 2, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         compact.pack(x, x, x, torch.zeros(8, dtype=torch.int32))
+
+
+def test_host_plan_value_runs():
+    """The selected-values copy plan: per head, the union of the selected
+    blocks (entries past a row's count and outside [0, nkb) ignored), runs
+    of consecutive blocks merged, and runs at most ``value_gap`` blocks apart
+    merged across the gap; the ragged last block ends at Lk."""
+    import torch
+
+    from cast_b200 import rcsa
+
+    hp = object.__new__(rcsa.RCSAHostPlan)
+    hp.shape = (1, 2, 1760, 10 * 100 - 40, 128)  # Lk = 960: 10 blocks of 100, the last ragged
+    hp.block_size = 100
+    hp.heads = [(4, 6)]
+    idx = torch.full((1, 2, 2, 6), -1, dtype=torch.int32)
+    idx[0, 0, 0, :4] = torch.tensor([3, 4, 7, 9])
+    idx[0, 0, 1, :5] = torch.tensor([0, 4, 12, -1, 9])  # 12 is out of range, -1 skipped
+    idx[0, 1, 0, :2] = torch.tensor([5, 2])
+    idx[0, 1, 1, :6] = torch.tensor([6, 6, 1, 8, 8, 8])  # only the first 3 counted
+    cnt = torch.tensor([[[4, 5], [2, 3]]], dtype=torch.int32)
+    hp._sel_host = [(idx, cnt)]
+    hp.value_gap = 0
+    assert hp._value_runs(0) == [(4, 0, 100), (4, 300, 500), (4, 700, 800), (4, 900, 960),
+                                 (5, 100, 300), (5, 500, 700)]
+    hp.value_gap = 1
+    assert hp._value_runs(0) == [(4, 0, 100), (4, 300, 500), (4, 700, 960), (5, 100, 300), (5, 500, 700)]
+    hp.value_gap = 2
+    assert hp._value_runs(0) == [(4, 0, 960), (5, 100, 700)]
