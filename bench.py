@@ -475,8 +475,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--policy", default="auto", choices=["auto", "int8", "bf16"])
     ap.add_argument("--shard", default="head", choices=["head", "rollout"])
-    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
-                    help="head sharding: the all-gather fused into the attention (peer) or NCCL after it")
+    ap.add_argument("--gather", default="nccl", choices=["peer", "nccl"],
+                    help="head sharding: NCCL's all-gather after the attention (nccl) or the gather fused "
+                         "into the attention (peer)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
