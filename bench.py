@@ -675,6 +675,26 @@ def main():
     par_line = par_measure(dev, peaks, peak_src, args.steps) if extras else None
     compact_line = compact_measure(dev, peaks, args.steps) if extras else None
     swap_line = swap_measure(dev, args.steps, not args.no_cpu_baseline) if extras else None
+    # the same layer call under the other QK^T precision policies (same inputs)
+    policy_line = None
+    if extras and args.config == 2:
+        policy_line = {}
+        for pol in ("int8", "bf16"):
+            if pol == args.policy:
+                continue
+            pplan = rcsa.RCSAPlan(q.shape[0], q.shape[1], q.shape[2], k.shape[2], q.shape[3], block_size=BLOCK,
+                                  budget=budget, policy=pol, device=dev)
+            for _ in range(args.warmup):
+                pplan(q, k, v)
+            graphs = {part: pplan.capture(q, k, v, part) for part in ("all", "attend", "select")}
+            for _ in range(3):
+                graphs["all"].replay()
+            policy_line[pol] = {part: timed(g.replay, args.steps) / args.steps * 1000.0
+                                for part, g in graphs.items()}
+            del graphs, pplan
+        policy_line["unit"] = "us/call"
+        policy_line["note"] = ("device time of the same layer call (all), its attention and its selection "
+                               "under the other QK^T precision policies, CUDA graph replay")
 
     # ---- max over ranks
     vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms, gather_ms,
@@ -761,6 +781,7 @@ def main():
         "par": par_line,
         "compact_and_lift": compact_line,
         "swap_router": swap_line,
+        "other_policies": policy_line,
         "gpu_launches": (KERNELS_PER_CALL[args.policy] + (1 if peer is not None else 0)) * args.steps,
         "clocks": clocks,
     }
