@@ -255,12 +255,35 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   const __nv_bfloat16 *vb = static_cast<const __nv_bfloat16 *>(v);
   // the masked variant only when a validity mask is given
   const bool masked = q_valid || k_valid;
-  // Auto policy: codes only for the blocks the int8 query blocks read,
-  // written after the selection (kernel 3); V codes keep the fused pass.
-  const bool lazy = policy == CAST_POLICY_AUTO && qk_mode && !v_codes;
+  // Blocks that fit in shared memory (unmasked, codes wanted, no V codes):
+  // kernel 1s stages each block and writes every block's codes from there,
+  // one read of Q and K in all.  Otherwise, under the auto policy, codes only
+  // for the blocks the int8 query blocks read, written after the selection
+  // (kernel 3); V codes keep the fused pass.
+  const size_t staged_bytes = castk::staged_block_bytes(block_size, D);
+  const bool staged = staged_bytes > 0 && !masked && !v_codes && q_codes && k_codes;
+  const bool lazy = !staged && policy == CAST_POLICY_AUTO && qk_mode && !v_codes;
   int8_t *qc1 = lazy ? nullptr : q_codes, *kc1 = lazy ? nullptr : k_codes;
   uint8_t *nf = lazy ? need_flags : nullptr;
-  if (D == 128 && !masked)
+  if (staged) {
+    static std::once_flag staged_once;
+    static cudaError_t staged_err = cudaSuccess;
+    std::call_once(staged_once, [] {
+      staged_err = cudaFuncSetAttribute(castk::pool_quant_staged_kernel<128>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      if (staged_err == cudaSuccess)
+        staged_err = cudaFuncSetAttribute(castk::pool_quant_staged_kernel<64>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    });
+    CAST_CUDA_TRY(staged_err);
+    dim3 gs(nqb + nkb, B * H);
+    if (D == 128)
+      castk::pool_quant_staged_kernel<128><<<gs, 256, staged_bytes, s>>>(qb, kb, Lq, Lk, block_size, nqb, nkb,
+                                                                        q_codes, qs, k_codes, ks, pooled_out, rms);
+    else
+      castk::pool_quant_staged_kernel<64><<<gs, 128, staged_bytes, s>>>(qb, kb, Lq, Lk, block_size, nqb, nkb,
+                                                                       q_codes, qs, k_codes, ks, pooled_out, rms);
+  } else if (D == 128 && !masked)
     castk::pool_quant_kernel<128, false><<<grid, 256, 0, s>>>(qb, kb, vb, q_valid, k_valid, Lq, Lk, block_size,
                                                               nqb, nkb, qc1, qs, kc1, ks, v_codes,
                                                               v_scales, pooled_out, rms, nf);

@@ -364,6 +364,164 @@ __global__ void __launch_bounds__(kSumLanes *(D / 8), 4)
                                   s_scale, s_amax >= 0x1p-90f, drop_pol);
 }
 
+// Kernel 1s: kernel 1 for unmasked Q/K blocks that fit in shared memory,
+// with the block staged there by bulk copies so the codes come from shared
+// memory instead of a second read of the block: HBM sees the block once and
+// the codes once.  The same threads take the same rows in the same order as
+// kernel 1, so the sums, amax, RMS, pooled vectors and codes are bit-identical
+// to it.  Dynamic shared memory: the block (rows x D bf16), reused for the
+// row-slot partial sums after the codes are written.  One CTA per SM.
+constexpr int kStageChunk = 32768;  // bytes per bulk copy
+
+template <int D>
+__global__ void __launch_bounds__(kSumLanes *(D / 8), 1)
+    pool_quant_staged_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
+                             int Lq, int Lk, int block, int nqb, int nkb, int8_t *q_codes,
+                             float *q_scales, int8_t *k_codes, float *k_scales, double *pooled,
+                             float *block_rms) {
+  constexpr int kGroups = D / 8;
+  constexpr int kThreads = kSumLanes * kGroups;
+  extern __shared__ __align__(128) unsigned char stage_raw[];
+  __shared__ __align__(8) uint64_t full_bar;
+  __shared__ int cta_abort;
+  __shared__ double mean_s[D];
+  __shared__ float wmax[kThreads / 32];
+  __shared__ float wsq[kThreads / 32];
+  __shared__ float s_scale;
+  __shared__ float s_amax;
+  __shared__ double s_denom;
+
+  const int tid = threadIdx.x;
+  const int grp = tid % kGroups;
+  const int slot = tid / kGroups;
+  const int bh = blockIdx.y;
+  int blk = blockIdx.x;
+  const bool is_q = blk < nqb;
+  if (!is_q) blk -= nqb;
+  const __nv_bfloat16 *X = is_q ? q : k;
+  const int L = is_q ? Lq : Lk;
+  int8_t *codes = is_q ? q_codes : k_codes;
+  float *scales = is_q ? q_scales : k_scales;
+  const int nb = is_q ? nqb : nkb;
+  const int b0 = blk * block;
+  const int rows = min(block, L - b0);
+  const unsigned char *src = reinterpret_cast<const unsigned char *>(X + ((size_t)bh * L + b0) * D);
+  const uint32_t bytes = (uint32_t)rows * D * 2;
+  __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(stage_raw);
+
+  if (tid == 0) {
+    cta_abort = 0;
+    castdev::mbar_init(&full_bar, 1);
+    castdev::fence_barrier_init();
+    castdev::mbar_arrive_expect_tx(&full_bar, bytes);
+    for (uint32_t off = 0; off < bytes; off += kStageChunk)
+      castdev::bulk_load(stage_raw + off, src + off, min((uint32_t)kStageChunk, bytes - off), &full_bar);
+  }
+  __syncthreads();
+  // the copies always complete; a wait that gives up leaves the statistics
+  // and codes of this block unwritten and sets the device error word
+  const bool ok = castdev::mbar_wait_drain(&full_bar, 0, &cta_abort);
+
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  float amax = 0.0f, sq = 0.0f;
+  const __nv_bfloat16 *base = st + grp * 8;
+  if (ok) {
+    for (int r = slot; r < rows; r += kSumLanes) {
+      float f[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4 *>(base + (size_t)r * D), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[i] = __fadd_rn(acc[i], f[i]);
+        amax = fmaxf(amax, fabsf(f[i]));
+        sq = fmaf(f[i], f[i], sq);
+      }
+    }
+  }
+#pragma unroll
+  for (int s2 = 16; s2 >= 1; s2 >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s2));
+    sq += __shfl_xor_sync(0xffffffffu, sq, s2);
+  }
+  if ((tid & 31) == 0) {
+    wmax[tid >> 5] = amax;
+    wsq[tid >> 5] = sq;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float m = 0.0f, s2 = 0.0f;
+    for (int w = 0; w < kThreads / 32; ++w) {
+      m = fmaxf(m, wmax[w]);
+      s2 += wsq[w];
+    }
+    const float sc = quant_scale_of(m);
+    s_scale = sc;
+    s_amax = m;
+    if (ok) {
+      scales[(size_t)bh * nb + blk] = sc;
+      block_rms[(size_t)bh * (nqb + nkb) + (is_q ? 0 : nqb) + blk] = sqrtf(s2 / (float)max(1, rows * D));
+    }
+  }
+  __syncthreads();
+  // codes from the staged block
+  if (ok && codes) {
+    const float sc = s_scale;
+    const bool fast = s_amax >= 0x1p-90f;
+    const float inv = __frcp_rn(sc);
+    const uint64_t invx2 = q2_pack(inv, inv), negsx2 = q2_pack(-sc, -sc);
+    const uint64_t drop_pol = l2_evict_first();
+    int8_t *cbase = codes + ((size_t)bh * L + b0) * D + grp * 8;
+    for (int r = slot; r < rows; r += kSumLanes) {
+      float f[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4 *>(base + (size_t)r * D), f);
+      uint2 c;
+      if (fast) {
+        c = quant8_fast(f, invx2, negsx2);
+      } else {
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) lo |= (uint32_t)(quant_code(f[i], sc, inv) & 0xFF) << (8 * i);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hi |= (uint32_t)(quant_code(f[4 + i], sc, inv) & 0xFF) << (8 * i);
+        c = make_uint2(lo, hi);
+      }
+      stg_v2_hint(cbase + (size_t)r * D, c, drop_pol);
+    }
+  }
+  __syncthreads();  // the staged block is no longer read: its first bytes hold the partial sums
+  float (*red)[D] = reinterpret_cast<float (*)[D]>(stage_raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[slot][grp * 8 + i] = acc[i];
+  __syncthreads();
+  if (tid < D) {
+    double t = (double)red[0][tid];
+#pragma unroll
+    for (int p = 1; p < kSumLanes; ++p) t = __dadd_rn(t, (double)red[p][tid]);
+    mean_s[tid] = __ddiv_rn(t, (double)max(rows, 1));
+  }
+  __syncthreads();
+  if (tid < 32) {
+    double part = __dmul_rn(mean_s[tid], mean_s[tid]);
+#pragma unroll
+    for (int d = tid + 32; d < D; d += 32) part = __dadd_rn(part, __dmul_rn(mean_s[d], mean_s[d]));
+#pragma unroll
+    for (int s2 = 16; s2 >= 1; s2 >>= 1) part = __dadd_rn(part, __shfl_xor_sync(0xffffffffu, part, s2));
+    if (tid == 0) s_denom = fmax(__dsqrt_rn(part), kNormEps);
+  }
+  __syncthreads();
+  if (ok && tid < D)
+    pooled[((size_t)bh * (nqb + nkb) + (is_q ? 0 : nqb) + blk) * D + tid] = __ddiv_rn(mean_s[tid], s_denom);
+}
+
+// Bytes of shared memory kernel 1s needs for a block (0: it does not fit).
+constexpr size_t kStagedStaticBytes = 4096;  // mean_s, the reductions, the barrier
+__host__ __device__ inline size_t staged_block_bytes(int block, int D) {
+  const size_t b = (size_t)block * D * 2;
+  if (block < 2 * kSumLanes) return 0;  // the partial sums reuse the buffer
+  return b + kStagedStaticBytes <= 227 * 1024 ? b : 0;
+}
+
 // Kernel 3 (auto policy): int8 codes only for the blocks an int8 query block
 // reads -- its own Q block and every K block it selected, which the
 // selection kernel marked in need_flags ([B*H][nQb + nKb], cleared by kernel
