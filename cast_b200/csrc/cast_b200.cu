@@ -269,11 +269,13 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
     static std::once_flag staged_once;
     static cudaError_t staged_err = cudaSuccess;
     std::call_once(staged_once, [] {
+      // the opt-in limit covers static and dynamic shared memory together
+      constexpr int kDyn = 227 * 1024 - (int)castk::kStagedStaticBytes;
       staged_err = cudaFuncSetAttribute(castk::pool_quant_staged_kernel<128>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kDyn);
       if (staged_err == cudaSuccess)
         staged_err = cudaFuncSetAttribute(castk::pool_quant_staged_kernel<64>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kDyn);
     });
     CAST_CUDA_TRY(staged_err);
     dim3 gs(nqb + nkb, B * H);
