@@ -255,13 +255,17 @@ extern "C" int cast_rcsa_select_quant(const void *q, const void *k, const void *
   const __nv_bfloat16 *vb = static_cast<const __nv_bfloat16 *>(v);
   // the masked variant only when a validity mask is given
   const bool masked = q_valid || k_valid;
-  // Blocks that fit in shared memory (unmasked, codes wanted, no V codes):
+  // Few blocks (one CTA per SM covers them all: a head-sharded call on many
+  // GPUs) that fit in shared memory (unmasked, codes wanted, no V codes):
   // kernel 1s stages each block and writes every block's codes from there,
-  // one read of Q and K in all.  Otherwise, under the auto policy, codes only
-  // for the blocks the int8 query blocks read, written after the selection
-  // (kernel 3); V codes keep the fused pass.
+  // one read of Q and K in all.  With more blocks than SMs its one CTA per
+  // SM keeps too few reads in flight (config 2, 24 heads: 92 against 87 us
+  // int8), so the two-pass kernel runs.  Otherwise, under the auto policy,
+  // codes only for the blocks the int8 query blocks read, written after the
+  // selection (kernel 3); V codes keep the fused pass.
   const size_t staged_bytes = castk::staged_block_bytes(block_size, D);
-  const bool staged = staged_bytes > 0 && !masked && !v_codes && q_codes && k_codes;
+  const bool staged = staged_bytes > 0 && !masked && !v_codes && q_codes && k_codes &&
+                      (long long)B * H * (nqb + nkb) <= n_sms;
   const bool lazy = !staged && policy == CAST_POLICY_AUTO && qk_mode && !v_codes;
   int8_t *qc1 = lazy ? nullptr : q_codes, *kc1 = lazy ? nullptr : k_codes;
   uint8_t *nf = lazy ? need_flags : nullptr;
