@@ -75,13 +75,14 @@ def test_head_sharded_equals_single_gpu(tmp_path):
         assert torch.equal(sel, plan.indices.cpu()[:, r * half:(r + 1) * half])
     # Both outputs are bf16 roundings of fp32 results that differ only in the
     # order of the partial merges (the fp32 rounding of sums over a row's
-    # keys): they agree to one bf16 unit in the last place of the row's
-    # largest output.
+    # keys): each is within half a bf16 unit in the last place (of the row's
+    # largest output) of its fp32 value, and the fp32 values differ by
+    # rounding noise, so the two agree to two such units.
     g, s = gathered.float(), single.float()
     d = (g - s).abs()
     row_max = torch.maximum(g.abs(), s.abs()).amax(dim=-1, keepdim=True).clamp_min(2.0 ** -126)
     ulp = torch.exp2(torch.floor(torch.log2(row_max)) - 7)
-    assert bool((d <= ulp).all()), float((d / ulp).max())
+    assert bool((d <= 2 * ulp).all()), float((d / ulp).max())
     assert float(d.mean()) < 2e-3
 
 
