@@ -475,9 +475,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--policy", default="auto", choices=["auto", "int8", "bf16"])
     ap.add_argument("--shard", default="head", choices=["head", "rollout"])
-    ap.add_argument("--gather", default="nccl", choices=["peer", "nccl"],
-                    help="head sharding: NCCL's all-gather after the attention (nccl) or the gather fused "
-                         "into the attention (peer)")
+    ap.add_argument("--gather", default="nccl", choices=["peer", "fused", "nccl"],
+                    help="head sharding: NCCL's all-gather after the attention (nccl), one streaming launch "
+                         "of peer stores after it (peer) or peer stores in the attention's epilogue (fused)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
@@ -576,7 +576,7 @@ def main():
     # NVLink, then waits for the peers' rows; one CUDA graph per gathered
     # buffer, alternating.
     peer = None
-    if gathered is not None and args.gather == "peer":
+    if gathered is not None and args.gather in ("peer", "fused"):
         peer = cdist.PeerGather(q.shape[0], q.shape[1], q.shape[2], q.shape[3], device=dev)
         peer_graphs, fused_graphs = [], []
         for par in (0, 1):
@@ -587,7 +587,11 @@ def main():
                 with torch.cuda.stream(side), torch.cuda.graph(gph, stream=side):
                     if with_select:
                         plan.select(q, k)
-                    plan.attend(q, k, v, out=peer.slot(par), peers=peer.peers(par))
+                    if args.gather == "fused":
+                        plan.attend(q, k, v, out=peer.slot(par), peers=peer.peers(par))
+                    else:
+                        plan.attend(q, k, v, out=peer.slot(par))
+                        peer.push(par)
                     peer.wait()
                 stream.wait_stream(side)
                 graphs.append(gph)
@@ -763,7 +767,9 @@ def main():
         "timing": (f"CUDA graph replay of the {KERNELS_PER_CALL[args.policy]}-kernel layer call"
                    + ("" if gathered is None else
                       " with the head outputs' all-gather fused into the attention (peer stores over "
-                      "NVLink) and the wait for the peers' rows" if peer is not None else
+                      "NVLink) and the wait for the peers' rows" if args.gather == "fused" else
+                      " + one launch streaming the head outputs into every peer over NVLink and the "
+                      "wait for the peers' rows" if args.gather == "peer" else
                       " + NCCL all-gather of the head outputs")
                    + "; CUDA events on the launching stream, max over ranks"),
         "roofline": {
@@ -782,7 +788,8 @@ def main():
         "compact_and_lift": compact_line,
         "swap_router": swap_line,
         "other_policies": policy_line,
-        "gpu_launches": (KERNELS_PER_CALL[args.policy] + (1 if peer is not None else 0)) * args.steps,
+        "gpu_launches": (KERNELS_PER_CALL[args.policy]
+                         + (0 if peer is None else 2 if args.gather == "peer" else 1)) * args.steps,
         "clocks": clocks,
     }
     if gathered is not None:
@@ -795,9 +802,10 @@ def main():
                 "kernel_us": fused_ms * 1000.0, "nvlink_bytes_per_gpu": link_bytes,
                 "link_us": t_link * 1e6, "compute_us": t_alg * 1e6,
                 "frac": max(t_alg, t_link) / (fused_ms * 1e-3),
-                "note": ("attention with the fused all-gather and the peers' wait (CUDA graph, max over "
-                         "ranks) against the slower of its tensor-core roofline and its NVLink bytes at "
-                         "the measured 770 GB/s per direction")}
+                "note": ("attention with its gather (fused into the epilogue, or the streaming launch "
+                         "after it) and the peers' wait (CUDA graph, max over ranks) against the slower of "
+                         "its tensor-core roofline and its NVLink bytes at the measured 770 GB/s per "
+                         "direction")}
             line["nccl_gather_value"] = {
                 "value": nccl_ms * 1000.0, "unit": "us/call",
                 "note": "the same call with a separate NCCL all-gather after it, max over ranks"}

@@ -913,6 +913,79 @@ __global__ void peer_wait_kernel(const uint32_t *flags, int n_src, int self_rank
 }
 }  // namespace castk
 
+namespace castk {
+struct PeerPushArgs {
+  int n_peers;
+  uint32_t *done_ticket;
+  const uint32_t *calls;
+  uint4 *dst[kMaxPeers];
+  uint32_t *flag[kMaxPeers];
+};
+
+// The gather as its own launch after the attention: every CTA streams a share
+// of this rank's output slot (16-byte loads, coalesced) into the same offset
+// of every peer's gathered buffer, fences its stores at system scope and takes
+// a ticket; the last CTA raises this rank's flag in every peer to the call's
+// number (*calls + 1) and resets the ticket.
+__global__ void __launch_bounds__(512) peer_push_kernel(const uint4 *__restrict__ src, size_t n16,
+                                                        PeerPushArgs a) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldcs(src + i + u * stride);
+    for (int r = 0; r < a.n_peers; ++r)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a.dst[r][i + u * stride] = v[u];
+  }
+  for (; i < n16; i += stride) {
+    const uint4 v = __ldcs(src + i);
+    for (int r = 0; r < a.n_peers; ++r) a.dst[r][i] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t t = atomicAdd(a.done_ticket, 1u);
+    if (t == gridDim.x - 1) {
+      __threadfence_system();
+      const uint32_t call = *reinterpret_cast<const volatile uint32_t *>(a.calls) + 1u;
+      for (int r = 0; r < a.n_peers; ++r) castdev::st_release_sys(a.flag[r], call);
+      atomicExch(a.done_ticket, 0u);
+    }
+  }
+}
+}  // namespace castk
+
+extern "C" int cast_peer_push(const void *src, size_t bytes, int n_peers, void *const *peer_dst,
+                              uint32_t *const *peer_flag, uint32_t *done_ticket, const uint32_t *calls,
+                              cast_stream_t stream) {
+  if (!src || !bytes || (bytes & 15) || !aligned16(src))
+    return fail(CAST_ERR_ALIGNMENT, "src must be 16-byte aligned, bytes a positive multiple of 16");
+  if (n_peers < 1 || n_peers > castk::kMaxPeers)
+    return fail(CAST_ERR_UNSUPPORTED, "%d peers (1..%d)", n_peers, castk::kMaxPeers);
+  if (!peer_dst || !peer_flag || !done_ticket || !calls)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "peer_dst, peer_flag, done_ticket and calls are required");
+  castk::PeerPushArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n_peers = n_peers;
+  a.done_ticket = done_ticket;
+  a.calls = calls;
+  for (int r = 0; r < n_peers; ++r) {
+    if (!peer_dst[r] || !peer_flag[r] || !aligned16(peer_dst[r]) || (reinterpret_cast<uintptr_t>(peer_flag[r]) & 3))
+      return fail(CAST_ERR_ALIGNMENT, "peer %d: destination must be 16-byte and its flag 4-byte aligned", r);
+    a.dst[r] = static_cast<uint4 *>(peer_dst[r]);
+    a.flag[r] = peer_flag[r];
+  }
+  int n_sms = 0;
+  int st = current_device_sm100(&n_sms);
+  if (st) return st;
+  castk::peer_push_kernel<<<n_sms, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4 *>(src), bytes / 16, a);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
 extern "C" int cast_peer_alloc(size_t bytes, void **ptr, void *ipc_handle) {
   if (!ptr || !ipc_handle || bytes == 0) return fail(CAST_ERR_INVALID_ARGUMENT, "bytes, ptr and handle required");
   int st = current_device_sm100(nullptr);

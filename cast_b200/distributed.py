@@ -137,6 +137,13 @@ class PeerGather:
         return (self.world - 1, ctypes.cast(self._peer_out[parity], ctypes.c_void_p),
                 ctypes.cast(self._peer_flag, ctypes.c_void_p), self.ticket, self.calls)
 
+    def push(self, parity: int) -> None:
+        """This rank's slot of gathered buffer ``parity`` into every peer's
+        buffer (``cast_peer_push``, a launch after the attention)."""
+        n, out, flag, ticket, calls = self.peers(parity)
+        _lib.call("cast_peer_push", self.slot(parity).data_ptr(), self.slot_bytes, n, out, flag, ticket,
+                  calls, torch.cuda.current_stream(self.device).cuda_stream)
+
     def wait(self) -> None:
         """Orders the stream after every peer's rows of this call."""
         _lib.call("cast_peer_wait", self.flags, self.world, self.rank, self.calls,
@@ -171,13 +178,18 @@ class HeadShardedRCSA:
     """One RCSA layer call split by heads over the ranks of a process group.
 
     Each rank holds a preallocated :class:`RCSAPlan` for its head range and a
-    gather buffer, so a call allocates nothing on the device.
+    gather buffer, so a call allocates nothing on the device.  ``gather``:
+    ``"nccl"`` (NCCL's all-gather after the attention), ``"peer"`` (one
+    streaming launch writes this rank's heads into every peer's buffer over
+    NVLink, :meth:`PeerGather.push`) or ``"fused"`` (the attention's epilogue
+    stores every row into the peers' buffers as it is produced).
     """
 
     def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int, budget: int,
                  policy: str = "auto", device: torch.device, group=None, gather: str = "nccl"):
-        if gather not in ("nccl", "peer"):
-            raise ValueError("gather must be 'nccl' or 'peer'")
+        if gather not in ("nccl", "peer", "fused"):
+            raise ValueError("gather must be 'nccl', 'peer' or 'fused'")
+        self.gather = gather
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.group = group
@@ -185,7 +197,7 @@ class HeadShardedRCSA:
         self.plan = RCSAPlan(B, self.hi - self.lo, Lq, Lk, D, block_size=block_size,
                              budget=budget, policy=policy, device=device)
         self.peer = (PeerGather(B, self.hi - self.lo, Lq, D, device=device, group=group)
-                     if gather == "peer" and self.world > 1 else None)
+                     if gather != "nccl" and self.world > 1 else None)
         self.gathered = None if self.peer else torch.empty(
             (self.world * B, self.hi - self.lo, Lq, D), dtype=torch.bfloat16, device=device)
 
@@ -202,7 +214,11 @@ class HeadShardedRCSA:
             return gather_heads(out, self.world, self.group, self.gathered)
         par = self.peer.calls_made & 1
         self.plan.select(q_local, k_local)
-        self.plan.attend(q_local, k_local, v_local, out=self.peer.slot(par), peers=self.peer.peers(par))
+        if self.gather == "fused":  # the attention's epilogue stores into the peers too
+            self.plan.attend(q_local, k_local, v_local, out=self.peer.slot(par), peers=self.peer.peers(par))
+        else:  # the attention, then one streaming launch into the peers
+            self.plan.attend(q_local, k_local, v_local, out=self.peer.slot(par))
+            self.peer.push(par)
         self.peer.wait()
         self.peer.calls_made += 1
         return self.peer.heads(par)

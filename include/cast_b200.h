@@ -285,6 +285,21 @@ CAST_API int cast_rcsa_attention_peers(
     const uint32_t *calls, cast_stream_t stream);
 
 /*
+ * The head outputs' gather as a launch of its own after the attention: one
+ * CTA per SM streams `bytes` (a multiple of 16) of this rank's output slot
+ * `src` into peer_dst[r] (r < n_peers <= 7; host array of device pointers to
+ * this rank's slot in each peer's gathered buffer, from cast_peer_open) with
+ * coalesced 16-byte peer stores; every CTA fences its stores at system scope
+ * and counts itself in *done_ticket; the last one stores the call's number
+ * (*calls + 1) to every *peer_flag[r] (release, system scope) and resets the
+ * ticket.  Same contracts as cast_rcsa_attention_peers; follow it with
+ * cast_peer_wait.
+ */
+CAST_API int cast_peer_push(const void *src, size_t bytes, int n_peers, void *const *peer_dst,
+                            uint32_t *const *peer_flag, uint32_t *done_ticket, const uint32_t *calls,
+                            cast_stream_t stream);
+
+/*
  * Peer buffers for the fused gather (CUDA IPC, no multicast): cast_peer_alloc
  * makes a zero-filled device buffer of `bytes` on the current device and
  * writes its 64-byte IPC handle to ipc_handle; another process opens it with

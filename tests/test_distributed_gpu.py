@@ -86,7 +86,7 @@ def test_head_sharded_equals_single_gpu(tmp_path):
     assert float(d.mean()) < 2e-3
 
 
-def _peer_worker(rank, world, port, out_dir):
+def _peer_worker(rank, world, port, out_dir, mode="peer"):
     from datetime import timedelta
 
     from cast_b200 import _lib
@@ -104,7 +104,7 @@ def _peer_worker(rank, world, port, out_dir):
         ref_layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, **kw)
         ql, kl, vl = (ref_layer.local_heads(t).to(dev) for t in (q, k, v))
         ref = ref_layer(ql, kl, vl).clone()
-        layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, gather="peer", **kw)
+        layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, gather=mode, **kw)
         outs = [layer(ql, kl, vl).clone() for _ in range(3)]  # both buffers, then the first again
         torch.cuda.synchronize()
         _lib.check_device(torch.cuda.current_stream(dev).cuda_stream, "peer gather")
@@ -117,7 +117,11 @@ def _peer_worker(rank, world, port, out_dir):
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
             layer.plan.select(ql, kl)
-            layer.plan.attend(ql, kl, vl, out=layer.peer.slot(par), peers=layer.peer.peers(par))
+            if mode == "fused":
+                layer.plan.attend(ql, kl, vl, out=layer.peer.slot(par), peers=layer.peer.peers(par))
+            else:
+                layer.plan.attend(ql, kl, vl, out=layer.peer.slot(par))
+                layer.peer.push(par)
             layer.peer.wait()
         layer.peer.gathered[par].zero_()
         dist.barrier()
@@ -135,14 +139,16 @@ def _peer_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_fused_peer_gather_equals_nccl_gather(tmp_path):
-    """The attention storing every output row into the peers' gathered
-    buffers over NVLink (plain peer stores, IPC buffers) gives the NCCL
-    all-gather's result bit for bit, on three calls in a row (both buffers)
-    and on CUDA-graph replays."""
+@pytest.mark.parametrize("mode", ["peer", "fused"])
+def test_peer_gather_equals_nccl_gather(tmp_path, mode):
+    """The head outputs written into the peers' gathered buffers over NVLink
+    (plain peer stores into IPC buffers: a streaming launch after the
+    attention, or the attention's own epilogue) give the NCCL all-gather's
+    result bit for bit, on three calls in a row (both buffers) and on
+    CUDA-graph replays."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
-    mp.start_processes(_peer_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_peer_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world,
+                       join=True, start_method="spawn")
     assert os.path.exists(os.path.join(tmp_path, "peer_ref.pt"))
