@@ -475,7 +475,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--policy", default="auto", choices=["auto", "int8", "bf16"])
     ap.add_argument("--shard", default="head", choices=["head", "rollout"])
-    ap.add_argument("--gather", default="nccl", choices=["peer", "fused", "nccl"],
+    ap.add_argument("--gather", default="peer", choices=["peer", "fused", "nccl"],
                     help="head sharding: NCCL's all-gather after the attention (nccl), one streaming launch "
                          "of peer stores after it (peer) or peer stores in the attention's epilogue (fused)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -186,7 +186,7 @@ class HeadShardedRCSA:
     """
 
     def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int, budget: int,
-                 policy: str = "auto", device: torch.device, group=None, gather: str = "nccl"):
+                 policy: str = "auto", device: torch.device, group=None, gather: str = "peer"):
         if gather not in ("nccl", "peer", "fused"):
             raise ValueError("gather must be 'nccl', 'peer' or 'fused'")
         self.gather = gather

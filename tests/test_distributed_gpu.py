@@ -45,7 +45,7 @@ def _worker(rank, world, port, out_dir):
     try:
         q, k, v = _inputs()
         layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, block_size=880, budget=3,
-                                   policy="auto", device=dev)
+                                   policy="auto", device=dev, gather="nccl")
         out = layer(*(layer.local_heads(t).to(dev) for t in (q, k, v)))
         torch.cuda.synchronize()
         torch.save(layer.plan.indices.cpu(), os.path.join(out_dir, f"sel{rank}.pt"))
@@ -101,7 +101,7 @@ def _peer_worker(rank, world, port, out_dir, mode="peer"):
     try:
         q, k, v = _inputs()
         kw = dict(block_size=880, budget=3, policy="auto", device=dev)
-        ref_layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, **kw)
+        ref_layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, gather="nccl", **kw)
         ql, kl, vl = (ref_layer.local_heads(t).to(dev) for t in (q, k, v))
         ref = ref_layer(ql, kl, vl).clone()
         layer = cd.HeadShardedRCSA(1, q.shape[1], q.shape[2], k.shape[2], 128, gather=mode, **kw)
