@@ -475,7 +475,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--policy", default="auto", choices=["auto", "int8", "bf16"])
     ap.add_argument("--shard", default="head", choices=["head", "rollout"])
-    ap.add_argument("--gather", default="peer", choices=["peer", "fused", "nccl"],
+    ap.add_argument("--gather", default="peer", choices=["peer", "fused", "ce", "nccl"],
                     help="head sharding: NCCL's all-gather after the attention (nccl), one streaming launch "
                          "of peer stores after it (peer) or peer stores in the attention's epilogue (fused)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -576,7 +576,7 @@ def main():
     # NVLink, then waits for the peers' rows; one CUDA graph per gathered
     # buffer, alternating.
     peer = None
-    if gathered is not None and args.gather in ("peer", "fused"):
+    if gathered is not None and args.gather in ("peer", "fused", "ce"):
         peer = cdist.PeerGather(q.shape[0], q.shape[1], q.shape[2], q.shape[3], device=dev)
         peer_graphs, fused_graphs = [], []
         for par in (0, 1):
@@ -589,6 +589,9 @@ def main():
                         plan.select(q, k)
                     if args.gather == "fused":
                         plan.attend(q, k, v, out=peer.slot(par), peers=peer.peers(par))
+                    elif args.gather == "ce":
+                        plan.attend(q, k, v, out=peer.slot(par))
+                        peer.send(par)
                     else:
                         plan.attend(q, k, v, out=peer.slot(par))
                         peer.push(par)
@@ -789,7 +792,8 @@ def main():
         "swap_router": swap_line,
         "other_policies": policy_line,
         "gpu_launches": (KERNELS_PER_CALL[args.policy]
-                         + (0 if peer is None else 2 if args.gather == "peer" else 1)) * args.steps,
+                         + (0 if peer is None else 2 if args.gather == "peer" else
+                            world if args.gather == "ce" else 1)) * args.steps,
         "clocks": clocks,
     }
     if gathered is not None:

@@ -67,6 +67,7 @@ SIGNATURES = {
          c_void_p, c_void_p, c_void_p],
     ),
     "cast_peer_push": (c_int, [c_void_p, c_size_t, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "cast_peer_send": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
     "cast_peer_alloc": (c_int, [c_size_t, c_void_p, c_void_p]),
     "cast_peer_open": (c_int, [c_void_p, c_void_p]),
     "cast_peer_close": (c_int, [c_void_p]),

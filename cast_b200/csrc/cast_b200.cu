@@ -986,6 +986,30 @@ extern "C" int cast_peer_push(const void *src, size_t bytes, int n_peers, void *
   return CAST_OK;
 }
 
+namespace castk {
+// After a copy engine has moved this rank's slot into a peer's buffer (the
+// copy precedes this launch in its stream): one thread raises this rank's
+// flag in that peer to the call's number.
+__global__ void peer_signal_kernel(uint32_t *peer_flag, const uint32_t *calls) {
+  __threadfence_system();
+  castdev::st_release_sys(peer_flag, *reinterpret_cast<const volatile uint32_t *>(calls) + 1u);
+}
+}  // namespace castk
+
+extern "C" int cast_peer_send(void *peer_dst, const void *src, size_t bytes, uint32_t *peer_flag,
+                              const uint32_t *calls, cast_stream_t stream) {
+  if (!peer_dst || !src || !bytes || !peer_flag || !calls)
+    return fail(CAST_ERR_INVALID_ARGUMENT, "peer_dst, src, bytes, peer_flag and calls are required");
+  if (reinterpret_cast<uintptr_t>(peer_flag) & 3) return fail(CAST_ERR_ALIGNMENT, "peer_flag must be 4-byte aligned");
+  int st = current_device_sm100(nullptr);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  CAST_CUDA_TRY(cudaMemcpyAsync(peer_dst, src, bytes, cudaMemcpyDeviceToDevice, s));
+  castk::peer_signal_kernel<<<1, 1, 0, s>>>(peer_flag, calls);
+  CAST_CUDA_TRY(cudaGetLastError());
+  return CAST_OK;
+}
+
 extern "C" int cast_peer_alloc(size_t bytes, void **ptr, void *ipc_handle) {
   if (!ptr || !ipc_handle || bytes == 0) return fail(CAST_ERR_INVALID_ARGUMENT, "bytes, ptr and handle required");
   int st = current_device_sm100(nullptr);

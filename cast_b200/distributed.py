@@ -126,6 +126,8 @@ class PeerGather:
             _DeviceArray(self._own, (2, self.world * B, heads_local, Lq, D), "<i2"),
             device=self.device).view(torch.bfloat16)
         self.calls_made = 0
+        # one copy stream per peer for send() (made here: never during a capture)
+        self._send_streams = [torch.cuda.Stream(self.device) for _ in range(self.world - 1)]
 
     def slot(self, parity: int) -> torch.Tensor:
         """This rank's ``[B, H/world, Lq, D]`` slot of gathered buffer ``parity``."""
@@ -143,6 +145,23 @@ class PeerGather:
         n, out, flag, ticket, calls = self.peers(parity)
         _lib.call("cast_peer_push", self.slot(parity).data_ptr(), self.slot_bytes, n, out, flag, ticket,
                   calls, torch.cuda.current_stream(self.device).cuda_stream)
+
+    def send(self, parity: int) -> None:
+        """This rank's slot of gathered buffer ``parity`` into every peer's
+        buffer on the copy engines (``cast_peer_send``: one copy and its flag
+        per peer, each on its own stream forked from the caller's stream and
+        joined back), leaving the SMs to the caller's kernels."""
+        cur = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(cur)
+        src = self.slot(parity).data_ptr()
+        outs, flags = self._peer_out[parity], self._peer_flag
+        for j, st in enumerate(self._send_streams):
+            st.wait_event(start)
+            _lib.call("cast_peer_send", outs[j], src, self.slot_bytes, flags[j], self.calls, st.cuda_stream)
+            done = torch.cuda.Event()
+            done.record(st)
+            cur.wait_event(done)
 
     def wait(self) -> None:
         """Orders the stream after every peer's rows of this call."""
@@ -182,13 +201,15 @@ class HeadShardedRCSA:
     ``"nccl"`` (NCCL's all-gather after the attention), ``"peer"`` (one
     streaming launch writes this rank's heads into every peer's buffer over
     NVLink, :meth:`PeerGather.push`) or ``"fused"`` (the attention's epilogue
-    stores every row into the peers' buffers as it is produced).
+    stores every row into the peers' buffers as it is produced) or ``"ce"``
+    (the copy engines move this rank's heads into every peer after the
+    attention, :meth:`PeerGather.send`).
     """
 
     def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, *, block_size: int, budget: int,
                  policy: str = "auto", device: torch.device, group=None, gather: str = "peer"):
-        if gather not in ("nccl", "peer", "fused"):
-            raise ValueError("gather must be 'nccl', 'peer' or 'fused'")
+        if gather not in ("nccl", "peer", "fused", "ce"):
+            raise ValueError("gather must be 'nccl', 'peer', 'fused' or 'ce'")
         self.gather = gather
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -216,9 +237,12 @@ class HeadShardedRCSA:
         self.plan.select(q_local, k_local)
         if self.gather == "fused":  # the attention's epilogue stores into the peers too
             self.plan.attend(q_local, k_local, v_local, out=self.peer.slot(par), peers=self.peer.peers(par))
-        else:  # the attention, then one streaming launch into the peers
+        else:  # the attention, then the copy into the peers (SMs or copy engines)
             self.plan.attend(q_local, k_local, v_local, out=self.peer.slot(par))
-            self.peer.push(par)
+            if self.gather == "ce":
+                self.peer.send(par)
+            else:
+                self.peer.push(par)
         self.peer.wait()
         self.peer.calls_made += 1
         return self.peer.heads(par)

@@ -300,6 +300,18 @@ CAST_API int cast_peer_push(const void *src, size_t bytes, int n_peers, void *co
                             cast_stream_t stream);
 
 /*
+ * One peer's share of the gather on a copy engine: on `stream`, one device-
+ * to-device copy of `bytes` from this rank's slot `src` to `peer_dst` (this
+ * rank's slot in the peer's gathered buffer, from cast_peer_open), then one
+ * thread stores the call's number (*calls + 1) to *peer_flag (release,
+ * system scope).  Issue one per peer on separate streams forked from the
+ * caller's stream after the attention, join them back before
+ * cast_peer_wait (which advances *calls).
+ */
+CAST_API int cast_peer_send(void *peer_dst, const void *src, size_t bytes, uint32_t *peer_flag,
+                            const uint32_t *calls, cast_stream_t stream);
+
+/*
  * Peer buffers for the fused gather (CUDA IPC, no multicast): cast_peer_alloc
  * makes a zero-filled device buffer of `bytes` on the current device and
  * writes its 64-byte IPC handle to ipc_handle; another process opens it with

@@ -121,7 +121,7 @@ def _peer_worker(rank, world, port, out_dir, mode="peer"):
                 layer.plan.attend(ql, kl, vl, out=layer.peer.slot(par), peers=layer.peer.peers(par))
             else:
                 layer.plan.attend(ql, kl, vl, out=layer.peer.slot(par))
-                layer.peer.push(par)
+                layer.peer.send(par) if mode == "ce" else layer.peer.push(par)
             layer.peer.wait()
         layer.peer.gathered[par].zero_()
         dist.barrier()
@@ -139,7 +139,7 @@ def _peer_worker(rank, world, port, out_dir, mode="peer"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["peer", "fused"])
+@pytest.mark.parametrize("mode", ["peer", "fused", "ce"])
 def test_peer_gather_equals_nccl_gather(tmp_path, mode):
     """The head outputs written into the peers' gathered buffers over NVLink
     (plain peer stores into IPC buffers: a streaming launch after the
