@@ -152,3 +152,47 @@ def test_peer_gather_equals_nccl_gather(tmp_path, mode):
     mp.start_processes(_peer_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world,
                        join=True, start_method="spawn")
     assert os.path.exists(os.path.join(tmp_path, "peer_ref.pt"))
+
+
+def _missing_rank_worker(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    from cast_b200 import _lib
+    from cast_b200 import distributed as cd
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    pg = None
+    try:
+        pg = cd.PeerGather(1, 2, 880, 128, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        if rank == 0:  # waits for a flag rank 1 never raises
+            pg.wait()
+            try:
+                _lib.check_device(stream, "peer wait")
+                status = "no error"
+            except _lib.CastError as exc:
+                status = str(exc.status)
+            with open(os.path.join(out_dir, "status.txt"), "w") as fh:
+                fh.write(status)
+        torch.cuda.synchronize(dev)
+    finally:
+        if pg is not None:
+            pg.close()
+        dist.destroy_process_group()
+
+
+def test_peer_wait_reports_a_missing_rank(tmp_path):
+    """A rank that makes no call: the other rank's bounded wait for its flag
+    gives up after a second and reports CAST_ERR_DEVICE_TIMEOUT; no hang, no
+    fault, and both ranks leave through the collective close."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    mp.start_processes(_missing_rank_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    with open(os.path.join(tmp_path, "status.txt")) as fh:
+        assert fh.read() == "6"  # CAST_ERR_DEVICE_TIMEOUT
