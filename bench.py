@@ -578,9 +578,9 @@ def main():
     peer = None
     if gathered is not None and args.gather in ("peer", "fused", "ce"):
         peer = cdist.PeerGather(q.shape[0], q.shape[1], q.shape[2], q.shape[3], device=dev)
-        peer_graphs, fused_graphs = [], []
+        peer_graphs, gather_graphs = [], []
         for par in (0, 1):
-            for graphs, with_select in ((peer_graphs, True), (fused_graphs, False)):
+            for graphs, with_select in ((peer_graphs, True), (gather_graphs, False)):
                 gph = torch.cuda.CUDAGraph()
                 side = torch.cuda.Stream(dev)
                 side.wait_stream(stream)
@@ -604,8 +604,8 @@ def main():
             peer_graphs[turn[0] & 1].replay()
             turn[0] += 1
 
-        def fused_step():  # the attention with its fused gather and the wait, alone
-            fused_graphs[turn[0] & 1].replay()
+        def gather_step():  # the attention with its gather and the wait, alone
+            gather_graphs[turn[0] & 1].replay()
             turn[0] += 1
     else:
         step = nccl_step
@@ -626,16 +626,16 @@ def main():
         _lib.check_device(stream.cuda_stream, "fused gather")
     att_ms = timed(g_att.replay, args.steps) / args.steps
     sel_ms = timed(g_sel.replay, args.steps) / args.steps
-    gather_ms = nccl_ms = fused_ms = 0.0
+    gather_ms = nccl_ms = gather_call_ms = 0.0
     if gathered is not None:
         if peer is not None:
-            fused_ms = timed(fused_step, args.steps) / args.steps
+            gather_call_ms = timed(gather_step, args.steps) / args.steps
         gather_ms = timed(lambda: dist.all_gather_into_tensor(gathered, plan.out), args.steps) / args.steps
         if peer is not None:  # the same call with the NCCL all-gather after it, for comparison
             for _ in range(3):
                 nccl_step()
             nccl_ms = timed(nccl_step, args.steps) / args.steps
-            del peer_graphs, fused_graphs
+            del peer_graphs, gather_graphs
             peer.close()
     sel = plan.selection()
     counts_cpu = sel.counts.cpu()
@@ -705,10 +705,10 @@ def main():
 
     # ---- max over ranks
     vals = torch.tensor([total_ms, att_ms, e2e["ms"] if e2e else 0.0, sel_ms, gather_ms,
-                         rollout_ms or 0.0, nccl_ms, fused_ms], dtype=torch.float64, device=dev)
+                         rollout_ms or 0.0, nccl_ms, gather_call_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, att_ms, e2e_ms, sel_ms, gather_ms, rollout_ms, nccl_ms, fused_ms = (
+    total_ms, att_ms, e2e_ms, sel_ms, gather_ms, rollout_ms, nccl_ms, gather_call_ms = (
         float(x) for x in vals.tolist())
     ms_per_step = total_ms / args.steps
     value_us = ms_per_step * 1000.0
@@ -802,10 +802,10 @@ def main():
         if peer is not None:
             link_bytes = (world - 1) * q.numel() * 2  # this rank's heads to every other rank
             t_link = link_bytes / 770e9
-            line["fused_gather_roofline"] = {
-                "kernel_us": fused_ms * 1000.0, "nvlink_bytes_per_gpu": link_bytes,
+            line["peer_gather_roofline"] = {
+                "kernel_us": gather_call_ms * 1000.0, "nvlink_bytes_per_gpu": link_bytes,
                 "link_us": t_link * 1e6, "compute_us": t_alg * 1e6,
-                "frac": max(t_alg, t_link) / (fused_ms * 1e-3),
+                "frac": max(t_alg, t_link) / (gather_call_ms * 1e-3),
                 "note": ("attention with its gather (fused into the epilogue, or the streaming launch "
                          "after it) and the peers' wait (CUDA graph, max over ranks) against the slower of "
                          "its tensor-core roofline and its NVLink bytes at the measured 770 GB/s per "
