@@ -7,8 +7,10 @@ so the layer splits without any exchange on its data path:
 * rollout sharding: independent rollouts (BASELINE config 5 runs 8) go one
   per GPU; no collective at all (weak scaling);
 * head sharding: the H heads of one layer call are split into contiguous
-  ranges, one per GPU, and the bf16 head outputs are all-gathered (the only
-  exchange a layer needs, 2.7 MB per GPU for config 2 at 8 GPUs).
+  ranges, one per GPU, and the bf16 head outputs are gathered on every GPU
+  (the only exchange a layer needs, 2.7 MB per GPU for config 2 at 8 GPUs):
+  by default with plain peer stores over NVLink into IPC-shared buffers
+  (:class:`PeerGather`), else with NCCL's all-gather.
 
 The reference runs on one device and has no collective; this module is the
 B200 partitioning around its per-head arithmetic.
