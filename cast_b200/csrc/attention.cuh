@@ -875,21 +875,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint4 *dst = reinterpret_cast<uint4 *>(p.out + off);
 #pragma unroll
         for (int c = 0; c < 4; ++c) dst[c] = w[c];
-      };
-      // The fused gather: the warp's rows (consecutive, so one contiguous
-      // run of 256-byte rows) read back from L2 and stored to every peer with
-      // coalesced 16-byte stores, while other CTAs still compute.
-      auto peer_copy = [&]() {
-        if (p.n_peers == 0) return;
-        const int nrows = __popc(__ballot_sync(0xffffffffu, row_valid));  // a prefix of the lanes
-        if (nrows == 0) return;
-        __syncwarp();
-        const int qrow0 = __shfl_sync(0xffffffffu, qrow, 0);
-        const size_t off = ((size_t)bh * p.Lq + qrow0) * 128;
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.out + off);
-        for (int i = lane; i < nrows * 16; i += 32) {
-          const uint4 val = __ldcg(src + i);
-          for (int r = 0; r < p.n_peers; ++r) reinterpret_cast<uint4 *>(p.peer_out[r] + off)[i] = val;
+        for (int r = 0; r < p.n_peers; ++r) {
+          uint4 *pd = reinterpret_cast<uint4 *>(p.peer_out[r] + off);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) pd[c] = w[c];
         }
       };
       if (n_live == 1) {
@@ -902,7 +891,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             load_o(cc, o);
             if (row_valid) store_row(cc, *reinterpret_cast<float(*)[32]>(o), inv_l);
           }
-          peer_copy();
           if (row_valid && p.lse)
             p.lse[(size_t)bh * p.Lq + qrow] = l_run > 0.0f ? m_run + __log2f(l_run) : -INFINITY;
         }
@@ -961,7 +949,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
             if (row_valid) store_row(cc, acc, inv_l);
           }
-          peer_copy();
           if (row_valid && p.lse)
             p.lse[(size_t)bh * p.Lq + qrow] = l > 0.0f ? m + __log2f(l) : -INFINITY;
         }
